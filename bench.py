@@ -1,0 +1,477 @@
+"""Benchmark of the FP8 E4M3 quantized-linear hot path on B200.
+
+Workload: one Whisper large-v3 encoder layer's linear set on
+M = 12000 rows (8 streams x 1500 positions): activation quantize -> QKV
+[1280->3840] + bias, quantize -> out-proj [1280->1280] + bias, quantize ->
+fc1 [1280->5120] + bias + GELU whose epilogue emits fc2's E4M3 input codes, and
+fc2 [5120->1280] + bias.  A step is one pass over that set: 4 tcgen05 GEMMs and
+3 quantize kernels = 471.86 GFLOP.  Inputs are seeded synthetic tensors
+(activations ~N(0,1) as after LayerNorm, weights ~N(0,0.02)); static activation
+scales are the calibration rule amax/448 applied once at set-up.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+With N > 1 (under torchrun) every rank runs the same per-GPU workload on its own
+GPU (independent stream batches, no collective on the data path); `value` is
+the whole-job TFLOP/s over the max-over-ranks time.  `--impl reference` times
+the CPU restatement of the reference's Q/DQ linear (oracle/, the reference has
+no CPU implementation of this path) on host cores, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+PACKAGE = "listenflow-fastest-whisper_b200"
+
+M = 12000  # 8 x 1500 encoder positions
+D = 1280
+FFN = 5120
+LINEARS = (  # name, K, N, gelu
+    ("qkv", D, 3 * D, False),
+    ("out_proj", D, D, False),
+    ("fc1", D, FFN, True),
+    ("fc2", FFN, D, False),
+)
+FLOPS_PER_STEP = sum(2 * M * k * n for _, k, n, _ in LINEARS)  # 471.86e9
+METRIC = "FP8 GEMM TFLOP/s (encoder layer linear set, M=12000)"
+CONFIG = {
+    "workload": "C2: Whisper large-v3 encoder layer FP8 linear set (QKV 1280->3840, out 1280->1280, "
+                "fc1 1280->5120 +GELU -> fc2 codes, fc2 5120->1280), M=12000 (8 x 1500 positions)",
+    "m": M,
+    "flops_per_step": FLOPS_PER_STEP,
+    "l2": "256 MiB buffer written between timed steps (outside the step events); the step's working set "
+          "(~330 MB) also exceeds L2",
+}
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--e2e-steps", type=int, default=5)
+    p.add_argument("--cpu-seconds", type=float, default=12.0,
+                   help="target CPU-baseline sample time (0 skips the CPU baseline, for profiling runs)")
+    return p.parse_args(argv)
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+def synthetic(seed: int):
+    """Seeded inputs: three fp16 activation tensors and four fp16 weights/biases."""
+    rng = np.random.default_rng(seed)
+    acts = {
+        "qkv": (rng.standard_normal((M, D), dtype=np.float32)).astype(np.float16),
+        "out_proj": (rng.standard_normal((M, D), dtype=np.float32)).astype(np.float16),
+        "fc1": (rng.standard_normal((M, D), dtype=np.float32)).astype(np.float16),
+    }
+    weights = {}
+    for name, k, n, _ in LINEARS:
+        w = (rng.standard_normal((n, k), dtype=np.float32) * 0.02).astype(np.float16)
+        b = (rng.standard_normal(n, dtype=np.float32) * 0.02).astype(np.float16)
+        weights[name] = (w, b)
+    return acts, weights
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling during the timed region.
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sms, reasons, max_mhz = [], set(), None
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                max_mhz = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": max_mhz,
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+def smi_id(torch, device) -> str:
+    """nvidia-smi --id for a torch device (PCI bus id; CUDA_VISIBLE_DEVICES-safe)."""
+    props = torch.cuda.get_device_properties(device)
+    try:
+        return f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+    except AttributeError:
+        return str(device.index)
+
+
+# ---------------------------------------------------------------------------
+# Our arm.
+
+def run_ours(args, rank, local_rank, world):
+    import torch
+
+    fp8 = importlib.import_module(PACKAGE + ".fp8")
+    native = importlib.import_module(PACKAGE + "._native")
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+
+    acts_np, weights_np = synthetic(seed=1234 + rank)
+    # Static activation scales: the calibration rule (amax/448) applied once.
+    scales = {name: float(np.float32(np.abs(a.astype(np.float32)).max()) / np.float32(448))
+              for name, a in acts_np.items()}
+    stream = torch.cuda.current_stream()
+    acts = {name: torch.from_numpy(a).to(device) for name, a in acts_np.items()}
+    weights = {}
+    for name, k, n, _ in LINEARS:
+        w, b = weights_np[name]
+        weights[name] = fp8.QuantizedWeight.from_half(torch.from_numpy(w).to(device), torch.from_numpy(b).to(device))
+    # fc2's input scale: calibrated on one fc1 pass (fp16 GELU output amax / 448).
+    codes_fc1 = fp8.quantize(acts["fc1"], scales["fc1"])
+    hidden, _ = fp8.linear(codes_fc1, weights["fc1"].codes, weights["fc1"].scales, scales["fc1"],
+                           bias=weights["fc1"].bias, gelu=True)
+    scales["fc2"] = float(hidden.abs().max().float().item()) / 448.0
+    del hidden
+
+    # Output / scratch buffers, allocated once.
+    codes = {name: torch.empty((M, D), dtype=torch.uint8, device=device) for name in acts}
+    fc2_codes = torch.empty((M, FFN), dtype=torch.uint8, device=device)
+    outs = {"qkv": torch.empty((M, 3 * D), dtype=torch.float16, device=device),
+            "out_proj": torch.empty((M, D), dtype=torch.float16, device=device),
+            "fc2": torch.empty((M, D), dtype=torch.float16, device=device)}
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    gemm_flops = {name: 2 * M * k * n for name, k, n, _ in LINEARS}
+
+    def step(events=None):
+        def mark(i):
+            if events is not None:
+                events[i].record(stream)
+        fp8.quantize(acts["qkv"], scales["qkv"], out=codes["qkv"])
+        mark(0)
+        fp8.linear(codes["qkv"], weights["qkv"].codes, weights["qkv"].scales, scales["qkv"],
+                   bias=weights["qkv"].bias, out=outs["qkv"])
+        mark(1)
+        fp8.quantize(acts["out_proj"], scales["out_proj"], out=codes["out_proj"])
+        mark(2)
+        fp8.linear(codes["out_proj"], weights["out_proj"].codes, weights["out_proj"].scales, scales["out_proj"],
+                   bias=weights["out_proj"].bias, out=outs["out_proj"])
+        mark(3)
+        fp8.quantize(acts["fc1"], scales["fc1"], out=codes["fc1"])
+        mark(4)
+        fp8.linear(codes["fc1"], weights["fc1"].codes, weights["fc1"].scales, scales["fc1"],
+                   bias=weights["fc1"].bias, gelu=True, want_y=False, next_scale=scales["fc2"],
+                   next_codes=fc2_codes)
+        mark(5)
+        fp8.linear(fc2_codes, weights["fc2"].codes, weights["fc2"].scales, scales["fc2"],
+                   bias=weights["fc2"].bias, out=outs["fc2"])
+        mark(6)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if native.device_error() != 0:
+        raise RuntimeError("device-side wait timed out during warm-up")
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(8)] for _ in range(args.steps)]
+    launches_before = native.launch_count()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(smi_id(torch, device)) as clocks:
+        for s in range(args.steps):
+            flush.zero_()  # L2 flush, outside the step's events
+            ev[s][7].record(stream)
+            step(ev[s])
+        torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    launches = native.launch_count() - launches_before
+    step_ms = [ev[s][7].elapsed_time(ev[s][6]) for s in range(args.steps)]
+    gemm_ms = [ev[s][0].elapsed_time(ev[s][1]) + ev[s][2].elapsed_time(ev[s][3]) +
+               ev[s][4].elapsed_time(ev[s][5]) + ev[s][5].elapsed_time(ev[s][6]) for s in range(args.steps)]
+    per_gemm = {
+        "qkv": statistics.mean(ev[s][0].elapsed_time(ev[s][1]) for s in range(args.steps)),
+        "out_proj": statistics.mean(ev[s][2].elapsed_time(ev[s][3]) for s in range(args.steps)),
+        "fc1": statistics.mean(ev[s][4].elapsed_time(ev[s][5]) for s in range(args.steps)),
+        "fc2": statistics.mean(ev[s][5].elapsed_time(ev[s][6]) for s in range(args.steps)),
+    }
+    total_ms = sum(step_ms)
+    total_gemm_ms = sum(gemm_ms)
+    if native.device_error() != 0:
+        raise RuntimeError("device-side wait timed out during the timed steps")
+
+    # End to end through the public API with host buffers: pinned fp16
+    # activations in, fp16 results out, every step.
+    import torch as _t
+
+    host_in = {name: _t.from_numpy(a).pin_memory() for name, a in acts_np.items()}
+    host_out = {name: _t.empty(tuple(t.shape), dtype=t.dtype).pin_memory() for name, t in outs.items()}
+    h2d = sum(t.numel() * t.element_size() for t in host_in.values())
+    d2h = sum(t.numel() * t.element_size() for t in host_out.values())
+    e_start, e_end = _t.cuda.Event(enable_timing=True), _t.cuda.Event(enable_timing=True)
+
+    def e2e_step():
+        for name, t in host_in.items():
+            acts[name].copy_(t, non_blocking=True)
+        step()
+        for name, t in host_out.items():
+            t.copy_(outs[name], non_blocking=True)
+
+    e2e_steps = max(1, args.e2e_steps)
+    e2e_step()
+    _t.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    e_start.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e_end.record(stream)
+    _t.cuda.synchronize()
+    e2e_ms = e_start.elapsed_time(e_end)
+
+    # Max over ranks.
+    times = np.array([total_ms, total_gemm_ms, e2e_ms], dtype=np.float64)
+    if dist is not None:
+        t = _t.tensor(times, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        times = t.cpu().numpy()
+    total_ms, total_gemm_ms, e2e_ms = (float(v) for v in times)
+
+    result = None
+    if rank == 0:
+        peaks = read_peaks()
+        ms_per_step = total_ms / args.steps
+        value = world * FLOPS_PER_STEP * args.steps / (total_ms / 1e3) / 1e12
+        gemm_launch_ms = total_gemm_ms / (4 * args.steps)
+        gemm_achieved = FLOPS_PER_STEP / 4 / (gemm_launch_ms / 1e3) / 1e12
+        peak, peak_src = peaks
+        traffic = read_traffic()
+        result = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "e4m3 x e4m3 -> fp32 accumulate, fp16 out",
+            "data": "synthetic (seeded; activations ~N(0,1), weights ~N(0,0.02))",
+            "config": dict(CONFIG, parallelism=f"replicas x{world} (no collective on the data path)"),
+            "impl": "ours",
+            "per_gemm_ms": {k: round(v, 4) for k, v in per_gemm.items()},
+            "per_gemm_tflops": {k: round(gemm_flops[k] / (per_gemm[k] / 1e3) / 1e12, 1) for k in per_gemm},
+            "roofline": {
+                "bound": "tensor",
+                "kernel": "fp8_gemm_kernel (tcgen05 kind::f8f6f4)",
+                "achieved": round(gemm_achieved, 1),
+                "peak": peak,
+                "peak_source": peak_src,
+                "unit": "TFLOP/s",
+                "frac": round(gemm_achieved / peak, 4),
+                "traffic": traffic,
+            },
+            "e2e": {
+                "value": round(world * FLOPS_PER_STEP * e2e_steps / (e2e_ms / 1e3) / 1e12, 2),
+                "unit": "TFLOP/s",
+                "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "api": "fp8.quantize / fp8.linear (C ABI lffw_fp8_quantize / lffw_fp8_linear)",
+            },
+            "gpu_launches": int(launches),
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and args.cpu_seconds > 0:
+            result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def read_peaks():
+    """FP8 dense denominator: MEASURED_PEAKS.json has bf16 only; B200's dense FP8
+    rate is twice its bf16 rate, so the measured burst bf16 figure x 2."""
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        data = json.loads(path.read_text())
+        return round(2 * float(data["bf16_tflops"]), 1), "2 x measured bf16_tflops (burst) of MEASURED_PEAKS.json"
+    except (OSError, KeyError, ValueError):
+        return round(2 * 1590.0, 1), "2 x fallback bf16 1.59 PFLOP/s"
+
+
+def read_traffic():
+    """DRAM bytes per GEMM launch from the committed ncu summary, or None."""
+    path = ROOT / "profiles" / "fp8_gemm_c2_traffic.json"
+    try:
+        return json.loads(path.read_text())["dram_bytes_per_launch"]
+    except (OSError, KeyError, ValueError):
+        return None
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle restatement of the Q/DQ linear on host cores.
+
+def cpu_sample(rows: int, seed: int = 4321):
+    from oracle import oracle
+
+    acts, weights = synthetic_small(rows, seed)
+    prepared = []
+    for name, k, n, gelu in LINEARS:
+        w, b = weights[name]
+        ws = oracle.weight_scales(w)
+        wq = oracle.quantize_rows(w, ws)
+        x = acts[name]
+        s = np.float32(oracle.amax(x)) / np.float32(448)
+        prepared.append((oracle.quantize(x, s), wq, s, ws, b, gelu))
+    return prepared
+
+
+def synthetic_small(rows, seed):
+    rng = np.random.default_rng(seed)
+    acts = {name: (rng.standard_normal((rows, k), dtype=np.float32)).astype(np.float16)
+            for name, k, _, _ in LINEARS}
+    weights = {name: ((rng.standard_normal((n, k), dtype=np.float32) * 0.02).astype(np.float16),
+                      (rng.standard_normal(n, dtype=np.float32) * 0.02).astype(np.float16))
+               for name, k, n, _ in LINEARS}
+    return acts, weights
+
+
+def cpu_step(prepared, threads: int):
+    from oracle import oracle
+
+    for xq, wq, s, ws, b, gelu in prepared:
+        oracle.fp8_linear(xq, wq, s, ws, b, gelu=gelu, threads=threads)
+
+
+def cpu_baseline(target_seconds: float):
+    from oracle import oracle
+
+    threads = oracle.threads()
+    probe_rows = max(threads, 8)
+    prepared = cpu_sample(probe_rows)
+    t0 = time.perf_counter()
+    cpu_step(prepared, threads)
+    probe = time.perf_counter() - t0
+    rows = int(min(M, max(probe_rows, probe_rows * target_seconds / max(probe, 1e-3) / 3)))
+    prepared = cpu_sample(rows)
+    times = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        cpu_step(prepared, threads)
+        times.append(time.perf_counter() - t0)
+    flops = FLOPS_PER_STEP * rows / M
+    return {"value": round(flops / statistics.median(times) / 1e12, 6), "unit": "TFLOP/s", "cores": threads,
+            "kind": "port",
+            "sample": f"{rows} of {M} rows of each of the 4 linears (oracle/lffw_oracle.c, float64 exact "
+                      f"accumulation, {threads} threads), median of 3"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    from oracle import oracle
+
+    threads = oracle.threads()
+    rows = 64
+    prepared = cpu_sample(rows)
+    t0 = time.perf_counter()
+    cpu_step(prepared, threads)
+    probe = time.perf_counter() - t0
+    # Size each step so the whole --steps/--warmup run stays within ~2 minutes.
+    per_step = min(4.0, 120.0 / max(1, args.steps + args.warmup))
+    rows = int(min(M, max(rows, rows * per_step / max(probe, 1e-3))))
+    prepared = cpu_sample(rows)
+    for _ in range(args.warmup):
+        cpu_step(prepared, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_step(prepared, threads)
+    elapsed = time.perf_counter() - t0
+    flops = FLOPS_PER_STEP * rows / M * args.steps
+    value = round(flops / elapsed / 1e12, 6)
+    sample = (f"{rows} of {M} rows of each of the 4 linears per step (CPU restatement oracle/lffw_oracle.c; "
+              f"the reference runs this path inside TensorRT, which has no CPU implementation)")
+    return {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> float64 exact accumulate, fp16 out",
+        "data": "synthetic (seeded)", "config": dict(CONFIG, parallelism="host CPU, rank 0"),
+        "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    rank, local_rank, world = dist_env()
+    if args.impl == "reference":
+        result = run_reference(args, rank, world)
+    else:
+        result = run_ours(args, rank, local_rank, world)
+    if result is not None and rank == 0:
+        print(json.dumps(result), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

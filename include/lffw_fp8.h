@@ -1,0 +1,214 @@
+/*
+ * lffw_fp8.h — C ABI of the B200 (sm_100a) FP8 E4M3 quantized-linear library.
+ *
+ * This is the drop-in boundary for listenflow-fastest-whisper's FP8 Q/DQ linear
+ * and its fp16 projection plugins.  Every pointer argument is caller-owned
+ * device memory unless stated otherwise; `stream` is a cudaStream_t (NULL = the
+ * legacy default stream).  Nothing here allocates device memory except where a
+ * comment says so.  No entry point throws; all return an lffw_status.
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   - FP8 linear:     cpp/src/network_graph.cpp:115-159 (graph::qdq + graph::linear),
+ *                     python/src/listenflow/fastest_whisper/_fp8.py:20-51
+ *   - fused GELU:     cpp/src/network_graph.cpp:168-183 (graph::gelu, graph::fc1)
+ *   - fp16 plugins:   cpp/fc1_plugin.cpp:74-106, cpp/qkv_plugin.cpp:74-107,
+ *                     cpp/plugin.cpp:70-92 (IPluginV3OneRuntime::enqueue) and the
+ *                     kernels they launch, cpp/kernels.cu:10-78
+ *   - plugin creators: cpp/fc1_plugin.cpp:125-155, cpp/qkv_plugin.cpp:126-156,
+ *                     cpp/plugin.cpp:95-153 (getCreators / createPlugin / fields)
+ *   - status codes:   cpp/include/listenflow/whisper_runtime.h:15-23
+ */
+#ifndef LFFW_FP8_H
+#define LFFW_FP8_H
+#include <stddef.h>
+#include <stdint.h>
+
+#define LFFW_FP8_ABI_MAJOR 1
+#define LFFW_FP8_ABI_MINOR 0
+#define LFFW_FP8_API __attribute__((visibility("default")))
+#if defined(__cplusplus)
+#define LFFW_FP8_NOEXCEPT noexcept
+extern "C" {
+#else
+#define LFFW_FP8_NOEXCEPT
+#endif
+
+/* Status values keep the numbering of whisper_runtime.h:17-22; 120+ are new. */
+typedef int32_t lffw_status;
+enum {
+    LFFW_SUCCESS = 0,
+    LFFW_INVALID_ARGUMENT = 1,
+    LFFW_ABI_MISMATCH = 2,
+    LFFW_OUT_OF_MEMORY = 3,
+    LFFW_INTERNAL_ERROR = 4,
+    LFFW_CUDA_ERROR = 6,
+    LFFW_UNSUPPORTED_PRECISION = 9, /* device is not sm_100 (FP8 gate) */
+    LFFW_DEVICE_TIMEOUT = 120       /* a bounded device-side wait expired */
+};
+
+/* Epilogue selection for lffw_fp8_linear. */
+enum { LFFW_EPILOGUE_NONE = 0, LFFW_EPILOGUE_GELU = 1 };
+
+/*
+ * One FP8 Q/DQ linear (replaces graph::linear in fp8 precision,
+ * network_graph.cpp:124-159):
+ *   acc[m,n] = sum_k E4M3(x_codes[m,k]) * E4M3(w_codes[n,k])      fp32 accumulate
+ *   y16      = half(acc * act_scale * w_scales[n])                  MatMul output edge
+ *   y16      = half(y16 + bias[n])                                  if bias
+ *   y16      = GELU with fp16 edges (network_graph.cpp:168-180)     if epilogue == GELU
+ *   y[m,n]   = y16                                                  if y
+ *   next_codes[m,n] = E4M3_rne_sat(fp32(y16 / next_scale))          if next_codes
+ * Layouts are row-major with K (resp. N) contiguous: x_codes [m,k], w_codes
+ * [n,k] (the reference's [out,in] weight, i.e. before its [1,in,out] transpose),
+ * y / next_codes [m,n].  The activation scale is the static `act_scale`, or is
+ * read from device memory when `act_scale_ptr` is non-NULL (dynamic amax/448).
+ * Requirements: m,n,k >= 1; k % 16 == 0; n % 16 == 0; 16-byte aligned pointers;
+ * act_scale (or *act_scale_ptr) finite and > 0; next_scale finite and > 0 when
+ * next_codes is set.
+ */
+typedef struct lffw_fp8_linear_args {
+    size_t struct_size; /* sizeof(lffw_fp8_linear_args) */
+    int64_t m, n, k;
+    const uint8_t *x_codes;
+    float act_scale;
+    const float *act_scale_ptr;
+    const uint8_t *w_codes;
+    const float *w_scales;
+    const uint16_t *bias;
+    int32_t epilogue;
+    uint16_t *y;
+    float next_scale;
+    uint8_t *next_codes;
+} lffw_fp8_linear_args;
+
+LFFW_FP8_API lffw_status lffw_fp8_linear(const lffw_fp8_linear_args *args,
+                                         void *stream) LFFW_FP8_NOEXCEPT;
+
+/* Q of an fp16 activation with one scalar scale (graph::qdq axis 0,
+ * network_graph.cpp:115-123): codes[i] = E4M3_rne_sat(fp32(x[i] / scale)).
+ * `scale_ptr` (device, may be NULL) overrides `scale`. */
+LFFW_FP8_API lffw_status lffw_fp8_quantize(const uint16_t *x, int64_t count, float scale,
+                                           const float *scale_ptr, uint8_t *codes,
+                                           void *stream) LFFW_FP8_NOEXCEPT;
+
+/* Q of an fp16 [rows, cols] weight with one scale per row (the per-output-channel
+ * weight Q of network_graph.cpp:140-152, axis 2 of the transposed constant). */
+LFFW_FP8_API lffw_status lffw_fp8_quantize_rows(const uint16_t *w, int64_t rows, int64_t cols,
+                                                const float *scales, uint8_t *codes,
+                                                void *stream) LFFW_FP8_NOEXCEPT;
+
+/* Per-output-channel weight scales: max|w[r,:]| / 448 in fp32, non-positive -> 1
+ * (network_graph.cpp:140-148, _fp8.py:37-42). */
+LFFW_FP8_API lffw_status lffw_fp8_weight_scales(const uint16_t *w, int64_t rows, int64_t cols,
+                                                float *scales, void *stream) LFFW_FP8_NOEXCEPT;
+
+/* Dynamic activation scale: *scale = amax(|x|)/448 (0 -> 1), NaN ignored, the
+ * calibration rule of python/scripts/calibrate_fp8.py:384-385 applied to one
+ * tensor.  `amax_out` (optional, device) receives the maximum itself. */
+LFFW_FP8_API lffw_status lffw_fp8_dynamic_scale(const uint16_t *x, int64_t count, float *scale,
+                                                float *amax_out, void *stream) LFFW_FP8_NOEXCEPT;
+
+/* fp16 single-token projections of the reference plugins (cpp/kernels.cu:51-78),
+ * rebuilt for sm_100a.  x [width], weight [rows, width] (row = output), all fp16.
+ *   fc1: y[r] = GELU-fp16-edges(half(half(x.W[r]) + bias[r])), rows = 5120, width = 1280
+ *   qkv: y[r] = half((x.W[r] + q_bias[r if r<width]) + v_bias[r-2w if r>=2w]), rows = 3*width */
+LFFW_FP8_API lffw_status lffw_fp16_fc1(const uint16_t *x, const uint16_t *weight,
+                                       const uint16_t *bias, uint16_t *y, int64_t rows,
+                                       int64_t width, void *stream) LFFW_FP8_NOEXCEPT;
+LFFW_FP8_API lffw_status lffw_fp16_qkv(const uint16_t *x, const uint16_t *weight,
+                                       const uint16_t *q_bias, const uint16_t *v_bias,
+                                       uint16_t *y, int64_t width,
+                                       void *stream) LFFW_FP8_NOEXCEPT;
+/* y[i] = half(x[i] + bias) (cpp/kernels.cu:10-17); 1 <= count <= INT32_MAX. */
+LFFW_FP8_API lffw_status lffw_fp16_bias(const uint16_t *x, uint16_t bias_bits, uint16_t *y,
+                                        int64_t count, void *stream) LFFW_FP8_NOEXCEPT;
+
+/* Device gate (replaces the sm86/89/120 gates of cpp/src/precision_policy.hpp:4-7,
+ * cpp/src/runtime_model.hpp:88-92 and cpp/fc1_plugin.cpp:90-98): SUCCESS only
+ * for compute capability 10.0 (B200, sm_100a); UNSUPPORTED_PRECISION otherwise. */
+LFFW_FP8_API lffw_status lffw_device_supported(int32_t device) LFFW_FP8_NOEXCEPT;
+
+/* Reads and clears the calling device's sticky error word, which bounded
+ * device-side waits set when they give up (LFFW_DEVICE_TIMEOUT).  Synchronizes
+ * the device.  `where` (optional) receives the role/site code that gave up. */
+LFFW_FP8_API lffw_status lffw_device_error(int32_t *where) LFFW_FP8_NOEXCEPT;
+
+/* Number of this library's kernels launched by this process so far. */
+LFFW_FP8_API uint64_t lffw_launch_count(void) LFFW_FP8_NOEXCEPT;
+
+LFFW_FP8_API const char *lffw_status_string(lffw_status status) LFFW_FP8_NOEXCEPT;
+LFFW_FP8_API void lffw_version(uint32_t *major, uint32_t *minor) LFFW_FP8_NOEXCEPT;
+
+/* ---- Plugin surface ------------------------------------------------------
+ * A C restatement of the reference's TensorRT IPluginV3 creators
+ * (namespace "listenflow.fastest_whisper"): LffwFp16Fc1 v"1", LffwFp16Qkv v"2",
+ * LffwFp16Bias v"1" with the same field names/types/lengths and the same shape,
+ * dtype and format checks, plus the FP8 family LffwFp8Linear v"1".  A TensorRT
+ * adapter forwards createPlugin / onShapeChange / getWorkspaceSize / enqueue to
+ * these calls one to one.  Enum values equal TensorRT's (DataType,
+ * TensorFormat, PluginFieldType, TensorRTPhase). */
+enum { LFFW_DT_FLOAT = 0, LFFW_DT_HALF = 1, LFFW_DT_INT8 = 2, LFFW_DT_INT32 = 3, LFFW_DT_FP8 = 6 };
+enum { LFFW_FORMAT_LINEAR = 0, LFFW_FORMAT_CHW2 = 1 };
+enum {
+    LFFW_FIELD_FLOAT16 = 0, LFFW_FIELD_FLOAT32 = 1, LFFW_FIELD_FLOAT64 = 2, LFFW_FIELD_INT8 = 3,
+    LFFW_FIELD_INT16 = 4, LFFW_FIELD_INT32 = 5, LFFW_FIELD_CHAR = 6
+};
+enum { LFFW_PHASE_BUILD = 0, LFFW_PHASE_RUNTIME = 1 };
+
+typedef struct lffw_plugin_field {
+    const char *name;
+    const void *data;
+    int32_t type;   /* LFFW_FIELD_* */
+    int32_t length; /* element count */
+} lffw_plugin_field;
+
+typedef struct lffw_tensor_desc {
+    int32_t nb_dims;
+    int64_t dims[8];
+    int32_t type;   /* LFFW_DT_* */
+    int32_t format; /* LFFW_FORMAT_* */
+} lffw_tensor_desc;
+
+typedef struct lffw_plugin lffw_plugin;
+
+/* extern "C" char const tensoracle_bundle_sha256[] of cpp/fc1_plugin.cpp:11,
+ * read by dlsym in network_graph.cpp:196-198 and ctypes in _plugins.py:33:
+ * here the SHA-256 (hex) of the kernel source this library was built from. */
+LFFW_FP8_API extern const char tensoracle_bundle_sha256[65];
+
+LFFW_FP8_API int32_t lffw_plugin_creator_count(void) LFFW_FP8_NOEXCEPT;
+/* Creator i: name, version, namespace and its declared fields (getFieldNames). */
+LFFW_FP8_API int32_t lffw_plugin_creator(int32_t index, const char **name, const char **version,
+                                         const char **plugin_namespace,
+                                         const lffw_plugin_field **fields,
+                                         int32_t *field_count) LFFW_FP8_NOEXCEPT;
+/* createPlugin: NULL when the creator is unknown, the phase is neither BUILD
+ * nor RUNTIME, or the fields are not exactly the declared set with a matching
+ * bundle_sha256 (fc1_plugin.cpp:32-37, 143-150). */
+LFFW_FP8_API lffw_plugin *lffw_plugin_create(const char *name, const char *version,
+                                             const char *plugin_namespace,
+                                             const lffw_plugin_field *fields, int32_t count,
+                                             int32_t phase) LFFW_FP8_NOEXCEPT;
+LFFW_FP8_API lffw_plugin *lffw_plugin_clone(const lffw_plugin *plugin) LFFW_FP8_NOEXCEPT;
+LFFW_FP8_API void lffw_plugin_destroy(lffw_plugin *plugin) LFFW_FP8_NOEXCEPT;
+/* onShapeChange / validate_shape: 0 when the descriptors are accepted, -1 otherwise. */
+LFFW_FP8_API int32_t lffw_plugin_validate(const lffw_plugin *plugin,
+                                          const lffw_tensor_desc *inputs, int32_t input_count,
+                                          const lffw_tensor_desc *output) LFFW_FP8_NOEXCEPT;
+/* getWorkspaceSize (bytes).  fp16 plugins: 0.  LffwFp8Linear with a HALF input:
+ * the E4M3 codes of that input (rows * k bytes, rounded up to 256). */
+LFFW_FP8_API int64_t lffw_plugin_workspace_size(const lffw_plugin *plugin,
+                                                const lffw_tensor_desc *inputs,
+                                                int32_t input_count) LFFW_FP8_NOEXCEPT;
+/* enqueue: 0 on success, -1 on a null pointer, wrong dtype/format/shape, an
+ * unsupported device or a launch failure (fc1_plugin.cpp:74-106). */
+LFFW_FP8_API int32_t lffw_plugin_enqueue(const lffw_plugin *plugin,
+                                         const lffw_tensor_desc *input_desc,
+                                         const lffw_tensor_desc *output_desc,
+                                         const void *const *inputs, void *const *outputs,
+                                         void *workspace, void *stream) LFFW_FP8_NOEXCEPT;
+
+#if defined(__cplusplus)
+}
+#endif
+#endif

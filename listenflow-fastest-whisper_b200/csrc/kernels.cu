@@ -1,0 +1,931 @@
+// sm_100a kernels of the FP8 E4M3 quantized-linear hot path.
+//
+//   fp8_gemm_kernel      tcgen05 kind::f8f6f4 GEMM, TMA-fed mbarrier ring, fp32
+//                        accumulators in TMEM (double buffered), fused epilogue
+//                        (per-channel scale, fp16 bias, fp16-edge GELU, fp16 out
+//                        and/or E4M3 codes for the next linear), TMA stores.
+//   fp8_gemv_kernel      small-M (decoder step) linear on CUDA cores: 128-bit
+//                        streaming of the E4M3 weight rows, warp-shuffle reduce.
+//   quantize kernels     fp16 -> E4M3 with a scalar or per-row scale.
+//   scale kernels        per-row weight scales, dynamic activation amax/448.
+//   fp16 projections     sm_100a rebuild of the reference plugins' fc1/qkv/bias.
+//
+// Semantics follow the reference's TensorRT graph: cpp/src/network_graph.cpp
+// :115-159 (Q/DQ + MatMul + bias) and :168-180 (GELU with fp16 edges), and the
+// fp16 plugin kernels of cpp/kernels.cu:10-78.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstring>
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "launch.h"
+#include "ptx.cuh"
+
+namespace lffw {
+
+namespace {
+std::atomic<uint64_t> g_launches{0};
+}
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
+
+// ---------------------------------------------------------------------------
+// Scalar helpers.  Explicit .rn on the f16 ops keeps ptxas from contracting a
+// multiply and an add into one fma: every fp16 graph edge rounds on its own.
+
+__device__ __forceinline__ float h2f(uint16_t h)
+{
+    float f;
+    asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"(h));
+    return f;
+}
+
+__device__ __forceinline__ uint16_t f2h_rn(float f)
+{
+    uint16_t h;
+    asm("cvt.rn.f16.f32 %0, %1;" : "=h"(h) : "f"(f));
+    return h;
+}
+
+__device__ __forceinline__ uint16_t hadd_rn(uint16_t a, uint16_t b)
+{
+    uint16_t r;
+    asm("add.rn.f16 %0, %1, %2;" : "=h"(r) : "h"(a), "h"(b));
+    return r;
+}
+
+__device__ __forceinline__ uint16_t hmul_rn(uint16_t a, uint16_t b)
+{
+    uint16_t r;
+    asm("mul.rn.f16 %0, %1, %2;" : "=h"(r) : "h"(a), "h"(b));
+    return r;
+}
+
+// GELU with the reference graph's fp16 edges: (x*0.5)*(1+erf(x*fp16(2^-1/2))).
+__device__ __forceinline__ uint16_t gelu_fp16_edges(uint16_t x)
+{
+    constexpr uint16_t kInvSqrt2 = 0x39A8; // 0.70703125 = fp16(2^-0.5)
+    constexpr uint16_t kHalf = 0x3800;
+    constexpr uint16_t kOne = 0x3C00;
+    uint16_t scaled = hmul_rn(x, kInvSqrt2);
+    uint16_t erf16 = f2h_rn(erff(h2f(scaled)));
+    uint16_t left = hmul_rn(x, kHalf);
+    uint16_t right = hadd_rn(kOne, erf16);
+    return hmul_rn(left, right);
+}
+
+// Two fp32 values -> two E4M3 codes (round to nearest even, saturate finite);
+// `lo` lands in the low byte.
+__device__ __forceinline__ uint16_t e4m3x2(float lo, float hi)
+{
+    uint16_t r;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+// Q of one fp16 value: fp32 IEEE quotient, then E4M3.
+__device__ __forceinline__ float q_quotient(uint16_t h, float scale)
+{
+    return __fdiv_rn(h2f(h), scale);
+}
+
+// ---------------------------------------------------------------------------
+// FP8 GEMM (tcgen05)
+
+namespace gemm {
+
+constexpr int kBM = 128;       // tile rows (TMEM lanes)
+constexpr int kBK = 128;       // K bytes per stage = one 128B swizzle row
+constexpr int kUmmaK = 32;     // K of one kind::f8f6f4 MMA
+constexpr int kThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int kEpiThreads = 128;
+constexpr int kChunk = 64;                         // epilogue columns per store
+constexpr int kYStageBytes = kBM * kChunk * 2;     // 128 rows x 128 B (SW128)
+constexpr int kCStageBytes = kBM * kChunk;         // 128 rows x 64 B  (SW64)
+
+template <int BN>
+struct Cfg {
+    static constexpr int kStages = BN == 256 ? 4 : 6;
+    static constexpr int kABytes = kBM * kBK;
+    static constexpr int kBBytes = BN * kBK;
+    static constexpr int kTmemCols = 2 * BN;
+    static constexpr int kOffB = kStages * kABytes;
+    static constexpr int kOffY = kOffB + kStages * kBBytes;
+    static constexpr int kOffC = kOffY + kYStageBytes;
+    static constexpr int kOffBar = kOffC + kCStageBytes;
+    static constexpr int kNumBars = 2 * kStages + 5; // full, empty, acc_full x2, acc_empty x2, drain
+    static constexpr int kOffSlot = kOffBar + kNumBars * 8;
+    static constexpr int kSmemBytes = kOffSlot + 16 + 1024; // + base alignment slack
+    static_assert(kSmemBytes <= 232448, "shared memory budget");
+    static_assert(kTmemCols <= 512, "TMEM columns");
+};
+
+struct Params {
+    int m, n, k;
+    int m_tiles, num_tiles, num_kb;
+    float act_scale;
+    const float *act_scale_ptr;
+    const float *w_scales;
+    const uint16_t *bias;
+    float next_scale;
+    int gelu, write_y, write_codes;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    fp8_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                    const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_c,
+                    const Params p)
+{
+    using C = Cfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+    const uint32_t sbase = smem_u32(smem);
+
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    const uint32_t bar_full = sbase + C::kOffBar;
+    const uint32_t bar_empty = bar_full + 8 * C::kStages;
+    const uint32_t bar_acc_full = bar_empty + 8 * C::kStages;
+    const uint32_t bar_acc_empty = bar_acc_full + 16;
+    const uint32_t bar_drain = bar_acc_empty + 16;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::kOffSlot);
+
+    if (threadIdx.x == 0) {
+        reinterpret_cast<volatile int *>(smem + C::kOffSlot)[1] = 0; // epilogue abort flag
+        for (int s = 0; s < C::kStages; ++s) {
+            mbar_init(bar_full + 8 * s, 1);
+            mbar_init(bar_empty + 8 * s, 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(bar_acc_full + 8 * a, 1);
+            mbar_init(bar_acc_empty + 8 * a, kEpiThreads);
+        }
+        mbar_init(bar_drain, 1);
+        fence_barrier_init();
+        prefetch_tensor_map(&tm_a);
+        prefetch_tensor_map(&tm_b);
+        if (p.write_y)
+            prefetch_tensor_map(&tm_y);
+        if (p.write_codes)
+            prefetch_tensor_map(&tm_c);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer (one thread) ----------------
+        if (lane == 0) {
+            uint32_t used_mask = 0, parity_mask = 0;
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+                const int m0 = (t % p.m_tiles) * kBM;
+                const int n0 = (t / p.m_tiles) * BN;
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(bar_empty + 8 * s, ph ^ 1u, kSiteProducerEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t full = bar_full + 8 * s;
+                    mbar_arrive_expect_tx(full, C::kABytes + C::kBBytes);
+                    tma_load_2d(sbase + s * C::kABytes, &tm_a, full, kb * kBK, m0);
+                    tma_load_2d(sbase + C::kOffB + s * C::kBBytes, &tm_b, full, kb * kBK, n0);
+                    used_mask |= 1u << s;
+                    parity_mask = (parity_mask & ~(1u << s)) | (ph << s);
+                    if (++s == C::kStages) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+            }
+            // Every issued load must land before the CTA's shared memory is released.
+            for (int i = 0; i < C::kStages; ++i)
+                if (used_mask & (1u << i)) {
+                    const uint32_t par = (parity_mask >> i) & 1u;
+                    for (int tries = 0; tries < (1 << 22) && !mbar_try_wait(bar_full + 8 * i, par); ++tries) {
+                    }
+                }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (one thread) ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_e4m3_f32<kBM, BN>();
+            int s = 0;
+            uint32_t ph = 0;
+            int local = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x, ++local) {
+                const uint32_t a = local & 1;
+                const uint32_t acc_ph = (local >> 1) & 1;
+                if (!mbar_wait(bar_acc_empty + 8 * a, acc_ph ^ 1u, kSiteMmaAccEmpty)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + a * BN;
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(bar_full + 8 * s, ph, kSiteMmaFull)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = sbase + s * C::kABytes;
+                    const uint32_t b_addr = sbase + C::kOffB + s * C::kBBytes;
+#pragma unroll
+                    for (int k = 0; k < kBK / kUmmaK; ++k) {
+                        const uint64_t da = smem_desc_k_sw128(a_addr + k * kUmmaK);
+                        const uint64_t db = smem_desc_k_sw128(b_addr + k * kUmmaK);
+                        mma_f8f6f4(d_tmem, da, db, idesc, (kb | k) != 0);
+                    }
+                    mma_commit(bar_empty + 8 * s); // frees the stage once these MMAs finish
+                    if (++s == C::kStages) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+                if (ok)
+                    mma_commit(bar_acc_full + 8 * a);
+            }
+            // Drain: all MMAs issued by this thread complete before TMEM is freed.
+            mma_commit(bar_drain);
+            for (int tries = 0; tries < (1 << 22) && !mbar_try_wait(bar_drain, 0); ++tries) {
+            }
+        }
+    } else {
+        // ---------------- Epilogue (4 warps, one TMEM lane = one row each) ----------------
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const int epi_tid = threadIdx.x - 64;
+        const float act_scale = p.act_scale_ptr ? *p.act_scale_ptr : p.act_scale;
+        const float next_scale = p.next_scale;
+        const uint32_t y_stage = sbase + C::kOffY;
+        const uint32_t c_stage = sbase + C::kOffC;
+        uint8_t *y_stage_ptr = smem + C::kOffY;
+        uint8_t *c_stage_ptr = smem + C::kOffC;
+        volatile int *epi_abort = reinterpret_cast<volatile int *>(smem + C::kOffSlot + 4);
+        int local = 0;
+        for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
+            const int m0 = (t % p.m_tiles) * kBM;
+            const int n0 = (t / p.m_tiles) * BN;
+            const uint32_t a = local & 1;
+            const uint32_t acc_ph = (local >> 1) & 1;
+            // All 128 epilogue threads take the same exit decision: the named
+            // barriers below would otherwise wait for threads that left.
+            if (!mbar_wait(bar_acc_full + 8 * a, acc_ph, kSiteEpilogueAccFull))
+                *epi_abort = 1;
+            named_barrier_sync(1, kEpiThreads);
+            if (*epi_abort)
+                break;
+            tc_fence_after();
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN;
+            // Chunks that start at or beyond N hold only padding: no TMA store
+            // starts outside the tensor.
+            const int chunks = min(BN / kChunk, (p.n - n0 + kChunk - 1) / kChunk);
+#pragma unroll 1
+            for (int c = 0; c < chunks; ++c) {
+                uint32_t v[kChunk];
+                tmem_ld_32x32b_x32(t_row + c * kChunk, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+                tmem_ld_32x32b_x32(t_row + c * kChunk + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+                tmem_wait_ld();
+                if (c == chunks - 1) {
+                    tc_fence_before();
+                    mbar_arrive(bar_acc_empty + 8 * a);
+                }
+                const int n_base = n0 + c * kChunk;
+#pragma unroll
+                for (int g = 0; g < kChunk / 8; ++g) {
+                    const int col0 = n_base + g * 8;
+                    float cs[8];
+                    uint16_t bb[8];
+                    if (col0 < p.n) {
+                        const float4 s0 = __ldg(reinterpret_cast<const float4 *>(p.w_scales + col0));
+                        const float4 s1 = __ldg(reinterpret_cast<const float4 *>(p.w_scales + col0) + 1);
+                        cs[0] = act_scale * s0.x; cs[1] = act_scale * s0.y;
+                        cs[2] = act_scale * s0.z; cs[3] = act_scale * s0.w;
+                        cs[4] = act_scale * s1.x; cs[5] = act_scale * s1.y;
+                        cs[6] = act_scale * s1.z; cs[7] = act_scale * s1.w;
+                        if (p.bias) {
+                            const uint4 braw = __ldg(reinterpret_cast<const uint4 *>(p.bias + col0));
+                            memcpy(bb, &braw, 16);
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            cs[i] = 0.0f;
+                            bb[i] = 0;
+                        }
+                    }
+                    uint16_t out[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        uint16_t z = f2h_rn(__uint_as_float(v[g * 8 + i]) * cs[i]);
+                        if (p.bias)
+                            z = hadd_rn(z, bb[i]);
+                        if (p.gelu)
+                            z = gelu_fp16_edges(z);
+                        out[i] = z;
+                    }
+                    if (p.write_y) {
+                        uint4 pk;
+                        memcpy(&pk, out, 16);
+                        const uint32_t chunk = static_cast<uint32_t>(g) ^ static_cast<uint32_t>(row & 7);
+                        *reinterpret_cast<uint4 *>(y_stage_ptr + row * 128 + chunk * 16) = pk;
+                    }
+                    if (p.write_codes) {
+                        uint16_t q[4];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            q[i] = e4m3x2(q_quotient(out[2 * i], next_scale),
+                                          q_quotient(out[2 * i + 1], next_scale));
+                        uint2 pk;
+                        memcpy(&pk, q, 8);
+                        const uint32_t chunk = static_cast<uint32_t>(g >> 1) ^ static_cast<uint32_t>((row >> 1) & 3);
+                        *reinterpret_cast<uint2 *>(c_stage_ptr + row * 64 + chunk * 16 + (g & 1) * 8) = pk;
+                    }
+                }
+                fence_proxy_async_smem();
+                named_barrier_sync(1, kEpiThreads);
+                if (epi_tid == 0) {
+                    if (p.write_y)
+                        tma_store_2d(&tm_y, y_stage, n_base, m0);
+                    if (p.write_codes)
+                        tma_store_2d(&tm_c, c_stage, n_base, m0);
+                    bulk_commit_group();
+                    bulk_wait_group_read0();
+                }
+                named_barrier_sync(1, kEpiThreads);
+            }
+        }
+        if (epi_tid == 0)
+            bulk_wait_group0();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::kTmemCols);
+    }
+}
+
+} // namespace gemm
+
+// ---------------------------------------------------------------------------
+// Small-M FP8 linear on CUDA cores (decoder step).
+
+namespace gemv {
+
+constexpr int kThreads = 256;
+constexpr int kRowsPerBlock = kThreads / 32; // one output row (n) per warp
+
+struct Params {
+    int m, n, k;
+    const uint8_t *x_codes;
+    const uint8_t *w_codes;
+    float act_scale;
+    const float *act_scale_ptr;
+    const float *w_scales;
+    const uint16_t *bias;
+    int gelu;
+    uint16_t *y;
+    float next_scale;
+    uint8_t *next_codes;
+};
+
+__device__ __forceinline__ uint4 ld_stream(const void *p)
+{
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void e4m3x16_to_f32(const uint4 &raw, float (&f)[16])
+{
+    const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const __nv_fp8x2_storage_t pair = static_cast<__nv_fp8x2_storage_t>(words[w] >> (16 * h));
+            const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3);
+            f[w * 4 + h * 2 + 0] = h2f(hr.x);
+            f[w * 4 + h * 2 + 1] = h2f(hr.y);
+        }
+    }
+}
+
+template <int MT>
+__global__ void __launch_bounds__(kThreads) fp8_gemv_kernel(const Params p)
+{
+    extern __shared__ uint4 xs[]; // [m][k/16] E4M3 codes
+    const int chunks = p.k / 16;
+    const int total = p.m * chunks;
+    const uint4 *xg = reinterpret_cast<const uint4 *>(p.x_codes);
+    for (int i = threadIdx.x; i < total; i += kThreads)
+        xs[i] = xg[i];
+    __syncthreads();
+
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    const int n = blockIdx.x * kRowsPerBlock + warp;
+    if (n >= p.n)
+        return;
+    float acc[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+        acc[m] = 0.0f;
+    const uint8_t *wrow = p.w_codes + static_cast<size_t>(n) * p.k;
+    for (int c = lane; c < chunks; c += 32) {
+        float wf[16];
+        e4m3x16_to_f32(ld_stream(wrow + static_cast<size_t>(c) * 16), wf);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            if (m < p.m) {
+                float xf[16];
+                e4m3x16_to_f32(xs[m * chunks + c], xf);
+                float s = acc[m];
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    s = fmaf(xf[i], wf[i], s);
+                acc[m] = s;
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+#pragma unroll
+        for (int off = 16; off > 0; off /= 2)
+            acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], off);
+    }
+    const float act_scale = p.act_scale_ptr ? *p.act_scale_ptr : p.act_scale;
+    const float cs = act_scale * p.w_scales[n];
+    const uint16_t b = p.bias ? p.bias[n] : 0;
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+        if (m < p.m && lane == (m & 31)) {
+            uint16_t z = f2h_rn(acc[m] * cs);
+            if (p.bias)
+                z = hadd_rn(z, b);
+            if (p.gelu)
+                z = gelu_fp16_edges(z);
+            const size_t o = static_cast<size_t>(m) * p.n + n;
+            if (p.y)
+                p.y[o] = z;
+            if (p.next_codes) {
+                const float q = q_quotient(z, p.next_scale);
+                p.next_codes[o] = static_cast<uint8_t>(e4m3x2(q, 0.0f) & 0xFF);
+            }
+        }
+    }
+}
+
+} // namespace gemv
+
+// ---------------------------------------------------------------------------
+// Quantize / scale kernels.
+
+namespace quant {
+
+constexpr int kThreads = 256;
+
+__global__ void __launch_bounds__(kThreads)
+    quantize_kernel(const uint16_t *__restrict__ x, int64_t count, float scale_value,
+                    const float *scale_ptr, uint8_t *__restrict__ codes)
+{
+    const float scale = scale_ptr ? *scale_ptr : scale_value;
+    const int64_t groups = count / 16;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+    for (int64_t g = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; g < groups; g += stride) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(x + g * 16);
+        uint4 h[2] = {src[0], src[1]};
+        uint16_t hv[16];
+        memcpy(hv, h, 32);
+        uint16_t q[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            q[i] = e4m3x2(q_quotient(hv[2 * i], scale), q_quotient(hv[2 * i + 1], scale));
+        uint4 out;
+        memcpy(&out, q, 16);
+        *reinterpret_cast<uint4 *>(codes + g * 16) = out;
+    }
+    // Tail (count % 16), handled by the first threads of block 0.
+    if (blockIdx.x == 0) {
+        const int64_t i = groups * 16 + threadIdx.x;
+        if (i < count)
+            codes[i] = static_cast<uint8_t>(e4m3x2(q_quotient(x[i], scale), 0.0f) & 0xFF);
+    }
+}
+
+// codes[r, :] = Q(w[r, :] / scales[r]); grid.x = row, grid.y strides the row.
+__global__ void __launch_bounds__(kThreads)
+    quantize_rows_kernel(const uint16_t *__restrict__ w, int64_t cols, const float *__restrict__ scales,
+                         uint8_t *__restrict__ codes)
+{
+    const int64_t r = blockIdx.x;
+    const float scale = scales[r];
+    const uint16_t *src = w + r * cols;
+    uint8_t *dst = codes + r * cols;
+    for (int64_t c = static_cast<int64_t>(blockIdx.y) * kThreads + threadIdx.x; c < cols;
+         c += static_cast<int64_t>(gridDim.y) * kThreads)
+        dst[c] = static_cast<uint8_t>(e4m3x2(q_quotient(src[c], scale), 0.0f) & 0xFF);
+}
+
+__device__ __forceinline__ float block_max(float v)
+{
+    __shared__ float partial[kThreads / 32];
+#pragma unroll
+    for (int off = 16; off > 0; off /= 2)
+        v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+    if (threadIdx.x % 32 == 0)
+        partial[threadIdx.x / 32] = v;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        v = threadIdx.x < kThreads / 32 ? partial[threadIdx.x] : 0.0f;
+#pragma unroll
+        for (int off = 16; off > 0; off /= 2)
+            v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+    }
+    return v;
+}
+
+// One block per weight row: scale = max|w| / 448 (IEEE division), <= 0 -> 1.
+__global__ void __launch_bounds__(kThreads)
+    weight_scales_kernel(const uint16_t *__restrict__ w, int64_t cols, float *__restrict__ scales)
+{
+    const uint16_t *row = w + static_cast<int64_t>(blockIdx.x) * cols;
+    float best = 0.0f;
+    for (int64_t c = threadIdx.x; c < cols; c += kThreads)
+        best = fmaxf(best, fabsf(h2f(row[c]))); // fmaxf drops NaN
+    best = block_max(best);
+    if (threadIdx.x == 0) {
+        const float s = __fdiv_rn(best, 448.0f);
+        scales[blockIdx.x] = s > 0.0f ? s : 1.0f;
+    }
+}
+
+// amax over the whole tensor into *bits (non-negative float bit patterns order as ints).
+__global__ void __launch_bounds__(kThreads)
+    amax_kernel(const uint16_t *__restrict__ x, int64_t count, int *bits)
+{
+    float best = 0.0f;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < count; i += stride)
+        best = fmaxf(best, fabsf(h2f(x[i])));
+    best = block_max(best);
+    if (threadIdx.x == 0)
+        atomicMax(bits, __float_as_int(best));
+}
+
+__global__ void finalize_scale_kernel(float *scale, float *amax_out)
+{
+    const float amax = *scale; // holds the amax bits written by amax_kernel
+    if (amax_out)
+        *amax_out = amax;
+    *scale = amax > 0.0f ? __fdiv_rn(amax, 448.0f) : 1.0f;
+}
+
+} // namespace quant
+
+// ---------------------------------------------------------------------------
+// fp16 single-token projections (the reference plugins' kernels on sm_100a).
+
+namespace proj {
+
+constexpr int kThreads = 256;
+
+// One warp per output row; each lane streams 8 halves per 128-bit load.
+template <bool kFc1>
+__global__ void __launch_bounds__(kThreads)
+    fp16_projection_kernel(const uint16_t *__restrict__ x, const uint16_t *__restrict__ w,
+                           const uint16_t *__restrict__ b0, const uint16_t *__restrict__ b1,
+                           uint16_t *__restrict__ y, int rows, int width)
+{
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    const int chunks = width / 8;
+    for (int r = blockIdx.x * (kThreads / 32) + warp; r < rows; r += gridDim.x * (kThreads / 32)) {
+        const uint16_t *wrow = w + static_cast<size_t>(r) * width;
+        float acc = 0.0f;
+        for (int c = lane; c < chunks; c += 32) {
+            const uint4 wv = gemv::ld_stream(wrow + c * 8);
+            const uint4 xv = __ldg(reinterpret_cast<const uint4 *>(x) + c);
+            uint16_t wh[8], xh[8];
+            memcpy(wh, &wv, 16);
+            memcpy(xh, &xv, 16);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                acc = fmaf(h2f(xh[i]), h2f(wh[i]), acc); // fp16 x fp16 products are exact in fp32
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off /= 2)
+            acc += __shfl_xor_sync(0xffffffffu, acc, off);
+        if (lane == 0) {
+            if (kFc1) {
+                const uint16_t value = hadd_rn(f2h_rn(acc), b0[r]);
+                y[r] = gelu_fp16_edges(value);
+            } else {
+                const float q = r < width ? h2f(b0[r]) : 0.0f;
+                const float v = r >= 2 * width ? h2f(b1[r - 2 * width]) : 0.0f;
+                y[r] = f2h_rn(__fadd_rn(__fadd_rn(acc, q), v));
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads)
+    fp16_bias_kernel(const uint16_t *__restrict__ x, uint16_t bias, uint16_t *__restrict__ y,
+                     uint32_t count)
+{
+    const float b = h2f(bias);
+    for (uint32_t i = blockIdx.x * kThreads + threadIdx.x; i < count; i += gridDim.x * kThreads)
+        y[i] = f2h_rn(__fadd_rn(h2f(x[i]), b));
+}
+
+} // namespace proj
+
+// ---------------------------------------------------------------------------
+// Host side.
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled()
+{
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult status{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &status) ==
+                cudaSuccess &&
+            status == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    });
+    return fn;
+}
+
+// 2-D row-major tensor [rows, cols] with `elem` bytes per element.
+bool make_map(CUtensorMap *map, CUtensorMapDataType type, int elem, const void *base, int64_t rows,
+              int64_t cols, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle)
+{
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn)
+        return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * elem)};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t estrides[2] = {1, 1};
+    return fn(map, type, 2, const_cast<void *>(base), dims, strides, box, estrides,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+constexpr int kMaxDevices = 64;
+
+int current_device()
+{
+    int device = 0;
+    cudaGetDevice(&device);
+    return device >= 0 && device < kMaxDevices ? device : 0;
+}
+
+int sm_count()
+{
+    static std::atomic<int> cache[kMaxDevices];
+    const int device = current_device();
+    int count = cache[device].load(std::memory_order_relaxed);
+    if (count <= 0) {
+        cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, device);
+        count = count > 0 ? count : 148;
+        cache[device].store(count, std::memory_order_relaxed);
+    }
+    return count;
+}
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device).
+// Keyed by the kernel's address: template instances share a pointer type.
+template <class Kernel>
+cudaError_t ensure_smem(Kernel kernel, int bytes)
+{
+    static std::mutex lock;
+    static std::set<std::pair<const void *, int>> done;
+    const std::pair<const void *, int> key{reinterpret_cast<const void *>(kernel), current_device()};
+    std::lock_guard<std::mutex> guard(lock);
+    if (done.count(key))
+        return cudaSuccess;
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (err == cudaSuccess)
+        done.insert(key);
+    return err;
+}
+
+template <int BN>
+cudaError_t run_gemm(const LinearLaunch &L, cudaStream_t stream)
+{
+    using C = gemm::Cfg<BN>;
+    CUtensorMap tm_a{}, tm_b{}, tm_y{}, tm_c{};
+    if (!make_map(&tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.x_codes, L.m, L.k, gemm::kBK, gemm::kBM,
+                  CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.w_codes, L.n, L.k, gemm::kBK, BN,
+                  CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    if (L.y && !make_map(&tm_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.y, L.m, L.n, gemm::kChunk,
+                         gemm::kBM, CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    if (L.next_codes && !make_map(&tm_c, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.next_codes, L.m, L.n,
+                                  gemm::kChunk, gemm::kBM, CU_TENSOR_MAP_SWIZZLE_64B))
+        return cudaErrorInvalidValue;
+    gemm::Params p{};
+    p.m = static_cast<int>(L.m);
+    p.n = static_cast<int>(L.n);
+    p.k = static_cast<int>(L.k);
+    p.m_tiles = static_cast<int>((L.m + gemm::kBM - 1) / gemm::kBM);
+    const int n_tiles = static_cast<int>((L.n + BN - 1) / BN);
+    p.num_tiles = p.m_tiles * n_tiles;
+    p.num_kb = static_cast<int>((L.k + gemm::kBK - 1) / gemm::kBK);
+    p.act_scale = L.act_scale;
+    p.act_scale_ptr = L.act_scale_ptr;
+    p.w_scales = L.w_scales;
+    p.bias = L.bias;
+    p.next_scale = L.next_scale;
+    p.gelu = L.gelu ? 1 : 0;
+    p.write_y = L.y ? 1 : 0;
+    p.write_codes = L.next_codes ? 1 : 0;
+
+    const cudaError_t attr = ensure_smem(gemm::fp8_gemm_kernel<BN>, C::kSmemBytes);
+    if (attr != cudaSuccess)
+        return attr;
+    const int grid = std::min(p.num_tiles, sm_count());
+    gemm::fp8_gemm_kernel<BN><<<grid, gemm::kThreads, C::kSmemBytes, stream>>>(tm_a, tm_b, tm_y, tm_c, p);
+    count_launch();
+    return cudaGetLastError();
+}
+
+} // namespace
+
+cudaError_t launch_fp8_gemm(const LinearLaunch &L, cudaStream_t stream)
+{
+    const int64_t m_tiles = (L.m + gemm::kBM - 1) / gemm::kBM;
+    const int64_t tiles256 = m_tiles * ((L.n + 255) / 256);
+    if (tiles256 >= sm_count())
+        return run_gemm<256>(L, stream);
+    return run_gemm<128>(L, stream);
+}
+
+cudaError_t launch_fp8_gemv(const LinearLaunch &L, cudaStream_t stream)
+{
+    gemv::Params p{};
+    p.m = static_cast<int>(L.m);
+    p.n = static_cast<int>(L.n);
+    p.k = static_cast<int>(L.k);
+    p.x_codes = L.x_codes;
+    p.w_codes = L.w_codes;
+    p.act_scale = L.act_scale;
+    p.act_scale_ptr = L.act_scale_ptr;
+    p.w_scales = L.w_scales;
+    p.bias = L.bias;
+    p.gelu = L.gelu ? 1 : 0;
+    p.y = L.y;
+    p.next_scale = L.next_scale;
+    p.next_codes = L.next_codes;
+    const size_t smem = static_cast<size_t>(L.m) * static_cast<size_t>(L.k);
+    const dim3 grid(static_cast<unsigned>((L.n + gemv::kRowsPerBlock - 1) / gemv::kRowsPerBlock));
+    cudaError_t err;
+    auto go = [&](auto kernel) {
+        err = ensure_smem(kernel, static_cast<int>(kGemvMaxSmem));
+        if (err != cudaSuccess)
+            return;
+        kernel<<<grid, gemv::kThreads, smem, stream>>>(p);
+        count_launch();
+        err = cudaGetLastError();
+    };
+    if (L.m <= 8)
+        go(gemv::fp8_gemv_kernel<8>);
+    else if (L.m <= 16)
+        go(gemv::fp8_gemv_kernel<16>);
+    else
+        go(gemv::fp8_gemv_kernel<32>);
+    return err;
+}
+
+cudaError_t launch_quantize(const uint16_t *x, int64_t count, float scale, const float *scale_ptr,
+                            uint8_t *codes, cudaStream_t stream)
+{
+    const int64_t groups = count / 16;
+    int64_t blocks = (groups + quant::kThreads - 1) / quant::kThreads;
+    blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, static_cast<int64_t>(sm_count()) * 8));
+    quant::quantize_kernel<<<static_cast<unsigned>(blocks), quant::kThreads, 0, stream>>>(
+        x, count, scale, scale_ptr, codes);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_rows(const uint16_t *w, int64_t rows, int64_t cols, const float *scales,
+                                 uint8_t *codes, cudaStream_t stream)
+{
+    const int64_t yblocks = std::min<int64_t>((cols + quant::kThreads - 1) / quant::kThreads, 16);
+    const dim3 grid(static_cast<unsigned>(rows), static_cast<unsigned>(yblocks));
+    quant::quantize_rows_kernel<<<grid, quant::kThreads, 0, stream>>>(w, cols, scales, codes);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_weight_scales(const uint16_t *w, int64_t rows, int64_t cols, float *scales,
+                                 cudaStream_t stream)
+{
+    quant::weight_scales_kernel<<<static_cast<unsigned>(rows), quant::kThreads, 0, stream>>>(w, cols, scales);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dynamic_scale(const uint16_t *x, int64_t count, float *scale, float *amax_out,
+                                 cudaStream_t stream)
+{
+    cudaError_t err = cudaMemsetAsync(scale, 0, sizeof(float), stream);
+    if (err != cudaSuccess)
+        return err;
+    int64_t blocks = (count + quant::kThreads - 1) / quant::kThreads;
+    blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, static_cast<int64_t>(sm_count()) * 4));
+    quant::amax_kernel<<<static_cast<unsigned>(blocks), quant::kThreads, 0, stream>>>(
+        x, count, reinterpret_cast<int *>(scale));
+    count_launch();
+    quant::finalize_scale_kernel<<<1, 1, 0, stream>>>(scale, amax_out);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_fp16_fc1(const uint16_t *x, const uint16_t *w, const uint16_t *bias, uint16_t *y,
+                            int64_t rows, int64_t width, cudaStream_t stream)
+{
+    const int64_t per_block = proj::kThreads / 32;
+    const unsigned blocks = static_cast<unsigned>((rows + per_block - 1) / per_block);
+    proj::fp16_projection_kernel<true><<<blocks, proj::kThreads, 0, stream>>>(
+        x, w, bias, nullptr, y, static_cast<int>(rows), static_cast<int>(width));
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_fp16_qkv(const uint16_t *x, const uint16_t *w, const uint16_t *q_bias,
+                            const uint16_t *v_bias, uint16_t *y, int64_t width, cudaStream_t stream)
+{
+    const int64_t rows = 3 * width;
+    const int64_t per_block = proj::kThreads / 32;
+    const unsigned blocks = static_cast<unsigned>((rows + per_block - 1) / per_block);
+    proj::fp16_projection_kernel<false><<<blocks, proj::kThreads, 0, stream>>>(
+        x, w, q_bias, v_bias, y, static_cast<int>(rows), static_cast<int>(width));
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_fp16_bias(const uint16_t *x, uint16_t bias, uint16_t *y, int64_t count,
+                             cudaStream_t stream)
+{
+    int64_t blocks = (count + proj::kThreads - 1) / proj::kThreads;
+    blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, static_cast<int64_t>(sm_count()) * 16));
+    proj::fp16_bias_kernel<<<static_cast<unsigned>(blocks), proj::kThreads, 0, stream>>>(
+        x, bias, y, static_cast<uint32_t>(count));
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t read_and_clear_device_error(int *site)
+{
+    cudaError_t err = cudaDeviceSynchronize();
+    if (err != cudaSuccess)
+        return err;
+    int value = 0;
+    err = cudaMemcpyFromSymbol(&value, g_device_error, sizeof(int));
+    if (err != cudaSuccess)
+        return err;
+    if (value != 0) {
+        const int zero = 0;
+        err = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+    }
+    if (site)
+        *site = value;
+    return err;
+}
+
+} // namespace lffw

@@ -1,0 +1,51 @@
+// Host-side launchers of the sm_100a kernels (defined in kernels.cu).  Argument
+// validation happens in capi.cpp before any of these is called; they only
+// encode tensor maps, pick a kernel variant and launch.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime_api.h>
+
+namespace lffw {
+
+struct LinearLaunch {
+    int64_t m, n, k;
+    const uint8_t *x_codes;
+    float act_scale;
+    const float *act_scale_ptr;
+    const uint8_t *w_codes;
+    const float *w_scales;
+    const uint16_t *bias;
+    bool gelu;
+    uint16_t *y;
+    float next_scale;
+    uint8_t *next_codes;
+};
+
+// Largest M served by the CUDA-core small-M kernel.
+constexpr int64_t kGemvMaxRows = 32;
+// Shared memory the small-M kernel may use for the activation codes (m * k bytes).
+constexpr int64_t kGemvMaxSmem = 200 * 1024;
+
+cudaError_t launch_fp8_gemm(const LinearLaunch &p, cudaStream_t stream);
+cudaError_t launch_fp8_gemv(const LinearLaunch &p, cudaStream_t stream);
+cudaError_t launch_quantize(const uint16_t *x, int64_t count, float scale, const float *scale_ptr,
+                            uint8_t *codes, cudaStream_t stream);
+cudaError_t launch_quantize_rows(const uint16_t *w, int64_t rows, int64_t cols,
+                                 const float *scales, uint8_t *codes, cudaStream_t stream);
+cudaError_t launch_weight_scales(const uint16_t *w, int64_t rows, int64_t cols, float *scales,
+                                 cudaStream_t stream);
+cudaError_t launch_dynamic_scale(const uint16_t *x, int64_t count, float *scale, float *amax_out,
+                                 cudaStream_t stream);
+cudaError_t launch_fp16_fc1(const uint16_t *x, const uint16_t *w, const uint16_t *bias, uint16_t *y,
+                            int64_t rows, int64_t width, cudaStream_t stream);
+cudaError_t launch_fp16_qkv(const uint16_t *x, const uint16_t *w, const uint16_t *q_bias,
+                            const uint16_t *v_bias, uint16_t *y, int64_t width,
+                            cudaStream_t stream);
+cudaError_t launch_fp16_bias(const uint16_t *x, uint16_t bias, uint16_t *y, int64_t count,
+                             cudaStream_t stream);
+
+cudaError_t read_and_clear_device_error(int *site);
+uint64_t launch_count();
+void count_launch();
+
+} // namespace lffw

@@ -1,0 +1,237 @@
+"""Host side of the FP8 E4M3 quantized linear, mirroring the reference's FP8 graph.
+
+`Fp8Graph` restates python/src/listenflow/fastest_whisper/_fp8.py:13-55
+(``_Fp8Graph``) over device tensors instead of a TensorRT network: the same
+constructor arguments (checkpoint + activation-scale mapping), the same
+``linear(x, key, bias=True)`` / ``decoder_fc1(x, key)`` methods, the same
+``ValueError("missing or invalid activation scale for <key>")`` on a missing,
+non-finite or non-positive scale (_fp8.py:34-36, network_graph.cpp:137-139),
+and the same weight-scale rule (max|W[n,:]|/448, zero rows -> 1).  Weights are
+quantized once per key and kept on the device, as TensorRT folds the weight
+Q into a constant at build time.
+
+Tensors here are torch CUDA tensors used only as device memory; every byte of
+arithmetic runs in liblffw_b200.so (sm_100a kernels) through the C ABI.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from collections.abc import Mapping
+from dataclasses import dataclass
+
+import torch
+
+from . import _native as native
+
+E4M3_MAX = 448.0
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream) -> int:
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, torch.cuda.Stream):
+        return stream.cuda_stream
+    return int(stream)
+
+
+def _require(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
+    if not t.is_cuda or t.dtype != dtype or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous CUDA {dtype} tensor")
+
+
+def _valid_scale(value) -> bool:
+    try:
+        v = float(value)
+    except (TypeError, ValueError):
+        return False
+    return math.isfinite(v) and v > 0
+
+
+def weight_scales(weight: torch.Tensor, stream=None) -> torch.Tensor:
+    """Per-output-channel scales max|W[n,:]|/448 (0 -> 1) of an fp16 [N, K] weight."""
+    _require(weight, torch.float16, "weight")
+    rows, cols = weight.shape
+    out = torch.empty(rows, dtype=torch.float32, device=weight.device)
+    native.check(native.library().lffw_fp8_weight_scales(weight.data_ptr(), rows, cols, out.data_ptr(),
+                                                         _stream(stream)), "lffw_fp8_weight_scales")
+    return out
+
+
+def quantize(x: torch.Tensor, scale, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """E4M3 codes of an fp16 tensor with one scale (float, or a 1-element fp32 CUDA tensor)."""
+    _require(x, torch.float16, "x")
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+    scale_ptr = None
+    value = 0.0
+    if isinstance(scale, torch.Tensor):
+        _require(scale, torch.float32, "scale")
+        scale_ptr = scale.data_ptr()
+    else:
+        value = float(scale)
+    native.check(native.library().lffw_fp8_quantize(x.data_ptr(), x.numel(), value, scale_ptr, out.data_ptr(),
+                                                    _stream(stream)), "lffw_fp8_quantize")
+    return out
+
+
+def quantize_rows(w: torch.Tensor, scales: torch.Tensor, stream=None) -> torch.Tensor:
+    """E4M3 codes of an fp16 [N, K] weight with one scale per row."""
+    _require(w, torch.float16, "w")
+    _require(scales, torch.float32, "scales")
+    rows, cols = w.shape
+    out = torch.empty(w.shape, dtype=torch.uint8, device=w.device)
+    native.check(native.library().lffw_fp8_quantize_rows(w.data_ptr(), rows, cols, scales.data_ptr(),
+                                                         out.data_ptr(), _stream(stream)),
+                 "lffw_fp8_quantize_rows")
+    return out
+
+
+def dynamic_scale(x: torch.Tensor, stream=None) -> tuple[torch.Tensor, torch.Tensor]:
+    """(scale, amax) as 1-element fp32 device tensors: scale = amax/448, 0 -> 1."""
+    _require(x, torch.float16, "x")
+    scale = torch.empty(1, dtype=torch.float32, device=x.device)
+    amax = torch.empty(1, dtype=torch.float32, device=x.device)
+    native.check(native.library().lffw_fp8_dynamic_scale(x.data_ptr(), x.numel(), scale.data_ptr(),
+                                                         amax.data_ptr(), _stream(stream)),
+                 "lffw_fp8_dynamic_scale")
+    return scale, amax
+
+
+def linear(x_codes: torch.Tensor, w_codes: torch.Tensor, w_scales: torch.Tensor, act_scale, *,
+           bias: torch.Tensor | None = None, gelu: bool = False, out: torch.Tensor | None = None,
+           want_y: bool = True, next_scale: float | None = None, next_codes: torch.Tensor | None = None,
+           stream=None) -> tuple[torch.Tensor | None, torch.Tensor | None]:
+    """One FP8 Q/DQ linear on E4M3 codes: x_codes [..., K], w_codes [N, K].
+
+    Returns (y fp16 [..., N] or None, next-linear E4M3 codes or None)."""
+    _require(x_codes, torch.uint8, "x_codes")
+    _require(w_codes, torch.uint8, "w_codes")
+    _require(w_scales, torch.float32, "w_scales")
+    k = x_codes.shape[-1]
+    m = x_codes.numel() // k
+    n = w_codes.shape[0]
+    lead = tuple(x_codes.shape[:-1])
+    if want_y and out is None:
+        out = torch.empty(lead + (n,), dtype=torch.float16, device=x_codes.device)
+    if next_scale is not None and next_codes is None:
+        next_codes = torch.empty(lead + (n,), dtype=torch.uint8, device=x_codes.device)
+    a = native.LinearArgs()
+    a.struct_size = ctypes.sizeof(native.LinearArgs)
+    a.m, a.n, a.k = m, n, k
+    a.x_codes = x_codes.data_ptr()
+    if isinstance(act_scale, torch.Tensor):
+        _require(act_scale, torch.float32, "act_scale")
+        a.act_scale_ptr = act_scale.data_ptr()
+    else:
+        a.act_scale = float(act_scale)
+    a.w_codes = w_codes.data_ptr()
+    a.w_scales = w_scales.data_ptr()
+    a.bias = _ptr(bias)
+    a.epilogue = native.EPILOGUE_GELU if gelu else native.EPILOGUE_NONE
+    a.y = _ptr(out) if want_y else None
+    a.next_scale = float(next_scale) if next_scale is not None else 0.0
+    a.next_codes = _ptr(next_codes)
+    native.check(native.library().lffw_fp8_linear(ctypes.byref(a), _stream(stream)), "lffw_fp8_linear")
+    return (out if want_y else None), next_codes
+
+
+@dataclass
+class QuantizedWeight:
+    """A linear's device-resident E4M3 weight, per-channel scales and fp16 bias."""
+
+    codes: torch.Tensor
+    scales: torch.Tensor
+    bias: torch.Tensor | None
+
+    @classmethod
+    def from_half(cls, weight: torch.Tensor, bias: torch.Tensor | None = None, stream=None) -> "QuantizedWeight":
+        scales = weight_scales(weight, stream)
+        return cls(quantize_rows(weight, scales, stream), scales, bias)
+
+
+class Fp8Graph:
+    """Device-tensor counterpart of ``_Fp8Graph`` (_fp8.py:13-55).
+
+    ``checkpoint`` maps ``"<key>.weight"`` -> fp16 [out, in] and
+    ``"<key>.bias"`` -> fp16 [out] CUDA tensors; ``scales`` maps each linear key
+    to its static activation scale (the calibrated amax/448 of
+    assets/fp8-scales.json)."""
+
+    def __init__(self, checkpoint: Mapping[str, torch.Tensor], scales: Mapping[str, float]):
+        self.checkpoint = checkpoint
+        self.scales = scales
+        self._weights: dict[tuple[str, bool], QuantizedWeight] = {}
+
+    def scale(self, key: str) -> float:
+        scale = self.scales.get(key)
+        if scale is None or not _valid_scale(scale):
+            raise ValueError(f"missing or invalid activation scale for {key}")
+        return float(scale)
+
+    def weight(self, key: str, bias: bool = True) -> QuantizedWeight:
+        cached = self._weights.get((key, bias))
+        if cached is None:
+            w = self.checkpoint[f"{key}.weight"].contiguous()
+            b = self.checkpoint[f"{key}.bias"].contiguous() if bias else None
+            cached = QuantizedWeight.from_half(w, b)
+            self._weights[(key, bias)] = cached
+        return cached
+
+    def linear(self, x: torch.Tensor, key: str, *, bias: bool = True, gelu: bool = False) -> torch.Tensor:
+        """fp16 x [..., in] -> fp16 [..., out]: Q(x) . DQ, Q(W) . DQ, MatMul, + bias."""
+        scale = self.scale(key)  # validated before anything is quantized
+        weight = self.weight(key, bias)
+        codes = quantize(x.contiguous(), scale)
+        y, _ = linear(codes, weight.codes, weight.scales, scale, bias=weight.bias, gelu=gelu)
+        return y
+
+    def decoder_fc1(self, x: torch.Tensor, key: str) -> torch.Tensor:
+        """gelu(linear(x, key)) with the GELU fused into the GEMM epilogue (_fp8.py:53-55)."""
+        return self.linear(x, key, gelu=True)
+
+    def mlp(self, x: torch.Tensor, fc1: str, fc2: str) -> torch.Tensor:
+        """fc2(gelu(fc1(x))): fc1's epilogue emits fc2's E4M3 input codes directly."""
+        s1, s2 = self.scale(fc1), self.scale(fc2)
+        w1, w2 = self.weight(fc1), self.weight(fc2)
+        codes = quantize(x.contiguous(), s1)
+        _, hidden = linear(codes, w1.codes, w1.scales, s1, bias=w1.bias, gelu=True, want_y=False,
+                           next_scale=s2)
+        y, _ = linear(hidden, w2.codes, w2.scales, s2, bias=w2.bias)
+        return y
+
+
+# ---- fp16 single-token projections (the reference plugins' kernels) ---------
+
+def fp16_fc1(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, out: torch.Tensor | None = None,
+             stream=None) -> torch.Tensor:
+    rows, width = weight.shape
+    if out is None:
+        out = torch.empty(rows, dtype=torch.float16, device=weight.device)
+    native.check(native.library().lffw_fp16_fc1(x.data_ptr(), weight.data_ptr(), bias.data_ptr(),
+                                                out.data_ptr(), rows, width, _stream(stream)), "lffw_fp16_fc1")
+    return out
+
+
+def fp16_qkv(x: torch.Tensor, weight: torch.Tensor, q_bias: torch.Tensor, v_bias: torch.Tensor,
+             out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    width = weight.shape[1]
+    if out is None:
+        out = torch.empty(3 * width, dtype=torch.float16, device=weight.device)
+    native.check(native.library().lffw_fp16_qkv(x.data_ptr(), weight.data_ptr(), q_bias.data_ptr(),
+                                                v_bias.data_ptr(), out.data_ptr(), width, _stream(stream)),
+                 "lffw_fp16_qkv")
+    return out
+
+
+def fp16_bias(x: torch.Tensor, bias_bits: int, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty_like(x)
+    native.check(native.library().lffw_fp16_bias(x.data_ptr(), int(bias_bits), out.data_ptr(), x.numel(),
+                                                 _stream(stream)), "lffw_fp16_bias")
+    return out

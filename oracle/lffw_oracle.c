@@ -1,0 +1,298 @@
+/*
+ * CPU oracle (test infrastructure only; see lffw_oracle.h).  Plain C99 +
+ * pthreads, IEEE arithmetic only: build without -ffast-math so that float
+ * division and double sums round exactly as written.
+ */
+#include "lffw_oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+#include <unistd.h>
+
+double oracle_half_to_double(uint16_t h)
+{
+    int sign = h >> 15, exponent = (h >> 10) & 31, fraction = h & 1023;
+    double magnitude;
+    if (exponent == 31)
+        magnitude = fraction ? NAN : INFINITY;
+    else if (exponent == 0)
+        magnitude = ldexp((double)fraction, -24);
+    else
+        magnitude = ldexp((double)(fraction | 1024), exponent - 25);
+    return sign ? -magnitude : magnitude;
+}
+
+uint16_t oracle_half_from_double(double v)
+{
+    uint16_t sign = signbit(v) ? 0x8000 : 0;
+    if (isnan(v))
+        return sign | 0x7e00;
+    double a = fabs(v);
+    /* 65520 is the midpoint between 65504 (odd significand) and 2^16: ties go up. */
+    if (a >= 65520.0)
+        return sign | 0x7c00;
+    if (a < 0x1p-14) /* subnormal quantum 2^-24; 1024 quanta is the smallest normal */
+        return sign | (uint16_t)nearbyint(a * 0x1p24);
+    int e;
+    frexp(a, &e); /* a = f * 2^e, f in [0.5, 1) */
+    int exponent = e - 1;
+    double r = nearbyint(ldexp(a, 10 - exponent)); /* in [1024, 2048] */
+    if (r == 2048.0) {
+        r = 1024.0;
+        ++exponent;
+    }
+    return sign | (uint16_t)((exponent + 15) << 10) | (uint16_t)((int)r - 1024);
+}
+
+uint16_t oracle_half_from_float(float v) { return oracle_half_from_double((double)v); }
+
+uint8_t oracle_e4m3_from_float(float v)
+{
+    uint8_t sign = signbit(v) ? 0x80 : 0;
+    if (isnan(v))
+        return sign | 0x7f;
+    float a = fabsf(v);
+    /* Every finite value at or above 448 rounds to 448 or overflows; satfinite
+     * clamps both (and infinities) to the largest finite code. */
+    if (a >= 448.0f)
+        return sign | 0x7e;
+    if (a < 0x1p-6f) /* subnormal quantum 2^-9; 8 quanta is the smallest normal */
+        return sign | (uint8_t)nearbyintf(a * 0x1p9f);
+    int e;
+    frexpf(a, &e);
+    int exponent = e - 1; /* a in [2^exponent, 2^(exponent+1)), exponent in [-6, 8] */
+    float r = nearbyintf(ldexpf(a, 3 - exponent)); /* in [8, 16] */
+    if (r == 16.0f) {
+        r = 8.0f;
+        ++exponent;
+    }
+    return sign | (uint8_t)((exponent + 7) << 3) | (uint8_t)((int)r - 8);
+}
+
+float oracle_e4m3_to_float(uint8_t code)
+{
+    int sign = code >> 7, exponent = (code >> 3) & 15, mantissa = code & 7;
+    float magnitude;
+    if (exponent == 15 && mantissa == 7)
+        magnitude = NAN;
+    else if (exponent == 0)
+        magnitude = ldexpf((float)mantissa, -9);
+    else
+        magnitude = ldexpf((float)(mantissa | 8), exponent - 10);
+    return sign ? -magnitude : magnitude;
+}
+
+void oracle_e4m3_from_floats(const float *v, size_t count, uint8_t *codes)
+{
+    for (size_t i = 0; i < count; ++i)
+        codes[i] = oracle_e4m3_from_float(v[i]);
+}
+
+void oracle_e4m3_to_floats(const uint8_t *codes, size_t count, float *v)
+{
+    for (size_t i = 0; i < count; ++i)
+        v[i] = oracle_e4m3_to_float(codes[i]);
+}
+
+void oracle_halves_from_doubles(const double *v, size_t count, uint16_t *h)
+{
+    for (size_t i = 0; i < count; ++i)
+        h[i] = oracle_half_from_double(v[i]);
+}
+
+void oracle_gelu_fp16_array(const uint16_t *x, size_t count, uint16_t *y)
+{
+    for (size_t i = 0; i < count; ++i)
+        y[i] = oracle_gelu_fp16(x[i]);
+}
+
+static inline float half_to_float(uint16_t h) { return (float)oracle_half_to_double(h); }
+
+static inline uint8_t quantize_one(uint16_t x, float scale)
+{
+    /* TensorRT Q on a half tensor with an fp32 scale: fp32 quotient, then
+     * round-to-nearest-even into E4M3 with saturation. */
+    float q = half_to_float(x) / scale;
+    return oracle_e4m3_from_float(q);
+}
+
+void oracle_quantize(const uint16_t *x, size_t count, float scale, uint8_t *codes)
+{
+    for (size_t i = 0; i < count; ++i)
+        codes[i] = quantize_one(x[i], scale);
+}
+
+void oracle_quantize_rows(const uint16_t *x, int64_t rows, int64_t cols, const float *scales,
+                          uint8_t *codes)
+{
+    for (int64_t r = 0; r < rows; ++r)
+        for (int64_t c = 0; c < cols; ++c)
+            codes[r * cols + c] = quantize_one(x[r * cols + c], scales[r]);
+}
+
+float oracle_amax(const uint16_t *x, size_t count)
+{
+    float best = 0.0f;
+    for (size_t i = 0; i < count; ++i) {
+        float v = fabsf(half_to_float(x[i]));
+        if (v > best) /* false for NaN */
+            best = v;
+    }
+    return best;
+}
+
+void oracle_weight_scales(const uint16_t *w, int64_t rows, int64_t cols, float *scales)
+{
+    /* cpp/src/network_graph.cpp:140-148: max in fp32, divide by 448.f, 0 -> 1. */
+    for (int64_t r = 0; r < rows; ++r) {
+        float best = 0.0f;
+        for (int64_t c = 0; c < cols; ++c) {
+            float v = fabsf(half_to_float(w[r * cols + c]));
+            best = best > v ? best : v;
+        }
+        best /= 448.0f;
+        scales[r] = best > 0.0f ? best : 1.0f;
+    }
+}
+
+static inline double round_half(double v) { return oracle_half_to_double(oracle_half_from_double(v)); }
+
+uint16_t oracle_gelu_fp16(uint16_t h)
+{
+    double x = oracle_half_to_double(h);
+    const double inv_sqrt2 = round_half(1.0 / sqrt(2.0)); /* 0.70703125 */
+    double scaled = round_half(x * inv_sqrt2);
+    double erf_value = round_half(erf(scaled));
+    double left = round_half(x * 0.5);
+    double right = round_half(1.0 + erf_value);
+    return oracle_half_from_double(left * right);
+}
+
+int oracle_threads(void)
+{
+    long n = sysconf(_SC_NPROCESSORS_ONLN);
+    return n > 0 ? (int)n : 1;
+}
+
+typedef struct {
+    const uint8_t *xq, *wq;
+    int64_t m, n, k;
+    float act_scale;
+    const float *w_scale;
+    const uint16_t *bias;
+    int gelu;
+    uint16_t *y;
+    float next_scale;
+    uint8_t *next_codes;
+    const float *table; /* e4m3 code -> value */
+    int64_t row_begin, row_end;
+} linear_job;
+
+static void *linear_rows(void *argument)
+{
+    linear_job *job = (linear_job *)argument;
+    double *xrow = (double *)malloc(sizeof(double) * (size_t)job->k);
+    for (int64_t r = job->row_begin; r < job->row_end; ++r) {
+        for (int64_t c = 0; c < job->k; ++c)
+            xrow[c] = job->table[job->xq[r * job->k + c]];
+        for (int64_t col = 0; col < job->n; ++col) {
+            const uint8_t *w = job->wq + col * job->k;
+            /* Each E4M3 product has <= 8 significant bits and lies in
+             * [2^-18, 2^17.6]; a sum of <= 2^20 of them is exact in binary64. */
+            double acc = 0.0;
+            /* Exact in any order, so the reduction may be vectorized. */
+#pragma omp simd reduction(+ : acc)
+            for (int64_t c = 0; c < job->k; ++c)
+                acc += xrow[c] * (double)job->table[w[c]];
+            double scale = (double)job->act_scale * (double)job->w_scale[col];
+            uint16_t y16 = oracle_half_from_double(acc * scale);
+            if (job->bias)
+                y16 = oracle_half_from_double(oracle_half_to_double(y16) +
+                                              oracle_half_to_double(job->bias[col]));
+            if (job->gelu)
+                y16 = oracle_gelu_fp16(y16);
+            if (job->y)
+                job->y[r * job->n + col] = y16;
+            if (job->next_codes)
+                job->next_codes[r * job->n + col] = quantize_one(y16, job->next_scale);
+        }
+    }
+    free(xrow);
+    return NULL;
+}
+
+void oracle_fp8_linear(const uint8_t *xq, const uint8_t *wq, int64_t m, int64_t n, int64_t k,
+                       float act_scale, const float *w_scale, const uint16_t *bias, int gelu,
+                       uint16_t *y, float next_scale, uint8_t *next_codes, int threads)
+{
+    float table[256];
+    for (int i = 0; i < 256; ++i) {
+        table[i] = oracle_e4m3_to_float((uint8_t)i);
+        if (isnan(table[i]))
+            table[i] = NAN;
+    }
+    if (threads <= 0)
+        threads = oracle_threads();
+    if (threads > m)
+        threads = m > 0 ? (int)m : 1;
+    if (threads > 256)
+        threads = 256;
+    pthread_t handles[256];
+    linear_job jobs[256];
+    int64_t per = (m + threads - 1) / threads;
+    int started = 0;
+    for (int t = 0; t < threads; ++t) {
+        linear_job job = {xq, wq, m, n, k, act_scale, w_scale, bias, gelu, y, next_scale,
+                          next_codes, table, t * per, (t + 1) * per < m ? (t + 1) * per : m};
+        jobs[t] = job;
+        if (job.row_begin >= job.row_end)
+            continue;
+        if (threads == 1 || pthread_create(&handles[t], NULL, linear_rows, &jobs[t]) != 0) {
+            linear_rows(&jobs[t]);
+            handles[t] = 0;
+            continue;
+        }
+        ++started;
+    }
+    for (int t = 0; t < threads; ++t)
+        if (jobs[t].row_begin < jobs[t].row_end && handles[t])
+            pthread_join(handles[t], NULL);
+    (void)started;
+}
+
+void oracle_fp16_fc1(const uint16_t *x, const uint16_t *w, const uint16_t *bias, uint16_t *y,
+                     int64_t rows, int64_t width)
+{
+    /* cpp/tests/kernel_reference.hpp:20-25,36-47: double dot, then the fp16 graph edges. */
+    for (int64_t r = 0; r < rows; ++r) {
+        double dot = 0.0;
+        for (int64_t c = 0; c < width; ++c)
+            dot += oracle_half_to_double(x[c]) * oracle_half_to_double(w[r * width + c]);
+        double value = round_half(round_half(dot) + oracle_half_to_double(bias[r]));
+        y[r] = oracle_gelu_fp16(oracle_half_from_double(value));
+    }
+}
+
+void oracle_fp16_qkv(const uint16_t *x, const uint16_t *w, const uint16_t *q_bias,
+                     const uint16_t *v_bias, uint16_t *y, int64_t width)
+{
+    /* cpp/tests/kernel_reference.hpp:44-46: Q rows get q_bias, K rows none, V rows v_bias. */
+    for (int64_t r = 0; r < 3 * width; ++r) {
+        double dot = 0.0;
+        for (int64_t c = 0; c < width; ++c)
+            dot += oracle_half_to_double(x[c]) * oracle_half_to_double(w[r * width + c]);
+        double q = r < width ? oracle_half_to_double(q_bias[r]) : 0.0;
+        double v = r >= 2 * width ? oracle_half_to_double(v_bias[r - 2 * width]) : 0.0;
+        y[r] = oracle_half_from_double(dot + q + v);
+    }
+}
+
+void oracle_fp16_bias(const uint16_t *x, uint16_t bias, uint16_t *y, int64_t count)
+{
+    /* cpp/kernels.cu:10-17 */
+    double b = oracle_half_to_double(bias);
+    for (int64_t i = 0; i < count; ++i)
+        y[i] = oracle_half_from_double(oracle_half_to_double(x[i]) + b);
+}
