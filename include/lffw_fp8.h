@@ -123,6 +123,12 @@ LFFW_FP8_API lffw_status lffw_fp16_qkv(const uint16_t *x, const uint16_t *weight
 LFFW_FP8_API lffw_status lffw_fp16_bias(const uint16_t *x, uint16_t bias_bits, uint16_t *y,
                                         int64_t count, void *stream) LFFW_FP8_NOEXCEPT;
 
+/* GELU with every graph edge rounded to fp16, elementwise on `count` halves:
+ * y = (x*0.5)*(1 + erf(x*fp16(2^-1/2))) (graph::gelu, network_graph.cpp:168-180).
+ * The same device code as the fused GEMM epilogue. */
+LFFW_FP8_API lffw_status lffw_fp16_gelu(const uint16_t *x, uint16_t *y, int64_t count,
+                                        void *stream) LFFW_FP8_NOEXCEPT;
+
 /* Device gate (replaces the sm86/89/120 gates of cpp/src/precision_policy.hpp:4-7,
  * cpp/src/runtime_model.hpp:88-92 and cpp/fc1_plugin.cpp:90-98): SUCCESS only
  * for compute capability 10.0 (B200, sm_100a); UNSUPPORTED_PRECISION otherwise. */

@@ -222,6 +222,16 @@ lffw_status lffw_fp16_bias(const uint16_t *x, uint16_t bias_bits, uint16_t *y, i
     return from_cuda(lffw::launch_fp16_bias(x, bias_bits, y, count, static_cast<cudaStream_t>(stream)));
 }
 
+lffw_status lffw_fp16_gelu(const uint16_t *x, uint16_t *y, int64_t count, void *stream) noexcept
+{
+    if (x == nullptr || y == nullptr || count < 1)
+        return LFFW_INVALID_ARGUMENT;
+    lffw_status s = current_device_gate();
+    if (s != LFFW_SUCCESS)
+        return s;
+    return from_cuda(lffw::launch_fp16_gelu(x, y, count, static_cast<cudaStream_t>(stream)));
+}
+
 lffw_status lffw_device_supported(int32_t device) noexcept { return device_gate(device); }
 
 lffw_status lffw_device_error(int32_t *where) noexcept

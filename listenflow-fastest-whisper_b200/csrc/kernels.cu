@@ -28,11 +28,18 @@
 #include "launch.h"
 #include "ptx.cuh"
 
+#include "erf_table.inc"
+
 namespace lffw {
 
 namespace {
 std::atomic<uint64_t> g_launches{0};
 }
+
+// Device copy of the fp16 erf table (see erf_table.inc); copied into shared
+// memory by the GELU epilogue at kernel start.  Padded to a whole number of
+// 32-bit words.
+__device__ __align__(16) const uint16_t g_erf_table[(LFFW_ERF_TABLE_SIZE + 1) / 2 * 2] = {LFFW_ERF_TABLE_VALUES};
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
 
@@ -98,33 +105,54 @@ __device__ __forceinline__ float q_quotient(uint16_t h, float scale)
 
 // ---------------------------------------------------------------------------
 // FP8 GEMM (tcgen05)
+//
+// Persistent, warp-specialized: warp 0 issues TMA loads into a ring of shared
+// memory stages, warp 1 issues tcgen05.mma (one thread) into one of two TMEM
+// accumulators, warps 2-9 drain the other accumulator through the epilogue.
+// Each epilogue warp owns 32 TMEM lanes (rows) x half the tile's columns and
+// stores its own 32 x 32 sub-blocks with TMA from a private double buffer, so
+// no epilogue warp ever waits for another.
 
 namespace gemm {
 
 constexpr int kBM = 128;       // tile rows (TMEM lanes)
 constexpr int kBK = 128;       // K bytes per stage = one 128B swizzle row
 constexpr int kUmmaK = 32;     // K of one kind::f8f6f4 MMA
-constexpr int kThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
-constexpr int kEpiThreads = 128;
-constexpr int kChunk = 64;                         // epilogue columns per store
-constexpr int kYStageBytes = kBM * kChunk * 2;     // 128 rows x 128 B (SW128)
-constexpr int kCStageBytes = kBM * kChunk;         // 128 rows x 64 B  (SW64)
+constexpr int kEpiWarps = 8;
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kThreads = 64 + kEpiThreads; // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+constexpr int kSub = 32;                   // columns per epilogue store
 
-template <int BN>
+enum : int { kEpiGelu = 1, kEpiY = 2, kEpiCodes = 4 };
+
+template <int BN, int EPI>
 struct Cfg {
-    static constexpr int kStages = BN == 256 ? 4 : 6;
+    static constexpr bool kGelu = (EPI & kEpiGelu) != 0;
+    static constexpr bool kY = (EPI & kEpiY) != 0;
+    static constexpr bool kCodes = (EPI & kEpiCodes) != 0;
     static constexpr int kABytes = kBM * kBK;
     static constexpr int kBBytes = BN * kBK;
-    static constexpr int kTmemCols = 2 * BN;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kYBuf = 32 * kSub * 2; // 32 rows x 64 B (fp16), 64B swizzle
+    static constexpr int kCBuf = 32 * kSub;     // 32 rows x 32 B (E4M3), 32B swizzle
+    static constexpr int kWarpStaging = 2 * ((kY ? kYBuf : 0) + (kCodes ? kCBuf : 0));
+    static constexpr int kStagingBytes = kEpiWarps * kWarpStaging;
+    static constexpr int kTableBytes = kGelu ? (LFFW_ERF_TABLE_SIZE * 2 + 1023) / 1024 * 1024 : 0;
+    static constexpr int kBarBytes = 256;
+    static constexpr int kBudget = 232448 - 1024; // opt-in maximum minus base alignment slack
+    static constexpr int kFit = (kBudget - kStagingBytes - kTableBytes - kBarBytes) / kStageBytes;
+    static constexpr int kStages = kFit > 6 ? 6 : kFit;
     static constexpr int kOffB = kStages * kABytes;
-    static constexpr int kOffY = kOffB + kStages * kBBytes;
-    static constexpr int kOffC = kOffY + kYStageBytes;
-    static constexpr int kOffBar = kOffC + kCStageBytes;
-    static constexpr int kNumBars = 2 * kStages + 5; // full, empty, acc_full x2, acc_empty x2, drain
-    static constexpr int kOffSlot = kOffBar + kNumBars * 8;
-    static constexpr int kSmemBytes = kOffSlot + 16 + 1024; // + base alignment slack
+    static constexpr int kOffStaging = kOffB + kStages * kBBytes;
+    static constexpr int kOffTable = kOffStaging + kStagingBytes;
+    static constexpr int kOffBar = kOffTable + kTableBytes;
+    static constexpr int kSmemBytes = kOffBar + kBarBytes + 1024;
+    static constexpr int kTmemCols = 2 * BN;
+    static_assert(kStages >= 3, "pipeline depth");
     static_assert(kSmemBytes <= 232448, "shared memory budget");
+    static_assert((2 * kStages + 5) * 8 + 8 <= kBarBytes, "barrier area");
     static_assert(kTmemCols <= 512, "TMEM columns");
+    static_assert(kY || kCodes, "an output is required");
 };
 
 struct Params {
@@ -135,16 +163,75 @@ struct Params {
     const float *w_scales;
     const uint16_t *bias;
     float next_scale;
-    int gelu, write_y, write_codes;
 };
 
-template <int BN>
+// fp16(erf(x)) for an fp16 x, rounded to nearest even: a table for
+// 2^-7 <= |x| < 2.5957 (bits 0x2000..0x4130), 1.0 above, and the odd series
+// (2/sqrt(pi)) (x - x^3/3) below, where it is exact to fp16.
+__device__ __forceinline__ uint32_t erf_fp16(uint32_t s, const uint16_t *table)
+{
+    const uint32_t a = s & 0x7FFFu;
+    uint32_t r;
+    if (a >= LFFW_ERF_TABLE_HI) {
+        r = a > 0x7C00u ? 0x7E00u : 0x3C00u;
+    } else if (a >= LFFW_ERF_TABLE_LO) {
+        r = table[a - LFFW_ERF_TABLE_LO];
+    } else {
+        const float x = h2f(static_cast<uint16_t>(a));
+        r = f2h_rn(x * fmaf(x * x, -0.37612638903183754f, 1.1283791670955126f));
+    }
+    return r | (s & 0x8000u);
+}
+
+__device__ __forceinline__ uint32_t cvt_f16x2(float lo, float hi)
+{
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t hadd2_rn(uint32_t a, uint32_t b)
+{
+    uint32_t r;
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t hmul2_rn(uint32_t a, uint32_t b)
+{
+    uint32_t r;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b)
+{
+    uint64_t x, y, z;
+    memcpy(&x, &a, 8);
+    memcpy(&y, &b, 8);
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(z) : "l"(x), "l"(y));
+    float2 r;
+    memcpy(&r, &z, 8);
+    return r;
+}
+
+// GELU on two fp16 values with every graph edge rounded to fp16.
+__device__ __forceinline__ uint32_t gelu_fp16x2(uint32_t x, const uint16_t *table)
+{
+    const uint32_t scaled = hmul2_rn(x, 0x39A839A8u); // x * fp16(2^-1/2)
+    const uint32_t e = erf_fp16(scaled & 0xFFFFu, table) | (erf_fp16(scaled >> 16, table) << 16);
+    const uint32_t left = hmul2_rn(x, 0x38003800u);   // x * 0.5
+    const uint32_t right = hadd2_rn(0x3C003C00u, e);  // 1 + erf
+    return hmul2_rn(left, right);
+}
+
+template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                     const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_c,
                     const Params p)
 {
-    using C = Cfg<BN>;
+    using C = Cfg<BN, EPI>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -157,26 +244,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t bar_acc_full = bar_empty + 8 * C::kStages;
     const uint32_t bar_acc_empty = bar_acc_full + 16;
     const uint32_t bar_drain = bar_acc_empty + 16;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::kOffSlot);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::kOffBar + (2 * C::kStages + 5) * 8);
+    uint16_t *erf_table = reinterpret_cast<uint16_t *>(smem + C::kOffTable);
 
     if (threadIdx.x == 0) {
-        reinterpret_cast<volatile int *>(smem + C::kOffSlot)[1] = 0; // epilogue abort flag
         for (int s = 0; s < C::kStages; ++s) {
             mbar_init(bar_full + 8 * s, 1);
             mbar_init(bar_empty + 8 * s, 1);
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(bar_acc_full + 8 * a, 1);
-            mbar_init(bar_acc_empty + 8 * a, kEpiThreads);
+            mbar_init(bar_acc_empty + 8 * a, kEpiWarps);
         }
         mbar_init(bar_drain, 1);
         fence_barrier_init();
         prefetch_tensor_map(&tm_a);
         prefetch_tensor_map(&tm_b);
-        if (p.write_y)
+        if (C::kY)
             prefetch_tensor_map(&tm_y);
-        if (p.write_codes)
+        if (C::kCodes)
             prefetch_tensor_map(&tm_c);
+    }
+    if (C::kGelu) {
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(g_erf_table);
+        uint32_t *dst = reinterpret_cast<uint32_t *>(erf_table);
+        for (int i = threadIdx.x; i < (LFFW_ERF_TABLE_SIZE + 1) / 2; i += kThreads)
+            dst[i] = src[i];
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
@@ -203,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     const uint32_t full = bar_full + 8 * s;
-                    mbar_arrive_expect_tx(full, C::kABytes + C::kBBytes);
+                    mbar_arrive_expect_tx(full, C::kStageBytes);
                     tma_load_2d(sbase + s * C::kABytes, &tm_a, full, kb * kBK, m0);
                     tma_load_2d(sbase + C::kOffB + s * C::kBBytes, &tm_b, full, kb * kBK, n0);
                     used_mask |= 1u << s;
@@ -268,111 +361,135 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else {
-        // ---------------- Epilogue (4 warps, one TMEM lane = one row each) ----------------
-        const int quarter = warp & 3;
-        const int row = quarter * 32 + lane;
-        const int epi_tid = threadIdx.x - 64;
+        // ---------------- Epilogue: 8 independent warps ----------------
+        const int ew = warp - 2;
+        const int quarter = warp & 3; // the TMEM lane quarter this warp may access
+        const int half = ew >> 2;     // which half of the tile's columns
         const float act_scale = p.act_scale_ptr ? *p.act_scale_ptr : p.act_scale;
         const float next_scale = p.next_scale;
-        const uint32_t y_stage = sbase + C::kOffY;
-        const uint32_t c_stage = sbase + C::kOffC;
-        uint8_t *y_stage_ptr = smem + C::kOffY;
-        uint8_t *c_stage_ptr = smem + C::kOffC;
-        volatile int *epi_abort = reinterpret_cast<volatile int *>(smem + C::kOffSlot + 4);
+        uint8_t *staging = smem + C::kOffStaging + ew * C::kWarpStaging;
+        const uint32_t staging_s = smem_u32(staging);
+        uint32_t stores = 0;
         int local = 0;
         for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
             const int m0 = (t % p.m_tiles) * kBM;
             const int n0 = (t / p.m_tiles) * BN;
             const uint32_t a = local & 1;
             const uint32_t acc_ph = (local >> 1) & 1;
-            // All 128 epilogue threads take the same exit decision: the named
-            // barriers below would otherwise wait for threads that left.
-            if (!mbar_wait(bar_acc_full + 8 * a, acc_ph, kSiteEpilogueAccFull))
-                *epi_abort = 1;
-            named_barrier_sync(1, kEpiThreads);
-            if (*epi_abort)
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(bar_acc_full + 8 * a, acc_ph, kSiteEpilogueAccFull));
+            if (!ok)
                 break;
             tc_fence_after();
-            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN;
-            // Chunks that start at or beyond N hold only padding: no TMA store
-            // starts outside the tensor.
-            const int chunks = min(BN / kChunk, (p.n - n0 + kChunk - 1) / kChunk);
+            const int col_begin = n0 + half * (BN / 2);
+            int subs = (p.n - col_begin + kSub - 1) / kSub;
+            subs = subs < 0 ? 0 : (subs > BN / 2 / kSub ? BN / 2 / kSub : subs);
+            const int row0 = m0 + quarter * 32;
+            if (row0 >= p.m)
+                subs = 0; // every row of this warp is padding: nothing to load or store
+            const uint32_t t_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN + half * (BN / 2);
 #pragma unroll 1
-            for (int c = 0; c < chunks; ++c) {
-                uint32_t v[kChunk];
-                tmem_ld_32x32b_x32(t_row + c * kChunk, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-                tmem_ld_32x32b_x32(t_row + c * kChunk + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
-                tmem_wait_ld();
-                if (c == chunks - 1) {
-                    tc_fence_before();
-                    mbar_arrive(bar_acc_empty + 8 * a);
+            for (int sub = 0; sub < subs; ++sub) {
+                const int col0 = col_begin + sub * kSub;
+                // Per-column scale and bias (broadcast loads), issued before the TMEM read.
+                float cs[kSub];
+                uint32_t bias2[kSub / 2];
+                // N % 16 == 0, so each group of 4 (8) columns is wholly inside or outside N.
+#pragma unroll
+                for (int i = 0; i < kSub / 4; ++i) {
+                    const float4 w4 = col0 + 4 * i < p.n
+                                          ? __ldg(reinterpret_cast<const float4 *>(p.w_scales + col0) + i)
+                                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    cs[4 * i + 0] = act_scale * w4.x;
+                    cs[4 * i + 1] = act_scale * w4.y;
+                    cs[4 * i + 2] = act_scale * w4.z;
+                    cs[4 * i + 3] = act_scale * w4.w;
                 }
-                const int n_base = n0 + c * kChunk;
+                if (p.bias) {
 #pragma unroll
-                for (int g = 0; g < kChunk / 8; ++g) {
-                    const int col0 = n_base + g * 8;
-                    float cs[8];
-                    uint16_t bb[8];
-                    if (col0 < p.n) {
-                        const float4 s0 = __ldg(reinterpret_cast<const float4 *>(p.w_scales + col0));
-                        const float4 s1 = __ldg(reinterpret_cast<const float4 *>(p.w_scales + col0) + 1);
-                        cs[0] = act_scale * s0.x; cs[1] = act_scale * s0.y;
-                        cs[2] = act_scale * s0.z; cs[3] = act_scale * s0.w;
-                        cs[4] = act_scale * s1.x; cs[5] = act_scale * s1.y;
-                        cs[6] = act_scale * s1.z; cs[7] = act_scale * s1.w;
-                        if (p.bias) {
-                            const uint4 braw = __ldg(reinterpret_cast<const uint4 *>(p.bias + col0));
-                            memcpy(bb, &braw, 16);
-                        }
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            cs[i] = 0.0f;
-                            bb[i] = 0;
-                        }
+                    for (int i = 0; i < kSub / 8; ++i) {
+                        const uint4 b4 = col0 + 8 * i < p.n
+                                             ? __ldg(reinterpret_cast<const uint4 *>(p.bias + col0) + i)
+                                             : make_uint4(0u, 0u, 0u, 0u);
+                        bias2[4 * i + 0] = b4.x;
+                        bias2[4 * i + 1] = b4.y;
+                        bias2[4 * i + 2] = b4.z;
+                        bias2[4 * i + 3] = b4.w;
                     }
-                    uint16_t out[8];
+                }
+                uint32_t v[kSub];
+                tmem_ld_32x32b_x32(t_base + sub * kSub, v);
+                tmem_wait_ld();
+                if (sub == subs - 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0)
+                        mbar_arrive(bar_acc_empty + 8 * a);
+                }
+                // Scale, round to fp16, bias, GELU: two columns per packed op.
+                uint32_t h[kSub / 2];
+#pragma unroll
+                for (int i = 0; i < kSub / 2; ++i) {
+                    const float2 y = fmul2(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])),
+                                           make_float2(cs[2 * i], cs[2 * i + 1]));
+                    uint32_t z = cvt_f16x2(y.x, y.y);
+                    if (p.bias)
+                        z = hadd2_rn(z, bias2[i]);
+                    if (C::kGelu)
+                        z = gelu_fp16x2(z, erf_table);
+                    h[i] = z;
+                }
+                const uint32_t buf = stores & 1u;
+                if (lane == 0)
+                    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                __syncwarp();
+                if (C::kY) {
+                    // 32 rows x 64 B, 64B swizzle: 16B chunk j of row r at chunk j ^ ((r >> 1) & 3).
+                    uint8_t *ybuf = staging + buf * C::kYBuf;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint32_t pos = static_cast<uint32_t>(j) ^ ((static_cast<uint32_t>(lane) >> 1) & 3u);
+                        *reinterpret_cast<uint4 *>(ybuf + lane * 64 + pos * 16) =
+                            make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+                    }
+                }
+                if (C::kCodes) {
+                    // 32 rows x 32 B, 32B swizzle: chunk j of row r at chunk j ^ ((r >> 2) & 1).
+                    uint8_t *cbuf = staging + (C::kY ? 2 * C::kYBuf : 0) + buf * C::kCBuf;
+                    uint32_t q[8];
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
-                        uint16_t z = f2h_rn(__uint_as_float(v[g * 8 + i]) * cs[i]);
-                        if (p.bias)
-                            z = hadd_rn(z, bb[i]);
-                        if (p.gelu)
-                            z = gelu_fp16_edges(z);
-                        out[i] = z;
+                        const uint32_t lo = e4m3x2(q_quotient(h[2 * i] & 0xFFFFu, next_scale),
+                                                   q_quotient(h[2 * i] >> 16, next_scale));
+                        const uint32_t hi = e4m3x2(q_quotient(h[2 * i + 1] & 0xFFFFu, next_scale),
+                                                   q_quotient(h[2 * i + 1] >> 16, next_scale));
+                        q[i] = lo | (hi << 16);
                     }
-                    if (p.write_y) {
-                        uint4 pk;
-                        memcpy(&pk, out, 16);
-                        const uint32_t chunk = static_cast<uint32_t>(g) ^ static_cast<uint32_t>(row & 7);
-                        *reinterpret_cast<uint4 *>(y_stage_ptr + row * 128 + chunk * 16) = pk;
-                    }
-                    if (p.write_codes) {
-                        uint16_t q[4];
 #pragma unroll
-                        for (int i = 0; i < 4; ++i)
-                            q[i] = e4m3x2(q_quotient(out[2 * i], next_scale),
-                                          q_quotient(out[2 * i + 1], next_scale));
-                        uint2 pk;
-                        memcpy(&pk, q, 8);
-                        const uint32_t chunk = static_cast<uint32_t>(g >> 1) ^ static_cast<uint32_t>((row >> 1) & 3);
-                        *reinterpret_cast<uint2 *>(c_stage_ptr + row * 64 + chunk * 16 + (g & 1) * 8) = pk;
+                    for (int j = 0; j < 2; ++j) {
+                        const uint32_t pos = static_cast<uint32_t>(j) ^ ((static_cast<uint32_t>(lane) >> 2) & 1u);
+                        *reinterpret_cast<uint4 *>(cbuf + lane * 32 + pos * 16) =
+                            make_uint4(q[4 * j], q[4 * j + 1], q[4 * j + 2], q[4 * j + 3]);
                     }
                 }
                 fence_proxy_async_smem();
-                named_barrier_sync(1, kEpiThreads);
-                if (epi_tid == 0) {
-                    if (p.write_y)
-                        tma_store_2d(&tm_y, y_stage, n_base, m0);
-                    if (p.write_codes)
-                        tma_store_2d(&tm_c, c_stage, n_base, m0);
+                __syncwarp();
+                if (lane == 0) {
+                    if (C::kY)
+                        tma_store_2d(&tm_y, staging_s + buf * C::kYBuf, col0, row0);
+                    if (C::kCodes)
+                        tma_store_2d(&tm_c, staging_s + (C::kY ? 2 * C::kYBuf : 0) + buf * C::kCBuf, col0, row0);
                     bulk_commit_group();
-                    bulk_wait_group_read0();
                 }
-                named_barrier_sync(1, kEpiThreads);
+                ++stores;
+            }
+            if (subs == 0) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive(bar_acc_empty + 8 * a);
             }
         }
-        if (epi_tid == 0)
+        if (lane == 0)
             bulk_wait_group0();
     }
 
@@ -650,6 +767,16 @@ __global__ void __launch_bounds__(kThreads)
     }
 }
 
+// Elementwise GELU with fp16 edges (graph::gelu, network_graph.cpp:168-180),
+// through the same erf path as the GEMM epilogue (table read from global).
+__global__ void __launch_bounds__(kThreads)
+    fp16_gelu_kernel(const uint16_t *__restrict__ x, uint16_t *__restrict__ y, int64_t count)
+{
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < count; i += stride)
+        y[i] = static_cast<uint16_t>(gemm::gelu_fp16x2(x[i], g_erf_table) & 0xFFFFu);
+}
+
 __global__ void __launch_bounds__(kThreads)
     fp16_bias_kernel(const uint16_t *__restrict__ x, uint16_t bias, uint16_t *__restrict__ y,
                      uint32_t count)
@@ -741,21 +868,22 @@ cudaError_t ensure_smem(Kernel kernel, int bytes)
     return err;
 }
 
-template <int BN>
+template <int BN, int EPI>
 cudaError_t run_gemm(const LinearLaunch &L, cudaStream_t stream)
 {
-    using C = gemm::Cfg<BN>;
+    using C = gemm::Cfg<BN, EPI>;
     CUtensorMap tm_a{}, tm_b{}, tm_y{}, tm_c{};
     if (!make_map(&tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.x_codes, L.m, L.k, gemm::kBK, gemm::kBM,
                   CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_map(&tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.w_codes, L.n, L.k, gemm::kBK, BN,
                   CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
-    if (L.y && !make_map(&tm_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.y, L.m, L.n, gemm::kChunk,
-                         gemm::kBM, CU_TENSOR_MAP_SWIZZLE_128B))
+    // Epilogue stores: one 32-row x 32-column box per warp and sub-chunk.
+    if (C::kY && !make_map(&tm_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.y, L.m, L.n, gemm::kSub, 32,
+                           CU_TENSOR_MAP_SWIZZLE_64B))
         return cudaErrorInvalidValue;
-    if (L.next_codes && !make_map(&tm_c, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.next_codes, L.m, L.n,
-                                  gemm::kChunk, gemm::kBM, CU_TENSOR_MAP_SWIZZLE_64B))
+    if (C::kCodes && !make_map(&tm_c, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.next_codes, L.m, L.n, gemm::kSub,
+                               32, CU_TENSOR_MAP_SWIZZLE_32B))
         return cudaErrorInvalidValue;
     gemm::Params p{};
     p.m = static_cast<int>(L.m);
@@ -770,17 +898,30 @@ cudaError_t run_gemm(const LinearLaunch &L, cudaStream_t stream)
     p.w_scales = L.w_scales;
     p.bias = L.bias;
     p.next_scale = L.next_scale;
-    p.gelu = L.gelu ? 1 : 0;
-    p.write_y = L.y ? 1 : 0;
-    p.write_codes = L.next_codes ? 1 : 0;
 
-    const cudaError_t attr = ensure_smem(gemm::fp8_gemm_kernel<BN>, C::kSmemBytes);
+    const cudaError_t attr = ensure_smem(gemm::fp8_gemm_kernel<BN, EPI>, C::kSmemBytes);
     if (attr != cudaSuccess)
         return attr;
     const int grid = std::min(p.num_tiles, sm_count());
-    gemm::fp8_gemm_kernel<BN><<<grid, gemm::kThreads, C::kSmemBytes, stream>>>(tm_a, tm_b, tm_y, tm_c, p);
+    gemm::fp8_gemm_kernel<BN, EPI><<<grid, gemm::kThreads, C::kSmemBytes, stream>>>(tm_a, tm_b, tm_y, tm_c, p);
     count_launch();
     return cudaGetLastError();
+}
+
+template <int BN>
+cudaError_t run_gemm_epilogue(const LinearLaunch &L, cudaStream_t stream)
+{
+    using namespace gemm;
+    const int epi = (L.gelu ? kEpiGelu : 0) | (L.y ? kEpiY : 0) | (L.next_codes ? kEpiCodes : 0);
+    switch (epi) {
+    case kEpiY: return run_gemm<BN, kEpiY>(L, stream);
+    case kEpiCodes: return run_gemm<BN, kEpiCodes>(L, stream);
+    case kEpiY | kEpiCodes: return run_gemm<BN, kEpiY | kEpiCodes>(L, stream);
+    case kEpiGelu | kEpiY: return run_gemm<BN, kEpiGelu | kEpiY>(L, stream);
+    case kEpiGelu | kEpiCodes: return run_gemm<BN, kEpiGelu | kEpiCodes>(L, stream);
+    case kEpiGelu | kEpiY | kEpiCodes: return run_gemm<BN, kEpiGelu | kEpiY | kEpiCodes>(L, stream);
+    default: return cudaErrorInvalidValue;
+    }
 }
 
 } // namespace
@@ -790,8 +931,8 @@ cudaError_t launch_fp8_gemm(const LinearLaunch &L, cudaStream_t stream)
     const int64_t m_tiles = (L.m + gemm::kBM - 1) / gemm::kBM;
     const int64_t tiles256 = m_tiles * ((L.n + 255) / 256);
     if (tiles256 >= sm_count())
-        return run_gemm<256>(L, stream);
-    return run_gemm<128>(L, stream);
+        return run_gemm_epilogue<256>(L, stream);
+    return run_gemm_epilogue<128>(L, stream);
 }
 
 cudaError_t launch_fp8_gemv(const LinearLaunch &L, cudaStream_t stream)
@@ -906,6 +1047,15 @@ cudaError_t launch_fp16_bias(const uint16_t *x, uint16_t bias, uint16_t *y, int6
     blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, static_cast<int64_t>(sm_count()) * 16));
     proj::fp16_bias_kernel<<<static_cast<unsigned>(blocks), proj::kThreads, 0, stream>>>(
         x, bias, y, static_cast<uint32_t>(count));
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_fp16_gelu(const uint16_t *x, uint16_t *y, int64_t count, cudaStream_t stream)
+{
+    int64_t blocks = (count + proj::kThreads - 1) / proj::kThreads;
+    blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, static_cast<int64_t>(sm_count()) * 16));
+    proj::fp16_gelu_kernel<<<static_cast<unsigned>(blocks), proj::kThreads, 0, stream>>>(x, y, count);
     count_launch();
     return cudaGetLastError();
 }

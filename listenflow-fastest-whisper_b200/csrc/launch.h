@@ -41,6 +41,7 @@ cudaError_t launch_fp16_fc1(const uint16_t *x, const uint16_t *w, const uint16_t
 cudaError_t launch_fp16_qkv(const uint16_t *x, const uint16_t *w, const uint16_t *q_bias,
                             const uint16_t *v_bias, uint16_t *y, int64_t width,
                             cudaStream_t stream);
+cudaError_t launch_fp16_gelu(const uint16_t *x, uint16_t *y, int64_t count, cudaStream_t stream);
 cudaError_t launch_fp16_bias(const uint16_t *x, uint16_t bias, uint16_t *y, int64_t count,
                              cudaStream_t stream);
 

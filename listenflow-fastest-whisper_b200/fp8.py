@@ -229,6 +229,16 @@ def fp16_qkv(x: torch.Tensor, weight: torch.Tensor, q_bias: torch.Tensor, v_bias
     return out
 
 
+def fp16_gelu(x: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """GELU with fp16 graph edges (graph::gelu), elementwise."""
+    _require(x, torch.float16, "x")
+    if out is None:
+        out = torch.empty_like(x)
+    native.check(native.library().lffw_fp16_gelu(x.data_ptr(), out.data_ptr(), x.numel(), _stream(stream)),
+                 "lffw_fp16_gelu")
+    return out
+
+
 def fp16_bias(x: torch.Tensor, bias_bits: int, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
     if out is None:
         out = torch.empty_like(x)

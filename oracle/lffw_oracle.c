@@ -159,6 +159,11 @@ void oracle_weight_scales(const uint16_t *w, int64_t rows, int64_t cols, float *
 
 static inline double round_half(double v) { return oracle_half_to_double(oracle_half_from_double(v)); }
 
+uint16_t oracle_erf_fp16(uint16_t h)
+{
+    return oracle_half_from_double(erf(oracle_half_to_double(h)));
+}
+
 uint16_t oracle_gelu_fp16(uint16_t h)
 {
     double x = oracle_half_to_double(h);

@@ -61,6 +61,8 @@ void oracle_fp8_linear(const uint8_t *xq, const uint8_t *wq, int64_t m, int64_t 
                        float act_scale, const float *w_scale, const uint16_t *bias, int gelu,
                        uint16_t *y, float next_scale, uint8_t *next_codes, int threads);
 
+/* fp16(erf(x)) of an fp16 x, erf in binary64, round to nearest even. */
+uint16_t oracle_erf_fp16(uint16_t x);
 /* GELU on an fp16 value with every graph edge rounded to fp16. */
 uint16_t oracle_gelu_fp16(uint16_t x);
 

@@ -54,6 +54,8 @@ def lib() -> ctypes.CDLL:
         L.oracle_fp16_qkv.argtypes = [_u16p, _u16p, _u16p, _u16p, _u16p, ctypes.c_int64]
         L.oracle_fp16_bias.argtypes = [_u16p, ctypes.c_uint16, _u16p, ctypes.c_int64]
         L.oracle_threads.restype = ctypes.c_int
+        L.oracle_erf_fp16.argtypes = [ctypes.c_uint16]
+        L.oracle_erf_fp16.restype = ctypes.c_uint16
         _lib = L
     return _lib
 
@@ -103,6 +105,12 @@ def gelu_fp16(x) -> np.ndarray:
     out = np.empty(b.shape, np.uint16)
     lib().oracle_gelu_fp16_array(_ptr(b, _u16p), b.size, _ptr(out, _u16p))
     return out
+
+
+def erf_fp16(x) -> np.ndarray:
+    b = bits16(x)
+    f = lib().oracle_erf_fp16
+    return np.array([f(int(v)) for v in b.ravel()], np.uint16).reshape(b.shape)
 
 
 def quantize(x, scale: float) -> np.ndarray:

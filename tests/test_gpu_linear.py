@@ -67,10 +67,19 @@ def test_linear_matches_oracle(cuda, fp8, oracle, native, m, n, k, gelu):
     y_ref, codes_ref = oracle.fp8_linear(d["xq_ref"], d["wq_ref"], d["act_scale"], d["ws_ref"], d["b"],
                                          gelu=gelu, next_scale=next_scale)
     y_bits = y.cpu().numpy().view(np.uint16)
-    max_abs, max_rel, excess, mismatches = compare_halves(y_bits, y_ref)
+    # GELU outputs: a one-ulp difference of the matmul output edge (fp32 vs
+    # exact accumulation) moves the fp16-edge GELU chain by at most two ulps.
+    rtol = 2 * RTOL if gelu else RTOL
+    max_abs, max_rel, excess, mismatches = compare_halves(y_bits, y_ref, rtol=rtol)
     print(f"m={m} n={n} k={k} gelu={gelu}: max_abs={max_abs:.3g} max_rel={max_rel:.3g} "
           f"mismatch={mismatches}/{y_bits.size}")
-    assert excess <= 0, f"fp16 output outside {ATOL}+{RTOL}*|ref| (max_abs {max_abs})"
+    assert excess <= 0, f"fp16 output outside {ATOL}+{rtol}*|ref| (max_abs {max_abs})"
+    assert mismatches <= max(8, y_bits.size // 500)
+    if gelu:
+        # The fused epilogue equals the oracle's GELU applied to the GPU's own
+        # pre-activation (same GEMM without GELU), bit for bit.
+        pre, _ = fp8.linear(d["xq"], d["wq"], d["ws"], float(d["act_scale"]), bias=d["bd"])
+        np.testing.assert_array_equal(y_bits, oracle.gelu_fp16(pre.cpu().numpy().view(np.uint16)))
     # Codes of the fused next-linear quantize are bit-exact wherever the fp16
     # value matches, and equal the oracle's Q of the GPU's own fp16 value.
     got = codes.cpu().numpy()

@@ -1,0 +1,79 @@
+"""E4M3 quantization and scale kernels on the GPU: bit-exact against the oracle
+and the hand-written edge table."""
+
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).parent / "golden"
+ALL_HALVES = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+
+
+def test_edge_table_on_gpu(cuda, fp8):
+    import torch
+
+    for e in json.loads((GOLDEN / "e4m3_edges.json").read_text()):
+        x = torch.tensor([e["x_bits"]] * 16, dtype=torch.int16).view(torch.float16).to(cuda)
+        got = fp8.quantize(x, e["scale"]).cpu().numpy()
+        assert np.all(got == e["code"]), (e["why"], got[0])
+
+
+@pytest.mark.parametrize("scale", [1.0, 0.011, 1 / 448, 3.7, 2.0**-10, 123.25])
+def test_every_half_bit_exact(cuda, fp8, oracle, scale):
+    import torch
+
+    x = torch.from_numpy(ALL_HALVES.view(np.float16).copy()).to(cuda)
+    got = fp8.quantize(x, scale).cpu().numpy()
+    want = oracle.quantize(ALL_HALVES, scale)
+    nan = np.isnan(ALL_HALVES.view(np.float16))
+    np.testing.assert_array_equal(got[~nan], want[~nan])
+    assert np.all(got[nan] & 0x7F == 0x7F)
+    # scale read from device memory gives the same codes
+    s = torch.tensor([scale], dtype=torch.float32, device=cuda)
+    np.testing.assert_array_equal(fp8.quantize(x, s).cpu().numpy(), got)
+
+
+@pytest.mark.parametrize("count", [1, 15, 16, 17, 1023, 4099, 1500 * 1280])
+def test_ragged_sizes_and_guard_band(cuda, fp8, oracle, count):
+    import torch
+
+    rng = np.random.default_rng(count)
+    x = (rng.standard_normal(count) * 3).astype(np.float16)
+    out = torch.full((count + 128,), 0xA5, dtype=torch.uint8, device=cuda)
+    fp8.quantize(torch.from_numpy(x).to(cuda), 0.02, out=out[:count])
+    got = out.cpu().numpy()
+    np.testing.assert_array_equal(got[:count], oracle.quantize(x, 0.02))
+    assert np.all(got[count:] == 0xA5), "quantize wrote past its output"
+
+
+def test_weight_prep_bit_exact(cuda, fp8, oracle):
+    import torch
+
+    rng = np.random.default_rng(9)
+    for rows, cols in ((3, 16), (5120, 1280), (1280, 5120), (7, 4112)):
+        w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float16)
+        w[rows // 2] = 0  # an all-zero row maps to scale 1 (network_graph.cpp:146-147)
+        wd = torch.from_numpy(w).to(cuda)
+        scales = fp8.weight_scales(wd)
+        want = oracle.weight_scales(w)
+        np.testing.assert_array_equal(scales.cpu().numpy(), want)
+        assert want[rows // 2] == 1.0
+        np.testing.assert_array_equal(fp8.quantize_rows(wd, scales).cpu().numpy(), oracle.quantize_rows(w, want))
+
+
+def test_gelu_every_half_matches_oracle(cuda, fp8, oracle):
+    import torch
+
+    x = torch.from_numpy(ALL_HALVES.view(np.float16).copy()).to(cuda)
+    got = fp8.fp16_gelu(x).cpu().numpy().view(np.uint16)
+    want = oracle.gelu_fp16(ALL_HALVES)
+    nan = np.isnan(want.view(np.float16))
+    assert np.all(np.isnan(got[nan].view(np.float16)))
+    mismatch = np.nonzero(got[~nan] != want[~nan])[0]
+    assert mismatch.size == 0, [(hex(ALL_HALVES[~nan][i]), hex(got[~nan][i]), hex(want[~nan][i]))
+                                for i in mismatch[:10]]
