@@ -63,8 +63,8 @@ enum { LFFW_EPILOGUE_NONE = 0, LFFW_EPILOGUE_GELU = 1 };
  * y / next_codes [m,n].  The activation scale is the static `act_scale`, or is
  * read from device memory when `act_scale_ptr` is non-NULL (dynamic amax/448).
  * Requirements: m,n,k >= 1; k % 16 == 0; n % 16 == 0; 16-byte aligned pointers;
- * act_scale (or *act_scale_ptr) finite and > 0; next_scale finite and > 0 when
- * next_codes is set.
+ * act_scale (or *act_scale_ptr) finite and > 0; next_scale in [2^-125, 2^125]
+ * (a normal float with a normal reciprocal) when next_codes is set.
  */
 typedef struct lffw_fp8_linear_args {
     size_t struct_size; /* sizeof(lffw_fp8_linear_args) */
@@ -86,7 +86,8 @@ LFFW_FP8_API lffw_status lffw_fp8_linear(const lffw_fp8_linear_args *args,
 
 /* Q of an fp16 activation with one scalar scale (graph::qdq axis 0,
  * network_graph.cpp:115-123): codes[i] = E4M3_rne_sat(fp32(x[i] / scale)).
- * `scale_ptr` (device, may be NULL) overrides `scale`. */
+ * `scale_ptr` (device, may be NULL) overrides `scale`; scales lie in
+ * [2^-125, 2^125].  x and codes are 16-byte aligned. */
 LFFW_FP8_API lffw_status lffw_fp8_quantize(const uint16_t *x, int64_t count, float scale,
                                            const float *scale_ptr, uint8_t *codes,
                                            void *stream) LFFW_FP8_NOEXCEPT;

@@ -27,6 +27,8 @@ using lffw::LinearLaunch;
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 bool positive_finite(float v) { return std::isfinite(v) && v > 0.0f; }
+// A scale whose reciprocal is also a normal float (Q divides by it).
+bool valid_scale(float v) { return std::isfinite(v) && v >= 0x1p-125f && v <= 0x1p125f; }
 
 lffw_status from_cuda(cudaError_t err)
 {
@@ -95,7 +97,7 @@ lffw_status validate_linear(const lffw_fp8_linear_args *a)
         return LFFW_INVALID_ARGUMENT;
     if (a->act_scale_ptr == nullptr && !positive_finite(a->act_scale))
         return LFFW_INVALID_ARGUMENT; // network_graph.cpp:137-139
-    if (a->next_codes != nullptr && !positive_finite(a->next_scale))
+    if (a->next_codes != nullptr && !valid_scale(a->next_scale))
         return LFFW_INVALID_ARGUMENT;
     if (a->epilogue != LFFW_EPILOGUE_NONE && a->epilogue != LFFW_EPILOGUE_GELU)
         return LFFW_INVALID_ARGUMENT;
@@ -141,7 +143,7 @@ lffw_status lffw_fp8_quantize(const uint16_t *x, int64_t count, float scale, con
 {
     if (x == nullptr || codes == nullptr || count < 1 || !aligned16(x) || !aligned16(codes))
         return LFFW_INVALID_ARGUMENT;
-    if (scale_ptr == nullptr && !positive_finite(scale))
+    if (scale_ptr == nullptr && !valid_scale(scale))
         return LFFW_INVALID_ARGUMENT;
     lffw_status s = current_device_gate();
     if (s != LFFW_SUCCESS)
@@ -396,11 +398,11 @@ bool valid_fields(const CreatorInfo &info, lffw_plugin &plugin)
         std::memcpy(&plugin.has_bias, find_field(fields, "has_bias")->bytes.data(), 4);
         if (plugin.has_bias != 0 && plugin.has_bias != 1)
             return false;
-        if (!positive_finite(plugin.act_scale)) // network_graph.cpp:137-139
+        if (!valid_scale(plugin.act_scale)) // network_graph.cpp:137-139 (+ normal reciprocal)
             return false;
         if (plugin.epilogue != LFFW_EPILOGUE_NONE && plugin.epilogue != LFFW_EPILOGUE_GELU)
             return false;
-        if (!(plugin.output_scale == 0.0f || positive_finite(plugin.output_scale)))
+        if (!(plugin.output_scale == 0.0f || valid_scale(plugin.output_scale)))
             return false;
     }
     return true;

@@ -103,6 +103,23 @@ __device__ __forceinline__ float q_quotient(uint16_t h, float scale)
     return __fdiv_rn(h2f(h), scale);
 }
 
+// The same quotient without a division: with y = RN(1/scale) (computed on the
+// host) and q0 = RN(x*y), the residual r = x - scale*q0 is exact in an fma and
+// q0 + r*y rounded once is the correctly rounded x/scale (Markstein's theorem,
+// valid for normal operands; fp16 values are normal fp32 numbers and scales are
+// validated normal).  Quotients too small to matter (< 2^-10 maps to code 0)
+// are unaffected by underflow.  Works on |x|; the sign is restored afterwards
+// so -0 stays -0.  Infinite x saturates, NaN stays NaN.
+__device__ __forceinline__ float q_quotient_fast(uint16_t h, float scale, float recip)
+{
+    const float x = h2f(h & 0x7FFFu);
+    const float q0 = x * recip;
+    const float r = fmaf(-scale, q0, x);
+    float q = fmaf(r, recip, q0);
+    q = (h & 0x7C00u) == 0x7C00u ? ((h & 0x3FFu) ? __int_as_float(0x7FC00000) : 1024.0f) : fminf(q, 1024.0f);
+    return (h & 0x8000u) ? -q : q;
+}
+
 // ---------------------------------------------------------------------------
 // FP8 GEMM (tcgen05)
 //
@@ -163,6 +180,7 @@ struct Params {
     const float *w_scales;
     const uint16_t *bias;
     float next_scale;
+    float next_recip; // RN(1 / next_scale)
 };
 
 // fp16(erf(x)) for an fp16 x, rounded to nearest even: a table for
@@ -170,16 +188,15 @@ struct Params {
 // (2/sqrt(pi)) (x - x^3/3) below, where it is exact to fp16.
 __device__ __forceinline__ uint32_t erf_fp16(uint32_t s, const uint16_t *table)
 {
+    // Branch-free so the table loads of neighbouring columns overlap.
     const uint32_t a = s & 0x7FFFu;
-    uint32_t r;
-    if (a >= LFFW_ERF_TABLE_HI) {
-        r = a > 0x7C00u ? 0x7E00u : 0x3C00u;
-    } else if (a >= LFFW_ERF_TABLE_LO) {
-        r = table[a - LFFW_ERF_TABLE_LO];
-    } else {
-        const float x = h2f(static_cast<uint16_t>(a));
-        r = f2h_rn(x * fmaf(x * x, -0.37612638903183754f, 1.1283791670955126f));
-    }
+    const uint32_t idx = min(max(a, static_cast<uint32_t>(LFFW_ERF_TABLE_LO)),
+                             static_cast<uint32_t>(LFFW_ERF_TABLE_HI - 1)) - LFFW_ERF_TABLE_LO;
+    const uint32_t looked = table[idx];
+    const float x = h2f(static_cast<uint16_t>(a));
+    const uint32_t series = f2h_rn(x * fmaf(x * x, -0.37612638903183754f, 1.1283791670955126f));
+    const uint32_t big = a > 0x7C00u ? 0x7E00u : 0x3C00u;
+    const uint32_t r = a >= LFFW_ERF_TABLE_HI ? big : (a >= LFFW_ERF_TABLE_LO ? looked : series);
     return r | (s & 0x8000u);
 }
 
@@ -367,6 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int half = ew >> 2;     // which half of the tile's columns
         const float act_scale = p.act_scale_ptr ? *p.act_scale_ptr : p.act_scale;
         const float next_scale = p.next_scale;
+        const float next_recip = p.next_recip;
         uint8_t *staging = smem + C::kOffStaging + ew * C::kWarpStaging;
         const uint32_t staging_s = smem_u32(staging);
         uint32_t stores = 0;
@@ -458,10 +476,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint32_t q[8];
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
-                        const uint32_t lo = e4m3x2(q_quotient(h[2 * i] & 0xFFFFu, next_scale),
-                                                   q_quotient(h[2 * i] >> 16, next_scale));
-                        const uint32_t hi = e4m3x2(q_quotient(h[2 * i + 1] & 0xFFFFu, next_scale),
-                                                   q_quotient(h[2 * i + 1] >> 16, next_scale));
+                        const uint32_t lo = e4m3x2(q_quotient_fast(h[2 * i] & 0xFFFFu, next_scale, next_recip),
+                                                   q_quotient_fast(h[2 * i] >> 16, next_scale, next_recip));
+                        const uint32_t hi = e4m3x2(q_quotient_fast(h[2 * i + 1] & 0xFFFFu, next_scale, next_recip),
+                                                   q_quotient_fast(h[2 * i + 1] >> 16, next_scale, next_recip));
                         q[i] = lo | (hi << 16);
                     }
 #pragma unroll
@@ -624,10 +642,11 @@ namespace quant {
 constexpr int kThreads = 256;
 
 __global__ void __launch_bounds__(kThreads)
-    quantize_kernel(const uint16_t *__restrict__ x, int64_t count, float scale_value,
+    quantize_kernel(const uint16_t *__restrict__ x, int64_t count, float scale_value, float recip_value,
                     const float *scale_ptr, uint8_t *__restrict__ codes)
 {
     const float scale = scale_ptr ? *scale_ptr : scale_value;
+    const float recip = scale_ptr ? __frcp_rn(scale) : recip_value;
     const int64_t groups = count / 16;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
     for (int64_t g = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; g < groups; g += stride) {
@@ -638,7 +657,7 @@ __global__ void __launch_bounds__(kThreads)
         uint16_t q[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i)
-            q[i] = e4m3x2(q_quotient(hv[2 * i], scale), q_quotient(hv[2 * i + 1], scale));
+            q[i] = e4m3x2(q_quotient_fast(hv[2 * i], scale, recip), q_quotient_fast(hv[2 * i + 1], scale, recip));
         uint4 out;
         memcpy(&out, q, 16);
         *reinterpret_cast<uint4 *>(codes + g * 16) = out;
@@ -898,6 +917,9 @@ cudaError_t run_gemm(const LinearLaunch &L, cudaStream_t stream)
     p.w_scales = L.w_scales;
     p.bias = L.bias;
     p.next_scale = L.next_scale;
+    // Correctly rounded reciprocal: binary64 quotient, one rounding to binary32
+    // (innocuous double rounding for division since 53 >= 2*24 + 2).
+    p.next_recip = L.next_codes ? static_cast<float>(1.0 / static_cast<double>(L.next_scale)) : 0.0f;
 
     const cudaError_t attr = ensure_smem(gemm::fp8_gemm_kernel<BN, EPI>, C::kSmemBytes);
     if (attr != cudaSuccess)
@@ -977,8 +999,9 @@ cudaError_t launch_quantize(const uint16_t *x, int64_t count, float scale, const
     const int64_t groups = count / 16;
     int64_t blocks = (groups + quant::kThreads - 1) / quant::kThreads;
     blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, static_cast<int64_t>(sm_count()) * 8));
+    const float recip = static_cast<float>(1.0 / static_cast<double>(scale));
     quant::quantize_kernel<<<static_cast<unsigned>(blocks), quant::kThreads, 0, stream>>>(
-        x, count, scale, scale_ptr, codes);
+        x, count, scale, recip, scale_ptr, codes);
     count_launch();
     return cudaGetLastError();
 }

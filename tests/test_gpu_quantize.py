@@ -18,7 +18,7 @@ def test_edge_table_on_gpu(cuda, fp8):
     import torch
 
     for e in json.loads((GOLDEN / "e4m3_edges.json").read_text()):
-        x = torch.tensor([e["x_bits"]] * 16, dtype=torch.int16).view(torch.float16).to(cuda)
+        x = torch.from_numpy(np.full(16, e["x_bits"], np.uint16).view(np.float16)).to(cuda)
         got = fp8.quantize(x, e["scale"]).cpu().numpy()
         assert np.all(got == e["code"]), (e["why"], got[0])
 
@@ -36,6 +36,18 @@ def test_every_half_bit_exact(cuda, fp8, oracle, scale):
     # scale read from device memory gives the same codes
     s = torch.tensor([scale], dtype=torch.float32, device=cuda)
     np.testing.assert_array_equal(fp8.quantize(x, s).cpu().numpy(), got)
+
+
+def test_random_scales_every_half(cuda, fp8, oracle):
+    """The division-free quotient equals IEEE fp32 division for every fp16 input."""
+    import torch
+
+    rng = np.random.default_rng(21)
+    x = torch.from_numpy(ALL_HALVES.view(np.float16).copy()).to(cuda)
+    nan = np.isnan(ALL_HALVES.view(np.float16))
+    for scale in np.exp2(rng.uniform(-20, 10, 48)).astype(np.float32):
+        got = fp8.quantize(x, float(scale)).cpu().numpy()
+        np.testing.assert_array_equal(got[~nan], oracle.quantize(ALL_HALVES, scale)[~nan], err_msg=str(scale))
 
 
 @pytest.mark.parametrize("count", [1, 15, 16, 17, 1023, 4099, 1500 * 1280])
