@@ -103,22 +103,29 @@ __device__ __forceinline__ float q_quotient(uint16_t h, float scale)
     return __fdiv_rn(h2f(h), scale);
 }
 
-// The same quotient without a division: with y = RN(1/scale) (computed on the
-// host) and q0 = RN(x*y), the residual r = x - scale*q0 is exact in an fma and
-// q0 + r*y rounded once is the correctly rounded x/scale (Markstein's theorem,
-// valid for normal operands; fp16 values are normal fp32 numbers and scales are
-// validated normal).  Quotients too small to matter (< 2^-10 maps to code 0)
-// are unaffected by underflow.  Works on |x|; the sign is restored afterwards
-// so -0 stays -0.  Infinite x saturates, NaN stays NaN.
-__device__ __forceinline__ float q_quotient_fast(uint16_t h, float scale, float recip)
+__device__ __forceinline__ uint64_t f2_bits(float lo, float hi)
 {
-    const float x = h2f(h & 0x7FFFu);
-    const float q0 = x * recip;
-    const float r = fmaf(-scale, q0, x);
-    float q = fmaf(r, recip, q0);
-    q = (h & 0x7C00u) == 0x7C00u ? ((h & 0x3FFu) ? __int_as_float(0x7FC00000) : 1024.0f) : fminf(q, 1024.0f);
-    return (h & 0x8000u) ? -q : q;
+    return static_cast<uint64_t>(__float_as_uint(lo)) | (static_cast<uint64_t>(__float_as_uint(hi)) << 32);
 }
+
+// Two E4M3 codes (low byte = low half) of the packed fp16 pair h2 divided by
+// `scale`, with y = RN(1/scale): the division-free quotient below on f32x2.
+// Zero and infinite inputs keep q0 (= +-0 or +-inf, whose codes are +-0 and
+// +-448), NaN stays NaN; everything else takes the corrected quotient.
+__device__ __forceinline__ uint32_t e4m3x2_quotient(uint32_t h2, uint64_t scale2_neg, uint64_t recip2)
+{
+    const uint64_t x = f2_bits(h2f(static_cast<uint16_t>(h2 & 0xFFFFu)), h2f(static_cast<uint16_t>(h2 >> 16)));
+    uint64_t q0, r, q1;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(q0) : "l"(x), "l"(recip2));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(scale2_neg), "l"(q0), "l"(x));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(q1) : "l"(r), "l"(recip2), "l"(q0));
+    const float q0l = __uint_as_float(static_cast<uint32_t>(q0)), q0h = __uint_as_float(static_cast<uint32_t>(q0 >> 32));
+    const float q1l = __uint_as_float(static_cast<uint32_t>(q1)), q1h = __uint_as_float(static_cast<uint32_t>(q1 >> 32));
+    const float ql = (fabsf(q0l) == 0.0f || fabsf(q0l) == __int_as_float(0x7F800000)) ? q0l : q1l;
+    const float qh = (fabsf(q0h) == 0.0f || fabsf(q0h) == __int_as_float(0x7F800000)) ? q0h : q1h;
+    return e4m3x2(ql, qh);
+}
+
 
 // ---------------------------------------------------------------------------
 // FP8 GEMM (tcgen05)
@@ -183,21 +190,17 @@ struct Params {
     float next_recip; // RN(1 / next_scale)
 };
 
-// fp16(erf(x)) for an fp16 x, rounded to nearest even: a table for
-// 2^-7 <= |x| < 2.5957 (bits 0x2000..0x4130), 1.0 above, and the odd series
-// (2/sqrt(pi)) (x - x^3/3) below, where it is exact to fp16.
-__device__ __forceinline__ uint32_t erf_fp16(uint32_t s, const uint16_t *table)
+// fp16(erf(x)) of two packed fp16 values, rounded to nearest even: one table
+// read per value.  The table covers every non-negative fp16 input up to
+// 0x4131, whose entry is 1.0 like erf of every larger input; NaN inputs read
+// 1.0 too, which leaves GELU's result NaN through its x*0.5 factor.
+__device__ __forceinline__ uint32_t erf_fp16x2(uint32_t s2, const uint16_t *table)
 {
-    // Branch-free so the table loads of neighbouring columns overlap.
-    const uint32_t a = s & 0x7FFFu;
-    const uint32_t idx = min(max(a, static_cast<uint32_t>(LFFW_ERF_TABLE_LO)),
-                             static_cast<uint32_t>(LFFW_ERF_TABLE_HI - 1)) - LFFW_ERF_TABLE_LO;
-    const uint32_t looked = table[idx];
-    const float x = h2f(static_cast<uint16_t>(a));
-    const uint32_t series = f2h_rn(x * fmaf(x * x, -0.37612638903183754f, 1.1283791670955126f));
-    const uint32_t big = a > 0x7C00u ? 0x7E00u : 0x3C00u;
-    const uint32_t r = a >= LFFW_ERF_TABLE_HI ? big : (a >= LFFW_ERF_TABLE_LO ? looked : series);
-    return r | (s & 0x8000u);
+    uint32_t idx;
+    asm("min.u16x2 %0, %1, %2;" : "=r"(idx) : "r"(s2 & 0x7FFF7FFFu), "r"(LFFW_ERF_TABLE_HI * 0x10001u));
+    const uint32_t lo = table[idx & 0xFFFFu];
+    const uint32_t hi = table[idx >> 16];
+    return (lo | (hi << 16)) | (s2 & 0x80008000u);
 }
 
 __device__ __forceinline__ uint32_t cvt_f16x2(float lo, float hi)
@@ -236,7 +239,7 @@ __device__ __forceinline__ float2 fmul2(float2 a, float2 b)
 __device__ __forceinline__ uint32_t gelu_fp16x2(uint32_t x, const uint16_t *table)
 {
     const uint32_t scaled = hmul2_rn(x, 0x39A839A8u); // x * fp16(2^-1/2)
-    const uint32_t e = erf_fp16(scaled & 0xFFFFu, table) | (erf_fp16(scaled >> 16, table) << 16);
+    const uint32_t e = erf_fp16x2(scaled, table);
     const uint32_t left = hmul2_rn(x, 0x38003800u);   // x * 0.5
     const uint32_t right = hadd2_rn(0x3C003C00u, e);  // 1 + erf
     return hmul2_rn(left, right);
@@ -383,8 +386,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int quarter = warp & 3; // the TMEM lane quarter this warp may access
         const int half = ew >> 2;     // which half of the tile's columns
         const float act_scale = p.act_scale_ptr ? *p.act_scale_ptr : p.act_scale;
-        const float next_scale = p.next_scale;
-        const float next_recip = p.next_recip;
+        const uint64_t neg_scale2 = f2_bits(-p.next_scale, -p.next_scale);
+        const uint64_t recip2 = f2_bits(p.next_recip, p.next_recip);
         uint8_t *staging = smem + C::kOffStaging + ew * C::kWarpStaging;
         const uint32_t staging_s = smem_u32(staging);
         uint32_t stores = 0;
@@ -475,13 +478,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint8_t *cbuf = staging + (C::kY ? 2 * C::kYBuf : 0) + buf * C::kCBuf;
                     uint32_t q[8];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const uint32_t lo = e4m3x2(q_quotient_fast(h[2 * i] & 0xFFFFu, next_scale, next_recip),
-                                                   q_quotient_fast(h[2 * i] >> 16, next_scale, next_recip));
-                        const uint32_t hi = e4m3x2(q_quotient_fast(h[2 * i + 1] & 0xFFFFu, next_scale, next_recip),
-                                                   q_quotient_fast(h[2 * i + 1] >> 16, next_scale, next_recip));
-                        q[i] = lo | (hi << 16);
-                    }
+                    for (int i = 0; i < 8; ++i)
+                        q[i] = e4m3x2_quotient(h[2 * i], neg_scale2, recip2) |
+                               (e4m3x2_quotient(h[2 * i + 1], neg_scale2, recip2) << 16);
 #pragma unroll
                     for (int j = 0; j < 2; ++j) {
                         const uint32_t pos = static_cast<uint32_t>(j) ^ ((static_cast<uint32_t>(lane) >> 2) & 1u);
@@ -655,9 +654,12 @@ __global__ void __launch_bounds__(kThreads)
         uint16_t hv[16];
         memcpy(hv, h, 32);
         uint16_t q[8];
+        const uint64_t neg_scale2 = f2_bits(-scale, -scale), recip2 = f2_bits(recip, recip);
+        uint32_t hw[8];
+        memcpy(hw, hv, 32);
 #pragma unroll
         for (int i = 0; i < 8; ++i)
-            q[i] = e4m3x2(q_quotient_fast(hv[2 * i], scale, recip), q_quotient_fast(hv[2 * i + 1], scale, recip));
+            q[i] = e4m3x2_quotient(hw[i], neg_scale2, recip2);
         uint4 out;
         memcpy(&out, q, 16);
         *reinterpret_cast<uint4 *>(codes + g * 16) = out;

@@ -45,7 +45,12 @@ def test_random_scales_every_half(cuda, fp8, oracle):
     rng = np.random.default_rng(21)
     x = torch.from_numpy(ALL_HALVES.view(np.float16).copy()).to(cuda)
     nan = np.isnan(ALL_HALVES.view(np.float16))
-    for scale in np.exp2(rng.uniform(-20, 10, 48)).astype(np.float32):
+    scales = list(np.exp2(rng.uniform(-20, 10, 96)).astype(np.float32))
+    # significands next to 2 and to 1: the reciprocal's rounding error is largest there
+    scales += [np.float32(np.nextafter(np.float32(2.0), np.float32(0)) * 2.0**e) for e in (-12, -3, 0, 5)]
+    scales += [np.float32(np.nextafter(np.float32(1.0), np.float32(2)) * 2.0**e) for e in (-9, 0, 7)]
+    scales += [np.float32(1 / 448), np.float32(3.0), np.float32(0.1), np.float32(2.0**-125), np.float32(2.0**125)]
+    for scale in scales:
         got = fp8.quantize(x, float(scale)).cpu().numpy()
         np.testing.assert_array_equal(got[~nan], oracle.quantize(ALL_HALVES, scale)[~nan], err_msg=str(scale))
 
