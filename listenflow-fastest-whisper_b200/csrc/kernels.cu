@@ -149,14 +149,21 @@ constexpr int kSub = 32;                   // columns per epilogue store
 
 enum : int { kEpiGelu = 1, kEpiY = 2, kEpiCodes = 4 };
 
-template <int BN, int EPI>
+// kPair: a cluster of two CTAs computes a 256 x BN tile with cta_group::2 MMAs.
+// Each CTA loads its 128 rows of A and its BN/2 rows of B (the pair's B tile is
+// split along N), holds its 128 rows of the accumulator in its own TMEM, and
+// runs its own epilogue.  Per SM that halves the B operand traffic.
+template <int BN, int EPI, bool kPair>
 struct Cfg {
     static constexpr bool kGelu = (EPI & kEpiGelu) != 0;
     static constexpr bool kY = (EPI & kEpiY) != 0;
     static constexpr bool kCodes = (EPI & kEpiCodes) != 0;
+    static constexpr int kTileM = kPair ? 2 * kBM : kBM;
+    static constexpr int kBRows = kPair ? BN / 2 : BN; // B rows this CTA loads
     static constexpr int kABytes = kBM * kBK;
-    static constexpr int kBBytes = BN * kBK;
-    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kBBytes = kBRows * kBK;
+    static constexpr int kStageBytes = kABytes + kBBytes;                // per CTA
+    static constexpr int kTxBytes = kPair ? 2 * kStageBytes : kStageBytes; // counted on the leader
     static constexpr int kYBuf = 32 * kSub * 2; // 32 rows x 64 B (fp16), 64B swizzle
     static constexpr int kCBuf = 32 * kSub;     // 32 rows x 32 B (E4M3), 32B swizzle
     static constexpr int kWarpStaging = 2 * ((kY ? kYBuf : 0) + (kCodes ? kCBuf : 0));
@@ -172,6 +179,7 @@ struct Cfg {
     static constexpr int kOffBar = kOffTable + kTableBytes;
     static constexpr int kSmemBytes = kOffBar + kBarBytes + 1024;
     static constexpr int kTmemCols = 2 * BN;
+    static constexpr int kAccEmptyArrivals = kPair ? 2 * kEpiWarps : kEpiWarps;
     static_assert(kStages >= 3, "pipeline depth");
     static_assert(kSmemBytes <= 232448, "shared memory budget");
     static_assert((2 * kStages + 5) * 8 + 8 <= kBarBytes, "barrier area");
@@ -245,13 +253,13 @@ __device__ __forceinline__ uint32_t gelu_fp16x2(uint32_t x, const uint16_t *tabl
     return hmul2_rn(left, right);
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                     const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_c,
                     const Params p)
 {
-    using C = Cfg<BN, EPI>;
+    using C = Cfg<BN, EPI, kPair>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -259,6 +267,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
+    const uint32_t rank = kPair ? cluster_ctarank() : 0u; // 0 = leader of the pair
+    const bool leader = rank == 0;
+    const int tile_step = kPair ? static_cast<int>(gridDim.x / 2) : static_cast<int>(gridDim.x);
+    const int tile_first = kPair ? static_cast<int>(blockIdx.x / 2) : static_cast<int>(blockIdx.x);
     const uint32_t bar_full = sbase + C::kOffBar;
     const uint32_t bar_empty = bar_full + 8 * C::kStages;
     const uint32_t bar_acc_full = bar_empty + 8 * C::kStages;
@@ -274,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(bar_acc_full + 8 * a, 1);
-            mbar_init(bar_acc_empty + 8 * a, kEpiWarps);
+            mbar_init(bar_acc_empty + 8 * a, C::kAccEmptyArrivals);
         }
         mbar_init(bar_drain, 1);
         fence_barrier_init();
@@ -292,11 +304,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             dst[i] = src[i];
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
-        tmem_relinquish();
+        if (kPair) {
+            tmem_alloc_pair(smem_u32(tmem_slot), C::kTmemCols);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if (kPair)
+        cluster_sync(); // the peer's barriers exist before any cross-CTA arrive
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
@@ -307,18 +326,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
-            for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
-                const int m0 = (t % p.m_tiles) * kBM;
-                const int n0 = (t / p.m_tiles) * BN;
+            for (int t = tile_first; ok && t < p.num_tiles; t += tile_step) {
+                const int m0 = (t % p.m_tiles) * C::kTileM + static_cast<int>(rank) * kBM;
+                const int n0 = (t / p.m_tiles) * BN + static_cast<int>(rank) * C::kBRows;
                 for (int kb = 0; kb < p.num_kb; ++kb) {
                     if (!mbar_wait(bar_empty + 8 * s, ph ^ 1u, kSiteProducerEmpty)) {
                         ok = false;
                         break;
                     }
                     const uint32_t full = bar_full + 8 * s;
-                    mbar_arrive_expect_tx(full, C::kStageBytes);
-                    tma_load_2d(sbase + s * C::kABytes, &tm_a, full, kb * kBK, m0);
-                    tma_load_2d(sbase + C::kOffB + s * C::kBBytes, &tm_b, full, kb * kBK, n0);
+                    if (kPair) {
+                        // Both CTAs' bytes complete on the leader's barrier, armed by the leader.
+                        const uint32_t leader_full = map_to_rank(full, 0);
+                        if (leader)
+                            mbar_arrive_expect_tx(full, C::kTxBytes);
+                        tma_load_2d_pair(sbase + s * C::kABytes, &tm_a, leader_full, kb * kBK, m0);
+                        tma_load_2d_pair(sbase + C::kOffB + s * C::kBBytes, &tm_b, leader_full, kb * kBK, n0);
+                    } else {
+                        mbar_arrive_expect_tx(full, C::kTxBytes);
+                        tma_load_2d(sbase + s * C::kABytes, &tm_a, full, kb * kBK, m0);
+                        tma_load_2d(sbase + C::kOffB + s * C::kBBytes, &tm_b, full, kb * kBK, n0);
+                    }
                     used_mask |= 1u << s;
                     parity_mask = (parity_mask & ~(1u << s)) | (ph << s);
                     if (++s == C::kStages) {
@@ -327,23 +355,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
-            // Every issued load must land before the CTA's shared memory is released.
-            for (int i = 0; i < C::kStages; ++i)
-                if (used_mask & (1u << i)) {
-                    const uint32_t par = (parity_mask >> i) & 1u;
-                    for (int tries = 0; tries < (1 << 22) && !mbar_try_wait(bar_full + 8 * i, par); ++tries) {
+            // Every issued load must land before shared memory is released.  In a
+            // pair the leader's full barriers count both CTAs' loads.
+            if (leader)
+                for (int i = 0; i < C::kStages; ++i)
+                    if (used_mask & (1u << i)) {
+                        const uint32_t par = (parity_mask >> i) & 1u;
+                        for (int tries = 0; tries < (1 << 22) && !mbar_try_wait(bar_full + 8 * i, par); ++tries) {
+                        }
                     }
-                }
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer (one thread) ----------------
-        if (lane == 0) {
-            constexpr uint32_t idesc = idesc_e4m3_f32<kBM, BN>();
+        // ---------------- MMA issuer (one thread of the leader) ----------------
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = idesc_e4m3_f32<C::kTileM, BN>();
             int s = 0;
             uint32_t ph = 0;
             int local = 0;
             bool ok = true;
-            for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x, ++local) {
+            for (int t = tile_first; ok && t < p.num_tiles; t += tile_step, ++local) {
                 const uint32_t a = local & 1;
                 const uint32_t acc_ph = (local >> 1) & 1;
                 if (!mbar_wait(bar_acc_empty + 8 * a, acc_ph ^ 1u, kSiteMmaAccEmpty)) {
@@ -364,19 +394,33 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int k = 0; k < kBK / kUmmaK; ++k) {
                         const uint64_t da = smem_desc_k_sw128(a_addr + k * kUmmaK);
                         const uint64_t db = smem_desc_k_sw128(b_addr + k * kUmmaK);
-                        mma_f8f6f4(d_tmem, da, db, idesc, (kb | k) != 0);
+                        if (kPair)
+                            mma_f8f6f4_pair(d_tmem, da, db, idesc, (kb | k) != 0);
+                        else
+                            mma_f8f6f4(d_tmem, da, db, idesc, (kb | k) != 0);
                     }
-                    mma_commit(bar_empty + 8 * s); // frees the stage once these MMAs finish
+                    // Frees the stage (in both CTAs of a pair) once these MMAs finish.
+                    if (kPair)
+                        mma_commit_pair_both(bar_empty + 8 * s);
+                    else
+                        mma_commit(bar_empty + 8 * s);
                     if (++s == C::kStages) {
                         s = 0;
                         ph ^= 1u;
                     }
                 }
-                if (ok)
-                    mma_commit(bar_acc_full + 8 * a);
+                if (ok) {
+                    if (kPair)
+                        mma_commit_pair_both(bar_acc_full + 8 * a);
+                    else
+                        mma_commit(bar_acc_full + 8 * a);
+                }
             }
             // Drain: all MMAs issued by this thread complete before TMEM is freed.
-            mma_commit(bar_drain);
+            if (kPair)
+                mma_commit_pair_local(bar_drain);
+            else
+                mma_commit(bar_drain);
             for (int tries = 0; tries < (1 << 22) && !mbar_try_wait(bar_drain, 0); ++tries) {
             }
         }
@@ -388,12 +432,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float act_scale = p.act_scale_ptr ? *p.act_scale_ptr : p.act_scale;
         const uint64_t neg_scale2 = f2_bits(-p.next_scale, -p.next_scale);
         const uint64_t recip2 = f2_bits(p.next_recip, p.next_recip);
+        // Accumulator release goes to the leader's barrier (a cluster address in a pair).
+        const uint32_t acc_empty_target = kPair ? map_to_rank(bar_acc_empty, 0) : bar_acc_empty;
         uint8_t *staging = smem + C::kOffStaging + ew * C::kWarpStaging;
         const uint32_t staging_s = smem_u32(staging);
         uint32_t stores = 0;
         int local = 0;
-        for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
-            const int m0 = (t % p.m_tiles) * kBM;
+        for (int t = tile_first; t < p.num_tiles; t += tile_step, ++local) {
+            const int m0 = (t % p.m_tiles) * C::kTileM + static_cast<int>(rank) * kBM;
             const int n0 = (t / p.m_tiles) * BN;
             const uint32_t a = local & 1;
             const uint32_t acc_ph = (local >> 1) & 1;
@@ -443,8 +489,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (sub == subs - 1) {
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0)
-                        mbar_arrive(bar_acc_empty + 8 * a);
+                    if (lane == 0) {
+                        if (kPair)
+                            mbar_arrive_cluster(acc_empty_target);
+                        else
+                            mbar_arrive(acc_empty_target);
+                    }
                 }
                 // Scale, round to fp16, bias, GELU: two columns per packed op.
                 uint32_t h[kSub / 2];
@@ -502,8 +552,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (subs == 0) {
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0)
-                    mbar_arrive(bar_acc_empty + 8 * a);
+                if (lane == 0) {
+                    if (kPair)
+                        mbar_arrive_cluster(acc_empty_target);
+                    else
+                        mbar_arrive(acc_empty_target);
+                }
             }
         }
         if (lane == 0)
@@ -512,9 +566,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     tc_fence_before();
     __syncthreads();
+    if (kPair)
+        cluster_sync(); // neither CTA leaves while its peer may still touch its barriers or TMEM
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, C::kTmemCols);
+        if (kPair)
+            tmem_dealloc_pair(tmem_base, C::kTmemCols);
+        else
+            tmem_dealloc(tmem_base, C::kTmemCols);
     }
 }
 
@@ -889,14 +948,14 @@ cudaError_t ensure_smem(Kernel kernel, int bytes)
     return err;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool kPair>
 cudaError_t run_gemm(const LinearLaunch &L, cudaStream_t stream)
 {
-    using C = gemm::Cfg<BN, EPI>;
+    using C = gemm::Cfg<BN, EPI, kPair>;
     CUtensorMap tm_a{}, tm_b{}, tm_y{}, tm_c{};
     if (!make_map(&tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.x_codes, L.m, L.k, gemm::kBK, gemm::kBM,
                   CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map(&tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.w_codes, L.n, L.k, gemm::kBK, BN,
+        !make_map(&tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.w_codes, L.n, L.k, gemm::kBK, C::kBRows,
                   CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
     // Epilogue stores: one 32-row x 32-column box per warp and sub-chunk.
@@ -910,7 +969,7 @@ cudaError_t run_gemm(const LinearLaunch &L, cudaStream_t stream)
     p.m = static_cast<int>(L.m);
     p.n = static_cast<int>(L.n);
     p.k = static_cast<int>(L.k);
-    p.m_tiles = static_cast<int>((L.m + gemm::kBM - 1) / gemm::kBM);
+    p.m_tiles = static_cast<int>((L.m + C::kTileM - 1) / C::kTileM);
     const int n_tiles = static_cast<int>((L.n + BN - 1) / BN);
     p.num_tiles = p.m_tiles * n_tiles;
     p.num_kb = static_cast<int>((L.k + gemm::kBK - 1) / gemm::kBK);
@@ -923,40 +982,72 @@ cudaError_t run_gemm(const LinearLaunch &L, cudaStream_t stream)
     // (innocuous double rounding for division since 53 >= 2*24 + 2).
     p.next_recip = L.next_codes ? static_cast<float>(1.0 / static_cast<double>(L.next_scale)) : 0.0f;
 
-    const cudaError_t attr = ensure_smem(gemm::fp8_gemm_kernel<BN, EPI>, C::kSmemBytes);
+    auto kernel = gemm::fp8_gemm_kernel<BN, EPI, kPair>;
+    const cudaError_t attr = ensure_smem(kernel, C::kSmemBytes);
     if (attr != cudaSuccess)
         return attr;
-    const int grid = std::min(p.num_tiles, sm_count());
-    gemm::fp8_gemm_kernel<BN, EPI><<<grid, gemm::kThreads, C::kSmemBytes, stream>>>(tm_a, tm_b, tm_y, tm_c, p);
+    const int units = kPair ? sm_count() / 2 : sm_count();
+    const int grid = std::min(p.num_tiles, units) * (kPair ? 2 : 1);
+    cudaLaunchConfig_t config{};
+    config.gridDim = dim3(static_cast<unsigned>(grid));
+    config.blockDim = dim3(gemm::kThreads);
+    config.dynamicSmemBytes = C::kSmemBytes;
+    config.stream = stream;
+    cudaLaunchAttribute attrs[1];
+    if (kPair) {
+        attrs[0].id = cudaLaunchAttributeClusterDimension;
+        attrs[0].val.clusterDim.x = 2;
+        attrs[0].val.clusterDim.y = 1;
+        attrs[0].val.clusterDim.z = 1;
+        config.attrs = attrs;
+        config.numAttrs = 1;
+    }
+    const cudaError_t err = cudaLaunchKernelEx(&config, kernel, tm_a, tm_b, tm_y, tm_c, p);
     count_launch();
-    return cudaGetLastError();
+    return err != cudaSuccess ? err : cudaGetLastError();
 }
 
-template <int BN>
+template <int BN, bool kPair>
 cudaError_t run_gemm_epilogue(const LinearLaunch &L, cudaStream_t stream)
 {
     using namespace gemm;
     const int epi = (L.gelu ? kEpiGelu : 0) | (L.y ? kEpiY : 0) | (L.next_codes ? kEpiCodes : 0);
     switch (epi) {
-    case kEpiY: return run_gemm<BN, kEpiY>(L, stream);
-    case kEpiCodes: return run_gemm<BN, kEpiCodes>(L, stream);
-    case kEpiY | kEpiCodes: return run_gemm<BN, kEpiY | kEpiCodes>(L, stream);
-    case kEpiGelu | kEpiY: return run_gemm<BN, kEpiGelu | kEpiY>(L, stream);
-    case kEpiGelu | kEpiCodes: return run_gemm<BN, kEpiGelu | kEpiCodes>(L, stream);
-    case kEpiGelu | kEpiY | kEpiCodes: return run_gemm<BN, kEpiGelu | kEpiY | kEpiCodes>(L, stream);
+    case kEpiY: return run_gemm<BN, kEpiY, kPair>(L, stream);
+    case kEpiCodes: return run_gemm<BN, kEpiCodes, kPair>(L, stream);
+    case kEpiY | kEpiCodes: return run_gemm<BN, kEpiY | kEpiCodes, kPair>(L, stream);
+    case kEpiGelu | kEpiY: return run_gemm<BN, kEpiGelu | kEpiY, kPair>(L, stream);
+    case kEpiGelu | kEpiCodes: return run_gemm<BN, kEpiGelu | kEpiCodes, kPair>(L, stream);
+    case kEpiGelu | kEpiY | kEpiCodes: return run_gemm<BN, kEpiGelu | kEpiY | kEpiCodes, kPair>(L, stream);
     default: return cudaErrorInvalidValue;
     }
+}
+
+// Fraction of the last wave that is busy when `tiles` tiles run on `units`
+// persistent workers.
+double wave_efficiency(int64_t tiles, int64_t units)
+{
+    const int64_t waves = (tiles + units - 1) / units;
+    return static_cast<double>(tiles) / static_cast<double>(waves * units);
 }
 
 } // namespace
 
 cudaError_t launch_fp8_gemm(const LinearLaunch &L, cudaStream_t stream)
 {
-    const int64_t m_tiles = (L.m + gemm::kBM - 1) / gemm::kBM;
-    const int64_t tiles256 = m_tiles * ((L.n + 255) / 256);
-    if (tiles256 >= sm_count())
-        return run_gemm_epilogue<256>(L, stream);
-    return run_gemm_epilogue<128>(L, stream);
+    // CTA pairs (256-row tiles) once M fills them; 1-CTA 128-row tiles below.
+    // Tile width: 256 unless 128 wastes clearly less of the last wave.
+    const int sms = sm_count();
+    const bool pair = L.m >= 512;
+    const int64_t tile_m = pair ? 256 : 128;
+    const int64_t units = pair ? sms / 2 : sms;
+    const int64_t m_tiles = (L.m + tile_m - 1) / tile_m;
+    const double e256 = wave_efficiency(m_tiles * ((L.n + 255) / 256), units);
+    const double e128 = wave_efficiency(m_tiles * ((L.n + 127) / 128), units);
+    const bool wide = !(e256 < 0.85 && e128 > e256 + 0.05);
+    if (pair)
+        return wide ? run_gemm_epilogue<256, true>(L, stream) : run_gemm_epilogue<128, true>(L, stream);
+    return wide ? run_gemm_epilogue<256, false>(L, stream) : run_gemm_epilogue<128, false>(L, stream);
 }
 
 cudaError_t launch_fp8_gemv(const LinearLaunch &L, cudaStream_t stream)

@@ -1,6 +1,7 @@
 // Thin inline-PTX wrappers for sm_100a: mbarriers with bounded waits, TMA
 // (cp.async.bulk.tensor) loads/stores, and the tcgen05 tensor-memory / MMA
-// instructions.  No cluster multicast is used anywhere in this library.
+// instructions.  No TMA load is ever multicast; the only multicast is
+// tcgen05.commit arriving on the barriers of both CTAs of a pair.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -234,13 +235,99 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t smem_addr)
 // Instruction descriptor, kind::f8f6f4: D fp32 (bits 4-5 = 1), A and B E4M3
 // (bits 7-9, 10-12 = 0), both K-major (bits 15, 16 = 0), N>>3 at bit 17,
 // M>>4 at bit 24.
+// M = 256 is the CTA-pair (cta_group::2) shape: each CTA of the pair holds
+// 128 rows of A and of the accumulator.
 template <int M, int N>
 __host__ __device__ constexpr uint32_t idesc_e4m3_f32()
 {
-    static_assert(M == 64 || M == 128, "cta_group::1 M");
-    static_assert(N % 16 == 0 && N >= 16 && N <= 256, "N for M=128");
+    static_assert(M == 64 || M == 128 || M == 256, "M");
+    static_assert(N % 16 == 0 && N >= 16 && N <= 256, "N for M=128/256");
     return (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
            (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// ---- CTA pairs (cluster of 2, cta_group::2) ---------------------------------
+// Used only without multicast TMA: each CTA loads its own halves of the
+// operands; only tcgen05.commit is multicast to both CTAs' barriers.
+
+__device__ __forceinline__ uint32_t cluster_ctarank()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address of the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t smem_addr, uint32_t rank)
+{
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+    return r;
+}
+
+// Arrive on an mbarrier that may live in the peer CTA (cluster address).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar)
+{
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+// TMA load into this CTA's shared memory whose completion is counted on an
+// mbarrier of either CTA of the pair (the leader's).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, uint32_t cluster_bar,
+                                                 int32_t x, int32_t y)
+{
+    asm volatile("cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+                 "l"(reinterpret_cast<uint64_t>(map)), "r"(cluster_bar), "r"(x), "r"(y)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t columns)
+{
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(columns)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair()
+{
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t columns)
+{
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(columns) : "memory");
+}
+
+// D[tmem of both CTAs] (+)= A (rows split over the pair) x B^T (columns split
+// over the pair); issued by the leader CTA only.
+__device__ __forceinline__ void mma_f8f6f4_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+                 "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+                 : "memory");
+}
+
+// Arrive once on the barrier at this offset in both CTAs of the pair when the
+// leader's previously issued tcgen05 ops complete.
+__device__ __forceinline__ void mma_commit_pair_both(uint32_t bar)
+{
+    const uint16_t mask = 3;
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+                 ::"r"(bar), "h"(mask)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mma_commit_pair_local(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
 } // namespace lffw

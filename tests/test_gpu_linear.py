@@ -50,6 +50,11 @@ CASES = [
     (7, 1280, 1280),
     (20, 3840, 1280),
     (32, 1280, 5120),
+    # CTA-pair tiles (M >= 512): a last pair tile whose second CTA holds only
+    # padding rows, ragged N, and both tile widths
+    (600, 272, 1280),
+    (1024, 3840, 1280),
+    (777, 1280, 5120),
 ]
 
 
@@ -114,3 +119,62 @@ def test_dynamic_scale_matches_oracle(cuda, fp8, oracle):
     zero = torch.zeros(100, dtype=torch.float16, device=cuda)
     scale, amax = fp8.dynamic_scale(zero)
     assert amax.item() == 0.0 and scale.item() == 1.0
+
+
+def test_config1_fc1_full_size(cuda, fp8, oracle):
+    """X [1500,1280] ~N(0,1), W [5120,1280] ~N(0,0.02), b ~N(0,0.02),
+    dynamic act scale amax(X)/448, per-row weight scales, fc1 + bias + GELU, fp16 out."""
+    import torch
+
+    gen = torch.Generator().manual_seed(0)
+    x = torch.randn(1500, 1280, generator=gen).half()
+    w = (torch.randn(5120, 1280, generator=gen) * 0.02).half()
+    b = (torch.randn(5120, generator=gen) * 0.02).half()
+    xd, wd, bd = x.to(cuda), w.to(cuda), b.to(cuda)
+    scale, amax = fp8.dynamic_scale(xd)
+    qw = fp8.QuantizedWeight.from_half(wd, bd)
+    xq = fp8.quantize(xd, scale)
+    y, _ = fp8.linear(xq, qw.codes, qw.scales, scale, bias=bd, gelu=True)
+    xn, wn, bn = x.numpy(), w.numpy(), b.numpy()
+    s = np.float32(oracle.amax(xn)) / np.float32(448)
+    assert scale.item() == s
+    ws = oracle.weight_scales(wn)
+    xq_ref, wq_ref = oracle.quantize(xn, s), oracle.quantize_rows(wn, ws)
+    np.testing.assert_array_equal(xq.cpu().numpy(), xq_ref)
+    np.testing.assert_array_equal(qw.codes.cpu().numpy(), wq_ref)
+    y_ref, _ = oracle.fp8_linear(xq_ref, wq_ref, s, ws, bn, gelu=True)
+    y_bits = y.cpu().numpy().view(np.uint16)
+    max_abs, max_rel, excess, mismatches = compare_halves(y_bits, y_ref, rtol=2 * RTOL)
+    print(f"config1: max_abs={max_abs:.3g} max_rel={max_rel:.3g} mismatch={mismatches}/{y_bits.size}")
+    assert excess <= 0 and mismatches <= y_bits.size // 500
+
+
+def test_config2_layer_set_rows_and_fusion(cuda, fp8, oracle):
+    """BASELINE config 2 shapes at M=12000: every linear checked on a row sample
+    against the oracle; the fc1 -> fc2 fused codes equal Q of the unfused fc1."""
+    import torch
+
+    m = 12000
+    rng = np.random.default_rng(2024)
+    rows = np.sort(rng.choice(m, 96, replace=False))
+    for name, k, n, gelu in (("qkv", 1280, 3840, False), ("out", 1280, 1280, False),
+                             ("fc1", 1280, 5120, True), ("fc2", 5120, 1280, False)):
+        x = halves(rng, (m, k))
+        w = halves(rng, (n, k), 0.02)
+        b = halves(rng, (n,), 0.02)
+        s = np.float32(oracle.amax(x)) / np.float32(448)
+        qw = fp8.QuantizedWeight.from_half(torch.from_numpy(w).to(cuda), torch.from_numpy(b).to(cuda))
+        xq = fp8.quantize(torch.from_numpy(x).to(cuda), float(s))
+        y, codes = fp8.linear(xq, qw.codes, qw.scales, float(s), bias=qw.bias, gelu=gelu,
+                              next_scale=0.0123 if gelu else None)
+        ws = oracle.weight_scales(w)
+        xq_rows = oracle.quantize(x[rows], s)
+        np.testing.assert_array_equal(xq.cpu().numpy()[rows], xq_rows)
+        y_ref, _ = oracle.fp8_linear(xq_rows, oracle.quantize_rows(w, ws), s, ws, b, gelu=gelu)
+        y_bits = y.cpu().numpy().view(np.uint16)
+        assert np.isfinite(y.float().cpu().numpy()).all()
+        max_abs, max_rel, excess, mismatches = compare_halves(y_bits[rows], y_ref, rtol=2 * RTOL if gelu else RTOL)
+        print(f"{name}: max_abs={max_abs:.3g} mismatch={mismatches}/{y_ref.size}")
+        assert excess <= 0
+        if gelu:
+            np.testing.assert_array_equal(codes.cpu().numpy(), oracle.quantize(y_bits, np.float32(0.0123)))
