@@ -432,8 +432,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float act_scale = p.act_scale_ptr ? *p.act_scale_ptr : p.act_scale;
         const uint64_t neg_scale2 = f2_bits(-p.next_scale, -p.next_scale);
         const uint64_t recip2 = f2_bits(p.next_recip, p.next_recip);
-        // Accumulator release goes to the leader's barrier (a cluster address in a pair).
-        const uint32_t acc_empty_target = kPair ? map_to_rank(bar_acc_empty, 0) : bar_acc_empty;
+        // Accumulator release goes to the leader's barriers (cluster addresses in a pair).
+        const uint32_t acc_empty_base = kPair ? map_to_rank(bar_acc_empty, 0) : bar_acc_empty;
         uint8_t *staging = smem + C::kOffStaging + ew * C::kWarpStaging;
         const uint32_t staging_s = smem_u32(staging);
         uint32_t stores = 0;
@@ -491,9 +491,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     __syncwarp();
                     if (lane == 0) {
                         if (kPair)
-                            mbar_arrive_cluster(acc_empty_target);
+                            mbar_arrive_cluster(acc_empty_base + 8 * a);
                         else
-                            mbar_arrive(acc_empty_target);
+                            mbar_arrive(acc_empty_base + 8 * a);
                     }
                 }
                 // Scale, round to fp16, bias, GELU: two columns per packed op.
@@ -554,9 +554,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) {
                     if (kPair)
-                        mbar_arrive_cluster(acc_empty_target);
+                        mbar_arrive_cluster(acc_empty_base + 8 * a);
                     else
-                        mbar_arrive(acc_empty_target);
+                        mbar_arrive(acc_empty_base + 8 * a);
                 }
             }
         }
