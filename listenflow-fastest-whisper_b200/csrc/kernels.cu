@@ -20,8 +20,10 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <string>
 #include <set>
 #include <utility>
 
@@ -1023,31 +1025,38 @@ cudaError_t run_gemm_epilogue(const LinearLaunch &L, cudaStream_t stream)
     }
 }
 
-// Fraction of the last wave that is busy when `tiles` tiles run on `units`
-// persistent workers.
-double wave_efficiency(int64_t tiles, int64_t units)
-{
-    const int64_t waves = (tiles + units - 1) / units;
-    return static_cast<double>(tiles) / static_cast<double>(waves * units);
-}
 
 } // namespace
 
+// LFFW_GEMM_TILE overrides the tile choice (tuning): "1x256", "1x128",
+// "2x256", "2x128" = CTAs per tile x tile width.  Read once per process.
+int tile_override()
+{
+    static const int mode = [] {
+        const char *v = std::getenv("LFFW_GEMM_TILE");
+        if (v == nullptr)
+            return 0;
+        const std::string s(v);
+        return s == "1x256" ? 1 : s == "1x128" ? 2 : s == "2x256" ? 3 : s == "2x128" ? 4 : 0;
+    }();
+    return mode;
+}
+
 cudaError_t launch_fp8_gemm(const LinearLaunch &L, cudaStream_t stream)
 {
-    // CTA pairs (256-row tiles) once M fills them; 1-CTA 128-row tiles below.
-    // Tile width: 256 unless 128 wastes clearly less of the last wave.
-    const int sms = sm_count();
-    const bool pair = L.m >= 512;
-    const int64_t tile_m = pair ? 256 : 128;
-    const int64_t units = pair ? sms / 2 : sms;
-    const int64_t m_tiles = (L.m + tile_m - 1) / tile_m;
-    const double e256 = wave_efficiency(m_tiles * ((L.n + 255) / 256), units);
-    const double e128 = wave_efficiency(m_tiles * ((L.n + 127) / 128), units);
-    const bool wide = !(e256 < 0.85 && e128 > e256 + 0.05);
-    if (pair)
-        return wide ? run_gemm_epilogue<256, true>(L, stream) : run_gemm_epilogue<128, true>(L, stream);
-    return wide ? run_gemm_epilogue<256, false>(L, stream) : run_gemm_epilogue<128, false>(L, stream);
+    switch (tile_override()) {
+    case 1: return run_gemm_epilogue<256, false>(L, stream);
+    case 2: return run_gemm_epilogue<128, false>(L, stream);
+    case 3: return run_gemm_epilogue<256, true>(L, stream);
+    case 4: return run_gemm_epilogue<128, true>(L, stream);
+    default: break;
+    }
+    // Measured on B200 (C2 shapes, M = 12000): 256-wide tiles beat 128-wide ones
+    // by ~30% even where 128 would fill the last wave better; CTA pairs (256-row
+    // tiles, half the B traffic per SM) win once the K loop is long, 1-CTA
+    // 128-row tiles win for K = 1280.
+    const bool pair = L.m >= 512 && L.k >= 4096;
+    return pair ? run_gemm_epilogue<256, true>(L, stream) : run_gemm_epilogue<256, false>(L, stream);
 }
 
 cudaError_t launch_fp8_gemv(const LinearLaunch &L, cudaStream_t stream)
