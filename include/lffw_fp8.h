@@ -146,6 +146,36 @@ LFFW_FP8_API uint64_t lffw_launch_count(void) LFFW_FP8_NOEXCEPT;
 LFFW_FP8_API const char *lffw_status_string(lffw_status status) LFFW_FP8_NOEXCEPT;
 LFFW_FP8_API void lffw_version(uint32_t *major, uint32_t *minor) LFFW_FP8_NOEXCEPT;
 
+/* ---- Allocation-free FP8 linear on fp16 activations ------------------------
+ * No counterpart in the reference: an addition of this library.
+ *
+ * The usual way to run a linear on fp16 activations is lffw_fp8_quantize into
+ * a codes buffer the caller allocated, then lffw_fp8_linear (or the
+ * LffwFp8Linear plugin with a workspace).  Some callers cannot allocate that
+ * buffer: a latency-critical streaming thread must not call cudaMalloc, which
+ * can synchronize the whole device and block for milliseconds; a plugin host
+ * may hand out only the workspace it sized before the run; a process whose
+ * device memory is already reserved by another allocator has nothing left to
+ * give.  This entry point keeps the E4M3 codes of x in a fixed buffer inside the
+ * library instead (LFFW_STATIC_SCRATCH_BYTES per GPU that loads the library,
+ * held until the process exits) and allocates nothing itself.
+ *
+ * Same arithmetic as lffw_fp8_quantize(x, m*k, act_scale) followed by
+ * lffw_fp8_linear with the same weights, bias and epilogue, writing fp16 y.
+ * Limits: m * k <= LFFW_STATIC_SCRATCH_BYTES, else LFFW_SCRATCH_TOO_SMALL and
+ * nothing runs; the other requirements of lffw_fp8_linear apply.
+ * The first call on a device looks up the buffer's device address once; make
+ * that first call before any stream capture.  Every call on a device shares
+ * the one buffer, and each call overwrites the part it reads: calls whose work
+ * overlaps on the GPU (different streams without ordering) race on it. */
+#define LFFW_STATIC_SCRATCH_BYTES (8u << 20) /* 8 MiB of E4M3 codes */
+enum { LFFW_SCRATCH_TOO_SMALL = 121 };
+LFFW_FP8_API lffw_status lffw_fp8_linear_half_static(const uint16_t *x, int64_t m, int64_t n, int64_t k,
+                                                     float act_scale, const uint8_t *w_codes,
+                                                     const float *w_scales, const uint16_t *bias,
+                                                     int32_t epilogue, uint16_t *y,
+                                                     void *stream) LFFW_FP8_NOEXCEPT;
+
 /* ---- Plugin surface ------------------------------------------------------
  * A C restatement of the reference's TensorRT IPluginV3 creators
  * (namespace "listenflow.fastest_whisper"): LffwFp16Fc1 v"1", LffwFp16Qkv v"2",

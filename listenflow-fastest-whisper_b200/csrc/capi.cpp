@@ -260,6 +260,7 @@ const char *lffw_status_string(lffw_status status) noexcept
     case LFFW_CUDA_ERROR: return "CUDA error";
     case LFFW_UNSUPPORTED_PRECISION: return "fp8 requires an sm_100 (B200) device";
     case LFFW_DEVICE_TIMEOUT: return "a bounded device-side wait expired";
+    case LFFW_SCRATCH_TOO_SMALL: return "m * k exceeds the library's static scratch (LFFW_STATIC_SCRATCH_BYTES)";
     default: return "unknown status";
     }
 }

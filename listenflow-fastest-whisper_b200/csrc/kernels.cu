@@ -20,6 +20,8 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cmath>
+#include <cstdint>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -28,6 +30,7 @@
 #include <utility>
 
 #include "launch.h"
+#include "lffw_fp8.h"
 #include "ptx.cuh"
 
 #include "erf_table.inc"
@@ -1204,3 +1207,88 @@ cudaError_t read_and_clear_device_error(int *site)
 }
 
 } // namespace lffw
+
+// ---------------------------------------------------------------------------
+// Allocation-free FP8 linear on fp16 activations (lffw_fp8_linear_half_static).
+//
+// The E4M3 codes of the activations live in this fixed device buffer instead
+// of memory the caller allocates, for callers that cannot allocate device
+// memory (see include/lffw_fp8.h).  Each GPU that loads the library holds one
+// copy until the process exits.  Nothing in it needs to start at zero: every
+// call first writes the m * k codes it then reads.
+
+static __device__ __align__(256) uint8_t g_static_scratch[LFFW_STATIC_SCRATCH_BYTES];
+
+namespace {
+
+// Device address of g_static_scratch per device, looked up once with the
+// device current.  The symbol's name in host code is only a host-side handle.
+cudaError_t static_scratch_address(uint8_t **out)
+{
+    static std::mutex lock;
+    static uint8_t *addresses[lffw::kMaxDevices] = {};
+    const int device = lffw::current_device();
+    std::lock_guard<std::mutex> guard(lock);
+    if (addresses[device] == nullptr) {
+        void *p = nullptr;
+        const cudaError_t err = cudaGetSymbolAddress(&p, g_static_scratch);
+        if (err != cudaSuccess)
+            return err;
+        addresses[device] = static_cast<uint8_t *>(p);
+    }
+    *out = addresses[device];
+    return cudaSuccess;
+}
+
+bool static_aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+} // namespace
+
+extern "C" LFFW_FP8_API lffw_status lffw_fp8_linear_half_static(const uint16_t *x, int64_t m, int64_t n, int64_t k,
+                                                                float act_scale, const uint8_t *w_codes,
+                                                                const float *w_scales, const uint16_t *bias,
+                                                                int32_t epilogue, uint16_t *y, void *stream) noexcept
+{
+    if (x == nullptr || w_codes == nullptr || w_scales == nullptr || y == nullptr || m < 1 || n < 1 || k < 1 ||
+        k % 16 != 0 || n % 16 != 0 || m > INT32_MAX || n > INT32_MAX || k > INT32_MAX)
+        return LFFW_INVALID_ARGUMENT;
+    if (!static_aligned16(x) || !static_aligned16(w_codes) || !static_aligned16(w_scales) ||
+        !static_aligned16(bias) || !static_aligned16(y))
+        return LFFW_INVALID_ARGUMENT;
+    if (!(std::isfinite(act_scale) && act_scale >= 0x1p-125f && act_scale <= 0x1p125f))
+        return LFFW_INVALID_ARGUMENT;
+    if (epilogue != LFFW_EPILOGUE_NONE && epilogue != LFFW_EPILOGUE_GELU)
+        return LFFW_INVALID_ARGUMENT;
+    if (m * k > static_cast<int64_t>(LFFW_STATIC_SCRATCH_BYTES))
+        return LFFW_SCRATCH_TOO_SMALL;
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) {
+        cudaGetLastError();
+        return LFFW_CUDA_ERROR;
+    }
+    const lffw_status gate = lffw_device_supported(device);
+    if (gate != LFFW_SUCCESS)
+        return gate;
+    uint8_t *codes = nullptr;
+    if (static_scratch_address(&codes) != cudaSuccess) {
+        cudaGetLastError();
+        return LFFW_CUDA_ERROR;
+    }
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (lffw::launch_quantize(x, m * k, act_scale, nullptr, codes, st) != cudaSuccess)
+        return LFFW_CUDA_ERROR;
+    lffw::LinearLaunch L{};
+    L.m = m;
+    L.n = n;
+    L.k = k;
+    L.x_codes = codes;
+    L.act_scale = act_scale;
+    L.w_codes = w_codes;
+    L.w_scales = w_scales;
+    L.bias = bias;
+    L.gelu = epilogue == LFFW_EPILOGUE_GELU;
+    L.y = y;
+    const bool small = m <= lffw::kGemvMaxRows && m * k <= lffw::kGemvMaxSmem;
+    const cudaError_t err = small ? lffw::launch_fp8_gemv(L, st) : lffw::launch_fp8_gemm(L, st);
+    return err == cudaSuccess ? LFFW_SUCCESS : LFFW_CUDA_ERROR;
+}
