@@ -61,7 +61,7 @@ CONFIG = {
 def parse_args(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--e2e-steps", type=int, default=5)
@@ -71,7 +71,7 @@ def parse_args(argv=None):
 
 
 def dist_env():
-    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    return importlib.import_module(PACKAGE + ".replicas").env_rank()
 
 
 def synthetic(seed: int):
@@ -94,64 +94,68 @@ def synthetic(seed: int):
 # Clock sampling during the timed region.
 
 class ClockSampler:
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """Samples SM clock and clock-event reasons through NVML every ~2 ms while
+    the timed region runs (a thread; reading settings only)."""
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.lines: list[str] = []
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, bus_id: str):
+        self.bus_id = bus_id
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._nvml = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except OSError:
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._handle = pynvml.nvmlDeviceGetHandleByPciBusId(self.bus_id)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        except Exception:  # no NVML: report no samples
+            self._nvml = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                clk = nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM)
+                why = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._handle)
+                self.samples.append((clk, why))
+            except Exception:
+                break
+            time.sleep(0.002)
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
+        self._stop.set()
+        if self._nvml is not None:
+            self._thread.join(timeout=2)
             try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+                self._nvml.nvmlShutdown()
+            except Exception:
+                pass
 
     def summary(self):
-        sms, reasons, max_mhz = [], set(), None
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sms.append(float(parts[1]))
-                max_mhz = float(parts[2])
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower() == "active":
+        clocks = [c for c, _ in self.samples]
+        reasons = set()
+        for _, bits in self.samples:
+            for bit, name in self.REASONS.items():
+                if bits & bit:
                     reasons.add(name)
-        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": max_mhz,
-                "reasons": sorted(reasons), "samples": len(sms)}
+        return {"sm_mhz": statistics.median(clocks) if clocks else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(clocks)}
 
 
-def smi_id(torch, device) -> str:
-    """nvidia-smi --id for a torch device (PCI bus id; CUDA_VISIBLE_DEVICES-safe)."""
+def pci_bus_id(torch, device) -> str:
+    """NVML bus id of a torch device (independent of CUDA_VISIBLE_DEVICES)."""
     props = torch.cuda.get_device_properties(device)
-    try:
-        return f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
-    except AttributeError:
-        return str(device.index)
+    return f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
 
 
 # ---------------------------------------------------------------------------
@@ -162,15 +166,10 @@ def run_ours(args, rank, local_rank, world):
 
     fp8 = importlib.import_module(PACKAGE + ".fp8")
     native = importlib.import_module(PACKAGE + "._native")
+    replicas = importlib.import_module(PACKAGE + ".replicas")
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    dist = replicas.init("nccl", device=device) if world > 1 else None
 
     acts_np, weights_np = synthetic(seed=1234 + rank)
     # Static activation scales: the calibration rule (amax/448) applied once.
@@ -233,7 +232,7 @@ def run_ours(args, rank, local_rank, world):
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(smi_id(torch, device)) as clocks:
+    with ClockSampler(pci_bus_id(torch, device)) as clocks:
         for s in range(args.steps):
             flush.zero_()  # L2 flush, outside the step's events
             ev[s][7].record(stream)
@@ -286,18 +285,13 @@ def run_ours(args, rank, local_rank, world):
     e2e_ms = e_start.elapsed_time(e_end)
 
     # Max over ranks.
-    times = np.array([total_ms, total_gemm_ms, e2e_ms], dtype=np.float64)
-    if dist is not None:
-        t = _t.tensor(times, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        times = t.cpu().numpy()
-    total_ms, total_gemm_ms, e2e_ms = (float(v) for v in times)
+    total_ms, total_gemm_ms, e2e_ms = replicas.max_over_ranks([total_ms, total_gemm_ms, e2e_ms], dist, device)
 
     result = None
     if rank == 0:
         peaks = read_peaks()
         ms_per_step = total_ms / args.steps
-        value = world * FLOPS_PER_STEP * args.steps / (total_ms / 1e3) / 1e12
+        value = replicas.whole_job_rate(FLOPS_PER_STEP * args.steps, world, total_ms / 1e3) / 1e12
         gemm_launch_ms = total_gemm_ms / (4 * args.steps)
         gemm_achieved = FLOPS_PER_STEP / 4 / (gemm_launch_ms / 1e3) / 1e12
         peak, peak_src = peaks
@@ -336,6 +330,11 @@ def run_ours(args, rank, local_rank, world):
                 "d2h_bytes_per_step": d2h,
                 "api": "fp8.quantize / fp8.linear (C ABI lffw_fp8_quantize / lffw_fp8_linear)",
             },
+            "encoder_linears_audio_s_per_s": round(
+                replicas.whole_job_rate(8 * 30.0, world, 32 * ms_per_step / 1e3), 1),
+            "encoder_linears_audio_note": "30 s streams/s through the FP8 linears of all 32 encoder layers "
+                                          "(8 streams per step and GPU); attention, LayerNorm, conv and "
+                                          "cross-K/V projections are not included",
             "gpu_launches": int(launches),
             "clocks": clocks.summary(),
         }
