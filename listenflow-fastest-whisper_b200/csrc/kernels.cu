@@ -137,19 +137,20 @@ __device__ __forceinline__ uint32_t e4m3x2_quotient(uint32_t h2, uint64_t scale2
 //
 // Persistent, warp-specialized: warp 0 issues TMA loads into a ring of shared
 // memory stages, warp 1 issues tcgen05.mma (one thread) into one of two TMEM
-// accumulators, warps 2-9 drain the other accumulator through the epilogue.
-// Each epilogue warp owns 32 TMEM lanes (rows) x half the tile's columns and
-// stores its own 32 x 32 sub-blocks with TMA from a private double buffer, so
-// no epilogue warp ever waits for another.
+// accumulators, warps 2-17 drain the other accumulator through the epilogue.
+// Each epilogue warp owns 32 TMEM lanes (rows) x a quarter of the tile's
+// columns and stores its own 32 x 32 sub-blocks with TMA from a private
+// staging buffer, so no epilogue warp ever waits for another; four warps per
+// lane quarter keep the scale / GELU / quotient arithmetic latency hidden.
 
 namespace gemm {
 
 constexpr int kBM = 128;       // tile rows (TMEM lanes)
 constexpr int kBK = 128;       // K bytes per stage = one 128B swizzle row
 constexpr int kUmmaK = 32;     // K of one kind::f8f6f4 MMA
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 16;             // 4 per TMEM lane quarter
 constexpr int kEpiThreads = kEpiWarps * 32;
-constexpr int kThreads = 64 + kEpiThreads; // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+constexpr int kThreads = 64 + kEpiThreads; // warp 0 TMA, warp 1 MMA, warps 2-17 epilogue
 constexpr int kSub = 32;                   // columns per epilogue store
 
 enum : int { kEpiGelu = 1, kEpiY = 2, kEpiCodes = 4 };
@@ -171,7 +172,7 @@ struct Cfg {
     static constexpr int kTxBytes = kPair ? 2 * kStageBytes : kStageBytes; // counted on the leader
     static constexpr int kYBuf = 32 * kSub * 2; // 32 rows x 64 B (fp16), 64B swizzle
     static constexpr int kCBuf = 32 * kSub;     // 32 rows x 32 B (E4M3), 32B swizzle
-    static constexpr int kWarpStaging = 2 * ((kY ? kYBuf : 0) + (kCodes ? kCBuf : 0));
+    static constexpr int kWarpStaging = (kY ? kYBuf : 0) + (kCodes ? kCBuf : 0);
     static constexpr int kStagingBytes = kEpiWarps * kWarpStaging;
     static constexpr int kTableBytes = kGelu ? (LFFW_ERF_TABLE_SIZE * 2 + 1023) / 1024 * 1024 : 0;
     static constexpr int kBarBytes = 256;
@@ -433,7 +434,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- Epilogue: 8 independent warps ----------------
         const int ew = warp - 2;
         const int quarter = warp & 3; // the TMEM lane quarter this warp may access
-        const int half = ew >> 2;     // which half of the tile's columns
+        const int slice = ew >> 2;    // which quarter of the tile's columns
         const float act_scale = p.act_scale_ptr ? *p.act_scale_ptr : p.act_scale;
         const uint64_t neg_scale2 = f2_bits(-p.next_scale, -p.next_scale);
         const uint64_t recip2 = f2_bits(p.next_recip, p.next_recip);
@@ -441,7 +442,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t acc_empty_base = kPair ? map_to_rank(bar_acc_empty, 0) : bar_acc_empty;
         uint8_t *staging = smem + C::kOffStaging + ew * C::kWarpStaging;
         const uint32_t staging_s = smem_u32(staging);
-        uint32_t stores = 0;
         int local = 0;
         for (int t = tile_first; t < p.num_tiles; t += tile_step, ++local) {
             const int m0 = (t % p.m_tiles) * C::kTileM + static_cast<int>(rank) * kBM;
@@ -452,107 +452,99 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok)
                 break;
             tc_fence_after();
-            const int col_begin = n0 + half * (BN / 2);
+            const int col_begin = n0 + slice * (BN / 4);
             int subs = (p.n - col_begin + kSub - 1) / kSub;
-            subs = subs < 0 ? 0 : (subs > BN / 2 / kSub ? BN / 2 / kSub : subs);
+            subs = subs < 0 ? 0 : (subs > BN / 4 / kSub ? BN / 4 / kSub : subs);
             const int row0 = m0 + quarter * 32;
             if (row0 >= p.m)
                 subs = 0; // every row of this warp is padding: nothing to load or store
-            const uint32_t t_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN + half * (BN / 2);
+            const uint32_t t_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN + slice * (BN / 4);
 #pragma unroll 1
             for (int sub = 0; sub < subs; ++sub) {
                 const int col0 = col_begin + sub * kSub;
-                // Per-column scale and bias (broadcast loads), issued before the TMEM read.
-                float cs[kSub];
-                uint32_t bias2[kSub / 2];
-                // N % 16 == 0, so each group of 4 (8) columns is wholly inside or outside N.
-#pragma unroll
-                for (int i = 0; i < kSub / 4; ++i) {
-                    const float4 w4 = col0 + 4 * i < p.n
-                                          ? __ldg(reinterpret_cast<const float4 *>(p.w_scales + col0) + i)
-                                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                    cs[4 * i + 0] = act_scale * w4.x;
-                    cs[4 * i + 1] = act_scale * w4.y;
-                    cs[4 * i + 2] = act_scale * w4.z;
-                    cs[4 * i + 3] = act_scale * w4.w;
-                }
-                if (p.bias) {
-#pragma unroll
-                    for (int i = 0; i < kSub / 8; ++i) {
-                        const uint4 b4 = col0 + 8 * i < p.n
-                                             ? __ldg(reinterpret_cast<const uint4 *>(p.bias + col0) + i)
-                                             : make_uint4(0u, 0u, 0u, 0u);
-                        bias2[4 * i + 0] = b4.x;
-                        bias2[4 * i + 1] = b4.y;
-                        bias2[4 * i + 2] = b4.z;
-                        bias2[4 * i + 3] = b4.w;
-                    }
-                }
-                uint32_t v[kSub];
-                tmem_ld_32x32b_x32(t_base + sub * kSub, v);
-                tmem_wait_ld();
-                if (sub == subs - 1) {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) {
-                        if (kPair)
-                            mbar_arrive_cluster(acc_empty_base + 8 * a);
-                        else
-                            mbar_arrive(acc_empty_base + 8 * a);
-                    }
-                }
-                // Scale, round to fp16, bias, GELU: two columns per packed op.
-                uint32_t h[kSub / 2];
-#pragma unroll
-                for (int i = 0; i < kSub / 2; ++i) {
-                    const float2 y = fmul2(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])),
-                                           make_float2(cs[2 * i], cs[2 * i + 1]));
-                    uint32_t z = cvt_f16x2(y.x, y.y);
-                    if (p.bias)
-                        z = hadd2_rn(z, bias2[i]);
-                    if (C::kGelu)
-                        z = gelu_fp16x2(z, erf_table);
-                    h[i] = z;
-                }
-                const uint32_t buf = stores & 1u;
+                // The previous store from this warp's staging buffer has read it.
                 if (lane == 0)
-                    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                    bulk_wait_group_read0();
                 __syncwarp();
-                if (C::kY) {
-                    // 32 rows x 64 B, 64B swizzle: 16B chunk j of row r at chunk j ^ ((r >> 1) & 3).
-                    uint8_t *ybuf = staging + buf * C::kYBuf;
+                // Two 16-column halves keep the live registers low.
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const uint32_t pos = static_cast<uint32_t>(j) ^ ((static_cast<uint32_t>(lane) >> 1) & 3u);
-                        *reinterpret_cast<uint4 *>(ybuf + lane * 64 + pos * 16) =
-                            make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+                for (int hf = 0; hf < 2; ++hf) {
+                    const int c0 = col0 + hf * 16;
+                    // Per-column scale and bias (broadcast loads), issued before the TMEM read.
+                    // N % 16 == 0, so a 16-column half is wholly inside or outside N.
+                    const bool inside = c0 < p.n;
+                    float4 w4[4];
+                    uint4 b4[2];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        w4[i] = inside ? __ldg(reinterpret_cast<const float4 *>(p.w_scales + c0) + i)
+                                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    if (p.bias) {
+#pragma unroll
+                        for (int i = 0; i < 2; ++i)
+                            b4[i] = inside ? __ldg(reinterpret_cast<const uint4 *>(p.bias + c0) + i)
+                                           : make_uint4(0u, 0u, 0u, 0u);
                     }
-                }
-                if (C::kCodes) {
-                    // 32 rows x 32 B, 32B swizzle: chunk j of row r at chunk j ^ ((r >> 2) & 1).
-                    uint8_t *cbuf = staging + (C::kY ? 2 * C::kYBuf : 0) + buf * C::kCBuf;
-                    uint32_t q[8];
+                    uint32_t v[16];
+                    tmem_ld_32x32b_x16(t_base + sub * kSub + hf * 16, v);
+                    tmem_wait_ld();
+                    if (sub == subs - 1 && hf == 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) {
+                            if (kPair)
+                                mbar_arrive_cluster(acc_empty_base + 8 * a);
+                            else
+                                mbar_arrive(acc_empty_base + 8 * a);
+                        }
+                    }
+                    // Scale, round to fp16, bias, GELU: two columns per packed op.
+                    const float2 act2 = make_float2(act_scale, act_scale);
+                    const uint32_t bias2[8] = {b4[0].x, b4[0].y, b4[0].z, b4[0].w, b4[1].x, b4[1].y, b4[1].z, b4[1].w};
+                    uint32_t h[8];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        q[i] = e4m3x2_quotient(h[2 * i], neg_scale2, recip2) |
-                               (e4m3x2_quotient(h[2 * i + 1], neg_scale2, recip2) << 16);
+                    for (int i = 0; i < 8; ++i) {
+                        const float4 &w = w4[i / 2];
+                        const float2 cs = fmul2(act2, (i & 1) ? make_float2(w.z, w.w) : make_float2(w.x, w.y));
+                        const float2 y = fmul2(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), cs);
+                        uint32_t z = cvt_f16x2(y.x, y.y);
+                        if (p.bias)
+                            z = hadd2_rn(z, bias2[i]);
+                        if (C::kGelu)
+                            z = gelu_fp16x2(z, erf_table);
+                        h[i] = z;
+                    }
+                    if (C::kY) {
+                        // 32 rows x 64 B, 64B swizzle: 16B chunk j of row r at chunk j ^ ((r >> 1) & 3).
 #pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        const uint32_t pos = static_cast<uint32_t>(j) ^ ((static_cast<uint32_t>(lane) >> 2) & 1u);
-                        *reinterpret_cast<uint4 *>(cbuf + lane * 32 + pos * 16) =
-                            make_uint4(q[4 * j], q[4 * j + 1], q[4 * j + 2], q[4 * j + 3]);
+                        for (int jj = 0; jj < 2; ++jj) {
+                            const uint32_t j = static_cast<uint32_t>(2 * hf + jj);
+                            const uint32_t pos = j ^ ((static_cast<uint32_t>(lane) >> 1) & 3u);
+                            *reinterpret_cast<uint4 *>(staging + lane * 64 + pos * 16) =
+                                make_uint4(h[4 * jj], h[4 * jj + 1], h[4 * jj + 2], h[4 * jj + 3]);
+                        }
+                    }
+                    if (C::kCodes) {
+                        // 32 rows x 32 B, 32B swizzle: chunk j of row r at chunk j ^ ((r >> 2) & 1).
+                        uint8_t *cbuf = staging + (C::kY ? C::kYBuf : 0);
+                        uint32_t q[4];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            q[i] = e4m3x2_quotient(h[2 * i], neg_scale2, recip2) |
+                                   (e4m3x2_quotient(h[2 * i + 1], neg_scale2, recip2) << 16);
+                        const uint32_t pos = static_cast<uint32_t>(hf) ^ ((static_cast<uint32_t>(lane) >> 2) & 1u);
+                        *reinterpret_cast<uint4 *>(cbuf + lane * 32 + pos * 16) = make_uint4(q[0], q[1], q[2], q[3]);
                     }
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
                     if (C::kY)
-                        tma_store_2d(&tm_y, staging_s + buf * C::kYBuf, col0, row0);
+                        tma_store_2d(&tm_y, staging_s, col0, row0);
                     if (C::kCodes)
-                        tma_store_2d(&tm_c, staging_s + (C::kY ? 2 * C::kYBuf : 0) + buf * C::kCBuf, col0, row0);
+                        tma_store_2d(&tm_c, staging_s + (C::kY ? C::kYBuf : 0), col0, row0);
                     bulk_commit_group();
                 }
-                ++stores;
             }
             if (subs == 0) {
                 tc_fence_before();
