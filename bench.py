@@ -65,6 +65,8 @@ def parse_args(argv=None):
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--e2e-steps", type=int, default=5)
+    p.add_argument("--decoder-steps", type=int, default=20,
+                   help="timed replays of the C3 decoder-step graph (0 skips it)")
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="target CPU-baseline sample time (0 skips the CPU baseline, for profiling runs)")
     return p.parse_args(argv)
@@ -284,6 +286,10 @@ def run_ours(args, rank, local_rank, world):
     _t.cuda.synchronize()
     e2e_ms = e_start.elapsed_time(e_end)
 
+    decoder = None
+    if args.decoder_steps > 0:
+        del flush
+        decoder = run_decoder(fp8, native, device, args.decoder_steps, 3, seed=77 + rank)
     # Max over ranks.
     total_ms, total_gemm_ms, e2e_ms = replicas.max_over_ranks([total_ms, total_gemm_ms, e2e_ms], dist, device)
 
@@ -338,12 +344,106 @@ def run_ours(args, rank, local_rank, world):
             "gpu_launches": int(launches),
             "clocks": clocks.summary(),
         }
+        if args.decoder_steps > 0:
+            result["decoder_step"] = decoder
         if world == 1 and args.cpu_seconds > 0:
             result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
     return result
+
+
+# ---------------------------------------------------------------------------
+# Decoder step: M = 20 rows (4 streams x 5 beams), 32 layers
+# of {self QKV 1280->3840, self out 1280->1280, cross q 1280->1280, cross out
+# 1280->1280, fc1 1280->5120 + GELU (emits fc2's codes), fc2 5120->1280} with
+# E4M3 weights, then the fp16 logits projection 1280->51866.  Memory-bound: the
+# metric is weight bytes streamed per second.
+
+DEC_M = 20
+DEC_LAYERS = 32
+VOCAB = 51866
+DEC_LINEARS = (("qkv", 1280, 3840), ("self_out", 1280, 1280), ("cross_q", 1280, 1280),
+               ("cross_out", 1280, 1280), ("fc1", 1280, 5120), ("fc2", 5120, 1280))
+
+
+def run_decoder(fp8, native, device, steps: int, warmup: int, seed: int):
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    layers = []
+    weight_bytes = 0
+    for _ in range(DEC_LAYERS):
+        layer = {}
+        for name, k, n in DEC_LINEARS:
+            w = (torch.randn(n, k, generator=g, device=device) * 0.02).half()
+            b = (torch.randn(n, generator=g, device=device) * 0.02).half()
+            layer[name] = fp8.QuantizedWeight.from_half(w, b)
+            weight_bytes += n * k + n * 4 + n * 2  # E4M3 codes + fp32 scales + fp16 bias
+            del w
+        layers.append(layer)
+    logits_w = (torch.randn(VOCAB, 1280, generator=g, device=device) * 0.02).half()
+    weight_bytes += VOCAB * 1280 * 2
+    x_codes = fp8.quantize(torch.randn(DEC_M, 1280, generator=g, device=device).half(), 0.01)
+    x16 = torch.randn(DEC_M, 1280, generator=g, device=device).half()
+    outs = {name: torch.empty(DEC_M, n, dtype=torch.float16, device=device) for name, _, n in DEC_LINEARS}
+    fc2_in = torch.empty(DEC_M, 5120, dtype=torch.uint8, device=device)
+    logits = torch.empty(DEC_M, VOCAB, dtype=torch.float16, device=device)
+
+    def step():
+        for layer in layers:
+            for name in ("qkv", "self_out", "cross_q", "cross_out"):
+                q = layer[name]
+                fp8.linear(x_codes, q.codes, q.scales, 0.01, bias=q.bias, out=outs[name])
+            q = layer["fc1"]
+            fp8.linear(x_codes, q.codes, q.scales, 0.01, bias=q.bias, gelu=True, want_y=False, next_scale=0.02,
+                       next_codes=fc2_in)
+            q = layer["fc2"]
+            fp8.linear(fc2_in, q.codes, q.scales, 0.02, bias=q.bias, out=outs["fc2"])
+        fp8.fp16_linear(x16, logits_w, out=logits)
+
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, warmup)):
+            step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    launches_per_step = DEC_LAYERS * 6 + 1
+    for _ in range(max(1, warmup)):
+        graph.replay()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    if native.device_error() != 0:
+        raise RuntimeError("device-side wait timed out in the decoder step")
+    ms = statistics.median(times)
+    hbm = read_hbm_peak()
+    gbs = weight_bytes / (ms / 1e3) / 1e9
+    del graph
+    return {"workload": "C3: decoder step, M=20 (4 streams x 5 beams), 32 layers x 6 E4M3 linears + fp16 logits "
+                        "1280->51866, one CUDA graph with programmatic dependent launches",
+            "ms_per_step": round(ms, 4), "weight_bytes_per_step": weight_bytes,
+            "value": round(gbs, 1), "unit": "GB/s (weights streamed)",
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm[0], "peak_source": hbm[1],
+                         "unit": "GB/s", "frac": round(gbs / hbm[0], 4)},
+            "launches_per_step": launches_per_step}
+
+
+def read_hbm_peak():
+    try:
+        return round(float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["hbm_gbs"]), 1), \
+            "MEASURED_PEAKS.json hbm_gbs (copy)"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback 6.65 TB/s"
 
 
 def read_peaks():

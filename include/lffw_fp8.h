@@ -124,6 +124,14 @@ LFFW_FP8_API lffw_status lffw_fp16_qkv(const uint16_t *x, const uint16_t *weight
 LFFW_FP8_API lffw_status lffw_fp16_bias(const uint16_t *x, uint16_t bias_bits, uint16_t *y,
                                         int64_t count, void *stream) LFFW_FP8_NOEXCEPT;
 
+/* fp16 linear for up to 32 rows (the decoder step's fp16 logits MatMul,
+ * 1280 -> vocabulary, cpp/src/network_graph.cpp:379-417): y[m,n] =
+ * half(sum_k x[m,k] w[n,k] (+ bias[n])), fp32 accumulate on tensor cores.
+ * x [m,k], w [n,k] fp16 row-major; 1 <= m <= 32; k % 8 == 0; bias may be NULL. */
+LFFW_FP8_API lffw_status lffw_fp16_linear(const uint16_t *x, const uint16_t *weight, const uint16_t *bias,
+                                          uint16_t *y, int64_t m, int64_t n, int64_t k,
+                                          void *stream) LFFW_FP8_NOEXCEPT;
+
 /* GELU with every graph edge rounded to fp16, elementwise on `count` halves:
  * y = (x*0.5)*(1 + erf(x*fp16(2^-1/2))) (graph::gelu, network_graph.cpp:168-180).
  * The same device code as the fused GEMM epilogue. */

@@ -119,6 +119,7 @@ def library() -> ctypes.CDLL:
         "lffw_fp16_qkv": ([_vp, _vp, _vp, _vp, _vp, _i64, _vp], _i32),
         "lffw_fp16_bias": ([_vp, ctypes.c_uint16, _vp, _i64, _vp], _i32),
         "lffw_fp16_gelu": ([_vp, _vp, _i64, _vp], _i32),
+        "lffw_fp16_linear": ([_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp], _i32),
         "lffw_device_supported": ([_i32], _i32),
         "lffw_device_error": ([ctypes.POINTER(_i32)], _i32),
         "lffw_launch_count": ([], ctypes.c_uint64),

@@ -120,8 +120,8 @@ lffw_status run_linear(const lffw_fp8_linear_args *a, cudaStream_t stream)
     L.y = a->y;
     L.next_scale = a->next_scale;
     L.next_codes = a->next_codes;
-    const bool small = a->m <= lffw::kGemvMaxRows && a->m * a->k <= lffw::kGemvMaxSmem;
-    return from_cuda(small ? lffw::launch_fp8_gemv(L, stream) : lffw::launch_fp8_gemm(L, stream));
+    const bool small = a->m <= lffw::kGemvMaxRows;
+    return from_cuda(small ? lffw::launch_fp8_skinny(L, stream) : lffw::launch_fp8_gemm(L, stream));
 }
 
 } // namespace
@@ -222,6 +222,18 @@ lffw_status lffw_fp16_bias(const uint16_t *x, uint16_t bias_bits, uint16_t *y, i
     if (s != LFFW_SUCCESS)
         return s;
     return from_cuda(lffw::launch_fp16_bias(x, bias_bits, y, count, static_cast<cudaStream_t>(stream)));
+}
+
+lffw_status lffw_fp16_linear(const uint16_t *x, const uint16_t *weight, const uint16_t *bias, uint16_t *y,
+                             int64_t m, int64_t n, int64_t k, void *stream) noexcept
+{
+    if (x == nullptr || weight == nullptr || y == nullptr || m < 1 || m > lffw::kGemvMaxRows || n < 1 ||
+        n > kMaxDim || k < 8 || k % 8 != 0 || k > kMaxDim || !aligned16(x) || !aligned16(weight))
+        return LFFW_INVALID_ARGUMENT;
+    lffw_status s = current_device_gate();
+    if (s != LFFW_SUCCESS)
+        return s;
+    return from_cuda(lffw::launch_fp16_skinny(x, weight, bias, y, m, n, k, static_cast<cudaStream_t>(stream)));
 }
 
 lffw_status lffw_fp16_gelu(const uint16_t *x, uint16_t *y, int64_t count, void *stream) noexcept

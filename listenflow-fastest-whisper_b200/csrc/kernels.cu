@@ -690,6 +690,218 @@ __global__ void __launch_bounds__(kThreads) fp8_gemv_kernel(const Params p)
 } // namespace gemv
 
 // ---------------------------------------------------------------------------
+// Skinny linear (decoder step, m <= 32) on tensor cores.
+//
+// Swap-AB: 128 weight rows are the MMA's M side and the (zero-padded) 32
+// activation rows its N side, D[n, m] = sum_k W[n, k] x[m, k] in TMEM (32
+// fp32 columns).  A cluster of S CTAs shares one 128-row block and splits K;
+// partial sums meet in distributed shared memory, each CTA reduces 128/S rows
+// in a fixed order (deterministic) and runs the epilogue for them.  Weights
+// stream through a TMA ring; the kernel arms its weight loads before waiting
+// on the previous grid (programmatic dependent launch), so back-to-back
+// linears overlap their weight streaming with the previous kernel's tail.
+
+namespace skinny {
+
+constexpr int kThreads = 128;
+constexpr int kRows = 128;  // weight rows per cluster (MMA M)
+constexpr int kAct = 32;    // activation rows per MMA (MMA N); m <= 32
+constexpr int kBK = 128;    // K bytes per stage
+constexpr int kStages = 4;
+constexpr int kWBytes = kRows * kBK;
+constexpr int kXBytes = kAct * kBK;
+constexpr int kStageBytes = kWBytes + kXBytes;
+constexpr int kRedStride = kAct + 1; // floats per reduction row (bank-conflict padding)
+constexpr int kOffX = kStages * kWBytes;
+constexpr int kOffRed = kOffX + kStages * kXBytes;
+constexpr int kOffBar = kOffRed + kRows * kRedStride * 4;
+constexpr int kSmemBytes = kOffBar + 128 + 1024;
+constexpr int kMaxCluster = 8;
+static_assert(kSmemBytes <= 113 * 1024, "two CTAs per SM");
+
+enum : int { kKindE4M3 = 0, kKindF16 = 1 };
+
+struct Params {
+    int m, n, num_kb;
+    int cluster; // CTAs per 128-row block (power of two, <= kMaxCluster)
+    float act_scale;
+    const float *act_scale_ptr;
+    const float *w_scales; // nullptr: unit scales (fp16 weights)
+    const uint16_t *bias;
+    uint16_t *y;
+    float next_scale, next_recip;
+    uint8_t *next_codes;
+};
+
+template <int KIND, int EPI>
+__global__ void __launch_bounds__(kThreads)
+    skinny_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, const Params p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+    const uint32_t sbase = smem_u32(smem);
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    const int S = p.cluster;
+    const int rank = static_cast<int>(blockIdx.x) % S;
+    const int n0 = (static_cast<int>(blockIdx.x) / S) * kRows;
+    const int kb_begin = static_cast<int>((static_cast<int64_t>(p.num_kb) * rank) / S);
+    const int kb_end = static_cast<int>((static_cast<int64_t>(p.num_kb) * (rank + 1)) / S);
+    const int nkb = kb_end - kb_begin;
+    const uint32_t bar_full = sbase + kOffBar;
+    const uint32_t bar_empty = bar_full + 8 * kStages;
+    const uint32_t bar_acc = bar_empty + 8 * kStages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 8 * (2 * kStages + 1));
+    float *red = reinterpret_cast<float *>(smem + kOffRed);
+
+    if (threadIdx.x == 0) {
+        griddepcontrol_launch_dependents();
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(bar_full + 8 * s, 1);
+            mbar_init(bar_empty + 8 * s, 1);
+        }
+        mbar_init(bar_acc, 1);
+        fence_barrier_init();
+        prefetch_tensor_map(&tm_w);
+        prefetch_tensor_map(&tm_x);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), 32);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // Weights do not depend on the previous kernel: arm the first stages now.
+        const int first = nkb < kStages ? nkb : kStages;
+        for (int i = 0; i < first; ++i) {
+            mbar_arrive_expect_tx(bar_full + 8 * i, kStageBytes);
+            tma_load_2d(sbase + i * kWBytes, &tm_w, bar_full + 8 * i, (kb_begin + i) * kBK / (KIND == kKindF16 ? 2 : 1), n0);
+        }
+        griddepcontrol_wait();
+        for (int i = 0; i < first; ++i)
+            tma_load_2d(sbase + kOffX + i * kXBytes, &tm_x, bar_full + 8 * i, (kb_begin + i) * kBK / (KIND == kKindF16 ? 2 : 1), 0);
+        for (int j = first; j < nkb; ++j) {
+            const int s = j % kStages;
+            const uint32_t ph = static_cast<uint32_t>(j / kStages) & 1u;
+            if (!mbar_wait(bar_empty + 8 * s, ph ^ 1u, kSiteProducerEmpty))
+                break;
+            const int xk = (kb_begin + j) * kBK / (KIND == kKindF16 ? 2 : 1);
+            mbar_arrive_expect_tx(bar_full + 8 * s, kStageBytes);
+            tma_load_2d(sbase + s * kWBytes, &tm_w, bar_full + 8 * s, xk, n0);
+            tma_load_2d(sbase + kOffX + s * kXBytes, &tm_x, bar_full + 8 * s, xk, 0);
+        }
+        // Drain: every issued load lands before shared memory is released.
+        for (int j = (nkb > kStages ? nkb - kStages : 0); j < nkb; ++j) {
+            const uint32_t par = static_cast<uint32_t>(j / kStages) & 1u;
+            for (int tries = 0; tries < (1 << 22) && !mbar_try_wait(bar_full + 8 * (j % kStages), par); ++tries) {
+            }
+        }
+    } else {
+        // Outputs of this grid may be inputs of the previous one: no global
+        // access before that grid is complete.
+        griddepcontrol_wait();
+    }
+    if (warp == 1 && lane == 0) {
+        constexpr uint32_t idesc = KIND == kKindF16 ? idesc_f16_f32<kRows, kAct>() : idesc_e4m3_f32<kRows, kAct>();
+        bool ok = true;
+        for (int j = 0; ok && j < nkb; ++j) {
+            const int s = j % kStages;
+            const uint32_t ph = static_cast<uint32_t>(j / kStages) & 1u;
+            if (!mbar_wait(bar_full + 8 * s, ph, kSiteMmaFull)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int k = 0; k < kBK / 32; ++k) {
+                const uint64_t da = smem_desc_k_sw128(sbase + s * kWBytes + k * 32);
+                const uint64_t db = smem_desc_k_sw128(sbase + kOffX + s * kXBytes + k * 32);
+                if (KIND == kKindF16)
+                    mma_f16(tmem_base, da, db, idesc, (j | k) != 0);
+                else
+                    mma_f8f6f4(tmem_base, da, db, idesc, (j | k) != 0);
+            }
+            mma_commit(bar_empty + 8 * s);
+        }
+        mma_commit(bar_acc);
+    }
+
+    // Read the accumulator: thread (warp w, lane) holds weight row 32w + lane,
+    // one fp32 per activation row.
+    uint32_t v[kAct];
+    const bool ok = nkb == 0 || __all_sync(0xffffffffu, mbar_wait(bar_acc, 0, kSiteEpilogueAccFull));
+    if (nkb > 0 && ok) {
+        tc_fence_after();
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(warp * 32) << 16), v);
+        tmem_wait_ld();
+    } else {
+#pragma unroll
+        for (int i = 0; i < kAct; ++i)
+            v[i] = 0u; // this CTA's K slice is empty
+    }
+    const float act_scale = p.act_scale_ptr ? *p.act_scale_ptr : p.act_scale;
+    const uint64_t neg_scale2 = f2_bits(-p.next_scale, -p.next_scale);
+    const uint64_t recip2 = f2_bits(p.next_recip, p.next_recip);
+    auto finish = [&](float acc, int m, int n) {
+        const float ws = p.w_scales ? p.w_scales[n] : 1.0f;
+        uint32_t z = f2h_rn(acc * (p.w_scales ? act_scale * ws : 1.0f));
+        if (p.bias)
+            z = hadd_rn(static_cast<uint16_t>(z), p.bias[n]);
+        if (EPI & 1)
+            z = gemm::gelu_fp16x2(z, g_erf_table) & 0xFFFFu;
+        const size_t o = static_cast<size_t>(m) * p.n + n;
+        if (p.y)
+            p.y[o] = static_cast<uint16_t>(z);
+        if (p.next_codes)
+            p.next_codes[o] = static_cast<uint8_t>(e4m3x2_quotient(z, neg_scale2, recip2) & 0xFFu);
+    };
+    if (S == 1) {
+        const int n = n0 + warp * 32 + lane;
+        if (n < p.n) {
+#pragma unroll
+            for (int m = 0; m < kAct; ++m)
+                if (m < p.m)
+                    finish(__uint_as_float(v[m]), m, n);
+        }
+    } else {
+        const int row = warp * 32 + lane;
+#pragma unroll
+        for (int i = 0; i < kAct; ++i)
+            red[row * kRedStride + i] = __uint_as_float(v[i]);
+        cluster_sync();
+        // This CTA reduces rows [rank * 128/S, (rank + 1) * 128/S), summing the
+        // cluster's partials in rank order.
+        const int rows_per = kRows / S;
+        for (int e = threadIdx.x; e < rows_per * kAct; e += kThreads) {
+            const int r = rank * rows_per + e / kAct;
+            const int m = e % kAct;
+            const uint32_t local = smem_u32(red + r * kRedStride + m);
+            float acc = 0.0f;
+            for (int q = 0; q < S; ++q)
+                acc += ld_shared_cluster_f32(map_to_rank(local, static_cast<uint32_t>(q)));
+            const int n = n0 + r;
+            if (m < p.m && n < p.n)
+                finish(acc, m, n);
+        }
+        cluster_sync(); // peers read this CTA's partials until here
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, 32);
+    }
+}
+
+} // namespace skinny
+
+// ---------------------------------------------------------------------------
 // Quantize / scale kernels.
 
 namespace quant {
@@ -1069,6 +1281,94 @@ cudaError_t launch_fp8_gemm(const LinearLaunch &L, cudaStream_t stream)
     return pair ? run_gemm_epilogue<256, true>(L, stream) : run_gemm_epilogue<256, false>(L, stream);
 }
 
+namespace {
+
+// Cluster size (CTAs sharing one 128-row block, splitting K): enough CTAs for
+// about two per SM, a power of two, at most 8 and at most the number of K blocks.
+int skinny_cluster(int64_t n, int num_kb)
+{
+    const int64_t blocks = (n + skinny::kRows - 1) / skinny::kRows;
+    const int64_t want = (2 * static_cast<int64_t>(sm_count()) + blocks - 1) / blocks;
+    int s = 1;
+    while (s < want && s * 2 <= skinny::kMaxCluster && s * 2 <= num_kb)
+        s *= 2;
+    return s;
+}
+
+template <int KIND, int EPI>
+cudaError_t run_skinny(const void *x, const void *w, int64_t m, int64_t n, int64_t k, const LinearLaunch &L,
+                       cudaStream_t stream)
+{
+    const int elem = KIND == skinny::kKindF16 ? 2 : 1;
+    const CUtensorMapDataType type = KIND == skinny::kKindF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                               : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    CUtensorMap tm_w{}, tm_x{};
+    if (!make_map(&tm_w, type, elem, w, n, k, skinny::kBK / elem, skinny::kRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&tm_x, type, elem, x, m, k, skinny::kBK / elem, skinny::kAct, CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    skinny::Params p{};
+    p.m = static_cast<int>(m);
+    p.n = static_cast<int>(n);
+    p.num_kb = static_cast<int>((k * elem + skinny::kBK - 1) / skinny::kBK);
+    p.cluster = skinny_cluster(n, p.num_kb);
+    p.act_scale = L.act_scale;
+    p.act_scale_ptr = L.act_scale_ptr;
+    p.w_scales = L.w_scales;
+    p.bias = L.bias;
+    p.y = L.y;
+    p.next_scale = L.next_scale;
+    p.next_recip = L.next_codes ? static_cast<float>(1.0 / static_cast<double>(L.next_scale)) : 0.0f;
+    p.next_codes = L.next_codes;
+    auto kernel = skinny::skinny_kernel<KIND, EPI>;
+    const cudaError_t attr = ensure_smem(kernel, skinny::kSmemBytes);
+    if (attr != cudaSuccess)
+        return attr;
+    const int64_t blocks = (n + skinny::kRows - 1) / skinny::kRows;
+    cudaLaunchConfig_t config{};
+    config.gridDim = dim3(static_cast<unsigned>(blocks * p.cluster));
+    config.blockDim = dim3(skinny::kThreads);
+    config.dynamicSmemBytes = skinny::kSmemBytes;
+    config.stream = stream;
+    cudaLaunchAttribute attrs[2];
+    int count = 0;
+    attrs[count].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[count].val.programmaticStreamSerializationAllowed = 1;
+    ++count;
+    if (p.cluster > 1) {
+        attrs[count].id = cudaLaunchAttributeClusterDimension;
+        attrs[count].val.clusterDim.x = static_cast<unsigned>(p.cluster);
+        attrs[count].val.clusterDim.y = 1;
+        attrs[count].val.clusterDim.z = 1;
+        ++count;
+    }
+    config.attrs = attrs;
+    config.numAttrs = count;
+    const cudaError_t err = cudaLaunchKernelEx(&config, kernel, tm_w, tm_x, p);
+    count_launch();
+    return err != cudaSuccess ? err : cudaGetLastError();
+}
+
+} // namespace
+
+cudaError_t launch_fp8_skinny(const LinearLaunch &L, cudaStream_t stream)
+{
+    if (L.gelu)
+        return run_skinny<skinny::kKindE4M3, 1>(L.x_codes, L.w_codes, L.m, L.n, L.k, L, stream);
+    return run_skinny<skinny::kKindE4M3, 0>(L.x_codes, L.w_codes, L.m, L.n, L.k, L, stream);
+}
+
+cudaError_t launch_fp16_skinny(const uint16_t *x, const uint16_t *w, const uint16_t *bias, uint16_t *y, int64_t m,
+                               int64_t n, int64_t k, cudaStream_t stream)
+{
+    LinearLaunch L{};
+    L.m = m;
+    L.n = n;
+    L.k = k;
+    L.bias = bias;
+    L.y = y;
+    return run_skinny<skinny::kKindF16, 0>(x, w, m, n, k, L, stream);
+}
+
 cudaError_t launch_fp8_gemv(const LinearLaunch &L, cudaStream_t stream)
 {
     gemv::Params p{};
@@ -1296,7 +1596,7 @@ extern "C" LFFW_FP8_API lffw_status lffw_fp8_linear_half_static(const uint16_t *
     L.bias = bias;
     L.gelu = epilogue == LFFW_EPILOGUE_GELU;
     L.y = y;
-    const bool small = m <= lffw::kGemvMaxRows && m * k <= lffw::kGemvMaxSmem;
-    const cudaError_t err = small ? lffw::launch_fp8_gemv(L, st) : lffw::launch_fp8_gemm(L, st);
+    const bool small = m <= lffw::kGemvMaxRows;
+    const cudaError_t err = small ? lffw::launch_fp8_skinny(L, st) : lffw::launch_fp8_gemm(L, st);
     return err == cudaSuccess ? LFFW_SUCCESS : LFFW_CUDA_ERROR;
 }

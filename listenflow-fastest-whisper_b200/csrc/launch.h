@@ -21,13 +21,17 @@ struct LinearLaunch {
     uint8_t *next_codes;
 };
 
-// Largest M served by the CUDA-core small-M kernel.
+// Largest M served by the small-M (skinny) kernels.
 constexpr int64_t kGemvMaxRows = 32;
 // Shared memory the small-M kernel may use for the activation codes (m * k bytes).
 constexpr int64_t kGemvMaxSmem = 200 * 1024;
 
 cudaError_t launch_fp8_gemm(const LinearLaunch &p, cudaStream_t stream);
 cudaError_t launch_fp8_gemv(const LinearLaunch &p, cudaStream_t stream);
+// m <= 32 on tensor cores (swap-AB, cluster split-K); fp16 weights for the logits.
+cudaError_t launch_fp8_skinny(const LinearLaunch &p, cudaStream_t stream);
+cudaError_t launch_fp16_skinny(const uint16_t *x, const uint16_t *w, const uint16_t *bias, uint16_t *y, int64_t m,
+                               int64_t n, int64_t k, cudaStream_t stream);
 cudaError_t launch_quantize(const uint16_t *x, int64_t count, float scale, const float *scale_ptr,
                             uint8_t *codes, cudaStream_t stream);
 cudaError_t launch_quantize_rows(const uint16_t *w, int64_t rows, int64_t cols,

@@ -258,6 +258,49 @@ __host__ __device__ constexpr uint32_t idesc_e4m3_f32()
            (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// kind::f16 instruction descriptor: fp16 x fp16 -> fp32 (format fields 0 = F16),
+// both K-major.
+template <int M, int N>
+__host__ __device__ constexpr uint32_t idesc_f16_f32()
+{
+    static_assert(M == 64 || M == 128, "M");
+    static_assert(N % 16 == 0 && N >= 16 && N <= 256, "N");
+    return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate)
+{
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+                 "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+                 : "memory");
+}
+
+// ---- programmatic dependent launch -----------------------------------------
+
+// Lets the next kernel in the stream start launching (it still waits for this
+// grid in griddepcontrol_wait before touching this grid's outputs).
+__device__ __forceinline__ void griddepcontrol_launch_dependents()
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Blocks until the preceding grid in the stream has completed and its memory
+// is visible (returns at once when there is no such dependency).
+__device__ __forceinline__ void griddepcontrol_wait()
+{
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t cluster_addr)
+{
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+    return v;
+}
+
 // ---- CTA pairs (cluster of 2, cta_group::2) ---------------------------------
 // Used only without multicast TMA: each CTA loads its own halves of the
 // operands; only tcgen05.commit is multicast to both CTAs' barriers.

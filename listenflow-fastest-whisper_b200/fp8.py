@@ -229,6 +229,20 @@ def fp16_qkv(x: torch.Tensor, weight: torch.Tensor, q_bias: torch.Tensor, v_bias
     return out
 
 
+def fp16_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
+                out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """fp16 [m <= 32, k] x fp16 [n, k]^T (+ bias) -> fp16 [m, n], fp32 accumulate (decoder logits)."""
+    _require(x, torch.float16, "x")
+    _require(weight, torch.float16, "weight")
+    m, k = x.shape
+    n = weight.shape[0]
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float16, device=x.device)
+    native.check(native.library().lffw_fp16_linear(x.data_ptr(), weight.data_ptr(), _ptr(bias), out.data_ptr(),
+                                                   m, n, k, _stream(stream)), "lffw_fp16_linear")
+    return out
+
+
 def fp16_gelu(x: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
     """GELU with fp16 graph edges (graph::gelu), elementwise."""
     _require(x, torch.float16, "x")

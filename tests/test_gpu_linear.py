@@ -190,3 +190,24 @@ def test_config2_layer_set_rows_and_fusion(cuda, fp8, oracle, native):
             np.testing.assert_array_equal(codes.cpu().numpy(), oracle.quantize(y_bits, np.float32(0.0123)))
     torch.cuda.synchronize()
     assert native.device_error() == 0
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 51866, 1280), (20, 51866, 1280), (20, 1280, 1280), (32, 5120, 640), (5, 1000, 1288)])
+def test_fp16_linear_small_m_matches_oracle(cuda, fp8, native, m, n, k):
+    """The decoder's fp16 logits MatMul: fp16 x fp16 -> fp32 accumulate -> fp16."""
+    import torch
+
+    rng = np.random.default_rng(m * 7 + n + k)
+    x = halves(rng, (m, k))
+    w = halves(rng, (n, k), 0.02)
+    b = halves(rng, (n,), 0.02)
+    y = fp8.fp16_linear(torch.from_numpy(x).to(cuda), torch.from_numpy(w).to(cuda), torch.from_numpy(b).to(cuda))
+    torch.cuda.synchronize()
+    assert native.device_error() == 0
+    exact = x.astype(np.float64) @ w.astype(np.float64).T  # fp16 x fp16 products are exact in binary64
+    want = (exact.astype(np.float16).astype(np.float64) + b.astype(np.float64)).astype(np.float16)
+    got = y.cpu().numpy()
+    mag = np.abs(x.astype(np.float64)) @ np.abs(w.astype(np.float64)).T
+    bound = ATOL + RTOL * np.abs(want.astype(np.float64)) + k * 2.0**-24 * mag
+    err = np.abs(got.astype(np.float64) - want.astype(np.float64))
+    assert np.all(err <= bound), float((err - bound).max())
