@@ -881,9 +881,15 @@ __global__ void __launch_bounds__(kThreads)
             const int r = rank * rows_per + e / kAct;
             const int m = e % kAct;
             const uint32_t local = smem_u32(red + r * kRedStride + m);
+            // All remote loads in flight before the (rank-ordered) sum.
+            float part[kMaxCluster];
+#pragma unroll
+            for (int q = 0; q < kMaxCluster; ++q)
+                part[q] = q < S ? ld_shared_cluster_f32(map_to_rank(local, static_cast<uint32_t>(q))) : 0.0f;
             float acc = 0.0f;
-            for (int q = 0; q < S; ++q)
-                acc += ld_shared_cluster_f32(map_to_rank(local, static_cast<uint32_t>(q)));
+#pragma unroll
+            for (int q = 0; q < kMaxCluster; ++q)
+                acc += part[q];
             const int n = n0 + r;
             if (m < p.m && n < p.n)
                 finish(acc, m, n);
