@@ -379,11 +379,13 @@ def run_decoder(fp8, native, device, steps: int, warmup: int, seed: int):
         for name, k, n in DEC_LINEARS:
             w = (torch.randn(n, k, generator=g, device=device) * 0.02).half()
             b = (torch.randn(n, generator=g, device=device) * 0.02).half()
-            layer[name] = fp8.QuantizedWeight.from_half(w, b)
+            q = fp8.QuantizedWeight.from_half(w, b)
+            layer[name] = (q, fp8.pack_skinny(q.codes))  # build-time re-layout for m <= 32
             weight_bytes += n * k + n * 4 + n * 2  # E4M3 codes + fp32 scales + fp16 bias
-            del w
+            del w, q.codes
         layers.append(layer)
     logits_w = (torch.randn(VOCAB, 1280, generator=g, device=device) * 0.02).half()
+    logits_packed = fp8.pack_skinny(logits_w)
     weight_bytes += VOCAB * 1280 * 2
     x_codes = fp8.quantize(torch.randn(DEC_M, 1280, generator=g, device=device).half(), 0.01)
     x16 = torch.randn(DEC_M, 1280, generator=g, device=device).half()
@@ -394,14 +396,14 @@ def run_decoder(fp8, native, device, steps: int, warmup: int, seed: int):
     def step():
         for layer in layers:
             for name in ("qkv", "self_out", "cross_q", "cross_out"):
-                q = layer[name]
-                fp8.linear(x_codes, q.codes, q.scales, 0.01, bias=q.bias, out=outs[name])
-            q = layer["fc1"]
-            fp8.linear(x_codes, q.codes, q.scales, 0.01, bias=q.bias, gelu=True, want_y=False, next_scale=0.02,
-                       next_codes=fc2_in)
-            q = layer["fc2"]
-            fp8.linear(fc2_in, q.codes, q.scales, 0.02, bias=q.bias, out=outs["fc2"])
-        fp8.fp16_linear(x16, logits_w, out=logits)
+                q, packed = layer[name]
+                fp8.linear(x_codes, None, q.scales, 0.01, bias=q.bias, out=outs[name], w_packed=packed)
+            q, packed = layer["fc1"]
+            fp8.linear(x_codes, None, q.scales, 0.01, bias=q.bias, gelu=True, want_y=False, next_scale=0.02,
+                       next_codes=fc2_in, w_packed=packed)
+            q, packed = layer["fc2"]
+            fp8.linear(fc2_in, None, q.scales, 0.02, bias=q.bias, out=outs["fc2"], w_packed=packed)
+        fp8.fp16_linear(x16, logits_w, out=logits, w_packed=logits_packed)
 
     stream = torch.cuda.Stream(device)
     with torch.cuda.stream(stream):

@@ -24,7 +24,7 @@
 #include <stdint.h>
 
 #define LFFW_FP8_ABI_MAJOR 1
-#define LFFW_FP8_ABI_MINOR 0
+#define LFFW_FP8_ABI_MINOR 1
 #define LFFW_FP8_API __attribute__((visibility("default")))
 #if defined(__cplusplus)
 #define LFFW_FP8_NOEXCEPT noexcept
@@ -48,6 +48,11 @@ enum {
 
 /* Epilogue selection for lffw_fp8_linear. */
 enum { LFFW_EPILOGUE_NONE = 0, LFFW_EPILOGUE_GELU = 1 };
+
+/* Weight layouts.  ROW_MAJOR: [n, k] with k contiguous.  SKINNY_TILES: the
+ * weight re-laid by lffw_pack_skinny_weights into contiguous 16 KB tiles that
+ * the small-m kernels stream sequentially (only for m <= 32). */
+enum { LFFW_WEIGHTS_ROW_MAJOR = 0, LFFW_WEIGHTS_SKINNY_TILES = 1 };
 
 /*
  * One FP8 Q/DQ linear (replaces graph::linear in fp8 precision,
@@ -79,6 +84,7 @@ typedef struct lffw_fp8_linear_args {
     uint16_t *y;
     float next_scale;
     uint8_t *next_codes;
+    int32_t w_layout; /* LFFW_WEIGHTS_*; absent (older struct_size) means ROW_MAJOR */
 } lffw_fp8_linear_args;
 
 LFFW_FP8_API lffw_status lffw_fp8_linear(const lffw_fp8_linear_args *args,
@@ -127,10 +133,19 @@ LFFW_FP8_API lffw_status lffw_fp16_bias(const uint16_t *x, uint16_t bias_bits, u
 /* fp16 linear for up to 32 rows (the decoder step's fp16 logits MatMul,
  * 1280 -> vocabulary, cpp/src/network_graph.cpp:379-417): y[m,n] =
  * half(sum_k x[m,k] w[n,k] (+ bias[n])), fp32 accumulate on tensor cores.
- * x [m,k], w [n,k] fp16 row-major; 1 <= m <= 32; k % 8 == 0; bias may be NULL. */
+ * x [m,k] fp16; weight fp16 in `w_layout` (LFFW_WEIGHTS_*); 1 <= m <= 32;
+ * k % 8 == 0; bias may be NULL. */
 LFFW_FP8_API lffw_status lffw_fp16_linear(const uint16_t *x, const uint16_t *weight, const uint16_t *bias,
-                                          uint16_t *y, int64_t m, int64_t n, int64_t k,
+                                          uint16_t *y, int64_t m, int64_t n, int64_t k, int32_t w_layout,
                                           void *stream) LFFW_FP8_NOEXCEPT;
+
+/* Size in bytes of a weight [n, k] (elem_bytes 1 = E4M3, 2 = fp16) in the
+ * LFFW_WEIGHTS_SKINNY_TILES layout; 0 for invalid arguments. */
+LFFW_FP8_API int64_t lffw_skinny_packed_bytes(int64_t n, int64_t k, int32_t elem_bytes) LFFW_FP8_NOEXCEPT;
+/* Re-lays a row-major weight into that layout (a build-time step, like
+ * TensorRT's weight reformatting); `packed` holds lffw_skinny_packed_bytes. */
+LFFW_FP8_API lffw_status lffw_pack_skinny_weights(const void *weight, int64_t n, int64_t k, int32_t elem_bytes,
+                                                  void *packed, void *stream) LFFW_FP8_NOEXCEPT;
 
 /* GELU with every graph edge rounded to fp16, elementwise on `count` halves:
  * y = (x*0.5)*(1 + erf(x*fp16(2^-1/2))) (graph::gelu, network_graph.cpp:168-180).

@@ -26,6 +26,8 @@ DEVICE_TIMEOUT = 120
 
 EPILOGUE_NONE = 0
 EPILOGUE_GELU = 1
+WEIGHTS_ROW_MAJOR = 0
+WEIGHTS_SKINNY_TILES = 1
 
 DT_FLOAT, DT_HALF, DT_INT8, DT_INT32, DT_FP8 = 0, 1, 2, 3, 6
 FORMAT_LINEAR, FORMAT_CHW2 = 0, 1
@@ -57,6 +59,7 @@ class LinearArgs(ctypes.Structure):
         ("y", ctypes.c_void_p),
         ("next_scale", ctypes.c_float),
         ("next_codes", ctypes.c_void_p),
+        ("w_layout", ctypes.c_int32),
     ]
 
 
@@ -119,7 +122,9 @@ def library() -> ctypes.CDLL:
         "lffw_fp16_qkv": ([_vp, _vp, _vp, _vp, _vp, _i64, _vp], _i32),
         "lffw_fp16_bias": ([_vp, ctypes.c_uint16, _vp, _i64, _vp], _i32),
         "lffw_fp16_gelu": ([_vp, _vp, _i64, _vp], _i32),
-        "lffw_fp16_linear": ([_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp], _i32),
+        "lffw_fp16_linear": ([_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp], _i32),
+        "lffw_skinny_packed_bytes": ([_i64, _i64, _i32], _i64),
+        "lffw_pack_skinny_weights": ([_vp, _i64, _i64, _i32, _vp, _vp], _i32),
         "lffw_device_supported": ([_i32], _i32),
         "lffw_device_error": ([ctypes.POINTER(_i32)], _i32),
         "lffw_launch_count": ([], ctypes.c_uint64),

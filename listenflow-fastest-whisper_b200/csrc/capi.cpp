@@ -6,6 +6,7 @@
 #include <cuda_runtime_api.h>
 
 #include <cmath>
+#include <cstddef>
 #include <cstring>
 #include <limits>
 #include <mutex>
@@ -77,11 +78,18 @@ lffw_status current_device_gate()
 
 constexpr int64_t kMaxDim = std::numeric_limits<int32_t>::max();
 
+// The layout field exists only in callers built against ABI 1.1+ headers.
+int32_t weight_layout(const lffw_fp8_linear_args *a)
+{
+    return a->struct_size >= offsetof(lffw_fp8_linear_args, w_layout) + sizeof(int32_t) ? a->w_layout
+                                                                                         : LFFW_WEIGHTS_ROW_MAJOR;
+}
+
 lffw_status validate_linear(const lffw_fp8_linear_args *a)
 {
     if (a == nullptr)
         return LFFW_INVALID_ARGUMENT;
-    if (a->struct_size < sizeof(lffw_fp8_linear_args))
+    if (a->struct_size < offsetof(lffw_fp8_linear_args, w_layout))
         return LFFW_ABI_MISMATCH;
     if (a->m < 1 || a->n < 1 || a->k < 1 || a->m > kMaxDim || a->n > kMaxDim || a->k > kMaxDim)
         return LFFW_INVALID_ARGUMENT;
@@ -100,6 +108,11 @@ lffw_status validate_linear(const lffw_fp8_linear_args *a)
     if (a->next_codes != nullptr && !valid_scale(a->next_scale))
         return LFFW_INVALID_ARGUMENT;
     if (a->epilogue != LFFW_EPILOGUE_NONE && a->epilogue != LFFW_EPILOGUE_GELU)
+        return LFFW_INVALID_ARGUMENT;
+    const int32_t layout = weight_layout(a);
+    if (layout != LFFW_WEIGHTS_ROW_MAJOR && layout != LFFW_WEIGHTS_SKINNY_TILES)
+        return LFFW_INVALID_ARGUMENT;
+    if (layout == LFFW_WEIGHTS_SKINNY_TILES && a->m > lffw::kGemvMaxRows)
         return LFFW_INVALID_ARGUMENT;
     return LFFW_SUCCESS;
 }
@@ -120,6 +133,7 @@ lffw_status run_linear(const lffw_fp8_linear_args *a, cudaStream_t stream)
     L.y = a->y;
     L.next_scale = a->next_scale;
     L.next_codes = a->next_codes;
+    L.w_packed = weight_layout(a) == LFFW_WEIGHTS_SKINNY_TILES;
     const bool small = a->m <= lffw::kGemvMaxRows;
     return from_cuda(small ? lffw::launch_fp8_skinny(L, stream) : lffw::launch_fp8_gemm(L, stream));
 }
@@ -225,15 +239,36 @@ lffw_status lffw_fp16_bias(const uint16_t *x, uint16_t bias_bits, uint16_t *y, i
 }
 
 lffw_status lffw_fp16_linear(const uint16_t *x, const uint16_t *weight, const uint16_t *bias, uint16_t *y,
-                             int64_t m, int64_t n, int64_t k, void *stream) noexcept
+                             int64_t m, int64_t n, int64_t k, int32_t w_layout, void *stream) noexcept
 {
     if (x == nullptr || weight == nullptr || y == nullptr || m < 1 || m > lffw::kGemvMaxRows || n < 1 ||
-        n > kMaxDim || k < 8 || k % 8 != 0 || k > kMaxDim || !aligned16(x) || !aligned16(weight))
+        n > kMaxDim || k < 8 || k % 8 != 0 || k > kMaxDim || !aligned16(x) || !aligned16(weight) ||
+        (w_layout != LFFW_WEIGHTS_ROW_MAJOR && w_layout != LFFW_WEIGHTS_SKINNY_TILES))
         return LFFW_INVALID_ARGUMENT;
     lffw_status s = current_device_gate();
     if (s != LFFW_SUCCESS)
         return s;
-    return from_cuda(lffw::launch_fp16_skinny(x, weight, bias, y, m, n, k, static_cast<cudaStream_t>(stream)));
+    return from_cuda(lffw::launch_fp16_skinny(x, weight, bias, y, m, n, k, w_layout == LFFW_WEIGHTS_SKINNY_TILES,
+                                              static_cast<cudaStream_t>(stream)));
+}
+
+int64_t lffw_skinny_packed_bytes(int64_t n, int64_t k, int32_t elem_bytes) noexcept
+{
+    if (n < 1 || k < 1 || (elem_bytes != 1 && elem_bytes != 2) || n > kMaxDim || k > kMaxDim)
+        return 0;
+    return lffw::skinny_packed_bytes(n, k * elem_bytes);
+}
+
+lffw_status lffw_pack_skinny_weights(const void *weight, int64_t n, int64_t k, int32_t elem_bytes, void *packed,
+                                     void *stream) noexcept
+{
+    if (weight == nullptr || packed == nullptr || lffw_skinny_packed_bytes(n, k, elem_bytes) == 0 ||
+        (k * elem_bytes) % 16 != 0 || !aligned16(weight) || !aligned16(packed))
+        return LFFW_INVALID_ARGUMENT;
+    lffw_status s = current_device_gate();
+    if (s != LFFW_SUCCESS)
+        return s;
+    return from_cuda(lffw::launch_pack_skinny(weight, n, k * elem_bytes, packed, static_cast<cudaStream_t>(stream)));
 }
 
 lffw_status lffw_fp16_gelu(const uint16_t *x, uint16_t *y, int64_t count, void *stream) noexcept

@@ -707,17 +707,23 @@ constexpr int kThreads = 128;
 constexpr int kRows = 128;  // weight rows per cluster (MMA M)
 constexpr int kAct = 32;    // activation rows per MMA (MMA N); m <= 32
 constexpr int kBK = 128;    // K bytes per stage
-constexpr int kStages = 4;
+// Two stages per CTA and small CTAs: measured on B200, more resident CTAs
+// (independent weight streams) per SM stream faster than deeper rings.
+constexpr int kStages = 2;
 constexpr int kWBytes = kRows * kBK;
 constexpr int kXBytes = kAct * kBK;
 constexpr int kStageBytes = kWBytes + kXBytes;
 constexpr int kRedStride = kAct + 1; // floats per reduction row (bank-conflict padding)
 constexpr int kOffX = kStages * kWBytes;
-constexpr int kOffRed = kOffX + kStages * kXBytes;
-constexpr int kOffBar = kOffRed + kRows * kRedStride * 4;
+constexpr int kRedBytes = kRows * kRedStride * 4;
+// The split-K reduction buffer reuses the stage memory: it is written only
+// after every load has landed and every MMA has completed.
+constexpr int kOffRed = 0;
+constexpr int kRingBytes = kOffX + kStages * kXBytes;
+constexpr int kOffBar = (kRingBytes > kRedBytes ? kRingBytes : kRedBytes + 1023) / 1024 * 1024;
 constexpr int kSmemBytes = kOffBar + 128 + 1024;
 constexpr int kMaxCluster = 8;
-static_assert(kSmemBytes <= 113 * 1024, "two CTAs per SM");
+static_assert(kSmemBytes <= 46 * 1024, "five CTAs per SM");
 
 enum : int { kKindE4M3 = 0, kKindF16 = 1 };
 
@@ -731,6 +737,7 @@ struct Params {
     uint16_t *y;
     float next_scale, next_recip;
     uint8_t *next_codes;
+    const uint8_t *w_packed; // non-null: weights in pre-swizzled 16 KB tiles (pack_kernel)
 };
 
 template <int KIND, int EPI>
@@ -777,10 +784,19 @@ __global__ void __launch_bounds__(kThreads)
 
     if (warp == 0 && lane == 0) {
         // Weights do not depend on the previous kernel: arm the first stages now.
+        // Packed weights: tile (row block, k block) is one contiguous 16 KB image.
+        const uint8_t *tiles =
+            p.w_packed ? p.w_packed + (static_cast<size_t>(n0 / kRows) * p.num_kb) * kWBytes : nullptr;
+        auto load_w = [&](int s, int kb) {
+            if (p.w_packed)
+                bulk_load(sbase + s * kWBytes, tiles + static_cast<size_t>(kb) * kWBytes, kWBytes, bar_full + 8 * s);
+            else
+                tma_load_2d(sbase + s * kWBytes, &tm_w, bar_full + 8 * s, kb * kBK / (KIND == kKindF16 ? 2 : 1), n0);
+        };
         const int first = nkb < kStages ? nkb : kStages;
         for (int i = 0; i < first; ++i) {
             mbar_arrive_expect_tx(bar_full + 8 * i, kStageBytes);
-            tma_load_2d(sbase + i * kWBytes, &tm_w, bar_full + 8 * i, (kb_begin + i) * kBK / (KIND == kKindF16 ? 2 : 1), n0);
+            load_w(i, kb_begin + i);
         }
         griddepcontrol_wait();
         for (int i = 0; i < first; ++i)
@@ -792,7 +808,7 @@ __global__ void __launch_bounds__(kThreads)
                 break;
             const int xk = (kb_begin + j) * kBK / (KIND == kKindF16 ? 2 : 1);
             mbar_arrive_expect_tx(bar_full + 8 * s, kStageBytes);
-            tma_load_2d(sbase + s * kWBytes, &tm_w, bar_full + 8 * s, xk, n0);
+            load_w(s, kb_begin + j);
             tma_load_2d(sbase + kOffX + s * kXBytes, &tm_x, bar_full + 8 * s, xk, 0);
         }
         // Drain: every issued load lands before shared memory is released.
@@ -903,6 +919,30 @@ __global__ void __launch_bounds__(kThreads)
         tc_fence_after();
         tmem_dealloc(tmem_base, 32);
     }
+}
+
+// Re-lays a row-major [n, row_bytes] weight as 16 KB tiles: tile (rb, kb)
+// holds rows [128 rb, 128 rb + 128) x bytes [128 kb, 128 kb + 128), each row's
+// 16-byte chunk c stored at chunk c ^ (row & 7) -- exactly the shared-memory
+// image a 128B-swizzled TMA load of that box produces.  Out-of-range rows and
+// bytes are zero.  One thread per 16-byte chunk.
+__global__ void __launch_bounds__(256)
+    pack_kernel(const uint8_t *__restrict__ w, int64_t n, int64_t row_bytes, int64_t num_kb,
+                uint8_t *__restrict__ packed)
+{
+    const int64_t chunk = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+    const int64_t tiles = (n + kRows - 1) / kRows * num_kb;
+    if (chunk >= tiles * (kWBytes / 16))
+        return;
+    const int64_t tile = chunk / (kWBytes / 16);
+    const int within = static_cast<int>(chunk % (kWBytes / 16));
+    const int r = within / 8, c = within % 8;
+    const int64_t row = (tile / num_kb) * kRows + r;
+    const int64_t col = (tile % num_kb) * kBK + c * 16;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (row < n && col < row_bytes)
+        v = *reinterpret_cast<const uint4 *>(w + row * row_bytes + col);
+    *reinterpret_cast<uint4 *>(packed + tile * kWBytes + r * 128 + ((c ^ (r & 7)) * 16)) = v;
 }
 
 } // namespace skinny
@@ -1303,13 +1343,14 @@ int skinny_cluster(int64_t n, int num_kb)
 
 template <int KIND, int EPI>
 cudaError_t run_skinny(const void *x, const void *w, int64_t m, int64_t n, int64_t k, const LinearLaunch &L,
-                       cudaStream_t stream)
+                       cudaStream_t stream, bool packed)
 {
     const int elem = KIND == skinny::kKindF16 ? 2 : 1;
     const CUtensorMapDataType type = KIND == skinny::kKindF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                                : CU_TENSOR_MAP_DATA_TYPE_UINT8;
     CUtensorMap tm_w{}, tm_x{};
-    if (!make_map(&tm_w, type, elem, w, n, k, skinny::kBK / elem, skinny::kRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+    if ((!packed && !make_map(&tm_w, type, elem, w, n, k, skinny::kBK / elem, skinny::kRows,
+                              CU_TENSOR_MAP_SWIZZLE_128B)) ||
         !make_map(&tm_x, type, elem, x, m, k, skinny::kBK / elem, skinny::kAct, CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
     skinny::Params p{};
@@ -1325,6 +1366,7 @@ cudaError_t run_skinny(const void *x, const void *w, int64_t m, int64_t n, int64
     p.next_scale = L.next_scale;
     p.next_recip = L.next_codes ? static_cast<float>(1.0 / static_cast<double>(L.next_scale)) : 0.0f;
     p.next_codes = L.next_codes;
+    p.w_packed = packed ? static_cast<const uint8_t *>(w) : nullptr;
     auto kernel = skinny::skinny_kernel<KIND, EPI>;
     const cudaError_t attr = ensure_smem(kernel, skinny::kSmemBytes);
     if (attr != cudaSuccess)
@@ -1359,12 +1401,12 @@ cudaError_t run_skinny(const void *x, const void *w, int64_t m, int64_t n, int64
 cudaError_t launch_fp8_skinny(const LinearLaunch &L, cudaStream_t stream)
 {
     if (L.gelu)
-        return run_skinny<skinny::kKindE4M3, 1>(L.x_codes, L.w_codes, L.m, L.n, L.k, L, stream);
-    return run_skinny<skinny::kKindE4M3, 0>(L.x_codes, L.w_codes, L.m, L.n, L.k, L, stream);
+        return run_skinny<skinny::kKindE4M3, 1>(L.x_codes, L.w_codes, L.m, L.n, L.k, L, stream, L.w_packed);
+    return run_skinny<skinny::kKindE4M3, 0>(L.x_codes, L.w_codes, L.m, L.n, L.k, L, stream, L.w_packed);
 }
 
 cudaError_t launch_fp16_skinny(const uint16_t *x, const uint16_t *w, const uint16_t *bias, uint16_t *y, int64_t m,
-                               int64_t n, int64_t k, cudaStream_t stream)
+                               int64_t n, int64_t k, bool packed, cudaStream_t stream)
 {
     LinearLaunch L{};
     L.m = m;
@@ -1372,7 +1414,24 @@ cudaError_t launch_fp16_skinny(const uint16_t *x, const uint16_t *w, const uint1
     L.k = k;
     L.bias = bias;
     L.y = y;
-    return run_skinny<skinny::kKindF16, 0>(x, w, m, n, k, L, stream);
+    return run_skinny<skinny::kKindF16, 0>(x, w, m, n, k, L, stream, packed);
+}
+
+int64_t skinny_packed_bytes(int64_t n, int64_t row_bytes)
+{
+    const int64_t blocks = (n + skinny::kRows - 1) / skinny::kRows;
+    const int64_t kbs = (row_bytes + skinny::kBK - 1) / skinny::kBK;
+    return blocks * kbs * skinny::kWBytes;
+}
+
+cudaError_t launch_pack_skinny(const void *w, int64_t n, int64_t row_bytes, void *packed, cudaStream_t stream)
+{
+    const int64_t kbs = (row_bytes + skinny::kBK - 1) / skinny::kBK;
+    const int64_t chunks = skinny_packed_bytes(n, row_bytes) / 16;
+    skinny::pack_kernel<<<static_cast<unsigned>((chunks + 255) / 256), 256, 0, stream>>>(
+        static_cast<const uint8_t *>(w), n, row_bytes, kbs, static_cast<uint8_t *>(packed));
+    count_launch();
+    return cudaGetLastError();
 }
 
 cudaError_t launch_fp8_gemv(const LinearLaunch &L, cudaStream_t stream)

@@ -19,6 +19,7 @@ struct LinearLaunch {
     uint16_t *y;
     float next_scale;
     uint8_t *next_codes;
+    bool w_packed; // w_codes holds skinny-packed tiles (m <= 32 path only)
 };
 
 // Largest M served by the small-M (skinny) kernels.
@@ -31,7 +32,10 @@ cudaError_t launch_fp8_gemv(const LinearLaunch &p, cudaStream_t stream);
 // m <= 32 on tensor cores (swap-AB, cluster split-K); fp16 weights for the logits.
 cudaError_t launch_fp8_skinny(const LinearLaunch &p, cudaStream_t stream);
 cudaError_t launch_fp16_skinny(const uint16_t *x, const uint16_t *w, const uint16_t *bias, uint16_t *y, int64_t m,
-                               int64_t n, int64_t k, cudaStream_t stream);
+                               int64_t n, int64_t k, bool packed, cudaStream_t stream);
+// Pre-swizzled 16 KB weight tiles for the skinny kernels (size, then the pack).
+int64_t skinny_packed_bytes(int64_t n, int64_t row_bytes);
+cudaError_t launch_pack_skinny(const void *w, int64_t n, int64_t row_bytes, void *packed, cudaStream_t stream);
 cudaError_t launch_quantize(const uint16_t *x, int64_t count, float scale, const float *scale_ptr,
                             uint8_t *codes, cudaStream_t stream);
 cudaError_t launch_quantize_rows(const uint16_t *w, int64_t rows, int64_t cols,

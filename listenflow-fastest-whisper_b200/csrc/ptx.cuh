@@ -106,6 +106,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
                  : "memory");
 }
 
+// Contiguous global -> shared copy (size and both addresses multiples of 16 B),
+// completion counted on an mbarrier.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t src, int32_t x,
                                              int32_t y)
 {

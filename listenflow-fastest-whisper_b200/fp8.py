@@ -103,19 +103,34 @@ def dynamic_scale(x: torch.Tensor, stream=None) -> tuple[torch.Tensor, torch.Ten
     return scale, amax
 
 
+def pack_skinny(weight: torch.Tensor, stream=None) -> torch.Tensor:
+    """Re-lays a row-major [N, K] weight (E4M3 codes as uint8, or fp16) into the
+    contiguous 16 KB tiles the small-m (m <= 32) kernels stream sequentially."""
+    if weight.dtype not in (torch.uint8, torch.float16) or not weight.is_cuda or not weight.is_contiguous():
+        raise ValueError("weight must be a contiguous CUDA uint8 (E4M3 codes) or float16 tensor")
+    n, k = weight.shape
+    elem = weight.element_size()
+    size = native.library().lffw_skinny_packed_bytes(n, k, elem)
+    out = torch.empty(size, dtype=torch.uint8, device=weight.device)
+    native.check(native.library().lffw_pack_skinny_weights(weight.data_ptr(), n, k, elem, out.data_ptr(),
+                                                           _stream(stream)), "lffw_pack_skinny_weights")
+    return out
+
+
 def linear(x_codes: torch.Tensor, w_codes: torch.Tensor, w_scales: torch.Tensor, act_scale, *,
            bias: torch.Tensor | None = None, gelu: bool = False, out: torch.Tensor | None = None,
            want_y: bool = True, next_scale: float | None = None, next_codes: torch.Tensor | None = None,
-           stream=None) -> tuple[torch.Tensor | None, torch.Tensor | None]:
+           w_packed: torch.Tensor | None = None, stream=None) -> tuple[torch.Tensor | None, torch.Tensor | None]:
     """One FP8 Q/DQ linear on E4M3 codes: x_codes [..., K], w_codes [N, K].
+    `w_packed` (from pack_skinny(w_codes)) replaces w_codes on the m <= 32 path.
 
     Returns (y fp16 [..., N] or None, next-linear E4M3 codes or None)."""
     _require(x_codes, torch.uint8, "x_codes")
-    _require(w_codes, torch.uint8, "w_codes")
+    _require(w_packed if w_packed is not None else w_codes, torch.uint8, "w_codes")
     _require(w_scales, torch.float32, "w_scales")
     k = x_codes.shape[-1]
     m = x_codes.numel() // k
-    n = w_codes.shape[0]
+    n = w_scales.shape[0]  # one scale per output channel
     lead = tuple(x_codes.shape[:-1])
     if want_y and out is None:
         out = torch.empty(lead + (n,), dtype=torch.float16, device=x_codes.device)
@@ -130,7 +145,8 @@ def linear(x_codes: torch.Tensor, w_codes: torch.Tensor, w_scales: torch.Tensor,
         a.act_scale_ptr = act_scale.data_ptr()
     else:
         a.act_scale = float(act_scale)
-    a.w_codes = w_codes.data_ptr()
+    a.w_codes = (w_codes if w_packed is None else w_packed).data_ptr()
+    a.w_layout = native.WEIGHTS_ROW_MAJOR if w_packed is None else native.WEIGHTS_SKINNY_TILES
     a.w_scales = w_scales.data_ptr()
     a.bias = _ptr(bias)
     a.epilogue = native.EPILOGUE_GELU if gelu else native.EPILOGUE_NONE
@@ -230,16 +246,19 @@ def fp16_qkv(x: torch.Tensor, weight: torch.Tensor, q_bias: torch.Tensor, v_bias
 
 
 def fp16_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
-                out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
-    """fp16 [m <= 32, k] x fp16 [n, k]^T (+ bias) -> fp16 [m, n], fp32 accumulate (decoder logits)."""
+                out: torch.Tensor | None = None, w_packed: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """fp16 [m <= 32, k] x fp16 [n, k]^T (+ bias) -> fp16 [m, n], fp32 accumulate (decoder logits).
+    `w_packed` (from pack_skinny(weight)) streams the weight as contiguous tiles."""
     _require(x, torch.float16, "x")
     _require(weight, torch.float16, "weight")
     m, k = x.shape
     n = weight.shape[0]
     if out is None:
         out = torch.empty((m, n), dtype=torch.float16, device=x.device)
-    native.check(native.library().lffw_fp16_linear(x.data_ptr(), weight.data_ptr(), _ptr(bias), out.data_ptr(),
-                                                   m, n, k, _stream(stream)), "lffw_fp16_linear")
+    w = weight if w_packed is None else w_packed
+    layout = native.WEIGHTS_ROW_MAJOR if w_packed is None else native.WEIGHTS_SKINNY_TILES
+    native.check(native.library().lffw_fp16_linear(x.data_ptr(), w.data_ptr(), _ptr(bias), out.data_ptr(),
+                                                   m, n, k, layout, _stream(stream)), "lffw_fp16_linear")
     return out
 
 

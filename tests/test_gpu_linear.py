@@ -211,3 +211,38 @@ def test_fp16_linear_small_m_matches_oracle(cuda, fp8, native, m, n, k):
     bound = ATOL + RTOL * np.abs(want.astype(np.float64)) + k * 2.0**-24 * mag
     err = np.abs(got.astype(np.float64) - want.astype(np.float64))
     assert np.all(err <= bound), float((err - bound).max())
+
+
+@pytest.mark.parametrize("m,n,k,gelu", [(20, 3840, 1280, False), (20, 5120, 1280, True), (7, 1280, 5120, False),
+                                        (32, 1008, 1296, False)])
+def test_skinny_packed_weights_match_row_major(cuda, fp8, native, m, n, k, gelu):
+    """The pre-swizzled tile layout gives bit-identical results to row-major weights."""
+    import torch
+
+    rng = np.random.default_rng(m + n + k)
+    w = torch.from_numpy(halves(rng, (n, k), 0.02)).to(cuda)
+    b = torch.from_numpy(halves(rng, (n,), 0.02)).to(cuda)
+    q = fp8.QuantizedWeight.from_half(w, b)
+    packed = fp8.pack_skinny(q.codes)
+    assert packed.numel() == ((n + 127) // 128) * ((k + 127) // 128) * 16384
+    xq = fp8.quantize(torch.from_numpy(halves(rng, (m, k))).to(cuda), 0.01)
+    y0, c0 = fp8.linear(xq, q.codes, q.scales, 0.01, bias=b, gelu=gelu, next_scale=0.02)
+    y1, c1 = fp8.linear(xq, q.codes, q.scales, 0.01, bias=b, gelu=gelu, next_scale=0.02, w_packed=packed)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(y0.cpu().numpy().view(np.uint16), y1.cpu().numpy().view(np.uint16))
+    np.testing.assert_array_equal(c0.cpu().numpy(), c1.cpu().numpy())
+    x16 = torch.from_numpy(halves(rng, (m, k))).to(cuda)
+    l0 = fp8.fp16_linear(x16, w, b)
+    l1 = fp8.fp16_linear(x16, w, b, w_packed=fp8.pack_skinny(w))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(l0.cpu().numpy().view(np.uint16), l1.cpu().numpy().view(np.uint16))
+    assert native.device_error() == 0
+
+
+def test_packed_layout_rejected_for_large_m(cuda, fp8, native):
+    import torch
+
+    q = fp8.QuantizedWeight.from_half(torch.zeros(256, 256, dtype=torch.float16, device=cuda))
+    xq = torch.zeros(64, 256, dtype=torch.uint8, device=cuda)
+    with pytest.raises(native.NativeError):
+        fp8.linear(xq, q.codes, q.scales, 0.01, w_packed=fp8.pack_skinny(q.codes))
