@@ -707,23 +707,34 @@ constexpr int kThreads = 128;
 constexpr int kRows = 128;  // weight rows per cluster (MMA M)
 constexpr int kAct = 32;    // activation rows per MMA (MMA N); m <= 32
 constexpr int kBK = 128;    // K bytes per stage
-// Two stages per CTA and small CTAs: measured on B200, more resident CTAs
-// (independent weight streams) per SM stream faster than deeper rings.
-constexpr int kStages = 2;
 constexpr int kWBytes = kRows * kBK;
 constexpr int kXBytes = kAct * kBK;
 constexpr int kStageBytes = kWBytes + kXBytes;
-constexpr int kRedStride = kAct + 1; // floats per reduction row (bank-conflict padding)
-constexpr int kOffX = kStages * kWBytes;
-constexpr int kRedBytes = kRows * kRedStride * 4;
+constexpr int kRedStride = kRows + 4; // floats per activation row of the partials (m-major)
+constexpr int kRedBytes = kAct * kRedStride * 4;
 // The split-K reduction buffer reuses the stage memory: it is written only
 // after every load has landed and every MMA has completed.
 constexpr int kOffRed = 0;
-constexpr int kRingBytes = kOffX + kStages * kXBytes;
-constexpr int kOffBar = (kRingBytes > kRedBytes ? kRingBytes : kRedBytes + 1023) / 1024 * 1024;
-constexpr int kSmemBytes = kOffBar + 128 + 1024;
+
+// Shared-memory ring of ST stages.  Two stages and small CTAs (five per SM)
+// stream fastest when there are many CTAs (measured on B200: more independent
+// weight streams per SM beat deeper rings); a deep ring is used when the grid
+// is small and each CTA owns more K blocks than two stages hold, so that all
+// of a CTA's weights are requested before it waits for the previous kernel.
+template <int ST>
+struct Ring {
+    static constexpr int kStages = ST;
+    static constexpr int kOffX = ST * kWBytes;
+    static constexpr int kRingBytes = kOffX + ST * kXBytes;
+    static constexpr int kOffBar = (kRingBytes > kRedBytes ? kRingBytes : kRedBytes + 1023) / 1024 * 1024;
+    static constexpr int kSmemBytes = kOffBar + 128 + 1024;
+    static_assert((2 * ST + 2) * 8 <= 128, "barrier area");
+};
+constexpr int kShallow = 2;
+constexpr int kDeep = 6;
+static_assert(Ring<kShallow>::kSmemBytes <= 46 * 1024, "five CTAs per SM");
+static_assert(Ring<kDeep>::kSmemBytes <= 227 * 1024, "shared memory budget");
 constexpr int kMaxCluster = 8;
-static_assert(kSmemBytes <= 46 * 1024, "five CTAs per SM");
 
 enum : int { kKindE4M3 = 0, kKindF16 = 1 };
 
@@ -740,10 +751,48 @@ struct Params {
     const uint8_t *w_packed; // non-null: weights in pre-swizzled 16 KB tiles (pack_kernel)
 };
 
-template <int KIND, int EPI>
+// Split-K reduction over a cluster of S CTAs.  Each CTA finishes 128 / S of
+// the 128 weight rows; a thread owns one of them (`row`) and the activation
+// rows m = g, g + S, g + 2S, ... below m_count, where g = threadIdx.x / (128 / S).
+// The partials are stored m-major, so a warp's remote loads read runs of
+// consecutive rows.  Every remote partial is requested before the sum, which
+// adds the cluster's partials in rank order.
+template <int S, class Finish>
+__device__ __forceinline__ void reduce_rows(const float *red, int row, int m_count, Finish &finish)
+{
+    constexpr int kPer = kAct / S; // activation rows per thread
+    const int g = static_cast<int>(threadIdx.x) / (kRows / S);
+    float part[kPer][S];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const int m = g + j * S;
+        if (m < m_count) {
+            const uint32_t local = smem_u32(red + m * kRedStride + row);
+#pragma unroll
+            for (int q = 0; q < S; ++q)
+                part[j][q] = ld_shared_cluster_f32(map_to_rank(local, static_cast<uint32_t>(q)));
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const int m = g + j * S;
+        if (m < m_count) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int q = 0; q < S; ++q)
+                acc += part[j][q];
+            finish(acc, m);
+        }
+    }
+}
+
+template <int KIND, int EPI, int ST>
 __global__ void __launch_bounds__(kThreads)
     skinny_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, const Params p)
 {
+    constexpr int kStages = Ring<ST>::kStages;
+    constexpr int kOffX = Ring<ST>::kOffX;
+    constexpr int kOffBar = Ring<ST>::kOffBar;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -781,6 +830,22 @@ __global__ void __launch_bounds__(kThreads)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+
+    // The output row this thread finishes (its own TMEM lane when S == 1, else
+    // row `threadIdx.x % (128 / S)` of this CTA's share of the reduction) and
+    // that row's weight scale and bias: constants of the layer, so they are
+    // read before waiting for the previous kernel.
+    const int my_row = S == 1 ? static_cast<int>(threadIdx.x)
+                              : rank * (kRows / S) + static_cast<int>(threadIdx.x) % (kRows / S);
+    const int my_n = n0 + my_row;
+    float my_ws = 1.0f;
+    uint16_t my_bias = 0;
+    if (my_n < p.n) {
+        if (p.w_scales)
+            my_ws = __ldg(p.w_scales + my_n);
+        if (p.bias)
+            my_bias = __ldg(p.bias + my_n);
+    }
 
     if (warp == 0 && lane == 0) {
         // Weights do not depend on the previous kernel: arm the first stages now.
@@ -849,6 +914,7 @@ __global__ void __launch_bounds__(kThreads)
 
     // Read the accumulator: thread (warp w, lane) holds weight row 32w + lane,
     // one fp32 per activation row.
+    const float act_scale = p.act_scale_ptr ? *p.act_scale_ptr : p.act_scale;
     uint32_t v[kAct];
     const bool ok = nkb == 0 || __all_sync(0xffffffffu, mbar_wait(bar_acc, 0, kSiteEpilogueAccFull));
     if (nkb > 0 && ok) {
@@ -860,55 +926,39 @@ __global__ void __launch_bounds__(kThreads)
         for (int i = 0; i < kAct; ++i)
             v[i] = 0u; // this CTA's K slice is empty
     }
-    const float act_scale = p.act_scale_ptr ? *p.act_scale_ptr : p.act_scale;
+    const float cs = p.w_scales ? act_scale * my_ws : 1.0f;
     const uint64_t neg_scale2 = f2_bits(-p.next_scale, -p.next_scale);
     const uint64_t recip2 = f2_bits(p.next_recip, p.next_recip);
-    auto finish = [&](float acc, int m, int n) {
-        const float ws = p.w_scales ? p.w_scales[n] : 1.0f;
-        uint32_t z = f2h_rn(acc * (p.w_scales ? act_scale * ws : 1.0f));
+    auto finish = [&](float acc, int m) {
+        uint32_t z = f2h_rn(acc * cs);
         if (p.bias)
-            z = hadd_rn(static_cast<uint16_t>(z), p.bias[n]);
+            z = hadd_rn(static_cast<uint16_t>(z), my_bias);
         if (EPI & 1)
             z = gemm::gelu_fp16x2(z, g_erf_table) & 0xFFFFu;
-        const size_t o = static_cast<size_t>(m) * p.n + n;
+        const size_t o = static_cast<size_t>(m) * p.n + my_n;
         if (p.y)
             p.y[o] = static_cast<uint16_t>(z);
         if (p.next_codes)
             p.next_codes[o] = static_cast<uint8_t>(e4m3x2_quotient(z, neg_scale2, recip2) & 0xFFu);
     };
     if (S == 1) {
-        const int n = n0 + warp * 32 + lane;
-        if (n < p.n) {
+        if (my_n < p.n) {
 #pragma unroll
             for (int m = 0; m < kAct; ++m)
                 if (m < p.m)
-                    finish(__uint_as_float(v[m]), m, n);
+                    finish(__uint_as_float(v[m]), m);
         }
     } else {
-        const int row = warp * 32 + lane;
 #pragma unroll
         for (int i = 0; i < kAct; ++i)
-            red[row * kRedStride + i] = __uint_as_float(v[i]);
+            red[i * kRedStride + threadIdx.x] = __uint_as_float(v[i]);
         cluster_sync();
-        // This CTA reduces rows [rank * 128/S, (rank + 1) * 128/S), summing the
-        // cluster's partials in rank order.
-        const int rows_per = kRows / S;
-        for (int e = threadIdx.x; e < rows_per * kAct; e += kThreads) {
-            const int r = rank * rows_per + e / kAct;
-            const int m = e % kAct;
-            const uint32_t local = smem_u32(red + r * kRedStride + m);
-            // All remote loads in flight before the (rank-ordered) sum.
-            float part[kMaxCluster];
-#pragma unroll
-            for (int q = 0; q < kMaxCluster; ++q)
-                part[q] = q < S ? ld_shared_cluster_f32(map_to_rank(local, static_cast<uint32_t>(q))) : 0.0f;
-            float acc = 0.0f;
-#pragma unroll
-            for (int q = 0; q < kMaxCluster; ++q)
-                acc += part[q];
-            const int n = n0 + r;
-            if (m < p.m && n < p.n)
-                finish(acc, m, n);
+        if (my_n < p.n) {
+            switch (S) {
+            case 2: reduce_rows<2>(red, my_row, p.m, finish); break;
+            case 4: reduce_rows<4>(red, my_row, p.m, finish); break;
+            default: reduce_rows<8>(red, my_row, p.m, finish); break;
+            }
         }
         cluster_sync(); // peers read this CTA's partials until here
     }
@@ -1330,15 +1380,29 @@ cudaError_t launch_fp8_gemm(const LinearLaunch &L, cudaStream_t stream)
 namespace {
 
 // Cluster size (CTAs sharing one 128-row block, splitting K): enough CTAs for
-// about two per SM, a power of two, at most 8 and at most the number of K blocks.
-int skinny_cluster(int64_t n, int num_kb)
+// about two per SM, a power of two, at most `max_cluster` and at most the
+// number of K blocks.
+int skinny_cluster(int64_t n, int num_kb, int max_cluster)
 {
     const int64_t blocks = (n + skinny::kRows - 1) / skinny::kRows;
     const int64_t want = (2 * static_cast<int64_t>(sm_count()) + blocks - 1) / blocks;
     int s = 1;
-    while (s < want && s * 2 <= skinny::kMaxCluster && s * 2 <= num_kb)
+    while (s < want && s * 2 <= max_cluster && s * 2 <= num_kb)
         s *= 2;
     return s;
+}
+
+// Largest cluster size the skinny kernel uses: 8 (measured on B200, 16-CTA
+// clusters reduce slower than they stream), or the LFFW_SKINNY_MAX_CLUSTER
+// tuning override (1 to 8), read once.
+int skinny_max_cluster()
+{
+    static const int value = [] {
+        const char *cap = std::getenv("LFFW_SKINNY_MAX_CLUSTER");
+        const int v = cap ? std::atoi(cap) : 0;
+        return v >= 1 && v <= skinny::kMaxCluster ? v : skinny::kMaxCluster;
+    }();
+    return value;
 }
 
 template <int KIND, int EPI>
@@ -1357,7 +1421,7 @@ cudaError_t run_skinny(const void *x, const void *w, int64_t m, int64_t n, int64
     p.m = static_cast<int>(m);
     p.n = static_cast<int>(n);
     p.num_kb = static_cast<int>((k * elem + skinny::kBK - 1) / skinny::kBK);
-    p.cluster = skinny_cluster(n, p.num_kb);
+    p.cluster = skinny_cluster(n, p.num_kb, skinny_max_cluster());
     p.act_scale = L.act_scale;
     p.act_scale_ptr = L.act_scale_ptr;
     p.w_scales = L.w_scales;
@@ -1367,15 +1431,21 @@ cudaError_t run_skinny(const void *x, const void *w, int64_t m, int64_t n, int64
     p.next_recip = L.next_codes ? static_cast<float>(1.0 / static_cast<double>(L.next_scale)) : 0.0f;
     p.next_codes = L.next_codes;
     p.w_packed = packed ? static_cast<const uint8_t *>(w) : nullptr;
-    auto kernel = skinny::skinny_kernel<KIND, EPI>;
-    const cudaError_t attr = ensure_smem(kernel, skinny::kSmemBytes);
+    const int64_t blocks = (n + skinny::kRows - 1) / skinny::kRows;
+    const int64_t grid = blocks * p.cluster;
+    const int per_cta = (p.num_kb + p.cluster - 1) / p.cluster;
+    // A grid of at most one CTA per SM whose CTAs own more K blocks than the
+    // shallow ring holds takes the deep ring.
+    const bool deep = grid <= sm_count() && per_cta > skinny::kShallow;
+    auto kernel = deep ? skinny::skinny_kernel<KIND, EPI, skinny::kDeep> : skinny::skinny_kernel<KIND, EPI, skinny::kShallow>;
+    const int smem = deep ? skinny::Ring<skinny::kDeep>::kSmemBytes : skinny::Ring<skinny::kShallow>::kSmemBytes;
+    const cudaError_t attr = ensure_smem(kernel, smem);
     if (attr != cudaSuccess)
         return attr;
-    const int64_t blocks = (n + skinny::kRows - 1) / skinny::kRows;
     cudaLaunchConfig_t config{};
-    config.gridDim = dim3(static_cast<unsigned>(blocks * p.cluster));
+    config.gridDim = dim3(static_cast<unsigned>(grid));
     config.blockDim = dim3(skinny::kThreads);
-    config.dynamicSmemBytes = skinny::kSmemBytes;
+    config.dynamicSmemBytes = smem;
     config.stream = stream;
     cudaLaunchAttribute attrs[2];
     int count = 0;

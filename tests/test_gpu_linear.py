@@ -50,6 +50,10 @@ CASES = [
     (7, 1280, 1280),
     (20, 3840, 1280),
     (32, 1280, 5120),
+    # small-M split-K cluster sizes 1, 2 and 4 (many 128-row blocks)
+    (3, 40960, 256),
+    (9, 20480, 640),
+    (20, 10240, 1280),
     # CTA-pair tiles (M >= 512): a last pair tile whose second CTA holds only
     # padding rows, ragged N, and both tile widths
     (600, 272, 1280),
