@@ -70,6 +70,14 @@ enum { LFFW_WEIGHTS_ROW_MAJOR = 0, LFFW_WEIGHTS_SKINNY_TILES = 1 };
  * Requirements: m,n,k >= 1; k % 16 == 0; n % 16 == 0; 16-byte aligned pointers;
  * act_scale (or *act_scale_ptr) finite and > 0; next_scale in [2^-125, 2^125]
  * (a normal float with a normal reciprocal) when next_codes is set.
+ * Stream overlap: the linear and quantize kernels use programmatic dependent
+ * launch.  Each lets the next launch on its stream start early, and each waits
+ * for the previous kernel before it reads activations or writes outputs, but a
+ * linear reads its weights (w_codes, w_scales, bias) before that wait.
+ * Weights are layer constants, so this is safe unless the kernel just before
+ * a linear is an lffw_fp8_quantize or lffw_fp8_linear call that writes those
+ * weights.  In that case, put any other stream operation (an event record, a
+ * copy) between the two calls.
  */
 typedef struct lffw_fp8_linear_args {
     size_t struct_size; /* sizeof(lffw_fp8_linear_args) */

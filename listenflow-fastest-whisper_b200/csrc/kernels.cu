@@ -131,6 +131,50 @@ __device__ __forceinline__ uint32_t e4m3x2_quotient(uint32_t h2, uint64_t scale2
     return e4m3x2(ql, qh);
 }
 
+// Scales for which the lean quotient below is exact: 65504 / 128 > 448, so a
+// magnitude clamped to 65504 (an infinity) still saturates, and
+// 65504 * 2^110 < 2^128, so no product overflows.
+__host__ __device__ __forceinline__ bool lean_scale(float scale)
+{
+    return scale >= 0x1p-110f && scale <= 128.0f;
+}
+
+// E4M3 codes of |h2| / scale (sign bits clear) for a lean scale: the magnitude
+// is clamped to 65504 with min.NaN (NaN stays NaN), then takes the same
+// corrected quotient as e4m3x2_quotient; zero needs no special case.
+__device__ __forceinline__ uint32_t e4m3x2_magnitude(uint32_t h2, uint64_t scale2_neg, uint64_t recip2)
+{
+    uint32_t a;
+    asm("min.NaN.f16x2 %0, %1, %2;" : "=r"(a) : "r"(h2 & 0x7FFF7FFFu), "r"(0x7BFF7BFFu));
+    const uint64_t x = f2_bits(h2f(static_cast<uint16_t>(a & 0xFFFFu)), h2f(static_cast<uint16_t>(a >> 16)));
+    uint64_t q0, r, q1;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(q0) : "l"(x), "l"(recip2));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(scale2_neg), "l"(q0), "l"(x));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(q1) : "l"(r), "l"(recip2), "l"(q0));
+    return e4m3x2(__uint_as_float(static_cast<uint32_t>(q1)), __uint_as_float(static_cast<uint32_t>(q1 >> 32)));
+}
+
+// Four E4M3 codes (byte i = half i of h01, h23) for a lean scale: magnitudes,
+// then each input's sign bit copied onto its code (prmt replicates the sign
+// of bytes 1, 3, 5, 7 -- the fp16 sign bits -- across result bytes 0-3).
+__device__ __forceinline__ uint32_t e4m3x4_lean(uint32_t h01, uint32_t h23, uint64_t scale2_neg, uint64_t recip2)
+{
+    const uint32_t lo = e4m3x2_magnitude(h01, scale2_neg, recip2);
+    const uint32_t hi = e4m3x2_magnitude(h23, scale2_neg, recip2);
+    uint32_t q, sign;
+    asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(q) : "r"(lo), "r"(hi));
+    asm("prmt.b32 %0, %1, %2, 0xFDB9;" : "=r"(sign) : "r"(h01), "r"(h23));
+    return q | (sign & 0x80808080u);
+}
+
+// Four codes by whichever quotient the scale admits (`lean` is uniform).
+__device__ __forceinline__ uint32_t e4m3x4(uint32_t h01, uint32_t h23, bool lean, uint64_t scale2_neg, uint64_t recip2)
+{
+    if (lean)
+        return e4m3x4_lean(h01, h23, scale2_neg, recip2);
+    return e4m3x2_quotient(h01, scale2_neg, recip2) | (e4m3x2_quotient(h23, scale2_neg, recip2) << 16);
+}
+
 
 // ---------------------------------------------------------------------------
 // FP8 GEMM (tcgen05)
@@ -202,6 +246,7 @@ struct Params {
     const uint16_t *bias;
     float next_scale;
     float next_recip; // RN(1 / next_scale)
+    int next_lean;    // lean_scale(next_scale)
 };
 
 // fp16(erf(x)) of two packed fp16 values, rounded to nearest even: one table
@@ -286,6 +331,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint16_t *erf_table = reinterpret_cast<uint16_t *>(smem + C::kOffTable);
 
     if (threadIdx.x == 0) {
+        // The next kernel on the stream may launch now; it waits for this grid
+        // to complete before it reads this grid's outputs.
+        griddepcontrol_launch_dependents();
         for (int s = 0; s < C::kStages; ++s) {
             mbar_init(bar_full + 8 * s, 1);
             mbar_init(bar_empty + 8 * s, 1);
@@ -332,26 +380,51 @@ __global__ void __launch_bounds__(kThreads, 1)
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
+            // The weights do not come from the previous kernel: the first stages'
+            // B tiles are requested before waiting for it (stages start empty).
+            const int pre = tile_first < p.num_tiles ? (p.num_kb < C::kStages ? p.num_kb : C::kStages) : 0;
+            for (int kb = 0; kb < pre; ++kb) {
+                const int n0 = (tile_first / p.m_tiles) * BN + static_cast<int>(rank) * C::kBRows;
+                const uint32_t full = bar_full + 8 * kb;
+                if (kPair) {
+                    if (leader)
+                        mbar_arrive_expect_tx(full, C::kTxBytes);
+                    tma_load_2d_pair(sbase + C::kOffB + kb * C::kBBytes, &tm_b, map_to_rank(full, 0), kb * kBK, n0);
+                } else {
+                    mbar_arrive_expect_tx(full, C::kTxBytes);
+                    tma_load_2d(sbase + C::kOffB + kb * C::kBBytes, &tm_b, full, kb * kBK, n0);
+                }
+            }
+            griddepcontrol_wait();
+            int issued = 0;
             for (int t = tile_first; ok && t < p.num_tiles; t += tile_step) {
                 const int m0 = (t % p.m_tiles) * C::kTileM + static_cast<int>(rank) * kBM;
                 const int n0 = (t / p.m_tiles) * BN + static_cast<int>(rank) * C::kBRows;
-                for (int kb = 0; kb < p.num_kb; ++kb) {
-                    if (!mbar_wait(bar_empty + 8 * s, ph ^ 1u, kSiteProducerEmpty)) {
-                        ok = false;
-                        break;
-                    }
+                for (int kb = 0; kb < p.num_kb; ++kb, ++issued) {
                     const uint32_t full = bar_full + 8 * s;
-                    if (kPair) {
-                        // Both CTAs' bytes complete on the leader's barrier, armed by the leader.
-                        const uint32_t leader_full = map_to_rank(full, 0);
-                        if (leader)
-                            mbar_arrive_expect_tx(full, C::kTxBytes);
-                        tma_load_2d_pair(sbase + s * C::kABytes, &tm_a, leader_full, kb * kBK, m0);
-                        tma_load_2d_pair(sbase + C::kOffB + s * C::kBBytes, &tm_b, leader_full, kb * kBK, n0);
+                    if (issued < pre) {
+                        // Armed with its B tile above: only the activations remain.
+                        if (kPair)
+                            tma_load_2d_pair(sbase + s * C::kABytes, &tm_a, map_to_rank(full, 0), kb * kBK, m0);
+                        else
+                            tma_load_2d(sbase + s * C::kABytes, &tm_a, full, kb * kBK, m0);
                     } else {
-                        mbar_arrive_expect_tx(full, C::kTxBytes);
-                        tma_load_2d(sbase + s * C::kABytes, &tm_a, full, kb * kBK, m0);
-                        tma_load_2d(sbase + C::kOffB + s * C::kBBytes, &tm_b, full, kb * kBK, n0);
+                        if (!mbar_wait(bar_empty + 8 * s, ph ^ 1u, kSiteProducerEmpty)) {
+                            ok = false;
+                            break;
+                        }
+                        if (kPair) {
+                            // Both CTAs' bytes complete on the leader's barrier, armed by the leader.
+                            const uint32_t leader_full = map_to_rank(full, 0);
+                            if (leader)
+                                mbar_arrive_expect_tx(full, C::kTxBytes);
+                            tma_load_2d_pair(sbase + s * C::kABytes, &tm_a, leader_full, kb * kBK, m0);
+                            tma_load_2d_pair(sbase + C::kOffB + s * C::kBBytes, &tm_b, leader_full, kb * kBK, n0);
+                        } else {
+                            mbar_arrive_expect_tx(full, C::kTxBytes);
+                            tma_load_2d(sbase + s * C::kABytes, &tm_a, full, kb * kBK, m0);
+                            tma_load_2d(sbase + C::kOffB + s * C::kBBytes, &tm_b, full, kb * kBK, n0);
+                        }
                     }
                     used_mask |= 1u << s;
                     parity_mask = (parity_mask & ~(1u << s)) | (ph << s);
@@ -431,10 +504,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else {
-        // ---------------- Epilogue: 8 independent warps ----------------
+        // ---------------- Epilogue: 16 independent warps ----------------
         const int ew = warp - 2;
         const int quarter = warp & 3; // the TMEM lane quarter this warp may access
         const int slice = ew >> 2;    // which quarter of the tile's columns
+        // A dynamic scale, and the buffers this grid writes, belong to the
+        // previous kernel until it completes.
+        griddepcontrol_wait();
         const float act_scale = p.act_scale_ptr ? *p.act_scale_ptr : p.act_scale;
         const uint64_t neg_scale2 = f2_bits(-p.next_scale, -p.next_scale);
         const uint64_t recip2 = f2_bits(p.next_recip, p.next_recip);
@@ -530,8 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         uint32_t q[4];
 #pragma unroll
                         for (int i = 0; i < 4; ++i)
-                            q[i] = e4m3x2_quotient(h[2 * i], neg_scale2, recip2) |
-                                   (e4m3x2_quotient(h[2 * i + 1], neg_scale2, recip2) << 16);
+                            q[i] = e4m3x4(h[2 * i], h[2 * i + 1], p.next_lean != 0, neg_scale2, recip2);
                         const uint32_t pos = static_cast<uint32_t>(hf) ^ ((static_cast<uint32_t>(lane) >> 2) & 1u);
                         *reinterpret_cast<uint4 *>(cbuf + lane * 32 + pos * 16) = make_uint4(q[0], q[1], q[2], q[3]);
                     }
@@ -1015,35 +1090,53 @@ __device__ __forceinline__ uint4 ld_stream16(const void *p)
 
 
 // A warp converts 1024 halves per iteration: four coalesced 512-byte loads
-// in flight per warp (16 bytes per lane each), four coalesced 256-byte stores,
-// streaming cache hints (the activations are read once).
+// per lane group (16 bytes per lane each), four coalesced 256-byte stores,
+// streaming cache hints (the activations are read once).  The next chunk's
+// loads are issued before the current chunk is converted, so each warp keeps
+// 4 KB in flight while its arithmetic runs.
 constexpr int64_t kQuantChunk = 1024;
+
+__device__ __forceinline__ void load_chunk(uint4 (&h)[4], const uint16_t *x, int64_t c, int lane)
+{
+    const uint16_t *src = x + c * kQuantChunk + lane * 8;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        h[i] = ld_stream16(src + 256 * i);
+}
 
 __global__ void __launch_bounds__(kThreads)
     quantize_kernel(const uint16_t *__restrict__ x, int64_t count, float scale_value, float recip_value,
                     const float *scale_ptr, uint8_t *__restrict__ codes)
 {
+    // Programmatic dependent launch: the next kernel may start its prologue
+    // now; this one waits for the previous kernel before reading its output.
+    if (threadIdx.x == 0)
+        griddepcontrol_launch_dependents();
+    griddepcontrol_wait();
     const float scale = scale_ptr ? *scale_ptr : scale_value;
     const float recip = scale_ptr ? __frcp_rn(scale) : recip_value;
+    const bool lean = lean_scale(scale);
     const uint64_t neg_scale2 = f2_bits(-scale, -scale), recip2 = f2_bits(recip, recip);
     const int lane = threadIdx.x % 32;
     const int64_t chunks = count / kQuantChunk;
     const int64_t warps = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
-    for (int64_t c = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + threadIdx.x / 32; c < chunks; c += warps) {
-        const uint16_t *src = x + c * kQuantChunk + lane * 8;
+    int64_t c = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + threadIdx.x / 32;
+    uint4 cur[4], next[4];
+    if (c < chunks)
+        load_chunk(cur, x, c, lane);
+    for (; c < chunks; c += warps) {
+        if (c + warps < chunks)
+            load_chunk(next, x, c + warps, lane);
         uint8_t *dst = codes + c * kQuantChunk + lane * 8;
-        uint4 h[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-            h[i] = ld_stream16(src + 256 * i);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const uint32_t lo = e4m3x2_quotient(h[i].x, neg_scale2, recip2) |
-                                (e4m3x2_quotient(h[i].y, neg_scale2, recip2) << 16);
-            const uint32_t hi = e4m3x2_quotient(h[i].z, neg_scale2, recip2) |
-                                (e4m3x2_quotient(h[i].w, neg_scale2, recip2) << 16);
+            const uint32_t lo = e4m3x4(cur[i].x, cur[i].y, lean, neg_scale2, recip2);
+            const uint32_t hi = e4m3x4(cur[i].z, cur[i].w, lean, neg_scale2, recip2);
             asm volatile("st.global.cs.v2.u32 [%0], {%1, %2};" ::"l"(dst + 256 * i), "r"(lo), "r"(hi) : "memory");
         }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            cur[i] = next[i];
     }
     // Tail (count % 1024), handled by block 0.
     if (blockIdx.x == 0)
@@ -1301,6 +1394,7 @@ cudaError_t run_gemm(const LinearLaunch &L, cudaStream_t stream)
     // Correctly rounded reciprocal: binary64 quotient, one rounding to binary32
     // (innocuous double rounding for division since 53 >= 2*24 + 2).
     p.next_recip = L.next_codes ? static_cast<float>(1.0 / static_cast<double>(L.next_scale)) : 0.0f;
+    p.next_lean = L.next_codes && lean_scale(L.next_scale) ? 1 : 0;
 
     auto kernel = gemm::fp8_gemm_kernel<BN, EPI, kPair>;
     const cudaError_t attr = ensure_smem(kernel, C::kSmemBytes);
@@ -1313,15 +1407,20 @@ cudaError_t run_gemm(const LinearLaunch &L, cudaStream_t stream)
     config.blockDim = dim3(gemm::kThreads);
     config.dynamicSmemBytes = C::kSmemBytes;
     config.stream = stream;
-    cudaLaunchAttribute attrs[1];
+    cudaLaunchAttribute attrs[2];
+    int count = 0;
+    attrs[count].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[count].val.programmaticStreamSerializationAllowed = 1;
+    ++count;
     if (kPair) {
-        attrs[0].id = cudaLaunchAttributeClusterDimension;
-        attrs[0].val.clusterDim.x = 2;
-        attrs[0].val.clusterDim.y = 1;
-        attrs[0].val.clusterDim.z = 1;
-        config.attrs = attrs;
-        config.numAttrs = 1;
+        attrs[count].id = cudaLaunchAttributeClusterDimension;
+        attrs[count].val.clusterDim.x = 2;
+        attrs[count].val.clusterDim.y = 1;
+        attrs[count].val.clusterDim.z = 1;
+        ++count;
     }
+    config.attrs = attrs;
+    config.numAttrs = count;
     const cudaError_t err = cudaLaunchKernelEx(&config, kernel, tm_a, tm_b, tm_y, tm_c, p);
     count_launch();
     return err != cudaSuccess ? err : cudaGetLastError();
@@ -1546,12 +1645,24 @@ cudaError_t launch_quantize(const uint16_t *x, int64_t count, float scale, const
     const int64_t chunks = count / quant::kQuantChunk;
     const int64_t warps_per_block = quant::kThreads / 32;
     int64_t blocks = (chunks + warps_per_block - 1) / warps_per_block;
-    blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, static_cast<int64_t>(sm_count()) * 8));
+    static const int per_sm = [] {
+        const char *v = std::getenv("LFFW_QUANT_BLOCKS_PER_SM");
+        return v && std::atoi(v) > 0 ? std::atoi(v) : 4;
+    }();
+    blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, static_cast<int64_t>(sm_count()) * per_sm));
     const float recip = static_cast<float>(1.0 / static_cast<double>(scale));
-    quant::quantize_kernel<<<static_cast<unsigned>(blocks), quant::kThreads, 0, stream>>>(
-        x, count, scale, recip, scale_ptr, codes);
+    cudaLaunchConfig_t config{};
+    config.gridDim = dim3(static_cast<unsigned>(blocks));
+    config.blockDim = dim3(quant::kThreads);
+    config.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    config.attrs = attr;
+    config.numAttrs = 1;
+    const cudaError_t err = cudaLaunchKernelEx(&config, quant::quantize_kernel, x, count, scale, recip, scale_ptr, codes);
     count_launch();
-    return cudaGetLastError();
+    return err != cudaSuccess ? err : cudaGetLastError();
 }
 
 cudaError_t launch_quantize_rows(const uint16_t *w, int64_t rows, int64_t cols, const float *scales,

@@ -102,6 +102,22 @@ def test_linear_matches_oracle(cuda, fp8, oracle, native, m, n, k, gelu):
     np.testing.assert_array_equal(got, oracle.quantize(y_bits, next_scale))
 
 
+@pytest.mark.parametrize("next_scale", [128.0, 2.0**-110, 200.0, 2.0**-115])
+def test_fused_codes_at_quotient_limits(cuda, fp8, oracle, native, next_scale):
+    """The fused next-linear codes at the limits of the magnitude quotient
+    (128 and 2^-110) and beyond them, where the general quotient runs."""
+    import torch
+
+    d = _prepare(torch, fp8, oracle, cuda, 300, 1280, 640, seed=77)
+    for gelu in (False, True):
+        y, codes = fp8.linear(d["xq"], d["wq"], d["ws"], float(d["act_scale"]), bias=d["bd"], gelu=gelu,
+                              next_scale=next_scale)
+        torch.cuda.synchronize()
+        y_bits = y.cpu().numpy().view(np.uint16)
+        np.testing.assert_array_equal(codes.cpu().numpy(), oracle.quantize(y_bits, np.float32(next_scale)))
+    assert native.device_error() == 0
+
+
 def test_linear_without_bias_and_codes_only(cuda, fp8, oracle):
     import torch
 

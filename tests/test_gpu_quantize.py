@@ -33,6 +33,9 @@ def test_every_half_bit_exact(cuda, fp8, oracle, scale):
     nan = np.isnan(ALL_HALVES.view(np.float16))
     np.testing.assert_array_equal(got[~nan], want[~nan])
     assert np.all(got[nan] & 0x7F == 0x7F)
+    # Scales in [2^-110, 128] take the magnitude quotient, which also keeps a
+    # NaN's sign as the oracle does.
+    np.testing.assert_array_equal(got, want)
     # scale read from device memory gives the same codes
     s = torch.tensor([scale], dtype=torch.float32, device=cuda)
     np.testing.assert_array_equal(fp8.quantize(x, s).cpu().numpy(), got)
