@@ -67,9 +67,13 @@ def parse_args(argv=None):
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--e2e-steps", type=int, default=5)
+    p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--decoder-steps", type=int, default=20,
                    help="timed replays of the C3 decoder-step graph (0 skips it)")
+    p.add_argument("--decoder-layers", type=int, default=32,
+                   help="decoder layers in the C3 step (32 is the measured configuration)")
+    p.add_argument("--only", choices=("all", "decoder"), default="all",
+                   help="'decoder': run only the C3 decoder step and print its line (profiling)")
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="target CPU-baseline sample time (0 skips the CPU baseline, for profiling runs)")
     return p.parse_args(argv)
@@ -203,28 +207,28 @@ def run_ours(args, rank, local_rank, world):
     scrub = torch.ones(64 * 1024 * 1024, dtype=torch.float32, device=device)  # 256 MiB, read to clean L2
     gemm_flops = {name: 2 * M * k * n for name, k, n, _ in LINEARS}
 
-    def step(events=None):
+    def step(events=None, a=acts, o=outs):
         def mark(i):
             if events is not None:
                 events[i].record(stream)
-        fp8.quantize(acts["qkv"], scales["qkv"], out=codes["qkv"])
+        fp8.quantize(a["qkv"], scales["qkv"], out=codes["qkv"])
         mark(0)
         fp8.linear(codes["qkv"], weights["qkv"].codes, weights["qkv"].scales, scales["qkv"],
-                   bias=weights["qkv"].bias, out=outs["qkv"])
+                   bias=weights["qkv"].bias, out=o["qkv"])
         mark(1)
-        fp8.quantize(acts["out_proj"], scales["out_proj"], out=codes["out_proj"])
+        fp8.quantize(a["out_proj"], scales["out_proj"], out=codes["out_proj"])
         mark(2)
         fp8.linear(codes["out_proj"], weights["out_proj"].codes, weights["out_proj"].scales, scales["out_proj"],
-                   bias=weights["out_proj"].bias, out=outs["out_proj"])
+                   bias=weights["out_proj"].bias, out=o["out_proj"])
         mark(3)
-        fp8.quantize(acts["fc1"], scales["fc1"], out=codes["fc1"])
+        fp8.quantize(a["fc1"], scales["fc1"], out=codes["fc1"])
         mark(4)
         fp8.linear(codes["fc1"], weights["fc1"].codes, weights["fc1"].scales, scales["fc1"],
                    bias=weights["fc1"].bias, gelu=True, want_y=False, next_scale=scales["fc2"],
                    next_codes=fc2_codes)
         mark(5)
         fp8.linear(fc2_codes, weights["fc2"].codes, weights["fc2"].scales, scales["fc2"],
-                   bias=weights["fc2"].bias, out=outs["fc2"])
+                   bias=weights["fc2"].bias, out=o["fc2"])
         mark(6)
 
     for _ in range(max(3, args.warmup)):
@@ -280,39 +284,69 @@ def run_ours(args, rank, local_rank, world):
     if native.device_error() != 0:
         raise RuntimeError("device-side wait timed out during the timed steps")
 
-    # End to end through the public API with host buffers: pinned fp16
-    # activations in, fp16 results out, every step.
+    # End to end through the public API with host buffers, every step: its
+    # three fp16 activation tensors are copied in from pinned host memory and
+    # its three fp16 outputs are copied back.  Copies in, the step's kernels
+    # and copies out run on three streams with two device buffer sets, so
+    # step i's outputs go out while step i+1 computes and step i+2's inputs
+    # come in (PCIe is full duplex).
     import torch as _t
 
     host_in = {name: _t.from_numpy(a).pin_memory() for name, a in acts_np.items()}
     host_out = {name: _t.empty(tuple(t.shape), dtype=t.dtype).pin_memory() for name, t in outs.items()}
     h2d = sum(t.numel() * t.element_size() for t in host_in.values())
     d2h = sum(t.numel() * t.element_size() for t in host_out.values())
-    e_start, e_end = _t.cuda.Event(enable_timing=True), _t.cuda.Event(enable_timing=True)
+    sets = [(acts, outs), ({k: _t.empty_like(v) for k, v in acts.items()},
+                           {k: _t.empty_like(v) for k, v in outs.items()})]
+    s_in, s_out = _t.cuda.Stream(device), _t.cuda.Stream(device)
 
-    def e2e_step():
-        for name, t in host_in.items():
-            acts[name].copy_(t, non_blocking=True)
-        step()
-        for name, t in host_out.items():
-            t.copy_(outs[name], non_blocking=True)
+    def e2e_run(n):
+        """n pipelined end-to-end steps; returns (start event on s_in, end event on s_out)."""
+        start, end = _t.cuda.Event(enable_timing=True), _t.cuda.Event(enable_timing=True)
+        loaded = [_t.cuda.Event() for _ in range(n)]
+        computed = [_t.cuda.Event() for _ in range(n)]
+        drained = [_t.cuda.Event() for _ in range(n)]
+        s_in.wait_stream(stream)
+        s_out.wait_stream(stream)
+        start.record(s_in)
+        for i in range(n):
+            a, o = sets[i % 2]
+            with _t.cuda.stream(s_in):
+                if i >= 2:
+                    s_in.wait_event(computed[i - 2])  # set i%2's inputs are free once step i-2 ran
+                for name, t in host_in.items():
+                    a[name].copy_(t, non_blocking=True)
+                loaded[i].record(s_in)
+            stream.wait_event(loaded[i])
+            if i >= 2:
+                stream.wait_event(drained[i - 2])     # set i%2's outputs were copied out
+            step(a=a, o=o)
+            computed[i].record(stream)
+            with _t.cuda.stream(s_out):
+                s_out.wait_event(computed[i])
+                for name, t in host_out.items():
+                    t.copy_(o[name], non_blocking=True)
+                drained[i].record(s_out)
+        s_out.wait_stream(s_in)
+        s_out.wait_stream(stream)
+        end.record(s_out)
+        return start, end
 
     e2e_steps = max(1, args.e2e_steps)
-    e2e_step()
+    e2e_run(2)
     _t.cuda.synchronize()
     if dist is not None:
         dist.barrier()
-    e_start.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    e_end.record(stream)
+    e_start, e_end = e2e_run(e2e_steps)
     _t.cuda.synchronize()
     e2e_ms = e_start.elapsed_time(e_end)
+    np.testing.assert_array_equal(host_out["fc2"].numpy(), sets[(e2e_steps - 1) % 2][1]["fc2"].cpu().numpy())
 
     decoder = None
     if args.decoder_steps > 0:
         del flush, scrub
-        decoder = run_decoder(fp8, native, device, args.decoder_steps, 3, seed=77 + rank)
+        decoder = run_decoder(fp8, native, device, args.decoder_steps, 3, seed=77 + rank,
+                              layers_count=args.decoder_layers)
     # Max over ranks.
     total_ms, total_gemm_ms, e2e_ms = replicas.max_over_ranks([total_ms, total_gemm_ms, e2e_ms], dist, device)
 
@@ -358,6 +392,7 @@ def run_ours(args, rank, local_rank, world):
                 "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "api": "fp8.quantize / fp8.linear (C ABI lffw_fp8_quantize / lffw_fp8_linear)",
+                "pipelining": "copies in, kernels and copies out on three streams, two device buffer sets",
             },
             "encoder_linears_audio_s_per_s": round(
                 replicas.whole_job_rate(8 * 30.0, world, 32 * ms_per_step / 1e3), 1),
@@ -391,13 +426,13 @@ DEC_LINEARS = (("qkv", 1280, 3840), ("self_out", 1280, 1280), ("cross_q", 1280, 
                ("cross_out", 1280, 1280), ("fc1", 1280, 5120), ("fc2", 5120, 1280))
 
 
-def run_decoder(fp8, native, device, steps: int, warmup: int, seed: int):
+def run_decoder(fp8, native, device, steps: int, warmup: int, seed: int, layers_count: int = DEC_LAYERS):
     import torch
 
     g = torch.Generator(device=device).manual_seed(seed)
     layers = []
     weight_bytes = 0
-    for _ in range(DEC_LAYERS):
+    for _ in range(layers_count):
         layer = {}
         for name, k, n in DEC_LINEARS:
             w = (torch.randn(n, k, generator=g, device=device) * 0.02).half()
@@ -436,7 +471,7 @@ def run_decoder(fp8, native, device, steps: int, warmup: int, seed: int):
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         step()
-    launches_per_step = DEC_LAYERS * 6 + 1
+    launches_per_step = layers_count * 6 + 1
     for _ in range(max(1, warmup)):
         graph.replay()
     torch.cuda.synchronize()
@@ -454,13 +489,27 @@ def run_decoder(fp8, native, device, steps: int, warmup: int, seed: int):
     hbm = read_hbm_peak()
     gbs = weight_bytes / (ms / 1e3) / 1e9
     del graph
-    return {"workload": "C3: decoder step, M=20 (4 streams x 5 beams), 32 layers x 6 E4M3 linears + fp16 logits "
-                        "1280->51866, one CUDA graph with programmatic dependent launches",
+    return {"workload": f"C3: decoder step, M=20 (4 streams x 5 beams), {layers_count} layers x 6 E4M3 linears + "
+                        "fp16 logits 1280->51866, one CUDA graph with programmatic dependent launches",
             "ms_per_step": round(ms, 4), "weight_bytes_per_step": weight_bytes,
             "value": round(gbs, 1), "unit": "GB/s (weights streamed)",
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm[0], "peak_source": hbm[1],
                          "unit": "GB/s", "frac": round(gbs / hbm[0], 4)},
             "launches_per_step": launches_per_step}
+
+
+def run_decoder_only(args, local_rank):
+    """The C3 decoder step alone (1 GPU): eager warm-up steps, then timed graph replays."""
+    import torch
+
+    fp8 = importlib.import_module(PACKAGE + ".fp8")
+    native = importlib.import_module(PACKAGE + "._native")
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    result = run_decoder(fp8, native, device, max(1, args.decoder_steps), max(1, args.warmup), seed=77,
+                         layers_count=args.decoder_layers)
+    result.update(metric="decoder-step weight streaming (C3)", n_gpus=1, higher_is_better=True, impl="ours")
+    return result
 
 
 def read_hbm_peak():
@@ -590,6 +639,8 @@ def main(argv=None):
     rank, local_rank, world = dist_env()
     if args.impl == "reference":
         result = run_reference(args, rank, world)
+    elif args.only == "decoder":
+        result = run_decoder_only(args, local_rank)
     else:
         result = run_ours(args, rank, local_rank, world)
     if result is not None and rank == 0:

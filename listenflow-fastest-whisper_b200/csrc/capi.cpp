@@ -112,7 +112,7 @@ lffw_status validate_linear(const lffw_fp8_linear_args *a)
     const int32_t layout = weight_layout(a);
     if (layout != LFFW_WEIGHTS_ROW_MAJOR && layout != LFFW_WEIGHTS_SKINNY_TILES)
         return LFFW_INVALID_ARGUMENT;
-    if (layout == LFFW_WEIGHTS_SKINNY_TILES && a->m > lffw::kGemvMaxRows)
+    if (layout == LFFW_WEIGHTS_SKINNY_TILES && a->m > lffw::kSmallMaxRows)
         return LFFW_INVALID_ARGUMENT;
     return LFFW_SUCCESS;
 }
@@ -134,7 +134,7 @@ lffw_status run_linear(const lffw_fp8_linear_args *a, cudaStream_t stream)
     L.next_scale = a->next_scale;
     L.next_codes = a->next_codes;
     L.w_packed = weight_layout(a) == LFFW_WEIGHTS_SKINNY_TILES;
-    const bool small = a->m <= lffw::kGemvMaxRows;
+    const bool small = a->m <= lffw::kSmallMaxRows;
     return from_cuda(small ? lffw::launch_fp8_skinny(L, stream) : lffw::launch_fp8_gemm(L, stream));
 }
 
@@ -241,7 +241,7 @@ lffw_status lffw_fp16_bias(const uint16_t *x, uint16_t bias_bits, uint16_t *y, i
 lffw_status lffw_fp16_linear(const uint16_t *x, const uint16_t *weight, const uint16_t *bias, uint16_t *y,
                              int64_t m, int64_t n, int64_t k, int32_t w_layout, void *stream) noexcept
 {
-    if (x == nullptr || weight == nullptr || y == nullptr || m < 1 || m > lffw::kGemvMaxRows || n < 1 ||
+    if (x == nullptr || weight == nullptr || y == nullptr || m < 1 || m > lffw::kSmallMaxRows || n < 1 ||
         n > kMaxDim || k < 8 || k % 8 != 0 || k > kMaxDim || !aligned16(x) || !aligned16(weight) ||
         (w_layout != LFFW_WEIGHTS_ROW_MAJOR && w_layout != LFFW_WEIGHTS_SKINNY_TILES))
         return LFFW_INVALID_ARGUMENT;

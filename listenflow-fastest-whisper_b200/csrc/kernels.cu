@@ -4,8 +4,9 @@
 //                        accumulators in TMEM (double buffered), fused epilogue
 //                        (per-channel scale, fp16 bias, fp16-edge GELU, fp16 out
 //                        and/or E4M3 codes for the next linear), TMA stores.
-//   fp8_gemv_kernel      small-M (decoder step) linear on CUDA cores: 128-bit
-//                        streaming of the E4M3 weight rows, warp-shuffle reduce.
+//   skinny_kernel        small-M (m <= 32, decoder step) linear on tensor cores:
+//                        swap-AB tcgen05 MMAs over streamed weight tiles, cluster
+//                        split-K reduced through distributed shared memory.
 //   quantize kernels     fp16 -> E4M3 with a scalar or per-row scale.
 //   scale kernels        per-row weight scales, dynamic activation amax/448.
 //   fp16 projections     sm_100a rebuild of the reference plugins' fc1/qkv/bias.
@@ -91,6 +92,16 @@ __device__ __forceinline__ uint16_t gelu_fp16_edges(uint16_t x)
     uint16_t left = hmul_rn(x, kHalf);
     uint16_t right = hadd_rn(kOne, erf16);
     return hmul_rn(left, right);
+}
+
+// 16 bytes read once: non-coherent, no L1 allocation.
+__device__ __forceinline__ uint4 ld_stream16(const void *p)
+{
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
 }
 
 // Two fp32 values -> two E4M3 codes (round to nearest even, saturate finite);
@@ -652,119 +663,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 } // namespace gemm
 
 // ---------------------------------------------------------------------------
-// Small-M FP8 linear on CUDA cores (decoder step).
-
-namespace gemv {
-
-constexpr int kThreads = 256;
-constexpr int kRowsPerBlock = kThreads / 32; // one output row (n) per warp
-
-struct Params {
-    int m, n, k;
-    const uint8_t *x_codes;
-    const uint8_t *w_codes;
-    float act_scale;
-    const float *act_scale_ptr;
-    const float *w_scales;
-    const uint16_t *bias;
-    int gelu;
-    uint16_t *y;
-    float next_scale;
-    uint8_t *next_codes;
-};
-
-__device__ __forceinline__ uint4 ld_stream(const void *p)
-{
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
-
-__device__ __forceinline__ void e4m3x16_to_f32(const uint4 &raw, float (&f)[16])
-{
-    const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const __nv_fp8x2_storage_t pair = static_cast<__nv_fp8x2_storage_t>(words[w] >> (16 * h));
-            const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3);
-            f[w * 4 + h * 2 + 0] = h2f(hr.x);
-            f[w * 4 + h * 2 + 1] = h2f(hr.y);
-        }
-    }
-}
-
-template <int MT>
-__global__ void __launch_bounds__(kThreads) fp8_gemv_kernel(const Params p)
-{
-    extern __shared__ uint4 xs[]; // [m][k/16] E4M3 codes
-    const int chunks = p.k / 16;
-    const int total = p.m * chunks;
-    const uint4 *xg = reinterpret_cast<const uint4 *>(p.x_codes);
-    for (int i = threadIdx.x; i < total; i += kThreads)
-        xs[i] = xg[i];
-    __syncthreads();
-
-    const int warp = threadIdx.x / 32;
-    const int lane = threadIdx.x % 32;
-    const int n = blockIdx.x * kRowsPerBlock + warp;
-    if (n >= p.n)
-        return;
-    float acc[MT];
-#pragma unroll
-    for (int m = 0; m < MT; ++m)
-        acc[m] = 0.0f;
-    const uint8_t *wrow = p.w_codes + static_cast<size_t>(n) * p.k;
-    for (int c = lane; c < chunks; c += 32) {
-        float wf[16];
-        e4m3x16_to_f32(ld_stream(wrow + static_cast<size_t>(c) * 16), wf);
-#pragma unroll
-        for (int m = 0; m < MT; ++m) {
-            if (m < p.m) {
-                float xf[16];
-                e4m3x16_to_f32(xs[m * chunks + c], xf);
-                float s = acc[m];
-#pragma unroll
-                for (int i = 0; i < 16; ++i)
-                    s = fmaf(xf[i], wf[i], s);
-                acc[m] = s;
-            }
-        }
-    }
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-#pragma unroll
-        for (int off = 16; off > 0; off /= 2)
-            acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], off);
-    }
-    const float act_scale = p.act_scale_ptr ? *p.act_scale_ptr : p.act_scale;
-    const float cs = act_scale * p.w_scales[n];
-    const uint16_t b = p.bias ? p.bias[n] : 0;
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-        if (m < p.m && lane == (m & 31)) {
-            uint16_t z = f2h_rn(acc[m] * cs);
-            if (p.bias)
-                z = hadd_rn(z, b);
-            if (p.gelu)
-                z = gelu_fp16_edges(z);
-            const size_t o = static_cast<size_t>(m) * p.n + n;
-            if (p.y)
-                p.y[o] = z;
-            if (p.next_codes) {
-                const float q = q_quotient(z, p.next_scale);
-                p.next_codes[o] = static_cast<uint8_t>(e4m3x2(q, 0.0f) & 0xFF);
-            }
-        }
-    }
-}
-
-} // namespace gemv
-
-// ---------------------------------------------------------------------------
 // Skinny linear (decoder step, m <= 32) on tensor cores.
 //
 // Swap-AB: 128 weight rows are the MMA's M side and the (zero-padded) 32
@@ -1079,14 +977,6 @@ namespace quant {
 
 constexpr int kThreads = 256;
 
-__device__ __forceinline__ uint4 ld_stream16(const void *p)
-{
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
 
 
 // A warp converts 1024 halves per iteration: four coalesced 512-byte loads
@@ -1235,7 +1125,7 @@ __global__ void __launch_bounds__(kThreads)
         const uint16_t *wrow = w + static_cast<size_t>(r) * width;
         float acc = 0.0f;
         for (int c = lane; c < chunks; c += 32) {
-            const uint4 wv = gemv::ld_stream(wrow + c * 8);
+            const uint4 wv = ld_stream16(wrow + c * 8);
             const uint4 xv = __ldg(reinterpret_cast<const uint4 *>(x) + c);
             uint16_t wh[8], xh[8];
             memcpy(wh, &wv, 16);
@@ -1603,53 +1493,15 @@ cudaError_t launch_pack_skinny(const void *w, int64_t n, int64_t row_bytes, void
     return cudaGetLastError();
 }
 
-cudaError_t launch_fp8_gemv(const LinearLaunch &L, cudaStream_t stream)
-{
-    gemv::Params p{};
-    p.m = static_cast<int>(L.m);
-    p.n = static_cast<int>(L.n);
-    p.k = static_cast<int>(L.k);
-    p.x_codes = L.x_codes;
-    p.w_codes = L.w_codes;
-    p.act_scale = L.act_scale;
-    p.act_scale_ptr = L.act_scale_ptr;
-    p.w_scales = L.w_scales;
-    p.bias = L.bias;
-    p.gelu = L.gelu ? 1 : 0;
-    p.y = L.y;
-    p.next_scale = L.next_scale;
-    p.next_codes = L.next_codes;
-    const size_t smem = static_cast<size_t>(L.m) * static_cast<size_t>(L.k);
-    const dim3 grid(static_cast<unsigned>((L.n + gemv::kRowsPerBlock - 1) / gemv::kRowsPerBlock));
-    cudaError_t err;
-    auto go = [&](auto kernel) {
-        err = ensure_smem(kernel, static_cast<int>(kGemvMaxSmem));
-        if (err != cudaSuccess)
-            return;
-        kernel<<<grid, gemv::kThreads, smem, stream>>>(p);
-        count_launch();
-        err = cudaGetLastError();
-    };
-    if (L.m <= 8)
-        go(gemv::fp8_gemv_kernel<8>);
-    else if (L.m <= 16)
-        go(gemv::fp8_gemv_kernel<16>);
-    else
-        go(gemv::fp8_gemv_kernel<32>);
-    return err;
-}
-
 cudaError_t launch_quantize(const uint16_t *x, int64_t count, float scale, const float *scale_ptr,
                             uint8_t *codes, cudaStream_t stream)
 {
     const int64_t chunks = count / quant::kQuantChunk;
     const int64_t warps_per_block = quant::kThreads / 32;
     int64_t blocks = (chunks + warps_per_block - 1) / warps_per_block;
-    static const int per_sm = [] {
-        const char *v = std::getenv("LFFW_QUANT_BLOCKS_PER_SM");
-        return v && std::atoi(v) > 0 ? std::atoi(v) : 4;
-    }();
-    blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, static_cast<int64_t>(sm_count()) * per_sm));
+    // Four blocks (32 warps) per SM, each warp looping over chunks with the next
+    // chunk's loads in flight.
+    blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, static_cast<int64_t>(sm_count()) * 4));
     const float recip = static_cast<float>(1.0 / static_cast<double>(scale));
     cudaLaunchConfig_t config{};
     config.gridDim = dim3(static_cast<unsigned>(blocks));
@@ -1842,7 +1694,7 @@ extern "C" LFFW_FP8_API lffw_status lffw_fp8_linear_half_static(const uint16_t *
     L.bias = bias;
     L.gelu = epilogue == LFFW_EPILOGUE_GELU;
     L.y = y;
-    const bool small = m <= lffw::kGemvMaxRows;
+    const bool small = m <= lffw::kSmallMaxRows;
     const cudaError_t err = small ? lffw::launch_fp8_skinny(L, st) : lffw::launch_fp8_gemm(L, st);
     return err == cudaSuccess ? LFFW_SUCCESS : LFFW_CUDA_ERROR;
 }

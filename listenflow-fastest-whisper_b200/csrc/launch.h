@@ -23,12 +23,9 @@ struct LinearLaunch {
 };
 
 // Largest M served by the small-M (skinny) kernels.
-constexpr int64_t kGemvMaxRows = 32;
-// Shared memory the small-M kernel may use for the activation codes (m * k bytes).
-constexpr int64_t kGemvMaxSmem = 200 * 1024;
+constexpr int64_t kSmallMaxRows = 32;
 
 cudaError_t launch_fp8_gemm(const LinearLaunch &p, cudaStream_t stream);
-cudaError_t launch_fp8_gemv(const LinearLaunch &p, cudaStream_t stream);
 // m <= 32 on tensor cores (swap-AB, cluster split-K); fp16 weights for the logits.
 cudaError_t launch_fp8_skinny(const LinearLaunch &p, cudaStream_t stream);
 cudaError_t launch_fp16_skinny(const uint16_t *x, const uint16_t *w, const uint16_t *bias, uint16_t *y, int64_t m,
