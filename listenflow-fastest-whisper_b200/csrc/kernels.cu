@@ -229,7 +229,13 @@ struct Cfg {
     static constexpr int kCBuf = 32 * kSub;     // 32 rows x 32 B (E4M3), 32B swizzle
     static constexpr int kWarpStaging = (kY ? kYBuf : 0) + (kCodes ? kCBuf : 0);
     static constexpr int kStagingBytes = kEpiWarps * kWarpStaging;
-    static constexpr int kTableBytes = kGelu ? (LFFW_ERF_TABLE_SIZE * 2 + 1023) / 1024 * 1024 : 0;
+    // GELU with E4M3 codes as the only output: the codes are a function of the
+    // 16-bit pre-GELU value alone, so the epilogue reads them from a 64 KB
+    // table (one code per fp16 bit pattern) built per launch.  Otherwise the
+    // GELU reads fp16(erf) from a table of the non-negative fp16 inputs.
+    static constexpr bool kCodeTable = kGelu && kCodes && !kY;
+    static constexpr int kTableBytes =
+        kCodeTable ? 65536 : (kGelu ? (LFFW_ERF_TABLE_SIZE * 2 + 1023) / 1024 * 1024 : 0);
     static constexpr int kBarBytes = 256;
     static constexpr int kBudget = 232448 - 1024; // opt-in maximum minus base alignment slack
     static constexpr int kFit = (kBudget - kStagingBytes - kTableBytes - kBarBytes) / kStageBytes;
@@ -362,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (C::kCodes)
             prefetch_tensor_map(&tm_c);
     }
-    if (C::kGelu) {
+    if (C::kGelu && !C::kCodeTable) {
         const uint32_t *src = reinterpret_cast<const uint32_t *>(g_erf_table);
         uint32_t *dst = reinterpret_cast<uint32_t *>(erf_table);
         for (int i = threadIdx.x; i < (LFFW_ERF_TABLE_SIZE + 1) / 2; i += kThreads)
@@ -519,12 +525,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ew = warp - 2;
         const int quarter = warp & 3; // the TMEM lane quarter this warp may access
         const int slice = ew >> 2;    // which quarter of the tile's columns
+        const uint64_t neg_scale2 = f2_bits(-p.next_scale, -p.next_scale);
+        const uint64_t recip2 = f2_bits(p.next_recip, p.next_recip);
+        uint8_t *code_table = smem + C::kOffTable;
+        if (C::kCodeTable) {
+            // code_table[z] = Q(GELU(z) / next_scale) for every fp16 bit pattern z,
+            // by the same functions the direct path uses; four patterns per step.
+            // It depends on kernel parameters only, so it is built while the
+            // previous kernel may still run, and while the first tile's MMAs do.
+            for (int i = static_cast<int>(threadIdx.x) - 64; i < 16384; i += kEpiThreads) {
+                const uint32_t z01 = static_cast<uint32_t>(4 * i) | (static_cast<uint32_t>(4 * i + 1) << 16);
+                const uint32_t z23 = static_cast<uint32_t>(4 * i + 2) | (static_cast<uint32_t>(4 * i + 3) << 16);
+                reinterpret_cast<uint32_t *>(code_table)[i] =
+                    e4m3x4(gelu_fp16x2(z01, g_erf_table), gelu_fp16x2(z23, g_erf_table), p.next_lean != 0,
+                           neg_scale2, recip2);
+            }
+            named_barrier_sync(1, kEpiThreads);
+        }
         // A dynamic scale, and the buffers this grid writes, belong to the
         // previous kernel until it completes.
         griddepcontrol_wait();
         const float act_scale = p.act_scale_ptr ? *p.act_scale_ptr : p.act_scale;
-        const uint64_t neg_scale2 = f2_bits(-p.next_scale, -p.next_scale);
-        const uint64_t recip2 = f2_bits(p.next_recip, p.next_recip);
         // Accumulator release goes to the leader's barriers (cluster addresses in a pair).
         const uint32_t acc_empty_base = kPair ? map_to_rank(bar_acc_empty, 0) : bar_acc_empty;
         uint8_t *staging = smem + C::kOffStaging + ew * C::kWarpStaging;
@@ -597,7 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         uint32_t z = cvt_f16x2(y.x, y.y);
                         if (p.bias)
                             z = hadd2_rn(z, bias2[i]);
-                        if (C::kGelu)
+                        if (C::kGelu && !C::kCodeTable)
                             z = gelu_fp16x2(z, erf_table);
                         h[i] = z;
                     }
@@ -616,8 +637,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                         uint8_t *cbuf = staging + (C::kY ? C::kYBuf : 0);
                         uint32_t q[4];
 #pragma unroll
-                        for (int i = 0; i < 4; ++i)
-                            q[i] = e4m3x4(h[2 * i], h[2 * i + 1], p.next_lean != 0, neg_scale2, recip2);
+                        for (int i = 0; i < 4; ++i) {
+                            if (C::kCodeTable) {
+                                // h holds pre-GELU fp16 pairs: one table byte per value.
+                                const uint32_t c0 = code_table[h[2 * i] & 0xFFFFu];
+                                const uint32_t c1 = code_table[h[2 * i] >> 16];
+                                const uint32_t c2 = code_table[h[2 * i + 1] & 0xFFFFu];
+                                const uint32_t c3 = code_table[h[2 * i + 1] >> 16];
+                                q[i] = c0 | (c1 << 8) | (c2 << 16) | (c3 << 24);
+                            } else {
+                                q[i] = e4m3x4(h[2 * i], h[2 * i + 1], p.next_lean != 0, neg_scale2, recip2);
+                            }
+                        }
                         const uint32_t pos = static_cast<uint32_t>(hf) ^ ((static_cast<uint32_t>(lane) >> 2) & 1u);
                         *reinterpret_cast<uint4 *>(cbuf + lane * 32 + pos * 16) = make_uint4(q[0], q[1], q[2], q[3]);
                     }

@@ -118,6 +118,49 @@ def test_fused_codes_at_quotient_limits(cuda, fp8, oracle, native, next_scale):
     assert native.device_error() == 0
 
 
+@pytest.mark.parametrize("next_scale", [0.02, 128.0, 200.0, 2.0**-115])
+def test_gelu_codes_table_every_half(cuda, fp8, oracle, native, next_scale):
+    """GELU with E4M3 codes as the only output reads the codes from a per-launch
+    table indexed by the fp16 pre-activation.  With zero weights the
+    pre-activation is +0 + bias, so a bias holding all 65,536 fp16 bit patterns
+    checks every table entry against the oracle."""
+    import torch
+
+    m, n, k = 128, 65536, 16
+    xq = torch.zeros((m, k), dtype=torch.uint8, device=cuda)
+    wq = torch.zeros((n, k), dtype=torch.uint8, device=cuda)
+    ws = torch.ones(n, dtype=torch.float32, device=cuda)
+    b = torch.from_numpy(np.arange(65536, dtype=np.uint32).astype(np.uint16).view(np.float16).copy()).to(cuda)
+    pre, _ = fp8.linear(xq, wq, ws, 1.0, bias=b)
+    _, codes = fp8.linear(xq, wq, ws, 1.0, bias=b, gelu=True, want_y=False, next_scale=next_scale)
+    torch.cuda.synchronize()
+    assert native.device_error() == 0
+    pre_bits = pre.cpu().numpy().view(np.uint16)[0]
+    got = codes.cpu().numpy()
+    assert np.all(got == got[0])  # every row sees the same pre-activations
+    want = oracle.quantize(oracle.gelu_fp16(pre_bits), np.float32(next_scale))
+    nan = np.isnan(oracle.gelu_fp16(pre_bits).view(np.float16))
+    np.testing.assert_array_equal(got[0][~nan], want[~nan])
+    assert np.all(got[0][nan] & 0x7F == 0x7F)
+
+
+@pytest.mark.parametrize("m,n,k", [(300, 1280, 640), (777, 1280, 5120), (1500, 5120, 1280)])
+def test_gelu_codes_table_matches_direct_path(cuda, fp8, oracle, native, m, n, k):
+    """Codes-only GELU (table) equals the codes of the GELU + fp16 output path
+    (computed directly) bit for bit, on 1-CTA and CTA-pair tiles."""
+    import torch
+
+    d = _prepare(torch, fp8, oracle, cuda, m, n, k, seed=91)
+    for next_scale in (0.011, 300.0):
+        _, direct = fp8.linear(d["xq"], d["wq"], d["ws"], float(d["act_scale"]), bias=d["bd"], gelu=True,
+                               next_scale=next_scale)
+        _, table = fp8.linear(d["xq"], d["wq"], d["ws"], float(d["act_scale"]), bias=d["bd"], gelu=True,
+                              want_y=False, next_scale=next_scale)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(table.cpu().numpy(), direct.cpu().numpy())
+    assert native.device_error() == 0
+
+
 def test_linear_without_bias_and_codes_only(cuda, fp8, oracle):
     import torch
 
