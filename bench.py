@@ -342,6 +342,7 @@ def run_ours(args, rank, local_rank, world):
     e2e_ms = e_start.elapsed_time(e_end)
     np.testing.assert_array_equal(host_out["fc2"].numpy(), sets[(e2e_steps - 1) % 2][1]["fc2"].cpu().numpy())
 
+    ln = run_ln_producer(fp8, native, device, 20, seed=31 + rank)
     decoder = None
     if args.decoder_steps > 0:
         del flush, scrub
@@ -402,6 +403,7 @@ def run_ours(args, rank, local_rank, world):
             "gpu_launches": int(launches),
             "clocks": clocks.summary(),
         }
+        result["ln_producer"] = ln
         if args.decoder_steps > 0:
             result["decoder_step"] = decoder
         if world == 1 and args.cpu_seconds > 0:
@@ -510,6 +512,58 @@ def run_decoder_only(args, local_rank):
                          layers_count=args.decoder_layers)
     result.update(metric="decoder-step weight streaming (C3)", n_gpus=1, higher_is_better=True, impl="ours")
     return result
+
+
+def run_ln_producer(fp8, native, device, reps: int, seed: int):
+    """LayerNorm producer at C2 shapes (12000 x 1280, residual add): the fused
+    kernel (residual sum + E4M3 codes for the next linear) against LayerNorm
+    writing fp16 followed by a separate quantize."""
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(M, D, generator=g, device=device).half()
+    r = torch.randn(M, D, generator=g, device=device).half()
+    gamma = (1 + 0.1 * torch.randn(D, generator=g, device=device)).float()
+    beta = (0.1 * torch.randn(D, generator=g, device=device)).float()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    scrub = torch.ones(64 * 1024 * 1024, dtype=torch.float32, device=device)
+
+    def fused():
+        fp8.layer_norm(x, gamma, beta, residual=r, code_scale=0.01, want_y=False, want_sum=True)
+
+    def separate():
+        _, y, _ = fp8.layer_norm(x, gamma, beta, residual=r, want_sum=True)
+        fp8.quantize(y, 0.01)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        ts = []
+        for _ in range(reps):
+            flush.zero_()
+            scrub.sum()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+
+    t_fused, t_sep = timed(fused), timed(separate)
+    if native.device_error() != 0:
+        raise RuntimeError("device-side wait timed out in the LayerNorm section")
+    elems = M * D
+    fused_bytes = elems * (2 + 2 + 2 + 1)  # x, residual in; sum, codes out
+    gbs = fused_bytes / (t_fused / 1e3) / 1e9
+    hbm = read_hbm_peak()
+    return {"workload": "LayerNorm producer, 12000 x 1280 fp16 + residual -> fp16 sum + E4M3 codes",
+            "fused_ms": round(t_fused, 4), "separate_ms": round(t_sep, 4),
+            "separate": "LayerNorm writing fp16 y (and the sum), then lffw_fp8_quantize of y",
+            "value": round(gbs, 1), "unit": "GB/s (algorithmic: 7 bytes per element)",
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm[0], "peak_source": hbm[1],
+                         "unit": "GB/s", "frac": round(gbs / hbm[0], 4)},
+            "l2": "flushed before every launch (256 MiB written, then 256 MiB read)"}
 
 
 def read_hbm_peak():

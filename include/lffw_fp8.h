@@ -24,7 +24,7 @@
 #include <stdint.h>
 
 #define LFFW_FP8_ABI_MAJOR 1
-#define LFFW_FP8_ABI_MINOR 1
+#define LFFW_FP8_ABI_MINOR 2
 #define LFFW_FP8_API __attribute__((visibility("default")))
 #if defined(__cplusplus)
 #define LFFW_FP8_NOEXCEPT noexcept
@@ -105,6 +105,35 @@ LFFW_FP8_API lffw_status lffw_fp8_linear(const lffw_fp8_linear_args *args,
 LFFW_FP8_API lffw_status lffw_fp8_quantize(const uint16_t *x, int64_t count, float scale,
                                            const float *scale_ptr, uint8_t *codes,
                                            void *stream) LFFW_FP8_NOEXCEPT;
+
+/* LayerNorm producer for the linear that follows it (network_graph.cpp:160-166
+ * `norm`, with the fp16 residual add of :285-287 before it), per row of `cols`:
+ *   s[i]    = half(x[i] + residual[i])   (s = x when residual is NULL)
+ *   sum_out = s                          (if sum_out: the new residual stream)
+ *   y[i]    = half((s[i] - mean) * rsqrt(var + epsilon) * gamma[i] + beta[i])
+ *             (fp32 statistics over the row; population variance)
+ *   codes   = E4M3_rne_sat(fp32(y[i] / code_scale))   (if codes)
+ * y and/or codes and/or sum_out are written (at least one).  The activation
+ * round trip a separate quantize would make (write y, read y) is skipped when
+ * y is NULL.  Requirements: rows >= 1; 8 <= cols <= 4096, cols % 8 == 0;
+ * 16-byte aligned pointers; gamma/beta fp32 [cols]; epsilon finite and >= 0;
+ * code_scale (or *code_scale_ptr, device) in [2^-125, 2^125] when codes is set. */
+typedef struct lffw_layer_norm_args {
+    size_t struct_size; /* sizeof(lffw_layer_norm_args) */
+    int64_t rows, cols;
+    const uint16_t *x;
+    const uint16_t *residual;
+    uint16_t *sum_out;
+    const float *gamma;
+    const float *beta;
+    float epsilon;
+    uint16_t *y;
+    float code_scale;
+    const float *code_scale_ptr;
+    uint8_t *codes;
+} lffw_layer_norm_args;
+
+LFFW_FP8_API lffw_status lffw_layer_norm(const lffw_layer_norm_args *args, void *stream) LFFW_FP8_NOEXCEPT;
 
 /* Q of an fp16 [rows, cols] weight with one scale per row (the per-output-channel
  * weight Q of network_graph.cpp:140-152, axis 2 of the transposed constant). */

@@ -63,6 +63,24 @@ class LinearArgs(ctypes.Structure):
     ]
 
 
+class LayerNormArgs(ctypes.Structure):
+    _fields_ = [
+        ("struct_size", ctypes.c_size_t),
+        ("rows", ctypes.c_int64),
+        ("cols", ctypes.c_int64),
+        ("x", ctypes.c_void_p),
+        ("residual", ctypes.c_void_p),
+        ("sum_out", ctypes.c_void_p),
+        ("gamma", ctypes.c_void_p),
+        ("beta", ctypes.c_void_p),
+        ("epsilon", ctypes.c_float),
+        ("y", ctypes.c_void_p),
+        ("code_scale", ctypes.c_float),
+        ("code_scale_ptr", ctypes.c_void_p),
+        ("codes", ctypes.c_void_p),
+    ]
+
+
 class PluginField(ctypes.Structure):
     _fields_ = [
         ("name", ctypes.c_char_p),
@@ -115,6 +133,7 @@ def library() -> ctypes.CDLL:
     sig = {
         "lffw_fp8_linear": ([ctypes.POINTER(LinearArgs), _vp], _i32),
         "lffw_fp8_quantize": ([_vp, _i64, ctypes.c_float, _vp, _vp, _vp], _i32),
+        "lffw_layer_norm": ([ctypes.POINTER(LayerNormArgs), _vp], _i32),
         "lffw_fp8_quantize_rows": ([_vp, _i64, _i64, _vp, _vp, _vp], _i32),
         "lffw_fp8_weight_scales": ([_vp, _i64, _i64, _vp, _vp], _i32),
         "lffw_fp8_dynamic_scale": ([_vp, _i64, _vp, _vp, _vp], _i32),

@@ -166,6 +166,42 @@ lffw_status lffw_fp8_quantize(const uint16_t *x, int64_t count, float scale, con
                                            static_cast<cudaStream_t>(stream)));
 }
 
+lffw_status lffw_layer_norm(const lffw_layer_norm_args *a, void *stream) noexcept
+{
+    if (a == nullptr || a->struct_size < sizeof(lffw_layer_norm_args))
+        return a == nullptr ? LFFW_INVALID_ARGUMENT : LFFW_ABI_MISMATCH;
+    if (a->rows < 1 || a->rows > kMaxDim || a->cols < 8 || a->cols % 8 != 0 || a->cols > lffw::kLayerNormMaxCols)
+        return LFFW_INVALID_ARGUMENT;
+    if (a->x == nullptr || a->gamma == nullptr || a->beta == nullptr)
+        return LFFW_INVALID_ARGUMENT;
+    if (a->y == nullptr && a->codes == nullptr && a->sum_out == nullptr)
+        return LFFW_INVALID_ARGUMENT;
+    if (!aligned16(a->x) || !aligned16(a->residual) || !aligned16(a->sum_out) || !aligned16(a->gamma) ||
+        !aligned16(a->beta) || !aligned16(a->y) || !aligned16(a->codes))
+        return LFFW_INVALID_ARGUMENT;
+    if (!(a->epsilon >= 0.0f) || !std::isfinite(a->epsilon))
+        return LFFW_INVALID_ARGUMENT;
+    if (a->codes != nullptr && a->code_scale_ptr == nullptr && !valid_scale(a->code_scale))
+        return LFFW_INVALID_ARGUMENT;
+    lffw_status s = current_device_gate();
+    if (s != LFFW_SUCCESS)
+        return s;
+    lffw::LayerNormLaunch L{};
+    L.rows = a->rows;
+    L.cols = a->cols;
+    L.x = a->x;
+    L.residual = a->residual;
+    L.sum_out = a->sum_out;
+    L.gamma = a->gamma;
+    L.beta = a->beta;
+    L.eps = a->epsilon;
+    L.y = a->y;
+    L.code_scale = a->code_scale;
+    L.code_scale_ptr = a->code_scale_ptr;
+    L.codes = a->codes;
+    return from_cuda(lffw::launch_layer_norm(L, static_cast<cudaStream_t>(stream)));
+}
+
 lffw_status lffw_fp8_quantize_rows(const uint16_t *w, int64_t rows, int64_t cols, const float *scales,
                                    uint8_t *codes, void *stream) noexcept
 {

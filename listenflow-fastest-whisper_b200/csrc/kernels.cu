@@ -257,6 +257,7 @@ struct Cfg {
 struct Params {
     int m, n, k;
     int m_tiles, num_tiles, num_kb;
+    int full_tiles; // tiles [0, full_tiles) are BN wide; the rest are BN/2-wide halves
     float act_scale;
     const float *act_scale_ptr;
     const float *w_scales;
@@ -265,6 +266,24 @@ struct Params {
     float next_recip; // RN(1 / next_scale)
     int next_lean;    // lean_scale(next_scale)
 };
+
+// Tile t of the launch: M-tile index, first output column and width.  Full
+// tiles run M-fastest; the last units of that order (the launch's final,
+// partial wave) are split into two BN/2-wide halves each, so that wave takes
+// half a tile's time.
+struct TileRef {
+    int mt, n0, width;
+};
+
+template <int BN>
+__device__ __forceinline__ TileRef tile_at(const Params &p, int t)
+{
+    if (t < p.full_tiles)
+        return {t % p.m_tiles, (t / p.m_tiles) * BN, BN};
+    const int h = t - p.full_tiles;
+    const int u = p.full_tiles + (h >> 1);
+    return {u % p.m_tiles, (u / p.m_tiles) * BN + (h & 1) * (BN / 2), BN / 2};
+}
 
 // fp16(erf(x)) of two packed fp16 values, rounded to nearest even: one table
 // read per value.  The table covers every non-negative fp16 input up to
@@ -401,7 +420,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             // B tiles are requested before waiting for it (stages start empty).
             const int pre = tile_first < p.num_tiles ? (p.num_kb < C::kStages ? p.num_kb : C::kStages) : 0;
             for (int kb = 0; kb < pre; ++kb) {
-                const int n0 = (tile_first / p.m_tiles) * BN + static_cast<int>(rank) * C::kBRows;
+                const TileRef first = tile_at<BN>(p, tile_first);
+                const int n0 = first.n0 + static_cast<int>(rank) * (kPair ? first.width / 2 : 0);
                 const uint32_t full = bar_full + 8 * kb;
                 if (kPair) {
                     if (leader)
@@ -415,8 +435,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             griddepcontrol_wait();
             int issued = 0;
             for (int t = tile_first; ok && t < p.num_tiles; t += tile_step) {
-                const int m0 = (t % p.m_tiles) * C::kTileM + static_cast<int>(rank) * kBM;
-                const int n0 = (t / p.m_tiles) * BN + static_cast<int>(rank) * C::kBRows;
+                // In a pair each CTA loads half of the tile's B rows.
+                const TileRef tile = tile_at<BN>(p, t);
+                const int m0 = tile.mt * C::kTileM + static_cast<int>(rank) * kBM;
+                const int n0 = tile.n0 + static_cast<int>(rank) * (kPair ? tile.width / 2 : 0);
                 for (int kb = 0; kb < p.num_kb; ++kb, ++issued) {
                     const uint32_t full = bar_full + 8 * s;
                     if (issued < pre) {
@@ -464,7 +486,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer (one thread of the leader) ----------------
         if (lane == 0 && leader) {
-            constexpr uint32_t idesc = idesc_e4m3_f32<C::kTileM, BN>();
+            constexpr uint32_t idesc_full = idesc_e4m3_f32<C::kTileM, BN>();
+            constexpr uint32_t idesc_half = idesc_e4m3_f32<C::kTileM, BN / 2>();
             int s = 0;
             uint32_t ph = 0;
             int local = 0;
@@ -478,6 +501,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + a * BN;
+                const uint32_t idesc = t < p.full_tiles ? idesc_full : idesc_half;
                 for (int kb = 0; kb < p.num_kb; ++kb) {
                     if (!mbar_wait(bar_full + 8 * s, ph, kSiteMmaFull)) {
                         ok = false;
@@ -552,16 +576,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t staging_s = smem_u32(staging);
         int local = 0;
         for (int t = tile_first; t < p.num_tiles; t += tile_step, ++local) {
-            const int m0 = (t % p.m_tiles) * C::kTileM + static_cast<int>(rank) * kBM;
-            const int n0 = (t / p.m_tiles) * BN;
+            const TileRef tile = tile_at<BN>(p, t);
+            const int m0 = tile.mt * C::kTileM + static_cast<int>(rank) * kBM;
+            const int n0 = tile.n0;
+            const int n_end = n0 + tile.width < p.n ? n0 + tile.width : p.n;
             const uint32_t a = local & 1;
             const uint32_t acc_ph = (local >> 1) & 1;
+            const int col_begin = n0 + slice * (BN / 4);
+            // This warp's 64 columns: lane i holds columns 2i and 2i + 1 (combined
+            // scale act * w and the fp16 bias pair), read before the accumulator wait.
+            float2 my_cs = make_float2(0.0f, 0.0f);
+            uint32_t my_b = 0u;
+            {
+                const int c = col_begin + 2 * lane;
+                if (c < p.n) {
+                    const float2 w = __ldg(reinterpret_cast<const float2 *>(p.w_scales + c));
+                    my_cs = make_float2(act_scale * w.x, act_scale * w.y);
+                    if (p.bias)
+                        my_b = __ldg(reinterpret_cast<const uint32_t *>(p.bias + c));
+                }
+            }
             const bool ok = __all_sync(0xffffffffu, mbar_wait(bar_acc_full + 8 * a, acc_ph, kSiteEpilogueAccFull));
             if (!ok)
                 break;
             tc_fence_after();
-            const int col_begin = n0 + slice * (BN / 4);
-            int subs = (p.n - col_begin + kSub - 1) / kSub;
+            int subs = (n_end - col_begin + kSub - 1) / kSub;
             subs = subs < 0 ? 0 : (subs > BN / 4 / kSub ? BN / 4 / kSub : subs);
             const int row0 = m0 + quarter * 32;
             if (row0 >= p.m)
@@ -577,22 +616,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // Two 16-column halves keep the live registers low.
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {
-                    const int c0 = col0 + hf * 16;
-                    // Per-column scale and bias (broadcast loads), issued before the TMEM read.
-                    // N % 16 == 0, so a 16-column half is wholly inside or outside N.
-                    const bool inside = c0 < p.n;
-                    float4 w4[4];
-                    uint4 b4[2];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-                        w4[i] = inside ? __ldg(reinterpret_cast<const float4 *>(p.w_scales + c0) + i)
-                                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                    if (p.bias) {
-#pragma unroll
-                        for (int i = 0; i < 2; ++i)
-                            b4[i] = inside ? __ldg(reinterpret_cast<const uint4 *>(p.bias + c0) + i)
-                                           : make_uint4(0u, 0u, 0u, 0u);
-                    }
                     uint32_t v[16];
                     tmem_ld_32x32b_x16(t_base + sub * kSub + hf * 16, v);
                     tmem_wait_ld();
@@ -606,18 +629,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 mbar_arrive(acc_empty_base + 8 * a);
                         }
                     }
-                    // Scale, round to fp16, bias, GELU: two columns per packed op.
-                    const float2 act2 = make_float2(act_scale, act_scale);
-                    const uint32_t bias2[8] = {b4[0].x, b4[0].y, b4[0].z, b4[0].w, b4[1].x, b4[1].y, b4[1].z, b4[1].w};
+                    // Scale, round to fp16, bias, GELU: two columns per packed op; the
+                    // pair's scale and bias come from lane (column offset / 2).
                     uint32_t h[8];
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
-                        const float4 &w = w4[i / 2];
-                        const float2 cs = fmul2(act2, (i & 1) ? make_float2(w.z, w.w) : make_float2(w.x, w.y));
+                        const int src = sub * (kSub / 2) + hf * 8 + i;
+                        const float2 cs = make_float2(__shfl_sync(0xffffffffu, my_cs.x, src),
+                                                      __shfl_sync(0xffffffffu, my_cs.y, src));
                         const float2 y = fmul2(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), cs);
                         uint32_t z = cvt_f16x2(y.x, y.y);
                         if (p.bias)
-                            z = hadd2_rn(z, bias2[i]);
+                            z = hadd2_rn(z, __shfl_sync(0xffffffffu, my_b, src));
                         if (C::kGelu && !C::kCodeTable)
                             z = gelu_fp16x2(z, erf_table);
                         h[i] = z;
@@ -1136,6 +1159,127 @@ __global__ void finalize_scale_kernel(float *scale, float *amax_out)
 } // namespace quant
 
 // ---------------------------------------------------------------------------
+// LayerNorm producer (cpp/src/network_graph.cpp:160-166, with the residual add
+// of :285-287): the fp16 residual sum, the fp16 LayerNorm output and/or its E4M3
+// codes for the next linear, in one pass over the row.
+
+namespace norm {
+
+constexpr int kThreads = 256; // one row per warp
+constexpr int kRowsPerBlock = kThreads / 32;
+
+struct Params {
+    int rows, cols;
+    const uint16_t *x, *residual;
+    uint16_t *sum_out;
+    const float *gamma, *beta;
+    float eps;
+    uint16_t *y;
+    float code_scale, code_recip;
+    const float *code_scale_ptr;
+    uint8_t *codes;
+};
+
+__device__ __forceinline__ float warp_sum(float v)
+{
+#pragma unroll
+    for (int off = 16; off > 0; off /= 2)
+        v += __shfl_xor_sync(0xffffffffu, v, off);
+    return v;
+}
+
+// KV: 16-byte vectors (8 halves) per lane; the row (cols / 8 vectors) is spread
+// over the lanes, vector v on lane v % 32, held in registers between passes.
+template <int KV>
+__global__ void __launch_bounds__(kThreads) layer_norm_kernel(const Params p)
+{
+    if (threadIdx.x == 0)
+        griddepcontrol_launch_dependents();
+    griddepcontrol_wait();
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    const int row = blockIdx.x * kRowsPerBlock + warp;
+    if (row >= p.rows)
+        return;
+    const int vecs = p.cols / 8;
+    const size_t base = static_cast<size_t>(row) * p.cols;
+    uint4 v[KV];
+#pragma unroll
+    for (int j = 0; j < KV; ++j) {
+        const int c = lane + 32 * j;
+        v[j] = make_uint4(0u, 0u, 0u, 0u);
+        if (c < vecs) {
+            v[j] = ld_stream16(p.x + base + 8 * c);
+            if (p.residual) {
+                const uint4 r = ld_stream16(p.residual + base + 8 * c);
+                v[j] = make_uint4(gemm::hadd2_rn(v[j].x, r.x), gemm::hadd2_rn(v[j].y, r.y),
+                                  gemm::hadd2_rn(v[j].z, r.z), gemm::hadd2_rn(v[j].w, r.w));
+            }
+            if (p.sum_out)
+                *reinterpret_cast<uint4 *>(p.sum_out + base + 8 * c) = v[j];
+        }
+    }
+    // Two-pass statistics in fp32 over the row held in registers.
+    float acc = 0.0f;
+#pragma unroll
+    for (int j = 0; j < KV; ++j) {
+        const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            acc += h2f(static_cast<uint16_t>(w[i] & 0xFFFFu)) + h2f(static_cast<uint16_t>(w[i] >> 16));
+    }
+    const float inv_cols = 1.0f / static_cast<float>(p.cols);
+    const float mean = warp_sum(acc) * inv_cols;
+    acc = 0.0f;
+#pragma unroll
+    for (int j = 0; j < KV; ++j) {
+        if (lane + 32 * j < vecs) {
+            const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float d0 = h2f(static_cast<uint16_t>(w[i] & 0xFFFFu)) - mean;
+                const float d1 = h2f(static_cast<uint16_t>(w[i] >> 16)) - mean;
+                acc += d0 * d0 + d1 * d1;
+            }
+        }
+    }
+    const float rstd = __frsqrt_rn(warp_sum(acc) * inv_cols + p.eps);
+    const float scale = p.code_scale_ptr ? *p.code_scale_ptr : p.code_scale;
+    const float recip = p.code_scale_ptr ? __frcp_rn(scale) : p.code_recip;
+    const bool lean = lean_scale(scale);
+    const uint64_t neg_scale2 = f2_bits(-scale, -scale), recip2 = f2_bits(recip, recip);
+#pragma unroll
+    for (int j = 0; j < KV; ++j) {
+        const int c = lane + 32 * j;
+        if (c >= vecs)
+            continue;
+        const float4 g0 = __ldg(reinterpret_cast<const float4 *>(p.gamma + 8 * c));
+        const float4 g1 = __ldg(reinterpret_cast<const float4 *>(p.gamma + 8 * c) + 1);
+        const float4 b0 = __ldg(reinterpret_cast<const float4 *>(p.beta + 8 * c));
+        const float4 b1 = __ldg(reinterpret_cast<const float4 *>(p.beta + 8 * c) + 1);
+        const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+        uint32_t out[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float y0 = fmaf((h2f(static_cast<uint16_t>(w[i] & 0xFFFFu)) - mean) * rstd, g[2 * i], b[2 * i]);
+            const float y1 = fmaf((h2f(static_cast<uint16_t>(w[i] >> 16)) - mean) * rstd, g[2 * i + 1], b[2 * i + 1]);
+            out[i] = gemm::cvt_f16x2(y0, y1);
+        }
+        if (p.y)
+            *reinterpret_cast<uint4 *>(p.y + base + 8 * c) = make_uint4(out[0], out[1], out[2], out[3]);
+        if (p.codes) {
+            const uint32_t lo = e4m3x4(out[0], out[1], lean, neg_scale2, recip2);
+            const uint32_t hi = e4m3x4(out[2], out[3], lean, neg_scale2, recip2);
+            asm volatile("st.global.v2.u32 [%0], {%1, %2};" ::"l"(p.codes + base + 8 * c), "r"(lo), "r"(hi) : "memory");
+        }
+    }
+}
+
+} // namespace norm
+
+// ---------------------------------------------------------------------------
 // fp16 single-token projections (the reference plugins' kernels on sm_100a).
 
 namespace proj {
@@ -1305,7 +1449,13 @@ cudaError_t run_gemm(const LinearLaunch &L, cudaStream_t stream)
     p.k = static_cast<int>(L.k);
     p.m_tiles = static_cast<int>((L.m + C::kTileM - 1) / C::kTileM);
     const int n_tiles = static_cast<int>((L.n + BN - 1) / BN);
-    p.num_tiles = p.m_tiles * n_tiles;
+    // Persistent grid of G CTAs (pairs).  When the final partial wave holds at
+    // most G/2 tiles, its tiles are split into halves: one half-time wave.
+    const int units = kPair ? sm_count() / 2 : sm_count();
+    const int whole = p.m_tiles * n_tiles;
+    const int rem = whole % units;
+    p.full_tiles = (rem > 0 && 2 * rem <= units) ? whole - rem : whole;
+    p.num_tiles = p.full_tiles + 2 * (whole - p.full_tiles);
     p.num_kb = static_cast<int>((L.k + gemm::kBK - 1) / gemm::kBK);
     p.act_scale = L.act_scale;
     p.act_scale_ptr = L.act_scale_ptr;
@@ -1321,7 +1471,6 @@ cudaError_t run_gemm(const LinearLaunch &L, cudaStream_t stream)
     const cudaError_t attr = ensure_smem(kernel, C::kSmemBytes);
     if (attr != cudaSuccess)
         return attr;
-    const int units = kPair ? sm_count() / 2 : sm_count();
     const int grid = std::min(p.num_tiles, units) * (kPair ? 2 : 1);
     cudaLaunchConfig_t config{};
     config.gridDim = dim3(static_cast<unsigned>(grid));
@@ -1544,6 +1693,45 @@ cudaError_t launch_quantize(const uint16_t *x, int64_t count, float scale, const
     config.attrs = attr;
     config.numAttrs = 1;
     const cudaError_t err = cudaLaunchKernelEx(&config, quant::quantize_kernel, x, count, scale, recip, scale_ptr, codes);
+    count_launch();
+    return err != cudaSuccess ? err : cudaGetLastError();
+}
+
+cudaError_t launch_layer_norm(const LayerNormLaunch &L, cudaStream_t stream)
+{
+    norm::Params p{};
+    p.rows = static_cast<int>(L.rows);
+    p.cols = static_cast<int>(L.cols);
+    p.x = L.x;
+    p.residual = L.residual;
+    p.sum_out = L.sum_out;
+    p.gamma = L.gamma;
+    p.beta = L.beta;
+    p.eps = L.eps;
+    p.y = L.y;
+    p.code_scale = L.code_scale;
+    p.code_recip = L.codes && !L.code_scale_ptr ? static_cast<float>(1.0 / static_cast<double>(L.code_scale)) : 0.0f;
+    p.code_scale_ptr = L.code_scale_ptr;
+    p.codes = L.codes;
+    const int per_lane = static_cast<int>((L.cols / 8 + 31) / 32);
+    cudaLaunchConfig_t config{};
+    config.gridDim = dim3(static_cast<unsigned>((L.rows + norm::kRowsPerBlock - 1) / norm::kRowsPerBlock));
+    config.blockDim = dim3(norm::kThreads);
+    config.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    config.attrs = attr;
+    config.numAttrs = 1;
+    cudaError_t err;
+    if (per_lane <= 2)
+        err = cudaLaunchKernelEx(&config, norm::layer_norm_kernel<2>, p);
+    else if (per_lane <= 5)
+        err = cudaLaunchKernelEx(&config, norm::layer_norm_kernel<5>, p);
+    else if (per_lane <= 8)
+        err = cudaLaunchKernelEx(&config, norm::layer_norm_kernel<8>, p);
+    else
+        err = cudaLaunchKernelEx(&config, norm::layer_norm_kernel<16>, p);
     count_launch();
     return err != cudaSuccess ? err : cudaGetLastError();
 }

@@ -33,6 +33,20 @@ cudaError_t launch_fp16_skinny(const uint16_t *x, const uint16_t *w, const uint1
 // Pre-swizzled 16 KB weight tiles for the skinny kernels (size, then the pack).
 int64_t skinny_packed_bytes(int64_t n, int64_t row_bytes);
 cudaError_t launch_pack_skinny(const void *w, int64_t n, int64_t row_bytes, void *packed, cudaStream_t stream);
+// LayerNorm producer: fp16 residual sum, fp16 LN output and/or E4M3 codes.
+constexpr int64_t kLayerNormMaxCols = 4096;
+struct LayerNormLaunch {
+    int64_t rows, cols; // cols % 8 == 0, cols <= 4096
+    const uint16_t *x, *residual;
+    uint16_t *sum_out;
+    const float *gamma, *beta;
+    float eps;
+    uint16_t *y;
+    float code_scale;
+    const float *code_scale_ptr;
+    uint8_t *codes;
+};
+cudaError_t launch_layer_norm(const LayerNormLaunch &p, cudaStream_t stream);
 cudaError_t launch_quantize(const uint16_t *x, int64_t count, float scale, const float *scale_ptr,
                             uint8_t *codes, cudaStream_t stream);
 cudaError_t launch_quantize_rows(const uint16_t *w, int64_t rows, int64_t cols,

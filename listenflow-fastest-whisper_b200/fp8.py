@@ -80,6 +80,51 @@ def quantize(x: torch.Tensor, scale, out: torch.Tensor | None = None, stream=Non
     return out
 
 
+def layer_norm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float = 1e-5, *,
+               residual: torch.Tensor | None = None, code_scale=None, want_y: bool = True,
+               want_sum: bool = False, stream=None):
+    """LayerNorm producer (network_graph.cpp:160-166 after the residual add of :285-287).
+
+    Returns (sum, y, codes): sum = x + residual in fp16 (if want_sum), y = the fp16
+    LayerNorm of it over the last axis with fp32 gamma/beta (if want_y), and the
+    E4M3 codes of y for the next linear when `code_scale` (float or 1-element fp32
+    CUDA tensor) is given."""
+    _require(x, torch.float16, "x")
+    _require(gamma, torch.float32, "gamma")
+    _require(beta, torch.float32, "beta")
+    if x.dim() != 2:
+        raise ValueError("x must be [rows, cols]")
+    rows, cols = x.shape
+    if gamma.numel() != cols or beta.numel() != cols:
+        raise ValueError("gamma and beta must have cols elements")
+    if residual is not None:
+        _require(residual, torch.float16, "residual")
+        if residual.shape != x.shape:
+            raise ValueError("residual must match x")
+    a = native.LayerNormArgs()
+    a.struct_size = ctypes.sizeof(native.LayerNormArgs)
+    a.rows, a.cols = rows, cols
+    a.x = x.data_ptr()
+    a.residual = residual.data_ptr() if residual is not None else None
+    a.gamma, a.beta = gamma.data_ptr(), beta.data_ptr()
+    a.epsilon = float(eps)
+    total = torch.empty_like(x) if want_sum else None
+    y = torch.empty_like(x) if want_y else None
+    codes = None
+    if code_scale is not None:
+        codes = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+        if isinstance(code_scale, torch.Tensor):
+            _require(code_scale, torch.float32, "code_scale")
+            a.code_scale_ptr = code_scale.data_ptr()
+        else:
+            a.code_scale = float(code_scale)
+        a.codes = codes.data_ptr()
+    a.sum_out = total.data_ptr() if total is not None else None
+    a.y = y.data_ptr() if y is not None else None
+    native.check(native.library().lffw_layer_norm(ctypes.byref(a), _stream(stream)), "lffw_layer_norm")
+    return total, y, codes
+
+
 def quantize_rows(w: torch.Tensor, scales: torch.Tensor, stream=None) -> torch.Tensor:
     """E4M3 codes of an fp16 [N, K] weight with one scale per row."""
     _require(w, torch.float16, "w")

@@ -124,6 +124,41 @@ void oracle_quantize(const uint16_t *x, size_t count, float scale, uint8_t *code
         codes[i] = quantize_one(x[i], scale);
 }
 
+void oracle_layer_norm(const uint16_t *x, const uint16_t *residual, int64_t rows, int64_t cols,
+                       const float *gamma, const float *beta, float eps, uint16_t *sum_out, uint16_t *y,
+                       float code_scale, uint8_t *codes)
+{
+    double *s = (double *)malloc((size_t)cols * sizeof(double));
+    if (!s)
+        return;
+    for (int64_t r = 0; r < rows; ++r) {
+        const uint16_t *xr = x + r * cols;
+        double mean = 0.0, var = 0.0;
+        for (int64_t c = 0; c < cols; ++c) {
+            uint16_t h = xr[c];
+            if (residual) /* fp16 add: exact sum in binary64, one rounding to fp16 */
+                h = oracle_half_from_double(oracle_half_to_double(h) + oracle_half_to_double(residual[r * cols + c]));
+            if (sum_out)
+                sum_out[r * cols + c] = h;
+            s[c] = oracle_half_to_double(h);
+            mean += s[c];
+        }
+        mean /= (double)cols;
+        for (int64_t c = 0; c < cols; ++c)
+            var += (s[c] - mean) * (s[c] - mean);
+        var /= (double)cols;
+        const double inv = 1.0 / sqrt(var + (double)eps);
+        for (int64_t c = 0; c < cols; ++c) {
+            const uint16_t out = oracle_half_from_double((s[c] - mean) * inv * (double)gamma[c] + (double)beta[c]);
+            if (y)
+                y[r * cols + c] = out;
+            if (codes)
+                codes[r * cols + c] = quantize_one(out, code_scale);
+        }
+    }
+    free(s);
+}
+
 void oracle_quantize_rows(const uint16_t *x, int64_t rows, int64_t cols, const float *scales,
                           uint8_t *codes)
 {

@@ -61,6 +61,18 @@ void oracle_fp8_linear(const uint8_t *xq, const uint8_t *wq, int64_t m, int64_t 
                        float act_scale, const float *w_scale, const uint16_t *bias, int gelu,
                        uint16_t *y, float next_scale, uint8_t *next_codes, int threads);
 
+/* LayerNorm producer (cpp/src/network_graph.cpp:160-166 with the residual add
+ * of :285-287): per row of cols fp16 values,
+ *   s[i]  = half(x[i] + residual[i])          (fp16 add; s = x when residual is NULL)
+ *   mean  = sum(s) / cols, var = sum((s - mean)^2) / cols        (binary64)
+ *   y[i]  = half((s[i] - mean) / sqrt(var + eps) * gamma[i] + beta[i])
+ *   codes = e4m3(fp32(y[i] / code_scale))      (if codes)
+ * TensorRT's normalization runs in fp32 in an unspecified order; this is the
+ * exactly rounded value that such an evaluation approximates. */
+void oracle_layer_norm(const uint16_t *x, const uint16_t *residual, int64_t rows, int64_t cols,
+                       const float *gamma, const float *beta, float eps, uint16_t *sum_out, uint16_t *y,
+                       float code_scale, uint8_t *codes);
+
 /* fp16(erf(x)) of an fp16 x, erf in binary64, round to nearest even. */
 uint16_t oracle_erf_fp16(uint16_t x);
 /* GELU on an fp16 value with every graph edge rounded to fp16. */

@@ -54,6 +54,10 @@ def lib() -> ctypes.CDLL:
         L.oracle_fp16_qkv.argtypes = [_u16p, _u16p, _u16p, _u16p, _u16p, ctypes.c_int64]
         L.oracle_fp16_bias.argtypes = [_u16p, ctypes.c_uint16, _u16p, ctypes.c_int64]
         L.oracle_threads.restype = ctypes.c_int
+        L.oracle_layer_norm.argtypes = [
+            _u16p, _u16p, ctypes.c_int64, ctypes.c_int64, _f32p, _f32p, ctypes.c_float, _u16p, _u16p,
+            ctypes.c_float, _u8p,
+        ]
         L.oracle_erf_fp16.argtypes = [ctypes.c_uint16]
         L.oracle_erf_fp16.restype = ctypes.c_uint16
         _lib = L
@@ -119,6 +123,26 @@ def quantize(x, scale: float) -> np.ndarray:
     out = np.empty(b.shape, np.uint8)
     lib().oracle_quantize(_ptr(b, _u16p), b.size, float(np.float32(scale)), _ptr(out, _u8p))
     return out
+
+
+def layer_norm(x, gamma, beta, eps: float = 1e-5, residual=None, code_scale=None):
+    """(sum, y, codes): s = half(x + residual) (or x), y = half(LN(s) * gamma + beta)
+    with binary64 statistics, codes = Q(y / code_scale) (None without a scale);
+    cpp/src/network_graph.cpp:160-166, 285-287."""
+    b = bits16(x)
+    rows, cols = b.shape
+    r = bits16(residual) if residual is not None else None
+    g = np.ascontiguousarray(gamma, dtype=np.float32)
+    be = np.ascontiguousarray(beta, dtype=np.float32)
+    assert g.shape == (cols,) and be.shape == (cols,)
+    s = np.empty(b.shape, np.uint16)
+    y = np.empty(b.shape, np.uint16)
+    codes = np.empty(b.shape, np.uint8) if code_scale is not None else None
+    lib().oracle_layer_norm(_ptr(b, _u16p), _ptr(r, _u16p), rows, cols, _ptr(g, _f32p), _ptr(be, _f32p),
+                            float(np.float32(eps)), _ptr(s, _u16p), _ptr(y, _u16p),
+                            float(np.float32(code_scale)) if code_scale is not None else 1.0,
+                            _ptr(codes, _u8p))
+    return s, y, codes
 
 
 def quantize_rows(w, scales) -> np.ndarray:

@@ -71,6 +71,38 @@ def test_other_entry_points_reject_invalid_arguments(native, lib):
     assert lib.lffw_fp16_gelu(None, 0x2000, 4, None) == bad
 
 
+def _norm_args(native, **over):
+    a = native.LayerNormArgs()
+    a.struct_size = ctypes.sizeof(native.LayerNormArgs)
+    a.rows, a.cols = 16, 1280
+    a.x, a.gamma, a.beta, a.codes = 0x10000, 0x20000, 0x30000, 0x40000
+    a.epsilon = 1e-5
+    a.code_scale = 0.01
+    for key, value in over.items():
+        setattr(a, key, value)
+    return a
+
+
+@pytest.mark.parametrize("change", [
+    {"rows": 0}, {"cols": 4}, {"cols": 1284}, {"cols": 4104}, {"x": None}, {"gamma": None},
+    {"beta": None}, {"x": 0x10008}, {"residual": 0x50004}, {"codes": None},
+    {"epsilon": -1.0}, {"epsilon": float("nan")}, {"epsilon": float("inf")},
+    {"code_scale": 0.0}, {"code_scale": float("nan")}, {"code_scale": 2.0**126},
+])
+def test_layer_norm_rejects_invalid_arguments(native, lib, change):
+    """No output at all, ragged or oversized rows, misaligned pointers, a bad
+    epsilon or code scale: rejected before any device call."""
+    a = _norm_args(native, **change)
+    assert lib.lffw_layer_norm(ctypes.byref(a), None) == native.INVALID_ARGUMENT
+
+
+def test_layer_norm_abi_mismatch_and_null(native, lib):
+    a = _norm_args(native)
+    a.struct_size = 8
+    assert lib.lffw_layer_norm(ctypes.byref(a), None) == native.ABI_MISMATCH
+    assert lib.lffw_layer_norm(None, None) == native.INVALID_ARGUMENT
+
+
 def test_device_gate_without_sm100(native, lib):
     import torch
 

@@ -161,6 +161,32 @@ def test_gelu_codes_table_matches_direct_path(cuda, fp8, oracle, native, m, n, k
     assert native.device_error() == 0
 
 
+@pytest.mark.parametrize("m,n,k,rows", [
+    # 1-CTA tiles: 40 x 4 = 160 tiles on 148 SMs -> 148 full tiles, 12 split into halves
+    (5120, 1024, 256, (0, 5120)),
+    # CTA pairs (K >= 4096): 20 x 4 = 80 pair tiles on 74 pairs -> 74 full, 6 split;
+    # rows 3328-3839 hold a full pair tile (M-tile 13) and a split one (M-tile 14)
+    (5120, 1024, 4096, (3328, 3840)),
+])
+def test_partial_wave_half_tiles(cuda, fp8, oracle, native, m, n, k, rows):
+    """A launch whose last wave is split into 128-column half tiles matches the
+    oracle on full and half tiles alike."""
+    import torch
+
+    d = _prepare(torch, fp8, oracle, cuda, m, n, k, seed=m + n + k)
+    y, codes = fp8.linear(d["xq"], d["wq"], d["ws"], float(d["act_scale"]), bias=d["bd"], next_scale=0.011)
+    torch.cuda.synchronize()
+    assert native.device_error() == 0
+    r0, r1 = rows
+    xq_rows = d["xq_ref"][r0:r1]
+    y_ref, _ = oracle.fp8_linear(xq_rows, d["wq_ref"], d["act_scale"], d["ws_ref"], d["b"])
+    y_bits = y.cpu().numpy().view(np.uint16)[r0:r1]
+    extra = accumulation_bound(oracle, xq_rows, d["wq_ref"], d["act_scale"], d["ws_ref"], k)
+    max_abs, max_rel, excess, mismatches = compare_halves(y_bits, y_ref, extra=extra)
+    assert excess <= 0, f"max_abs {max_abs}"
+    np.testing.assert_array_equal(codes.cpu().numpy()[r0:r1], oracle.quantize(y_bits, np.float32(0.011)))
+
+
 def test_linear_without_bias_and_codes_only(cuda, fp8, oracle):
     import torch
 
