@@ -257,7 +257,6 @@ struct Cfg {
 struct Params {
     int m, n, k;
     int m_tiles, num_tiles, num_kb;
-    int full_tiles; // tiles [0, full_tiles) are BN wide; the rest are BN/2-wide halves
     float act_scale;
     const float *act_scale_ptr;
     const float *w_scales;
@@ -266,24 +265,6 @@ struct Params {
     float next_recip; // RN(1 / next_scale)
     int next_lean;    // lean_scale(next_scale)
 };
-
-// Tile t of the launch: M-tile index, first output column and width.  Full
-// tiles run M-fastest; the last units of that order (the launch's final,
-// partial wave) are split into two BN/2-wide halves each, so that wave takes
-// half a tile's time.
-struct TileRef {
-    int mt, n0, width;
-};
-
-template <int BN>
-__device__ __forceinline__ TileRef tile_at(const Params &p, int t)
-{
-    if (t < p.full_tiles)
-        return {t % p.m_tiles, (t / p.m_tiles) * BN, BN};
-    const int h = t - p.full_tiles;
-    const int u = p.full_tiles + (h >> 1);
-    return {u % p.m_tiles, (u / p.m_tiles) * BN + (h & 1) * (BN / 2), BN / 2};
-}
 
 // fp16(erf(x)) of two packed fp16 values, rounded to nearest even: one table
 // read per value.  The table covers every non-negative fp16 input up to
@@ -419,26 +400,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             // The weights do not come from the previous kernel: the first stages'
             // B tiles are requested before waiting for it (stages start empty).
             const int pre = tile_first < p.num_tiles ? (p.num_kb < C::kStages ? p.num_kb : C::kStages) : 0;
-            for (int kb = 0; kb < pre; ++kb) {
-                const TileRef first = tile_at<BN>(p, tile_first);
-                const int n0 = first.n0 + static_cast<int>(rank) * (kPair ? first.width / 2 : 0);
-                const uint32_t full = bar_full + 8 * kb;
+            // Arms stage `stage` for a full stage and loads its B (weight) rows; in a
+            // pair both CTAs' bytes complete on the leader's barrier, armed by the leader.
+            auto arm_and_load_b = [&](int stage, int kb, int n0) {
+                const uint32_t full = bar_full + 8 * stage;
                 if (kPair) {
                     if (leader)
                         mbar_arrive_expect_tx(full, C::kTxBytes);
-                    tma_load_2d_pair(sbase + C::kOffB + kb * C::kBBytes, &tm_b, map_to_rank(full, 0), kb * kBK, n0);
+                    tma_load_2d_pair(sbase + C::kOffB + stage * C::kBBytes, &tm_b, map_to_rank(full, 0), kb * kBK, n0);
                 } else {
                     mbar_arrive_expect_tx(full, C::kTxBytes);
-                    tma_load_2d(sbase + C::kOffB + kb * C::kBBytes, &tm_b, full, kb * kBK, n0);
+                    tma_load_2d(sbase + C::kOffB + stage * C::kBBytes, &tm_b, full, kb * kBK, n0);
                 }
-            }
+            };
+            for (int kb = 0; kb < pre; ++kb)
+                arm_and_load_b(kb, kb, (tile_first / p.m_tiles) * BN + static_cast<int>(rank) * C::kBRows);
             griddepcontrol_wait();
             int issued = 0;
             for (int t = tile_first; ok && t < p.num_tiles; t += tile_step) {
                 // In a pair each CTA loads half of the tile's B rows.
-                const TileRef tile = tile_at<BN>(p, t);
-                const int m0 = tile.mt * C::kTileM + static_cast<int>(rank) * kBM;
-                const int n0 = tile.n0 + static_cast<int>(rank) * (kPair ? tile.width / 2 : 0);
+                const int m0 = (t % p.m_tiles) * C::kTileM + static_cast<int>(rank) * kBM;
+                const int n0 = (t / p.m_tiles) * BN + static_cast<int>(rank) * C::kBRows;
                 for (int kb = 0; kb < p.num_kb; ++kb, ++issued) {
                     const uint32_t full = bar_full + 8 * s;
                     if (issued < pre) {
@@ -452,18 +434,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                             ok = false;
                             break;
                         }
-                        if (kPair) {
-                            // Both CTAs' bytes complete on the leader's barrier, armed by the leader.
-                            const uint32_t leader_full = map_to_rank(full, 0);
-                            if (leader)
-                                mbar_arrive_expect_tx(full, C::kTxBytes);
-                            tma_load_2d_pair(sbase + s * C::kABytes, &tm_a, leader_full, kb * kBK, m0);
-                            tma_load_2d_pair(sbase + C::kOffB + s * C::kBBytes, &tm_b, leader_full, kb * kBK, n0);
-                        } else {
-                            mbar_arrive_expect_tx(full, C::kTxBytes);
+                        arm_and_load_b(s, kb, n0);
+                        if (kPair)
+                            tma_load_2d_pair(sbase + s * C::kABytes, &tm_a, map_to_rank(full, 0), kb * kBK, m0);
+                        else
                             tma_load_2d(sbase + s * C::kABytes, &tm_a, full, kb * kBK, m0);
-                            tma_load_2d(sbase + C::kOffB + s * C::kBBytes, &tm_b, full, kb * kBK, n0);
-                        }
                     }
                     used_mask |= 1u << s;
                     parity_mask = (parity_mask & ~(1u << s)) | (ph << s);
@@ -486,8 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer (one thread of the leader) ----------------
         if (lane == 0 && leader) {
-            constexpr uint32_t idesc_full = idesc_e4m3_f32<C::kTileM, BN>();
-            constexpr uint32_t idesc_half = idesc_e4m3_f32<C::kTileM, BN / 2>();
+            constexpr uint32_t idesc = idesc_e4m3_f32<C::kTileM, BN>();
             int s = 0;
             uint32_t ph = 0;
             int local = 0;
@@ -501,7 +475,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + a * BN;
-                const uint32_t idesc = t < p.full_tiles ? idesc_full : idesc_half;
                 for (int kb = 0; kb < p.num_kb; ++kb) {
                     if (!mbar_wait(bar_full + 8 * s, ph, kSiteMmaFull)) {
                         ok = false;
@@ -576,10 +549,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t staging_s = smem_u32(staging);
         int local = 0;
         for (int t = tile_first; t < p.num_tiles; t += tile_step, ++local) {
-            const TileRef tile = tile_at<BN>(p, t);
-            const int m0 = tile.mt * C::kTileM + static_cast<int>(rank) * kBM;
-            const int n0 = tile.n0;
-            const int n_end = n0 + tile.width < p.n ? n0 + tile.width : p.n;
+            const int m0 = (t % p.m_tiles) * C::kTileM + static_cast<int>(rank) * kBM;
+            const int n0 = (t / p.m_tiles) * BN;
             const uint32_t a = local & 1;
             const uint32_t acc_ph = (local >> 1) & 1;
             const int col_begin = n0 + slice * (BN / 4);
@@ -600,7 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok)
                 break;
             tc_fence_after();
-            int subs = (n_end - col_begin + kSub - 1) / kSub;
+            int subs = (p.n - col_begin + kSub - 1) / kSub;
             subs = subs < 0 ? 0 : (subs > BN / 4 / kSub ? BN / 4 / kSub : subs);
             const int row0 = m0 + quarter * 32;
             if (row0 >= p.m)
@@ -1449,13 +1420,8 @@ cudaError_t run_gemm(const LinearLaunch &L, cudaStream_t stream)
     p.k = static_cast<int>(L.k);
     p.m_tiles = static_cast<int>((L.m + C::kTileM - 1) / C::kTileM);
     const int n_tiles = static_cast<int>((L.n + BN - 1) / BN);
-    // Persistent grid of G CTAs (pairs).  When the final partial wave holds at
-    // most G/2 tiles, its tiles are split into halves: one half-time wave.
-    const int units = kPair ? sm_count() / 2 : sm_count();
-    const int whole = p.m_tiles * n_tiles;
-    const int rem = whole % units;
-    p.full_tiles = (rem > 0 && 2 * rem <= units) ? whole - rem : whole;
-    p.num_tiles = p.full_tiles + 2 * (whole - p.full_tiles);
+    const int units = kPair ? sm_count() / 2 : sm_count(); // persistent CTAs (pairs)
+    p.num_tiles = p.m_tiles * n_tiles;
     p.num_kb = static_cast<int>((L.k + gemm::kBK - 1) / gemm::kBK);
     p.act_scale = L.act_scale;
     p.act_scale_ptr = L.act_scale_ptr;

@@ -162,15 +162,15 @@ def test_gelu_codes_table_matches_direct_path(cuda, fp8, oracle, native, m, n, k
 
 
 @pytest.mark.parametrize("m,n,k,rows", [
-    # 1-CTA tiles: 40 x 4 = 160 tiles on 148 SMs -> 148 full tiles, 12 split into halves
+    # 1-CTA tiles: 40 x 4 = 160 tiles on 148 persistent CTAs (a partial second wave)
     (5120, 1024, 256, (0, 5120)),
-    # CTA pairs (K >= 4096): 20 x 4 = 80 pair tiles on 74 pairs -> 74 full, 6 split;
-    # rows 3328-3839 hold a full pair tile (M-tile 13) and a split one (M-tile 14)
+    # CTA pairs (K >= 4096): 20 x 4 = 80 pair tiles on 74 pairs; rows 3328-3839 hold
+    # M-tiles 13 and 14 (the latter in the partial second wave)
     (5120, 1024, 4096, (3328, 3840)),
 ])
-def test_partial_wave_half_tiles(cuda, fp8, oracle, native, m, n, k, rows):
-    """A launch whose last wave is split into 128-column half tiles matches the
-    oracle on full and half tiles alike."""
+def test_partial_second_wave(cuda, fp8, oracle, native, m, n, k, rows):
+    """A launch with slightly more tiles than persistent CTAs (one CTA takes two
+    tiles, the rest one) matches the oracle, with 1-CTA tiles and CTA pairs."""
     import torch
 
     d = _prepare(torch, fp8, oracle, cuda, m, n, k, seed=m + n + k)
