@@ -343,6 +343,7 @@ def run_ours(args, rank, local_rank, world):
     np.testing.assert_array_equal(host_out["fc2"].numpy(), sets[(e2e_steps - 1) % 2][1]["fc2"].cpu().numpy())
 
     ln = run_ln_producer(fp8, native, device, 20, seed=31 + rank)
+    attention = run_cross_attention(fp8, native, device, 10, seed=41 + rank)
     decoder = None
     if args.decoder_steps > 0:
         del flush, scrub
@@ -404,6 +405,7 @@ def run_ours(args, rank, local_rank, world):
             "clocks": clocks.summary(),
         }
         result["ln_producer"] = ln
+        result["cross_attention"] = attention
         if args.decoder_steps > 0:
             result["decoder_step"] = decoder
         if world == 1 and args.cpu_seconds > 0:
@@ -564,6 +566,63 @@ def run_ln_producer(fp8, native, device, reps: int, seed: int):
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm[0], "peak_source": hbm[1],
                          "unit": "GB/s", "frac": round(gbs / hbm[0], 4)},
             "l2": "flushed before every launch (256 MiB written, then 256 MiB read)"}
+
+
+def run_cross_attention(fp8, native, device, steps: int, seed: int):
+    """Decoder cross-attention over cached encoder K/V for all 32 layers of one
+    decoder step, as one CUDA graph: C3 (4 streams x 5 beams) and C5 (16 greedy
+    streams per GPU, 128 streams over 8 GPUs).  Each layer reads its own K/V
+    (streams x 20 heads x 1500 keys x 64), so the step streams K/V from HBM;
+    out_proj's E4M3 codes are the output."""
+    import torch
+
+    results = {}
+    for name, streams, queries in (("c3_4x5", 4, 5), ("c5_16x1", 16, 1)):
+        g = torch.Generator(device=device).manual_seed(seed)
+        layers = DEC_LAYERS
+        shape = (layers, streams, 20, 1500, 64)
+        k = torch.randn(shape, generator=g, device=device).half()
+        v = torch.randn(shape, generator=g, device=device).half()
+        q = torch.randn((layers, streams * queries, 1280), generator=g, device=device).half()
+        stream = torch.cuda.Stream(device)
+
+        def step():
+            for layer in range(layers):
+                fp8.cross_attention(q[layer], k[layer], v[layer], queries, code_scale=0.004, want_out=False)
+
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                step()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        graph.replay()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        if native.device_error() != 0:
+            raise RuntimeError("device-side wait timed out in the cross-attention section")
+        ms = statistics.median(times)
+        kv_bytes = 2 * k.numel() * 2
+        gbs = kv_bytes / (ms / 1e3) / 1e9
+        hbm = read_hbm_peak()
+        results[name] = {"streams": streams, "queries_per_stream": queries, "layers": layers,
+                         "ms_per_step": round(ms, 4), "kv_bytes_per_step": kv_bytes,
+                         "value": round(gbs, 1), "unit": "GB/s (K/V streamed)",
+                         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm[0],
+                                      "peak_source": hbm[1], "unit": "GB/s", "frac": round(gbs / hbm[0], 4)}}
+        del graph, k, v, q
+        torch.cuda.empty_cache()
+    results["workload"] = ("decoder cross-attention, 20 heads x 1500 keys x 64, 32 layers per step (one graph), "
+                           "out_proj E4M3 codes out")
+    return results
 
 
 def read_hbm_peak():

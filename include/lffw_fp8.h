@@ -24,7 +24,7 @@
 #include <stdint.h>
 
 #define LFFW_FP8_ABI_MAJOR 1
-#define LFFW_FP8_ABI_MINOR 2
+#define LFFW_FP8_ABI_MINOR 3
 #define LFFW_FP8_API __attribute__((visibility("default")))
 #if defined(__cplusplus)
 #define LFFW_FP8_NOEXCEPT noexcept
@@ -134,6 +134,35 @@ typedef struct lffw_layer_norm_args {
 } lffw_layer_norm_args;
 
 LFFW_FP8_API lffw_status lffw_layer_norm(const lffw_layer_norm_args *args, void *stream) LFFW_FP8_NOEXCEPT;
+
+/* Decoder cross-attention over a cached encoder K/V for one layer
+ * (network_graph.cpp:235-244 `attend`, cross_keys/cross_values of :401-404), per
+ * stream s, head h, query row t (the beams of a stream share its K/V):
+ *   c        = half(head_dim^-0.25)
+ *   q', k'   = half(q * c), half(k * c)
+ *   score[j] = half(q' . k'[j])                        (fp32 accumulate)
+ *   p[j]     = half(softmax_fp32(score)[j])            (over all keys)
+ *   out[s*queries + t][h*head_dim + d] = half(sum_j p[j] v[j][d])   (fp32 accumulate)
+ *   out_codes = E4M3_rne_sat(fp32(out / code_scale))   (if out_codes: out_proj's input)
+ * q and out are fp16 [streams*queries, heads*head_dim] (the q_proj output and the
+ * out_proj input, merge_heads layout); k and v are fp16 [streams, heads, keys,
+ * head_dim].  Requirements: head_dim == 64; 1 <= queries <= 16; 1 <= keys <= 4096;
+ * streams, heads >= 1 with streams*heads*keys < 2^31; 16-byte aligned pointers;
+ * out and/or out_codes set; code_scale (or *code_scale_ptr) in [2^-125, 2^125]. */
+typedef struct lffw_cross_attention_args {
+    size_t struct_size; /* sizeof(lffw_cross_attention_args) */
+    int32_t streams, queries, heads, head_dim, keys;
+    const uint16_t *q;
+    const uint16_t *k;
+    const uint16_t *v;
+    uint16_t *out;
+    float code_scale;
+    const float *code_scale_ptr;
+    uint8_t *out_codes;
+} lffw_cross_attention_args;
+
+LFFW_FP8_API lffw_status lffw_cross_attention(const lffw_cross_attention_args *args,
+                                              void *stream) LFFW_FP8_NOEXCEPT;
 
 /* Q of an fp16 [rows, cols] weight with one scale per row (the per-output-channel
  * weight Q of network_graph.cpp:140-152, axis 2 of the transposed constant). */

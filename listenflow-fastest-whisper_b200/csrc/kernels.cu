@@ -751,12 +751,12 @@ struct Params {
 
 // Split-K reduction over a cluster of S CTAs.  Each CTA finishes 128 / S of
 // the 128 weight rows; a thread owns one of them (`row`) and the activation
-// rows m = g, g + S, g + 2S, ... below m_count, where g = threadIdx.x / (128 / S).
+// rows m = g + j*S (j < 32 / S) below m_count, where g = threadIdx.x / (128 / S).
 // The partials are stored m-major, so a warp's remote loads read runs of
-// consecutive rows.  Every remote partial is requested before the sum, which
-// adds the cluster's partials in rank order.
-template <int S, class Finish>
-__device__ __forceinline__ void reduce_rows(const float *red, int row, int m_count, Finish &finish)
+// consecutive rows.  Every remote partial is requested before the sums, which
+// add the cluster's partials in rank order into acc[j].
+template <int S>
+__device__ __forceinline__ void reduce_rows(const float *red, int row, int m_count, float (&acc)[kAct / 2])
 {
     constexpr int kPer = kAct / S; // activation rows per thread
     const int g = static_cast<int>(threadIdx.x) / (kRows / S);
@@ -773,15 +773,23 @@ __device__ __forceinline__ void reduce_rows(const float *red, int row, int m_cou
     }
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
-        const int m = g + j * S;
-        if (m < m_count) {
-            float acc = 0.0f;
+        float sum = 0.0f;
 #pragma unroll
-            for (int q = 0; q < S; ++q)
-                acc += part[j][q];
-            finish(acc, m);
-        }
+        for (int q = 0; q < S; ++q)
+            sum += g + j * S < m_count ? part[j][q] : 0.0f;
+        acc[j] = sum;
     }
+}
+
+// The epilogue of the rows reduce_rows<S> summed: finish(acc[j], m) per row m.
+template <int S, class Finish>
+__device__ __forceinline__ void finish_rows(const float (&acc)[kAct / 2], int m_count, Finish &finish)
+{
+    const int g = static_cast<int>(threadIdx.x) / (kRows / S);
+#pragma unroll
+    for (int j = 0; j < kAct / S; ++j)
+        if (g + j * S < m_count)
+            finish(acc[j], g + j * S);
 }
 
 template <int KIND, int EPI, int ST>
@@ -951,14 +959,25 @@ __global__ void __launch_bounds__(kThreads)
         for (int i = 0; i < kAct; ++i)
             red[i * kRedStride + threadIdx.x] = __uint_as_float(v[i]);
         cluster_sync();
+        float acc[kAct / 2];
         if (my_n < p.n) {
             switch (S) {
-            case 2: reduce_rows<2>(red, my_row, p.m, finish); break;
-            case 4: reduce_rows<4>(red, my_row, p.m, finish); break;
-            default: reduce_rows<8>(red, my_row, p.m, finish); break;
+            case 2: reduce_rows<2>(red, my_row, p.m, acc); break;
+            case 4: reduce_rows<4>(red, my_row, p.m, acc); break;
+            default: reduce_rows<8>(red, my_row, p.m, acc); break;
             }
         }
-        cluster_sync(); // peers read this CTA's partials until here
+        // This thread's remote reads have returned (their values are summed):
+        // arrive now and wait only before exiting, so the barrier's latency
+        // overlaps the epilogue.  Peers read this CTA's partials until the wait.
+        cluster_arrive();
+        if (my_n < p.n) {
+            switch (S) {
+            case 2: finish_rows<2>(acc, p.m, finish); break;
+            case 4: finish_rows<4>(acc, p.m, finish); break;
+            default: finish_rows<8>(acc, p.m, finish); break;
+            }
+        }
     }
 
     tc_fence_before();
@@ -967,6 +986,8 @@ __global__ void __launch_bounds__(kThreads)
         tc_fence_after();
         tmem_dealloc(tmem_base, 32);
     }
+    if (S > 1)
+        cluster_wait();
 }
 
 // Re-lays a row-major [n, row_bytes] weight as 16 KB tiles: tile (rb, kb)
@@ -1249,6 +1270,358 @@ __global__ void __launch_bounds__(kThreads) layer_norm_kernel(const Params p)
 }
 
 } // namespace norm
+
+// ---------------------------------------------------------------------------
+// Decoder cross-attention over the cached encoder K/V (cpp/src/network_graph.cpp
+// :235-244 `attend`, with the cross-K/V cache of :401-404).  A cluster of S CTAs
+// serves one (stream, head); all query rows (beams) of the stream share one pass
+// over the head's K and V, each CTA over a contiguous range of the keys.
+// Pass 1 streams K and forms fp16 scores with m16n8k16 MMAs.  The softmax is
+// over all keys: the CTAs exchange their rows' maxima and then their sums of
+// exp through distributed shared memory, so every probability is
+// half(exp(s - max) / sum) with the global max and sum.  Pass 2 streams V and
+// forms each CTA's part of P.V; the parts are summed in rank order by the CTA
+// owning each group of output columns.  K/V tiles arrive by TMA (128B-swizzled,
+// so the ldmatrix fragment reads are conflict-free) through a ring fed by one
+// producer warp.  Peers push values into each other's shared memory and arrive
+// on each other's mbarriers, so only the consumer warps take part in exchanges.
+
+namespace attn {
+
+constexpr int kDim = 64;         // head dimension
+constexpr int kChunk = 128;      // keys per stage: one 128-row x 128-byte box
+constexpr int kMaxStages = 4; // ring depth is chosen per launch (3 or 4)
+constexpr int kStageBytes = kChunk * kDim * 2;
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kThreads = kConsumers + 32; // + the producer warp
+constexpr int kMaxQueries = 16;           // MMA M
+constexpr int kMaxCluster = 8;
+// Exchange area: row maxima and sums from every rank, then the P.V parts each
+// rank sends to the owner of its columns ([source rank][query row][64 columns]).
+constexpr int kXMax = 0;
+constexpr int kXSum = kXMax + kMaxCluster * kMaxQueries * 4;
+constexpr int kXOut = kXSum + kMaxCluster * kMaxQueries * 4;
+
+struct Params {
+    int streams, queries, heads, keys;
+    int cluster; // CTAs per (stream, head)
+    int kpc;     // keys per CTA (multiple of 16); CTA r takes [r*kpc, min(keys, (r+1)*kpc))
+    int pstride; // fp16 elements per score row: kpc + 8 (conflict-free ldmatrix rows)
+    int stages;      // K/V ring depth
+    int score_bytes; // queries score rows, then a 16-byte zero block (the MMA's padding rows)
+    int xch_bytes;
+    const uint16_t *q;
+    uint16_t *out;
+    uint32_t scale2; // fp16 head_dim^-0.25 in both halves
+    float code_scale, code_recip;
+    const float *code_scale_ptr;
+    uint8_t *codes;
+};
+
+// Score rows exist for the real query rows only; the MMA's rows past them read
+// a 16-byte zero block that follows the rows.
+__host__ __device__ constexpr int score_bytes(int queries, int pstride) { return (queries * pstride * 2 + 31) / 16 * 16; }
+__host__ __device__ constexpr int xch_bytes(int queries, int cluster) { return kXOut + cluster * queries * kDim * 4; }
+__host__ __device__ constexpr int smem_bytes(int stages, int queries, int pstride, int cluster)
+{
+    return 1024 + stages * kStageBytes + score_bytes(queries, pstride) + xch_bytes(queries, cluster) + 128;
+}
+
+__device__ __forceinline__ float warp_max(float v)
+{
+#pragma unroll
+    for (int off = 16; off > 0; off /= 2)
+        v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+    return v;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    cross_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                           const Params p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t ring = sbase;
+    const int depth = p.stages; // ring stages
+    uint16_t *scores = reinterpret_cast<uint16_t *>(smem + depth * kStageBytes);
+    const uint32_t scores_s = smem_u32(scores);
+    const uint32_t zero_s = scores_s + static_cast<uint32_t>(p.score_bytes) - 16;
+    float *xch = reinterpret_cast<float *>(smem + depth * kStageBytes + p.score_bytes);
+    const uint32_t xch_s = smem_u32(xch);
+    const uint32_t bar_full = xch_s + p.xch_bytes;
+    const uint32_t bar_empty = bar_full + 8 * depth;
+    const uint32_t bar_max = bar_empty + 8 * depth; // S arrivals: every rank's maxima are here
+    const uint32_t bar_sum = bar_max + 8;             // S arrivals: every rank's sums
+    const uint32_t bar_out = bar_sum + 8;             // S arrivals: every rank's parts of my columns
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    const int S = p.cluster;
+    const int rank = static_cast<int>(blockIdx.x) % S;
+    const int sh = static_cast<int>(blockIdx.x) / S;
+    const int head = sh % p.heads;
+    const int stream = sh / p.heads;
+    const int width = p.heads * kDim;
+    const int kbeg = rank * p.kpc;
+    const int kend = kbeg + p.kpc < p.keys ? kbeg + p.kpc : p.keys;
+    const int lk = kend > kbeg ? kend - kbeg : 0; // this CTA's keys
+    const int nchunks = (lk + kChunk - 1) / kChunk;
+
+    if (threadIdx.x == 0) {
+        griddepcontrol_launch_dependents();
+        for (int i = 0; i < depth; ++i) {
+            mbar_init(bar_full + 8 * i, 1);
+            mbar_init(bar_empty + 8 * i, kConsumerWarps);
+        }
+        mbar_init(bar_max, S);
+        mbar_init(bar_sum, S);
+        mbar_init(bar_out, S);
+        fence_barrier_init();
+        prefetch_tensor_map(&tm_k);
+        prefetch_tensor_map(&tm_v);
+    }
+    // Scores start at zero: keys past the last 16-key step stay zero, and so does
+    // the zero block the padding rows read, so they add nothing to P.V.
+    for (int i = threadIdx.x; i < p.score_bytes / 16; i += kThreads)
+        reinterpret_cast<uint4 *>(scores)[i] = make_uint4(0u, 0u, 0u, 0u);
+    __syncthreads();
+    if (S > 1)
+        cluster_sync(); // every rank's barriers exist before any peer arrives on them
+    griddepcontrol_wait(); // q, K and V are written by earlier kernels
+
+    const int row0 = sh * p.keys + kbeg; // first K/V row of this CTA
+    const int total = 2 * nchunks;       // K chunks, then V chunks
+
+    if (warp == kConsumerWarps) {
+        // ---------------- producer (one thread) ----------------
+        if (lane == 0) {
+            int issued = 0;
+            for (int c = 0; c < total; ++c, ++issued) {
+                const int st = c % depth;
+                if (!mbar_wait(bar_empty + 8 * st, ((c / depth) & 1u) ^ 1u, kSiteProducerEmpty))
+                    break;
+                mbar_arrive_expect_tx(bar_full + 8 * st, kStageBytes);
+                const int kc = c < nchunks ? c : c - nchunks;
+                tma_load_2d(ring + st * kStageBytes, c < nchunks ? &tm_k : &tm_v, bar_full + 8 * st, 0,
+                            row0 + kc * kChunk);
+            }
+            // Every issued load lands before shared memory is released.
+            for (int c = issued > depth ? issued - depth : 0; c < issued; ++c)
+                for (int tries = 0; tries < (1 << 22) &&
+                                    !mbar_try_wait(bar_full + 8 * (c % depth), (c / depth) & 1u);
+                     ++tries) {
+                }
+        }
+    } else {
+        const int g = lane >> 2, tig = lane & 3;
+        // Q' = half(q * c) as MMA A fragments (rows = query rows, K = 64 dims in 4 steps).
+        uint32_t qa[4][4];
+        {
+            const uint16_t *q0 = p.q + static_cast<size_t>(stream * p.queries + g) * width + head * kDim;
+            const uint16_t *q8 = q0 + static_cast<size_t>(8) * width;
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+                const int col = ks * 16 + 2 * tig;
+                qa[ks][0] = g < p.queries ? *reinterpret_cast<const uint32_t *>(q0 + col) : 0u;
+                qa[ks][1] = g + 8 < p.queries ? *reinterpret_cast<const uint32_t *>(q8 + col) : 0u;
+                qa[ks][2] = g < p.queries ? *reinterpret_cast<const uint32_t *>(q0 + col + 8) : 0u;
+                qa[ks][3] = g + 8 < p.queries ? *reinterpret_cast<const uint32_t *>(q8 + col + 8) : 0u;
+#pragma unroll
+                for (int r = 0; r < 4; ++r)
+                    qa[ks][r] = gemm::hmul2_rn(qa[ks][r], p.scale2);
+            }
+        }
+        bool ok = true;
+        // ---------------- pass 1: scores = half(Q' K'^T) over this CTA's keys ----------------
+        for (int c = 0; c < nchunks; ++c) {
+            const int st = c % depth;
+            ok = ok && __all_sync(0xffffffffu, mbar_wait(bar_full + 8 * st, (c / depth) & 1u, kSiteMmaFull));
+            const int kc = lk - c * kChunk < kChunk ? lk - c * kChunk : kChunk;
+            const uint32_t stage = ring + st * kStageBytes;
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                const int kb = warp * 16 + nt * 8; // first key of this 8-key n-tile
+                if (!ok || kb >= kc)
+                    continue;
+                uint32_t b[8];
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    // matrices (k-step 2*half + (i >> 1), 8-dim chunk i & 1) for lanes 8i..8i+7
+                    const int mi = lane >> 3, key = kb + (lane & 7);
+                    const int chunk16 = 2 * (2 * half + (mi >> 1)) + (mi & 1);
+                    uint32_t r[4];
+                    ldmatrix_x4(stage + key * 128 + ((chunk16 ^ (key & 7)) << 4), r);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        b[4 * half + i] = gemm::hmul2_rn(r[i], p.scale2); // K' = half(k * c)
+                }
+                float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks)
+                    mma_m16n8k16_f16_f32(acc, qa[ks], b[2 * ks], b[2 * ks + 1]);
+                const int key = c * kChunk + kb + 2 * tig;
+                const uint32_t lo = gemm::cvt_f16x2(acc[0], acc[1]), hi = gemm::cvt_f16x2(acc[2], acc[3]);
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    if (key + e >= lk)
+                        continue;
+                    if (g < p.queries)
+                        scores[g * p.pstride + key + e] = static_cast<uint16_t>(lo >> (16 * e));
+                    if (g + 8 < p.queries)
+                        scores[(g + 8) * p.pstride + key + e] = static_cast<uint16_t>(hi >> (16 * e));
+                }
+            }
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(bar_empty + 8 * st);
+        }
+        named_barrier_sync(1, kConsumers);
+        // ---------------- softmax over all keys of the head ----------------
+        if (S == 1) {
+            // The CTA holds every key: p = half(exp(s - max) / sum) from its own rows.
+            for (int row = warp; row < p.queries; row += kConsumerWarps) {
+                uint16_t *sr = scores + row * p.pstride;
+                float mx = -INFINITY;
+                for (int j = lane; j < lk; j += 32)
+                    mx = fmaxf(mx, h2f(sr[j]));
+                mx = warp_max(mx);
+                float sum = 0.0f;
+                for (int j = lane; j < lk; j += 32)
+                    sum += expf(h2f(sr[j]) - mx);
+                sum = norm::warp_sum(sum);
+                for (int j = lane; j < lk; j += 32)
+                    sr[j] = f2h_rn(__fdiv_rn(expf(h2f(sr[j]) - mx), sum));
+            }
+        } else {
+        // Row maxima of this CTA's keys, pushed to every rank: xch[kXMax][rank][row].
+        for (int row = warp; row < kMaxQueries; row += kConsumerWarps) {
+            float mx = -INFINITY;
+            if (row < p.queries)
+                for (int j = lane; j < lk; j += 32)
+                    mx = fmaxf(mx, h2f(scores[row * p.pstride + j]));
+            mx = warp_max(mx);
+            if (lane < S)
+                st_shared_cluster_f32(map_to_rank(xch_s + kXMax + (rank * kMaxQueries + row) * 4, lane), mx);
+        }
+        fence_cluster();
+        named_barrier_sync(1, kConsumers);
+        if (threadIdx.x < S)
+            mbar_arrive_cluster(map_to_rank(bar_max, threadIdx.x));
+        ok = ok && __all_sync(0xffffffffu, mbar_wait_cluster(bar_max, 0, kSiteClusterExchange));
+        for (int row = warp; row < kMaxQueries; row += kConsumerWarps) {
+            float mx = -INFINITY;
+            for (int r = 0; r < S; ++r)
+                mx = fmaxf(mx, xch[kXMax / 4 + r * kMaxQueries + row]);
+            float sum = 0.0f;
+            if (row < p.queries && mx != -INFINITY)
+                for (int j = lane; j < lk; j += 32)
+                    sum += expf(h2f(scores[row * p.pstride + j]) - mx);
+            sum = norm::warp_sum(sum);
+            if (lane < S)
+                st_shared_cluster_f32(map_to_rank(xch_s + kXSum + (rank * kMaxQueries + row) * 4, lane), sum);
+        }
+        fence_cluster();
+        named_barrier_sync(1, kConsumers);
+        if (threadIdx.x < S)
+            mbar_arrive_cluster(map_to_rank(bar_sum, threadIdx.x));
+        ok = ok && __all_sync(0xffffffffu, mbar_wait_cluster(bar_sum, 0, kSiteClusterExchange));
+        // p = half(exp(s - max) / sum), the sum over ranks taken in rank order.
+        for (int row = warp; row < p.queries; row += kConsumerWarps) {
+            float mx = -INFINITY, sum = 0.0f;
+            for (int r = 0; r < S; ++r) {
+                mx = fmaxf(mx, xch[kXMax / 4 + r * kMaxQueries + row]);
+                sum += xch[kXSum / 4 + r * kMaxQueries + row];
+            }
+            for (int j = lane; j < lk; j += 32)
+                scores[row * p.pstride + j] =
+                    f2h_rn(__fdiv_rn(expf(h2f(scores[row * p.pstride + j]) - mx), sum));
+        }
+        }
+        named_barrier_sync(1, kConsumers);
+        // ---------------- pass 2: this CTA's P.V, warp w owns columns 8w..8w+7 ----------------
+        float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int c = 0; c < nchunks; ++c) {
+            const int seq = nchunks + c, st = seq % depth;
+            ok = ok && __all_sync(0xffffffffu, mbar_wait(bar_full + 8 * st, (seq / depth) & 1u, kSiteMmaFull));
+            const int kc = lk - c * kChunk < kChunk ? lk - c * kChunk : kChunk;
+            const uint32_t stage = ring + st * kStageBytes;
+            const int steps = ok ? (kc + 15) / 16 : 0;
+            for (int ks = 0; ks < steps; ++ks) {
+                uint32_t a[4], bv[2];
+                {
+                    const int mi = lane >> 3, r = lane & 7;
+                    const int row = r + (mi & 1) * 8, key = c * kChunk + ks * 16 + (mi >> 1) * 8;
+                    ldmatrix_x4(row < p.queries ? scores_s + static_cast<uint32_t>((row * p.pstride + key) * 2) : zero_s, a);
+                }
+                {
+                    const int key = ks * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+                    ldmatrix_x2_trans(stage + key * 128 + ((warp ^ (key & 7)) << 4), bv);
+                }
+                mma_m16n8k16_f16_f32(o, a, bv[0], bv[1]);
+            }
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(bar_empty + 8 * st);
+        }
+        const float scale = p.code_scale_ptr ? *p.code_scale_ptr : p.code_scale;
+        const float recip = p.code_scale_ptr ? __frcp_rn(scale) : p.code_recip;
+        const uint64_t neg_scale2 = f2_bits(-scale, -scale), recip2 = f2_bits(recip, recip);
+        auto store_pair = [&](int row, int col, float v0, float v1) {
+            const uint32_t pair = gemm::cvt_f16x2(v0, v1);
+            const size_t idx = static_cast<size_t>(stream * p.queries + row) * width + head * kDim + col;
+            if (p.out)
+                *reinterpret_cast<uint32_t *>(p.out + idx) = pair;
+            if (p.codes)
+                *reinterpret_cast<uint16_t *>(p.codes + idx) =
+                    static_cast<uint16_t>(e4m3x2_quotient(pair, neg_scale2, recip2));
+        };
+        if (S == 1) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e)
+                if (ok && g + 8 * e < p.queries)
+                    store_pair(g + 8 * e, warp * 8 + 2 * tig, o[2 * e], o[2 * e + 1]);
+        } else {
+        // Parts of P.V go to the owner of their columns: rank r owns 64/S columns.
+        const int cols_per = kDim / S;
+        const int owner = (warp * 8) / cols_per;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int row = g + 8 * e;
+            const int col = warp * 8 + 2 * tig;
+            if (row >= p.queries)
+                continue;
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const uint32_t dst = xch_s + kXOut + ((rank * p.queries + row) * kDim + col + i) * 4;
+                st_shared_cluster_f32(map_to_rank(dst, static_cast<uint32_t>(owner)), o[2 * e + i]);
+            }
+        }
+        fence_cluster();
+        named_barrier_sync(1, kConsumers);
+        if (threadIdx.x < S)
+            mbar_arrive_cluster(map_to_rank(bar_out, threadIdx.x));
+        ok = ok && __all_sync(0xffffffffu, mbar_wait_cluster(bar_out, 0, kSiteClusterExchange));
+        // My columns [rank*cols_per, +cols_per) for every query row: sum the parts in rank order.
+        for (int e = threadIdx.x; ok && e < p.queries * (cols_per / 2); e += kConsumers) {
+            const int row = e / (cols_per / 2);
+            const int col = rank * cols_per + 2 * (e % (cols_per / 2));
+            float s0 = 0.0f, s1 = 0.0f;
+            for (int r = 0; r < S; ++r) {
+                s0 += xch[kXOut / 4 + (r * p.queries + row) * kDim + col];
+                s1 += xch[kXOut / 4 + (r * p.queries + row) * kDim + col + 1];
+            }
+            store_pair(row, col, s0, s1);
+        }
+        }
+    }
+    __syncthreads();
+    if (S > 1)
+        cluster_sync(); // no CTA leaves while stores to its peers may be in flight
+}
+
+} // namespace attn
 
 // ---------------------------------------------------------------------------
 // fp16 single-token projections (the reference plugins' kernels on sm_100a).
@@ -1698,6 +2071,90 @@ cudaError_t launch_layer_norm(const LayerNormLaunch &L, cudaStream_t stream)
         err = cudaLaunchKernelEx(&config, norm::layer_norm_kernel<8>, p);
     else
         err = cudaLaunchKernelEx(&config, norm::layer_norm_kernel<16>, p);
+    count_launch();
+    return err != cudaSuccess ? err : cudaGetLastError();
+}
+
+cudaError_t launch_cross_attention(const CrossAttentionLaunch &L, cudaStream_t stream)
+{
+    attn::Params p{};
+    p.streams = L.streams;
+    p.queries = L.queries;
+    p.heads = L.heads;
+    p.keys = L.keys;
+    // CTAs per (stream, head) and ring depth: the most CTAs (each keeping at
+    // least 128 keys) that run in one wave given how many fit an SM's shared
+    // memory, the deeper ring when both depths fit.
+    const int pairs = L.streams * L.heads;
+    auto kpc_for = [&](int cl) { return ((L.keys + cl - 1) / cl + 15) / 16 * 16; };
+    auto per_sm = [&](int cl, int st) {
+        const int bytes = attn::smem_bytes(st, L.queries, kpc_for(cl) + 8, cl) + 1024; // + the per-CTA reserve
+        return std::max(1, 233472 / bytes);
+    };
+    int S = 1, stages = attn::kMaxStages;
+    for (int cl = 1; cl <= attn::kMaxCluster; cl *= 2) {
+        if (cl > 1 && (L.keys + cl - 1) / cl < attn::kChunk)
+            break;
+        if (kpc_for(cl) > kAttentionMaxKeysPerCta)
+            continue;
+        for (int st = attn::kMaxStages; st >= 3; --st)
+            if (static_cast<int64_t>(pairs) * cl <= static_cast<int64_t>(per_sm(cl, st)) * sm_count()) {
+                S = cl;
+                stages = st;
+                break;
+            }
+    }
+    while (kpc_for(S) > kAttentionMaxKeysPerCta && S < attn::kMaxCluster)
+        S *= 2;
+    p.cluster = S;
+    p.stages = stages;
+    p.kpc = ((L.keys + S - 1) / S + 15) / 16 * 16;
+    p.pstride = p.kpc + 8;
+    p.score_bytes = attn::score_bytes(L.queries, p.pstride);
+    p.xch_bytes = attn::xch_bytes(L.queries, S);
+    p.q = L.q;
+    p.out = L.out;
+    const uint16_t c = __half_as_ushort(__float2half_rn(static_cast<float>(std::pow(double(attn::kDim), -0.25))));
+    p.scale2 = static_cast<uint32_t>(c) * 0x10001u;
+    p.code_scale = L.code_scale;
+    p.code_recip = L.codes && !L.code_scale_ptr ? static_cast<float>(1.0 / static_cast<double>(L.code_scale)) : 0.0f;
+    p.code_scale_ptr = L.code_scale_ptr;
+    p.codes = L.codes;
+    const int64_t rows = static_cast<int64_t>(L.streams) * L.heads * L.keys;
+    CUtensorMap tm_k{}, tm_v{};
+    if (!make_map(&tm_k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.k, rows, attn::kDim, attn::kDim, attn::kChunk,
+                  CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&tm_v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.v, rows, attn::kDim, attn::kDim, attn::kChunk,
+                  CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    const int smem = attn::smem_bytes(p.stages, L.queries, p.pstride, S);
+    // The attribute is set once, for the largest shared memory the launcher picks.
+    constexpr int kMaxSmem =
+        attn::smem_bytes(attn::kMaxStages, attn::kMaxQueries, kAttentionMaxKeysPerCta + 8, attn::kMaxCluster);
+    static_assert(kMaxSmem <= 232448, "shared memory budget");
+    const cudaError_t attr = ensure_smem(attn::cross_attention_kernel, kMaxSmem);
+    if (attr != cudaSuccess)
+        return attr;
+    cudaLaunchConfig_t config{};
+    config.gridDim = dim3(static_cast<unsigned>(pairs * S));
+    config.blockDim = dim3(attn::kThreads);
+    config.dynamicSmemBytes = smem;
+    config.stream = stream;
+    cudaLaunchAttribute attrs[2];
+    int count = 0;
+    attrs[count].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[count].val.programmaticStreamSerializationAllowed = 1;
+    ++count;
+    if (S > 1) {
+        attrs[count].id = cudaLaunchAttributeClusterDimension;
+        attrs[count].val.clusterDim.x = static_cast<unsigned>(S);
+        attrs[count].val.clusterDim.y = 1;
+        attrs[count].val.clusterDim.z = 1;
+        ++count;
+    }
+    config.attrs = attrs;
+    config.numAttrs = count;
+    const cudaError_t err = cudaLaunchKernelEx(&config, attn::cross_attention_kernel, tm_k, tm_v, p);
     count_launch();
     return err != cudaSuccess ? err : cudaGetLastError();
 }

@@ -47,6 +47,19 @@ struct LayerNormLaunch {
     uint8_t *codes;
 };
 cudaError_t launch_layer_norm(const LayerNormLaunch &p, cudaStream_t stream);
+// Decoder cross-attention over a cached encoder K/V (head_dim 64).
+constexpr int kAttentionMaxQueries = 16;
+constexpr int kAttentionMaxKeys = 4096;
+constexpr int kAttentionMaxKeysPerCta = 2048; // score rows in shared memory
+struct CrossAttentionLaunch {
+    int streams, queries, heads, keys;
+    const uint16_t *q, *k, *v;
+    uint16_t *out;
+    float code_scale;
+    const float *code_scale_ptr;
+    uint8_t *codes;
+};
+cudaError_t launch_cross_attention(const CrossAttentionLaunch &p, cudaStream_t stream);
 cudaError_t launch_quantize(const uint16_t *x, int64_t count, float scale, const float *scale_ptr,
                             uint8_t *codes, cudaStream_t stream);
 cudaError_t launch_quantize_rows(const uint16_t *w, int64_t rows, int64_t cols,

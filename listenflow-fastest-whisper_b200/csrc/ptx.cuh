@@ -20,6 +20,7 @@ enum WaitSite : int {
     kSiteMmaAccEmpty = 3,
     kSiteEpilogueAccFull = 4,
     kSiteDrain = 5,
+    kSiteClusterExchange = 6,
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p)
@@ -326,6 +327,17 @@ __device__ __forceinline__ void cluster_sync()
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// The two halves of cluster_sync, for work between arriving and waiting.
+__device__ __forceinline__ void cluster_arrive()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait()
+{
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // Address of the same shared-memory offset in CTA `rank` of this cluster.
 __device__ __forceinline__ uint32_t map_to_rank(uint32_t smem_addr, uint32_t rank)
 {
@@ -338,6 +350,49 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t smem_addr, uint32_t ran
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar)
 {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+// Orders this thread's prior shared/global accesses (including stores to
+// peers' shared memory) before its later ones, at cluster scope.
+__device__ __forceinline__ void fence_cluster()
+{
+    asm volatile("fence.acq_rel.cluster;" ::: "memory");
+}
+
+// Store into another CTA's shared memory (a cluster address from map_to_rank).
+__device__ __forceinline__ void st_shared_cluster_f32(uint32_t cluster_addr, float v)
+{
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
+}
+
+// Parity wait with cluster-scope acquire: stores that peers made before their
+// release.cluster arrivals on this barrier are visible after it returns.
+// Bounded like mbar_wait.
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int site,
+                                                  uint64_t limit_ns = 2000000000ull)
+{
+    uint64_t start = 0;
+    for (uint32_t spin = 0;; ++spin) {
+        uint32_t done;
+        asm volatile("{\n\t.reg .pred p;\n\t"
+                     "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+                     "selp.u32 %0, 1, 0, p;\n\t}"
+                     : "=r"(done)
+                     : "r"(bar), "r"(parity)
+                     : "memory");
+        if (done)
+            return true;
+        if (spin == 0)
+            start = global_timer_ns();
+        if ((spin & 255u) == 255u) {
+            if (*reinterpret_cast<volatile int *>(&g_device_error) != 0)
+                return false;
+            if (global_timer_ns() - start > limit_ns) {
+                atomicCAS(&g_device_error, 0, site);
+                return false;
+            }
+        }
+    }
 }
 
 // TMA load into this CTA's shared memory whose completion is counted on an
@@ -392,6 +447,35 @@ __device__ __forceinline__ void mma_commit_pair_both(uint32_t bar)
 __device__ __forceinline__ void mma_commit_pair_local(uint32_t bar)
 {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Warp-level fp16 MMA (m16n8k16, fp32 accumulate) and its shared-memory
+// fragment loads, for the small attention products.
+
+// Four 8x8 fp16 matrices; lanes 8i..8i+7 give the row addresses of matrix i.
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t (&r)[4])
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+// Two 8x8 fp16 matrices, transposed on the way (lanes 0-15 give row addresses).
+__device__ __forceinline__ void ldmatrix_x2_trans(uint32_t addr, uint32_t (&r)[2])
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
+                 : "=r"(r[0]), "=r"(r[1])
+                 : "r"(addr));
+}
+
+// d += a (16x16, row) * b (16x8, col), fp16 inputs, fp32 accumulators.
+__device__ __forceinline__ void mma_m16n8k16_f16_f32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+                 "{%8, %9}, {%0, %1, %2, %3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 } // namespace lffw

@@ -125,6 +125,39 @@ def layer_norm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: fl
     return total, y, codes
 
 
+def cross_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, queries: int, *, code_scale=None,
+                    want_out: bool = True, stream=None):
+    """Decoder cross-attention over cached encoder K/V (network_graph.cpp:235-244, 401-404).
+
+    q: fp16 [streams * queries, heads * 64] (q_proj output, beams of a stream adjacent);
+    k, v: fp16 [streams, heads, keys, 64].  Returns (out, codes): out fp16 like q
+    (out_proj's input), and its E4M3 codes when `code_scale` is given."""
+    for t, name in ((q, "q"), (k, "k"), (v, "v")):
+        _require(t, torch.float16, name)
+    if k.dim() != 4 or v.shape != k.shape:
+        raise ValueError("k and v must be [streams, heads, keys, head_dim] of one shape")
+    streams, heads, keys, dim = k.shape
+    if q.shape != (streams * queries, heads * dim):
+        raise ValueError("q must be [streams * queries, heads * head_dim]")
+    a = native.CrossAttentionArgs()
+    a.struct_size = ctypes.sizeof(native.CrossAttentionArgs)
+    a.streams, a.queries, a.heads, a.head_dim, a.keys = streams, queries, heads, dim, keys
+    a.q, a.k, a.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
+    out = torch.empty_like(q) if want_out else None
+    codes = None
+    if code_scale is not None:
+        codes = torch.empty(q.shape, dtype=torch.uint8, device=q.device)
+        if isinstance(code_scale, torch.Tensor):
+            _require(code_scale, torch.float32, "code_scale")
+            a.code_scale_ptr = code_scale.data_ptr()
+        else:
+            a.code_scale = float(code_scale)
+        a.out_codes = codes.data_ptr()
+    a.out = out.data_ptr() if out is not None else None
+    native.check(native.library().lffw_cross_attention(ctypes.byref(a), _stream(stream)), "lffw_cross_attention")
+    return out, codes
+
+
 def quantize_rows(w: torch.Tensor, scales: torch.Tensor, stream=None) -> torch.Tensor:
     """E4M3 codes of an fp16 [N, K] weight with one scale per row."""
     _require(w, torch.float16, "w")

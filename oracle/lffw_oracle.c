@@ -159,6 +159,60 @@ void oracle_layer_norm(const uint16_t *x, const uint16_t *residual, int64_t rows
     free(s);
 }
 
+void oracle_cross_attention(const uint16_t *q, const uint16_t *k, const uint16_t *v, int streams, int queries,
+                            int heads, int dim, int keys, uint16_t *out, float code_scale, uint8_t *codes)
+{
+    const uint16_t c = oracle_half_from_float((float)pow((double)dim, -0.25));
+    const double cd = oracle_half_to_double(c);
+    const int width = heads * dim;
+    double *qs = (double *)malloc((size_t)dim * sizeof(double));
+    double *score = (double *)malloc((size_t)keys * sizeof(double));
+    if (!qs || !score) {
+        free(qs);
+        free(score);
+        return;
+    }
+    for (int s = 0; s < streams; ++s)
+        for (int h = 0; h < heads; ++h) {
+            const uint16_t *kh = k + ((size_t)s * heads + h) * (size_t)keys * dim;
+            const uint16_t *vh = v + ((size_t)s * heads + h) * (size_t)keys * dim;
+            for (int t = 0; t < queries; ++t) {
+                const size_t row = (size_t)s * queries + t;
+                for (int d = 0; d < dim; ++d)
+                    qs[d] = oracle_half_to_double(
+                        oracle_half_from_double(oracle_half_to_double(q[row * width + h * dim + d]) * cd));
+                double best = -INFINITY;
+                for (int j = 0; j < keys; ++j) {
+                    double acc = 0.0; /* products of halves are exact in binary64; the sum rounds little */
+                    for (int d = 0; d < dim; ++d)
+                        acc += qs[d] * oracle_half_to_double(
+                                           oracle_half_from_double(oracle_half_to_double(kh[(size_t)j * dim + d]) * cd));
+                    score[j] = oracle_half_to_double(oracle_half_from_double(acc));
+                    if (score[j] > best)
+                        best = score[j];
+                }
+                double total = 0.0;
+                for (int j = 0; j < keys; ++j) {
+                    score[j] = exp(score[j] - best);
+                    total += score[j];
+                }
+                for (int j = 0; j < keys; ++j)
+                    score[j] = oracle_half_to_double(oracle_half_from_double(score[j] / total));
+                for (int d = 0; d < dim; ++d) {
+                    double acc = 0.0;
+                    for (int j = 0; j < keys; ++j)
+                        acc += score[j] * oracle_half_to_double(vh[(size_t)j * dim + d]);
+                    const uint16_t o = oracle_half_from_double(acc);
+                    out[row * width + h * dim + d] = o;
+                    if (codes)
+                        codes[row * width + h * dim + d] = quantize_one(o, code_scale);
+                }
+            }
+        }
+    free(qs);
+    free(score);
+}
+
 void oracle_quantize_rows(const uint16_t *x, int64_t rows, int64_t cols, const float *scales,
                           uint8_t *codes)
 {

@@ -73,6 +73,20 @@ void oracle_layer_norm(const uint16_t *x, const uint16_t *residual, int64_t rows
                        const float *gamma, const float *beta, float eps, uint16_t *sum_out, uint16_t *y,
                        float code_scale, uint8_t *codes);
 
+/* Decoder cross-attention over a cached encoder K/V (cpp/src/network_graph.cpp:235-244
+ * `attend`, with the cross-K/V cache of :401-404), per stream s, head h and query row t:
+ *   c        = half(head_dim^-0.25)
+ *   q'[d]    = half(q[s,t][h*dim + d] * c),  k'[j][d] = half(k[s][h][j][d] * c)
+ *   score[j] = half(sum_d q'[d] k'[j][d])                  (fp16 MatMul output, exact sum)
+ *   p[j]     = half(exp(score[j] - max) / sum_i exp(score[i] - max))   (fp32 softmax -> half)
+ *   out[s,t][h*dim + d] = half(sum_j p[j] v[s][h][j][d])   (fp16 MatMul output, exact sum)
+ *   codes    = e4m3(fp32(out / code_scale))                 (if codes)
+ * q / out: fp16 [streams * queries, heads * dim] (row s * queries + t); k, v: fp16
+ * [streams, heads, keys, dim].  The softmax is evaluated in binary64 and rounded once:
+ * the value TensorRT's fp32 softmax approximates. */
+void oracle_cross_attention(const uint16_t *q, const uint16_t *k, const uint16_t *v, int streams, int queries,
+                            int heads, int dim, int keys, uint16_t *out, float code_scale, uint8_t *codes);
+
 /* fp16(erf(x)) of an fp16 x, erf in binary64, round to nearest even. */
 uint16_t oracle_erf_fp16(uint16_t x);
 /* GELU on an fp16 value with every graph edge rounded to fp16. */

@@ -58,6 +58,10 @@ def lib() -> ctypes.CDLL:
             _u16p, _u16p, ctypes.c_int64, ctypes.c_int64, _f32p, _f32p, ctypes.c_float, _u16p, _u16p,
             ctypes.c_float, _u8p,
         ]
+        L.oracle_cross_attention.argtypes = [
+            _u16p, _u16p, _u16p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _u16p,
+            ctypes.c_float, _u8p,
+        ]
         L.oracle_erf_fp16.argtypes = [ctypes.c_uint16]
         L.oracle_erf_fp16.restype = ctypes.c_uint16
         _lib = L
@@ -143,6 +147,20 @@ def layer_norm(x, gamma, beta, eps: float = 1e-5, residual=None, code_scale=None
                             float(np.float32(code_scale)) if code_scale is not None else 1.0,
                             _ptr(codes, _u8p))
     return s, y, codes
+
+
+def cross_attention(q, k, v, queries: int, code_scale=None):
+    """(out, codes) of the decoder cross-attention (network_graph.cpp:235-244, 401-404):
+    q [streams * queries, heads * dim], k/v [streams, heads, keys, dim] fp16."""
+    qb, kb, vb = bits16(q), bits16(k), bits16(v)
+    streams, heads, keys, dim = kb.shape
+    assert vb.shape == kb.shape and qb.shape == (streams * queries, heads * dim)
+    out = np.empty(qb.shape, np.uint16)
+    codes = np.empty(qb.shape, np.uint8) if code_scale is not None else None
+    lib().oracle_cross_attention(_ptr(qb, _u16p), _ptr(kb, _u16p), _ptr(vb, _u16p), streams, queries, heads, dim,
+                                 keys, _ptr(out, _u16p),
+                                 float(np.float32(code_scale)) if code_scale is not None else 1.0, _ptr(codes, _u8p))
+    return out, codes
 
 
 def quantize_rows(w, scales) -> np.ndarray:

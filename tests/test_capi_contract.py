@@ -103,6 +103,33 @@ def test_layer_norm_abi_mismatch_and_null(native, lib):
     assert lib.lffw_layer_norm(None, None) == native.INVALID_ARGUMENT
 
 
+def _attn_args(native, **over):
+    a = native.CrossAttentionArgs()
+    a.struct_size = ctypes.sizeof(native.CrossAttentionArgs)
+    a.streams, a.queries, a.heads, a.head_dim, a.keys = 4, 5, 20, 64, 1500
+    a.q, a.k, a.v, a.out = 0x10000, 0x20000, 0x30000, 0x40000
+    for key, value in over.items():
+        setattr(a, key, value)
+    return a
+
+
+@pytest.mark.parametrize("change", [
+    {"head_dim": 128}, {"queries": 0}, {"queries": 17}, {"keys": 0}, {"keys": 4097}, {"streams": 0},
+    {"heads": 0}, {"streams": 2**20, "heads": 2**10}, {"q": None}, {"k": None}, {"v": None}, {"out": None},
+    {"q": 0x10002}, {"v": 0x30008}, {"out_codes": 0x50000, "code_scale": 0.0},
+])
+def test_cross_attention_rejects_invalid_arguments(native, lib, change):
+    a = _attn_args(native, **change)
+    assert lib.lffw_cross_attention(ctypes.byref(a), None) == native.INVALID_ARGUMENT
+
+
+def test_cross_attention_abi_mismatch_and_null(native, lib):
+    a = _attn_args(native)
+    a.struct_size = 16
+    assert lib.lffw_cross_attention(ctypes.byref(a), None) == native.ABI_MISMATCH
+    assert lib.lffw_cross_attention(None, None) == native.INVALID_ARGUMENT
+
+
 def test_device_gate_without_sm100(native, lib):
     import torch
 

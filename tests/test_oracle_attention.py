@@ -1,0 +1,47 @@
+"""The oracle's decoder cross-attention (cpp/src/network_graph.cpp:235-244 `attend`
+over the cross-K/V cache of :401-404) against an independent float64 restatement
+with torch: half(q*c), half(k*c), fp16 scores, softmax rounded to fp16, fp16 output."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from helpers import halves
+
+
+def _reference(q, k, v, queries):
+    import torch
+
+    streams, heads, keys, dim = k.shape
+    c = np.float16(dim ** -0.25)
+    qs = (q.astype(np.float32) * np.float32(c)).astype(np.float16).astype(np.float64)
+    qs = qs.reshape(streams, queries, heads, dim).transpose(0, 2, 1, 3)
+    ks = (k.astype(np.float32) * np.float32(c)).astype(np.float16).astype(np.float64)
+    scores = np.einsum("shtd,shjd->shtj", qs, ks).astype(np.float16).astype(np.float64)
+    p = torch.softmax(torch.from_numpy(scores), -1).numpy().astype(np.float16).astype(np.float64)
+    out = np.einsum("shtj,shjd->shtd", p, v.astype(np.float64)).astype(np.float16)
+    return out.transpose(0, 2, 1, 3).reshape(streams * queries, heads * dim)
+
+
+@pytest.mark.parametrize("streams,queries,heads,keys", [(1, 1, 2, 7), (2, 5, 3, 130), (1, 16, 1, 257)])
+def test_cross_attention_matches_float64_restatement(oracle, streams, queries, heads, keys):
+    rng = np.random.default_rng(streams * 100 + keys)
+    q = halves(rng, (streams * queries, heads * 64))
+    k = halves(rng, (streams, heads, keys, 64))
+    v = halves(rng, (streams, heads, keys, 64))
+    out, codes = oracle.cross_attention(q, k, v, queries, code_scale=0.004)
+    np.testing.assert_array_equal(out, _reference(q, k, v, queries).view(np.uint16))
+    np.testing.assert_array_equal(codes, oracle.quantize(out, np.float32(0.004)))
+
+
+def test_uniform_scores_average_the_values(oracle):
+    """Identical keys give equal probabilities: the output is the mean of v (here
+    all v rows equal, so out = v exactly)."""
+    q = np.ones((1, 64), np.float16)
+    k = np.ones((1, 1, 10, 64), np.float16)
+    v = np.tile(np.linspace(-2, 2, 64, dtype=np.float16), (1, 1, 10, 1))
+    out, _ = oracle.cross_attention(q, k, v, 1)
+    # p = half(1/10) each; sum of 10 * half(0.1) * v differs from v by the rounding of 0.1
+    expected = (np.float64(np.float16(0.1)) * 10 * v[0, 0, 0].astype(np.float64)).astype(np.float16)
+    np.testing.assert_array_equal(out[0], expected.view(np.uint16))
