@@ -72,8 +72,9 @@ def parse_args(argv=None):
                    help="timed replays of the C3 decoder-step graph (0 skips it)")
     p.add_argument("--decoder-layers", type=int, default=32,
                    help="decoder layers in the C3 step (32 is the measured configuration)")
-    p.add_argument("--only", choices=("all", "decoder"), default="all",
-                   help="'decoder': run only the C3 decoder step and print its line (profiling)")
+    p.add_argument("--only", choices=("all", "c2", "ln", "attention", "decoder"), default="all",
+                   help="run one section alone and print its line (profiling): 'c2' the timed C2 steps, "
+                        "'ln' the LayerNorm producer, 'attention' the cross-attention, 'decoder' the C3 step")
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="target CPU-baseline sample time (0 skips the CPU baseline, for profiling runs)")
     return p.parse_args(argv)
@@ -342,10 +343,11 @@ def run_ours(args, rank, local_rank, world):
     e2e_ms = e_start.elapsed_time(e_end)
     np.testing.assert_array_equal(host_out["fc2"].numpy(), sets[(e2e_steps - 1) % 2][1]["fc2"].cpu().numpy())
 
-    ln = run_ln_producer(fp8, native, device, 20, seed=31 + rank)
-    attention = run_cross_attention(fp8, native, device, 10, seed=41 + rank)
+    full = args.only == "all" # 'c2': the timed C2 steps (and e2e) only
+    ln = run_ln_producer(fp8, native, device, 20, seed=31 + rank) if full else None
+    attention = run_cross_attention(fp8, native, device, 10, seed=41 + rank) if full else None
     decoder = None
-    if args.decoder_steps > 0:
+    if full and args.decoder_steps > 0:
         del flush, scrub
         decoder = run_decoder(fp8, native, device, args.decoder_steps, 3, seed=77 + rank,
                               layers_count=args.decoder_layers)
@@ -404,11 +406,12 @@ def run_ours(args, rank, local_rank, world):
             "gpu_launches": int(launches),
             "clocks": clocks.summary(),
         }
-        result["ln_producer"] = ln
-        result["cross_attention"] = attention
-        if args.decoder_steps > 0:
+        if full:
+            result["ln_producer"] = ln
+            result["cross_attention"] = attention
+        if decoder is not None:
             result["decoder_step"] = decoder
-        if world == 1 and args.cpu_seconds > 0:
+        if full and world == 1 and args.cpu_seconds > 0:
             result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     if dist is not None:
         dist.barrier()
@@ -502,17 +505,26 @@ def run_decoder(fp8, native, device, steps: int, warmup: int, seed: int, layers_
             "launches_per_step": launches_per_step}
 
 
-def run_decoder_only(args, local_rank):
-    """The C3 decoder step alone (1 GPU): eager warm-up steps, then timed graph replays."""
+def run_section_only(args, local_rank):
+    """One secondary section alone on one GPU (profiling): the C3 decoder step,
+    the LayerNorm producer or the cross-attention (--decoder-layers layers)."""
     import torch
 
     fp8 = importlib.import_module(PACKAGE + ".fp8")
     native = importlib.import_module(PACKAGE + "._native")
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    result = run_decoder(fp8, native, device, max(1, args.decoder_steps), max(1, args.warmup), seed=77,
-                         layers_count=args.decoder_layers)
-    result.update(metric="decoder-step weight streaming (C3)", n_gpus=1, higher_is_better=True, impl="ours")
+    if args.only == "decoder":
+        result = run_decoder(fp8, native, device, max(1, args.decoder_steps), max(1, args.warmup), seed=77,
+                             layers_count=args.decoder_layers)
+        result.update(metric="decoder-step weight streaming (C3)")
+    elif args.only == "ln":
+        result = run_ln_producer(fp8, native, device, max(1, args.steps), seed=31)
+        result.update(metric="LayerNorm producer HBM throughput")
+    else:
+        result = run_cross_attention(fp8, native, device, max(1, args.steps), seed=41, layers=args.decoder_layers)
+        result.update(metric="decoder cross-attention K/V throughput")
+    result.update(n_gpus=1, higher_is_better=True, impl="ours")
     return result
 
 
@@ -568,7 +580,7 @@ def run_ln_producer(fp8, native, device, reps: int, seed: int):
             "l2": "flushed before every launch (256 MiB written, then 256 MiB read)"}
 
 
-def run_cross_attention(fp8, native, device, steps: int, seed: int):
+def run_cross_attention(fp8, native, device, steps: int, seed: int, layers: int = DEC_LAYERS):
     """Decoder cross-attention over cached encoder K/V for all 32 layers of one
     decoder step, as one CUDA graph: C3 (4 streams x 5 beams) and C5 (16 greedy
     streams per GPU, 128 streams over 8 GPUs).  Each layer reads its own K/V
@@ -579,7 +591,6 @@ def run_cross_attention(fp8, native, device, steps: int, seed: int):
     results = {}
     for name, streams, queries in (("c3_4x5", 4, 5), ("c5_16x1", 16, 1)):
         g = torch.Generator(device=device).manual_seed(seed)
-        layers = DEC_LAYERS
         shape = (layers, streams, 20, 1500, 64)
         k = torch.randn(shape, generator=g, device=device).half()
         v = torch.randn(shape, generator=g, device=device).half()
@@ -620,8 +631,8 @@ def run_cross_attention(fp8, native, device, steps: int, seed: int):
                                       "peak_source": hbm[1], "unit": "GB/s", "frac": round(gbs / hbm[0], 4)}}
         del graph, k, v, q
         torch.cuda.empty_cache()
-    results["workload"] = ("decoder cross-attention, 20 heads x 1500 keys x 64, 32 layers per step (one graph), "
-                           "out_proj E4M3 codes out")
+    results["workload"] = (f"decoder cross-attention, 20 heads x 1500 keys x 64, {layers} layers per step "
+                           "(one graph), out_proj E4M3 codes out")
     return results
 
 
@@ -752,8 +763,8 @@ def main(argv=None):
     rank, local_rank, world = dist_env()
     if args.impl == "reference":
         result = run_reference(args, rank, world)
-    elif args.only == "decoder":
-        result = run_decoder_only(args, local_rank)
+    elif args.only in ("decoder", "ln", "attention"):
+        result = run_section_only(args, local_rank)
     else:
         result = run_ours(args, rank, local_rank, world)
     if result is not None and rank == 0:
