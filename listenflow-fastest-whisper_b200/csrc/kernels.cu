@@ -1182,18 +1182,33 @@ __device__ __forceinline__ float warp_sum(float v)
 
 // KV: 16-byte vectors (8 halves) per lane; the row (cols / 8 vectors) is spread
 // over the lanes, vector v on lane v % 32, held in registers between passes.
+// Warps loop over rows (grid-stride) and pull their next row into L2 first.
+__device__ __forceinline__ void prefetch_l2(const void *ptr)
+{
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+}
+
 template <int KV>
-__global__ void __launch_bounds__(kThreads) layer_norm_kernel(const Params p)
+__global__ void __launch_bounds__(kThreads, KV <= 5 ? 4 : 1) layer_norm_kernel(const Params p)
 {
     if (threadIdx.x == 0)
         griddepcontrol_launch_dependents();
     griddepcontrol_wait();
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
-    const int row = blockIdx.x * kRowsPerBlock + warp;
-    if (row >= p.rows)
-        return;
     const int vecs = p.cols / 8;
+    const int stride = static_cast<int>(gridDim.x) * kRowsPerBlock;
+    for (int row = blockIdx.x * kRowsPerBlock + warp; row < p.rows; row += stride) {
+    {
+        // The next row of this warp moves into L2 while this one is processed.
+        const int next = row + stride;
+        if (next < p.rows)
+            for (int c = lane; c < vecs; c += 32) {
+                prefetch_l2(p.x + static_cast<size_t>(next) * p.cols + 8 * c);
+                if (p.residual)
+                    prefetch_l2(p.residual + static_cast<size_t>(next) * p.cols + 8 * c);
+            }
+    }
     const size_t base = static_cast<size_t>(row) * p.cols;
     uint4 v[KV];
 #pragma unroll
@@ -1266,6 +1281,7 @@ __global__ void __launch_bounds__(kThreads) layer_norm_kernel(const Params p)
             const uint32_t hi = e4m3x4(out[2], out[3], lean, neg_scale2, recip2);
             asm volatile("st.global.v2.u32 [%0], {%1, %2};" ::"l"(p.codes + base + 8 * c), "r"(lo), "r"(hi) : "memory");
         }
+    }
     }
 }
 
@@ -2054,7 +2070,8 @@ cudaError_t launch_layer_norm(const LayerNormLaunch &L, cudaStream_t stream)
     p.codes = L.codes;
     const int per_lane = static_cast<int>((L.cols / 8 + 31) / 32);
     cudaLaunchConfig_t config{};
-    config.gridDim = dim3(static_cast<unsigned>((L.rows + norm::kRowsPerBlock - 1) / norm::kRowsPerBlock));
+    const int64_t row_blocks = (L.rows + norm::kRowsPerBlock - 1) / norm::kRowsPerBlock;
+    config.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>(row_blocks, static_cast<int64_t>(sm_count()) * 4)));
     config.blockDim = dim3(norm::kThreads);
     config.stream = stream;
     cudaLaunchAttribute attr[1];
