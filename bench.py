@@ -72,7 +72,7 @@ def parse_args(argv=None):
                    help="timed replays of the C3 decoder-step graph (0 skips it)")
     p.add_argument("--decoder-layers", type=int, default=32,
                    help="decoder layers in the C3 step (32 is the measured configuration)")
-    p.add_argument("--only", choices=("all", "c2", "ln", "attention", "decoder"), default="all",
+    p.add_argument("--only", choices=("all", "c2", "ln", "attention", "self_attention", "decoder"), default="all",
                    help="run one section alone and print its line (profiling): 'c2' the timed C2 steps, "
                         "'ln' the LayerNorm producer, 'attention' the cross-attention, 'decoder' the C3 step")
     p.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -346,6 +346,7 @@ def run_ours(args, rank, local_rank, world):
     full = args.only == "all" # 'c2': the timed C2 steps (and e2e) only
     ln = run_ln_producer(fp8, native, device, 20, seed=31 + rank) if full else None
     attention = run_cross_attention(fp8, native, device, 10, seed=41 + rank) if full else None
+    self_attn = run_self_attention(fp8, native, device, 10, seed=51 + rank) if full else None
     decoder = None
     if full and args.decoder_steps > 0:
         del flush, scrub
@@ -409,6 +410,7 @@ def run_ours(args, rank, local_rank, world):
         if full:
             result["ln_producer"] = ln
             result["cross_attention"] = attention
+            result["self_attention"] = self_attn
         if decoder is not None:
             result["decoder_step"] = decoder
         if full and world == 1 and args.cpu_seconds > 0:
@@ -521,9 +523,12 @@ def run_section_only(args, local_rank):
     elif args.only == "ln":
         result = run_ln_producer(fp8, native, device, max(1, args.steps), seed=31)
         result.update(metric="LayerNorm producer HBM throughput")
-    else:
+    elif args.only == "attention":
         result = run_cross_attention(fp8, native, device, max(1, args.steps), seed=41, layers=args.decoder_layers)
         result.update(metric="decoder cross-attention K/V throughput")
+    else:
+        result = run_self_attention(fp8, native, device, max(1, args.steps), seed=51)
+        result.update(metric="encoder self-attention TFLOP/s")
     result.update(n_gpus=1, higher_is_better=True, impl="ours")
     return result
 
@@ -634,6 +639,44 @@ def run_cross_attention(fp8, native, device, steps: int, seed: int, layers: int 
     results["workload"] = (f"decoder cross-attention, 20 heads x 1500 keys x 64, {layers} layers per step "
                            "(one graph), out_proj E4M3 codes out")
     return results
+
+
+def run_self_attention(fp8, native, device, steps: int, seed: int):
+    """Encoder self-attention for one layer at C2 shapes (8 streams x 1500 tokens x
+    20 heads), read in place from a fused QKV output.  Work: 4 * tokens^2 * 64 flops
+    per (stream, head) (QK^T and P.V); the kernel recomputes QK^T once more for the
+    exact fp16 probabilities, which the rate does not count."""
+    import torch
+
+    streams, tokens, heads = 8, 1500, 20
+    g = torch.Generator(device=device).manual_seed(seed)
+    qkv = torch.randn((streams * tokens, 3 * heads * 64), generator=g, device=device).half()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    for _ in range(3):
+        fp8.self_attention(qkv, streams, heads, code_scale=0.004, want_out=False)
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fp8.self_attention(qkv, streams, heads, code_scale=0.004, want_out=False)
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    if native.device_error() != 0:
+        raise RuntimeError("device-side wait timed out in the self-attention section")
+    ms = statistics.median(ts)
+    flops = 4 * tokens * tokens * 64 * heads * streams
+    tflops = flops / (ms / 1e3) / 1e12
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    return {"workload": "encoder self-attention, 8 streams x 1500 tokens x 20 heads x 64, one layer, "
+                        "out_proj E4M3 codes out (m16n8k16 fp16 MMAs)",
+            "ms": round(ms, 4), "flops": flops, "value": round(tflops, 1), "unit": "TFLOP/s (QK^T + P.V)",
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak,
+                         "peak_source": "measured dense bf16 of MEASURED_PEAKS.json (fp16 runs at the bf16 rate)",
+                         "unit": "TFLOP/s", "frac": round(tflops / peak, 4)}}
 
 
 def read_hbm_peak():
@@ -763,7 +806,7 @@ def main(argv=None):
     rank, local_rank, world = dist_env()
     if args.impl == "reference":
         result = run_reference(args, rank, world)
-    elif args.only in ("decoder", "ln", "attention"):
+    elif args.only in ("decoder", "ln", "attention", "self_attention"):
         result = run_section_only(args, local_rank)
     else:
         result = run_ours(args, rank, local_rank, world)

@@ -24,7 +24,7 @@
 #include <stdint.h>
 
 #define LFFW_FP8_ABI_MAJOR 1
-#define LFFW_FP8_ABI_MINOR 3
+#define LFFW_FP8_ABI_MINOR 4
 #define LFFW_FP8_API __attribute__((visibility("default")))
 #if defined(__cplusplus)
 #define LFFW_FP8_NOEXCEPT noexcept
@@ -163,6 +163,33 @@ typedef struct lffw_cross_attention_args {
 
 LFFW_FP8_API lffw_status lffw_cross_attention(const lffw_cross_attention_args *args,
                                               void *stream) LFFW_FP8_NOEXCEPT;
+
+/* Encoder self-attention for one layer (network_graph.cpp:235-247 `attention`: `attend`
+ * on the layer's own projections, no mask), with the same fp16 edges as
+ * lffw_cross_attention, per stream s over its `tokens` rows.  q, k and v are read in
+ * place: element (s * tokens + t, h * head_dim + d) of each lies at row
+ * s * tokens + t, column h * head_dim + d, with row strides q_ld, k_ld, v_ld
+ * (elements).  For the fused QKV linear output [rows, 3 * width], pass q = y,
+ * k = y + width, v = y + 2 * width and all strides 3 * width.  out: fp16
+ * [streams * tokens, heads * head_dim] (out_proj's input) and/or its E4M3 codes.
+ * Requirements: head_dim == 64; tokens >= 1; streams * tokens < 2^31; strides
+ * >= heads * 64 and multiples of 8; 16-byte aligned pointers; out and/or out_codes
+ * set; code_scale (or *code_scale_ptr) in [2^-125, 2^125]. */
+typedef struct lffw_self_attention_args {
+    size_t struct_size; /* sizeof(lffw_self_attention_args) */
+    int32_t streams, tokens, heads, head_dim;
+    const uint16_t *q;
+    const uint16_t *k;
+    const uint16_t *v;
+    int64_t q_ld, k_ld, v_ld;
+    uint16_t *out;
+    float code_scale;
+    const float *code_scale_ptr;
+    uint8_t *out_codes;
+} lffw_self_attention_args;
+
+LFFW_FP8_API lffw_status lffw_self_attention(const lffw_self_attention_args *args,
+                                             void *stream) LFFW_FP8_NOEXCEPT;
 
 /* Q of an fp16 [rows, cols] weight with one scale per row (the per-output-channel
  * weight Q of network_graph.cpp:140-152, axis 2 of the transposed constant). */

@@ -99,6 +99,26 @@ class CrossAttentionArgs(ctypes.Structure):
     ]
 
 
+class SelfAttentionArgs(ctypes.Structure):
+    _fields_ = [
+        ("struct_size", ctypes.c_size_t),
+        ("streams", ctypes.c_int32),
+        ("tokens", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("q", ctypes.c_void_p),
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("q_ld", ctypes.c_int64),
+        ("k_ld", ctypes.c_int64),
+        ("v_ld", ctypes.c_int64),
+        ("out", ctypes.c_void_p),
+        ("code_scale", ctypes.c_float),
+        ("code_scale_ptr", ctypes.c_void_p),
+        ("out_codes", ctypes.c_void_p),
+    ]
+
+
 class PluginField(ctypes.Structure):
     _fields_ = [
         ("name", ctypes.c_char_p),
@@ -153,6 +173,7 @@ def library() -> ctypes.CDLL:
         "lffw_fp8_quantize": ([_vp, _i64, ctypes.c_float, _vp, _vp, _vp], _i32),
         "lffw_layer_norm": ([ctypes.POINTER(LayerNormArgs), _vp], _i32),
         "lffw_cross_attention": ([ctypes.POINTER(CrossAttentionArgs), _vp], _i32),
+        "lffw_self_attention": ([ctypes.POINTER(SelfAttentionArgs), _vp], _i32),
         "lffw_fp8_quantize_rows": ([_vp, _i64, _i64, _vp, _vp, _vp], _i32),
         "lffw_fp8_weight_scales": ([_vp, _i64, _i64, _vp, _vp], _i32),
         "lffw_fp8_dynamic_scale": ([_vp, _i64, _vp, _vp, _vp], _i32),

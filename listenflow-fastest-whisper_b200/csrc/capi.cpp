@@ -235,6 +235,44 @@ lffw_status lffw_cross_attention(const lffw_cross_attention_args *a, void *strea
     return from_cuda(lffw::launch_cross_attention(L, static_cast<cudaStream_t>(stream)));
 }
 
+lffw_status lffw_self_attention(const lffw_self_attention_args *a, void *stream) noexcept
+{
+    if (a == nullptr || a->struct_size < sizeof(lffw_self_attention_args))
+        return a == nullptr ? LFFW_INVALID_ARGUMENT : LFFW_ABI_MISMATCH;
+    if (a->head_dim != 64 || a->tokens < 1 || a->streams < 1 || a->heads < 1)
+        return LFFW_INVALID_ARGUMENT;
+    const int64_t width = static_cast<int64_t>(a->heads) * 64;
+    if (static_cast<int64_t>(a->streams) * a->tokens >= (int64_t(1) << 31) || width > kMaxDim)
+        return LFFW_INVALID_ARGUMENT;
+    for (const int64_t ld : {a->q_ld, a->k_ld, a->v_ld})
+        if (ld < width || ld % 8 != 0)
+            return LFFW_INVALID_ARGUMENT;
+    if (a->q == nullptr || a->k == nullptr || a->v == nullptr || (a->out == nullptr && a->out_codes == nullptr))
+        return LFFW_INVALID_ARGUMENT;
+    if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->out) || !aligned16(a->out_codes))
+        return LFFW_INVALID_ARGUMENT;
+    if (a->out_codes != nullptr && a->code_scale_ptr == nullptr && !valid_scale(a->code_scale))
+        return LFFW_INVALID_ARGUMENT;
+    lffw_status s = current_device_gate();
+    if (s != LFFW_SUCCESS)
+        return s;
+    lffw::SelfAttentionLaunch L{};
+    L.streams = a->streams;
+    L.tokens = a->tokens;
+    L.heads = a->heads;
+    L.q = a->q;
+    L.k = a->k;
+    L.v = a->v;
+    L.q_ld = a->q_ld;
+    L.k_ld = a->k_ld;
+    L.v_ld = a->v_ld;
+    L.out = a->out;
+    L.code_scale = a->code_scale;
+    L.code_scale_ptr = a->code_scale_ptr;
+    L.codes = a->out_codes;
+    return from_cuda(lffw::launch_self_attention(L, static_cast<cudaStream_t>(stream)));
+}
+
 lffw_status lffw_fp8_quantize_rows(const uint16_t *w, int64_t rows, int64_t cols, const float *scales,
                                    uint8_t *codes, void *stream) noexcept
 {

@@ -1640,6 +1640,303 @@ __global__ void __launch_bounds__(kThreads, 1)
 } // namespace attn
 
 // ---------------------------------------------------------------------------
+// Encoder self-attention (cpp/src/network_graph.cpp:235-247 `attention`: `attend`
+// on the layer's own q/k/v projections, no mask) with the graph's fp16 edges:
+// q' = half(q c), k' = half(k c), scores half(q'.k'), p = half(softmax_fp32),
+// out = half(p.v).  A CTA takes 128 query rows of one (stream, head): eight MMA
+// warps of 16 rows and a producer warp.  Pass 1 streams K and keeps each row's
+// running max and sum of exp; pass 2 streams K and V again, recomputes the same
+// fp16 scores and forms p = half(exp(s - max) / sum) with the final max and sum,
+// straight from the score accumulators into the A fragments of P.V.  The
+// exponentials use the hardware's approximate 2^x (relative error about 2^-22),
+// far below the fp16 rounding of p.  q, k and v
+// are read in place from the projections' rows (for instance the fused QKV
+// output), through 128B-swizzled TMA boxes.
+
+namespace sattn {
+
+constexpr int kDim = 64;
+constexpr int kBQ = 128;    // query rows per CTA
+constexpr int kChunk = 128; // keys per stage
+constexpr int kStages = 4;
+constexpr int kStageBytes = kChunk * kDim * 2;
+constexpr int kQBytes = kBQ * kDim * 2;
+constexpr int kMathWarps = kBQ / 16;
+constexpr int kThreads = (kMathWarps + 1) * 32; // + the producer warp
+constexpr int kSmemBytes = 1024 + kQBytes + kStages * kStageBytes + 128;
+
+struct Params {
+    int streams, tokens, heads;
+    int qblocks; // ceil(tokens / kBQ)
+    int nchunks; // ceil(tokens / 128)
+    uint16_t *out;
+    uint32_t scale2; // fp16 head_dim^-0.25 in both halves
+    float code_scale, code_recip;
+    const float *code_scale_ptr;
+    uint8_t *codes;
+};
+
+// 2^x by the hardware's approximate exponential (relative error about 2^-22), and
+// log2(x) likewise: exp(s - m) = 2^(s log2(e) - m log2(e)).
+__device__ __forceinline__ float fast_exp2(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float fast_log2(float x)
+{
+    float y;
+    asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Scores of one 8-key n-tile: acc = Q'(16 rows) K'^T(8 keys) from the swizzled
+// K stage, then rounded to fp16 (the MatMul output edge) and returned as floats.
+__device__ __forceinline__ void score_tile(const uint32_t (&qa)[4][4], uint32_t stage, int kb, int lane,
+                                           uint32_t scale2, float (&s)[4])
+{
+    uint32_t b[8];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        const int mi = lane >> 3, key = kb + (lane & 7);
+        const int chunk16 = 2 * (2 * half + (mi >> 1)) + (mi & 1);
+        uint32_t r[4];
+        ldmatrix_x4(stage + key * 128 + ((chunk16 ^ (key & 7)) << 4), r);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            b[4 * half + i] = gemm::hmul2_rn(r[i], scale2);
+    }
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks)
+        mma_m16n8k16_f16_f32(acc, qa[ks], b[2 * ks], b[2 * ks + 1]);
+    const uint32_t lo = gemm::cvt_f16x2(acc[0], acc[1]), hi = gemm::cvt_f16x2(acc[2], acc[3]);
+    s[0] = h2f(static_cast<uint16_t>(lo & 0xFFFFu));
+    s[1] = h2f(static_cast<uint16_t>(lo >> 16));
+    s[2] = h2f(static_cast<uint16_t>(hi & 0xFFFFu));
+    s[3] = h2f(static_cast<uint16_t>(hi >> 16));
+}
+
+__global__ void __launch_bounds__(kThreads)
+    self_attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                          const __grid_constant__ CUtensorMap tm_v, const Params p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t qs = sbase;
+    const uint32_t ring = sbase + kQBytes;
+    const uint32_t bar_full = ring + kStages * kStageBytes;
+    const uint32_t bar_empty = bar_full + 8 * kStages;
+    const uint32_t bar_q = bar_empty + 8 * kStages;
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    const int qb = static_cast<int>(blockIdx.x) % p.qblocks;
+    const int sh = static_cast<int>(blockIdx.x) / p.qblocks;
+    const int head = sh % p.heads;
+    const int stream = sh / p.heads;
+    const int row_base = stream * p.tokens; // token rows of this stream
+    const int q0 = qb * kBQ;
+    const int total = 3 * p.nchunks;        // K (pass 1), then K and V interleaved (pass 2)
+
+    if (threadIdx.x == 0) {
+        griddepcontrol_launch_dependents();
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(bar_full + 8 * i, 1);
+            mbar_init(bar_empty + 8 * i, kMathWarps);
+        }
+        mbar_init(bar_q, 1);
+        fence_barrier_init();
+        prefetch_tensor_map(&tm_q);
+        prefetch_tensor_map(&tm_k);
+        prefetch_tensor_map(&tm_v);
+    }
+    __syncthreads();
+    griddepcontrol_wait(); // the projections are written by earlier kernels
+
+    if (warp == kMathWarps) {
+        // ---------------- producer (one thread) ----------------
+        if (lane == 0) {
+            mbar_arrive_expect_tx(bar_q, kQBytes);
+            tma_load_2d(qs, &tm_q, bar_q, head * kDim, row_base + q0);
+            int issued = 0;
+            for (int i = 0; i < total; ++i, ++issued) {
+                const int st = i % kStages;
+                if (!mbar_wait(bar_empty + 8 * st, ((i / kStages) & 1u) ^ 1u, kSiteProducerEmpty))
+                    break;
+                const bool is_v = i >= p.nchunks && ((i - p.nchunks) & 1);
+                const int c = i < p.nchunks ? i : (i - p.nchunks) >> 1;
+                mbar_arrive_expect_tx(bar_full + 8 * st, kStageBytes);
+                tma_load_2d(ring + st * kStageBytes, is_v ? &tm_v : &tm_k, bar_full + 8 * st, head * kDim,
+                            row_base + c * kChunk);
+            }
+            for (int i = issued > kStages ? issued - kStages : 0; i < issued; ++i)
+                for (int tries = 0; tries < (1 << 22) &&
+                                    !mbar_try_wait(bar_full + 8 * (i % kStages), (i / kStages) & 1u);
+                     ++tries) {
+                }
+            for (int tries = 0; tries < (1 << 22) && !mbar_try_wait(bar_q, 0); ++tries) {
+            }
+        }
+    } else {
+        const int g = lane >> 2, tig = lane & 3;
+        bool ok = __all_sync(0xffffffffu, mbar_wait(bar_q, 0, kSiteMmaFull));
+        // Q' = half(q * c) as A fragments for this warp's 16 rows (4 k-steps of 16 dims).
+        uint32_t qa[4][4];
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+            const int mi = lane >> 3;
+            const int row = warp * 16 + (lane & 7) + (mi & 1) * 8;
+            const int chunk16 = ks * 2 + (mi >> 1);
+            uint32_t r[4];
+            ldmatrix_x4(qs + row * 128 + ((chunk16 ^ (row & 7)) << 4), r);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                qa[ks][i] = gemm::hmul2_rn(r[i], p.scale2);
+        }
+        // ---------------- pass 1: row max and sum of exp over all keys ----------------
+        float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f}; // rows g and g + 8 (this thread's part of l)
+        for (int c = 0; c < p.nchunks; ++c) {
+            const int st = c % kStages;
+            ok = ok && __all_sync(0xffffffffu, mbar_wait(bar_full + 8 * st, (c / kStages) & 1u, kSiteMmaFull));
+            const uint32_t stage = ring + st * kStageBytes;
+            const int kc = p.tokens - c * kChunk < kChunk ? p.tokens - c * kChunk : kChunk;
+            for (int sub = 0; ok && sub * 32 < kc; ++sub) {
+                float sv[4][4];
+#pragma unroll
+                for (int nt = 0; nt < 4; ++nt) {
+                    const int kb = sub * 32 + nt * 8;
+                    if (kb < kc)
+                        score_tile(qa, stage, kb, lane, p.scale2, sv[nt]);
+                }
+                if (sub * 32 + 32 > kc) { // keys past the stream's tokens (the last block only)
+#pragma unroll
+                    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            if (sub * 32 + nt * 8 + 2 * tig + (e & 1) >= kc)
+                                sv[nt][e] = -INFINITY;
+                }
+#pragma unroll
+                for (int r = 0; r < 2; ++r) {
+                    float bm = -INFINITY;
+#pragma unroll
+                    for (int nt = 0; nt < 4; ++nt)
+                        bm = fmaxf(bm, fmaxf(sv[nt][2 * r], sv[nt][2 * r + 1]));
+                    bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 1));
+                    bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 2));
+                    const float mn = fmaxf(m[r], bm);
+                    const float mn2 = mn * kLog2e;
+                    float add = 0.0f;
+#pragma unroll
+                    for (int nt = 0; nt < 4; ++nt)
+                        add += fast_exp2(fmaf(sv[nt][2 * r], kLog2e, -mn2)) +
+                               fast_exp2(fmaf(sv[nt][2 * r + 1], kLog2e, -mn2));
+                    l[r] = (m[r] == -INFINITY ? 0.0f : l[r] * fast_exp2((m[r] - mn) * kLog2e)) + add;
+                    m[r] = mn;
+                }
+            }
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(bar_empty + 8 * st);
+        }
+        // p = exp(s - m) / sum = 2^(s log2(e) - (m log2(e) + log2(sum))): one fma and one ex2.
+        float off[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            float t = l[r];
+            t += __shfl_xor_sync(0xffffffffu, t, 1);
+            t += __shfl_xor_sync(0xffffffffu, t, 2);
+            off[r] = m[r] * kLog2e + fast_log2(t);
+        }
+        // ---------------- pass 2: p = half(exp(s - max) / sum), out = P.V ----------------
+        float o[8][4];
+#pragma unroll
+        for (int d = 0; d < 8; ++d)
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                o[d][e] = 0.0f;
+        for (int c = 0; c < p.nchunks; ++c) {
+            const int ik = p.nchunks + 2 * c, iv = ik + 1;
+            const int sk = ik % kStages, sv_st = iv % kStages;
+            ok = ok && __all_sync(0xffffffffu, mbar_wait(bar_full + 8 * sk, (ik / kStages) & 1u, kSiteMmaFull));
+            ok = ok && __all_sync(0xffffffffu, mbar_wait(bar_full + 8 * sv_st, (iv / kStages) & 1u, kSiteMmaFull));
+            const uint32_t kst = ring + sk * kStageBytes, vst = ring + sv_st * kStageBytes;
+            const int kc = p.tokens - c * kChunk < kChunk ? p.tokens - c * kChunk : kChunk;
+            for (int sub = 0; ok && sub * 32 < kc; ++sub) {
+                uint32_t pa[2][4]; // A fragments of P for two 16-key steps
+#pragma unroll
+                for (int nt = 0; nt < 4; ++nt) {
+                    const int kb = sub * 32 + nt * 8;
+                    float sv[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                    if (kb < kc)
+                        score_tile(qa, kst, kb, lane, p.scale2, sv);
+                    float pv[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        pv[e] = fast_exp2(fmaf(sv[e], kLog2e, -off[e >> 1]));
+                    if (kb + 8 > kc) // keys past the stream's tokens (the last block only)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            if (kb + 2 * tig + (e & 1) >= kc)
+                                pv[e] = 0.0f;
+                    // n-tile nt is keys (nt & 1) * 8 .. + 7 of 16-key step nt >> 1
+                    pa[nt >> 1][(nt & 1) * 2 + 0] = gemm::cvt_f16x2(pv[0], pv[1]); // row g
+                    pa[nt >> 1][(nt & 1) * 2 + 1] = gemm::cvt_f16x2(pv[2], pv[3]); // row g + 8
+                }
+#pragma unroll
+                for (int kk = 0; kk < 2; ++kk) {
+                    const int kbase = sub * 32 + kk * 16;
+#pragma unroll
+                    for (int dn = 0; dn < 8; dn += 2) {
+                        const int mi = lane >> 3;
+                        const int key = kbase + (mi & 1) * 8 + (lane & 7);
+                        const int chunk16 = dn + (mi >> 1);
+                        uint32_t r[4];
+                        ldmatrix_x4_trans(vst + key * 128 + ((chunk16 ^ (key & 7)) << 4), r);
+                        mma_m16n8k16_f16_f32(o[dn], pa[kk], r[0], r[1]);
+                        mma_m16n8k16_f16_f32(o[dn + 1], pa[kk], r[2], r[3]);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(bar_empty + 8 * sk);
+                mbar_arrive(bar_empty + 8 * sv_st);
+            }
+        }
+        const float scale = p.code_scale_ptr ? *p.code_scale_ptr : p.code_scale;
+        const float recip = p.code_scale_ptr ? __frcp_rn(scale) : p.code_recip;
+        const uint64_t neg_scale2 = f2_bits(-scale, -scale), recip2 = f2_bits(recip, recip);
+        const int width = p.heads * kDim;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int token = q0 + warp * 16 + g + 8 * e;
+            if (!ok || token >= p.tokens)
+                continue;
+#pragma unroll
+            for (int dn = 0; dn < 8; ++dn) {
+                const uint32_t pair = gemm::cvt_f16x2(o[dn][2 * e], o[dn][2 * e + 1]);
+                const size_t idx = static_cast<size_t>(row_base + token) * width + head * kDim + dn * 8 + 2 * tig;
+                if (p.out)
+                    *reinterpret_cast<uint32_t *>(p.out + idx) = pair;
+                if (p.codes)
+                    *reinterpret_cast<uint16_t *>(p.codes + idx) =
+                        static_cast<uint16_t>(e4m3x2_quotient(pair, neg_scale2, recip2));
+            }
+        }
+    }
+    __syncthreads();
+}
+
+} // namespace sattn
+
+// ---------------------------------------------------------------------------
 // fp16 single-token projections (the reference plugins' kernels on sm_100a).
 
 namespace proj {
@@ -1732,6 +2029,23 @@ EncodeTiledFn encode_tiled()
 }
 
 // 2-D row-major tensor [rows, cols] with `elem` bytes per element.
+// 2-D tensor map over [rows, cols] elements whose rows are `ld` elements apart
+// (ld >= cols: a column window of a wider matrix).
+bool make_map_ld(CUtensorMap *map, CUtensorMapDataType type, int elem, const void *base, int64_t rows,
+                 int64_t cols, int64_t ld, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle)
+{
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn)
+        return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * elem)};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t estrides[2] = {1, 1};
+    return fn(map, type, 2, const_cast<void *>(base), dims, strides, box, estrides,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool make_map(CUtensorMap *map, CUtensorMapDataType type, int elem, const void *base, int64_t rows,
               int64_t cols, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle)
 {
@@ -2172,6 +2486,49 @@ cudaError_t launch_cross_attention(const CrossAttentionLaunch &L, cudaStream_t s
     config.attrs = attrs;
     config.numAttrs = count;
     const cudaError_t err = cudaLaunchKernelEx(&config, attn::cross_attention_kernel, tm_k, tm_v, p);
+    count_launch();
+    return err != cudaSuccess ? err : cudaGetLastError();
+}
+
+cudaError_t launch_self_attention(const SelfAttentionLaunch &L, cudaStream_t stream)
+{
+    sattn::Params p{};
+    p.streams = L.streams;
+    p.tokens = L.tokens;
+    p.heads = L.heads;
+    p.qblocks = (L.tokens + sattn::kBQ - 1) / sattn::kBQ;
+    p.nchunks = (L.tokens + sattn::kChunk - 1) / sattn::kChunk;
+    p.out = L.out;
+    const uint16_t c = __half_as_ushort(__float2half_rn(static_cast<float>(std::pow(double(sattn::kDim), -0.25))));
+    p.scale2 = static_cast<uint32_t>(c) * 0x10001u;
+    p.code_scale = L.code_scale;
+    p.code_recip = L.codes && !L.code_scale_ptr ? static_cast<float>(1.0 / static_cast<double>(L.code_scale)) : 0.0f;
+    p.code_scale_ptr = L.code_scale_ptr;
+    p.codes = L.codes;
+    const int64_t rows = static_cast<int64_t>(L.streams) * L.tokens;
+    const int64_t width = static_cast<int64_t>(L.heads) * sattn::kDim;
+    CUtensorMap tm_q{}, tm_k{}, tm_v{};
+    if (!make_map_ld(&tm_q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.q, rows, width, L.q_ld, sattn::kDim, sattn::kBQ,
+                     CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map_ld(&tm_k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.k, rows, width, L.k_ld, sattn::kDim,
+                     sattn::kChunk, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map_ld(&tm_v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.v, rows, width, L.v_ld, sattn::kDim,
+                     sattn::kChunk, CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    const cudaError_t attr = ensure_smem(sattn::self_attention_kernel, sattn::kSmemBytes);
+    if (attr != cudaSuccess)
+        return attr;
+    cudaLaunchConfig_t config{};
+    config.gridDim = dim3(static_cast<unsigned>(static_cast<int64_t>(L.streams) * L.heads * p.qblocks));
+    config.blockDim = dim3(sattn::kThreads);
+    config.dynamicSmemBytes = sattn::kSmemBytes;
+    config.stream = stream;
+    cudaLaunchAttribute attr_pdl[1];
+    attr_pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr_pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    config.attrs = attr_pdl;
+    config.numAttrs = 1;
+    const cudaError_t err = cudaLaunchKernelEx(&config, sattn::self_attention_kernel, tm_q, tm_k, tm_v, p);
     count_launch();
     return err != cudaSuccess ? err : cudaGetLastError();
 }

@@ -60,6 +60,17 @@ struct CrossAttentionLaunch {
     uint8_t *codes;
 };
 cudaError_t launch_cross_attention(const CrossAttentionLaunch &p, cudaStream_t stream);
+// Encoder self-attention (head_dim 64) on q/k/v rows read in place.
+struct SelfAttentionLaunch {
+    int streams, tokens, heads;
+    const uint16_t *q, *k, *v;
+    int64_t q_ld, k_ld, v_ld;
+    uint16_t *out;
+    float code_scale;
+    const float *code_scale_ptr;
+    uint8_t *codes;
+};
+cudaError_t launch_self_attention(const SelfAttentionLaunch &p, cudaStream_t stream);
 cudaError_t launch_quantize(const uint16_t *x, int64_t count, float scale, const float *scale_ptr,
                             uint8_t *codes, cudaStream_t stream);
 cudaError_t launch_quantize_rows(const uint16_t *w, int64_t rows, int64_t cols,

@@ -469,6 +469,14 @@ __device__ __forceinline__ void ldmatrix_x2_trans(uint32_t addr, uint32_t (&r)[2
                  : "r"(addr));
 }
 
+// Four 8x8 fp16 matrices, transposed on the way.
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t (&r)[4])
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
 // d += a (16x16, row) * b (16x8, col), fp16 inputs, fp32 accumulators.
 __device__ __forceinline__ void mma_m16n8k16_f16_f32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
 {

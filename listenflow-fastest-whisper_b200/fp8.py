@@ -158,6 +158,39 @@ def cross_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, queries: 
     return out, codes
 
 
+def self_attention(qkv: torch.Tensor, streams: int, heads: int, *, code_scale=None, want_out: bool = True,
+                   stream=None):
+    """Encoder self-attention (network_graph.cpp:235-247) read in place from the fused
+    QKV linear output qkv [streams * tokens, 3 * heads * 64] (q | k | v columns).
+
+    Returns (out, codes): out fp16 [streams * tokens, heads * 64] (out_proj's input),
+    and its E4M3 codes when `code_scale` is given."""
+    _require(qkv, torch.float16, "qkv")
+    rows, cols = qkv.shape
+    width = heads * 64
+    if cols != 3 * width or rows % streams != 0:
+        raise ValueError("qkv must be [streams * tokens, 3 * heads * 64]")
+    a = native.SelfAttentionArgs()
+    a.struct_size = ctypes.sizeof(native.SelfAttentionArgs)
+    a.streams, a.tokens, a.heads, a.head_dim = streams, rows // streams, heads, 64
+    base = qkv.data_ptr()
+    a.q, a.k, a.v = base, base + 2 * width, base + 4 * width
+    a.q_ld = a.k_ld = a.v_ld = cols
+    out = torch.empty((rows, width), dtype=torch.float16, device=qkv.device) if want_out else None
+    codes = None
+    if code_scale is not None:
+        codes = torch.empty((rows, width), dtype=torch.uint8, device=qkv.device)
+        if isinstance(code_scale, torch.Tensor):
+            _require(code_scale, torch.float32, "code_scale")
+            a.code_scale_ptr = code_scale.data_ptr()
+        else:
+            a.code_scale = float(code_scale)
+        a.out_codes = codes.data_ptr()
+    a.out = out.data_ptr() if out is not None else None
+    native.check(native.library().lffw_self_attention(ctypes.byref(a), _stream(stream)), "lffw_self_attention")
+    return out, codes
+
+
 def quantize_rows(w: torch.Tensor, scales: torch.Tensor, stream=None) -> torch.Tensor:
     """E4M3 codes of an fp16 [N, K] weight with one scale per row."""
     _require(w, torch.float16, "w")

@@ -213,6 +213,97 @@ void oracle_cross_attention(const uint16_t *q, const uint16_t *k, const uint16_t
     free(score);
 }
 
+struct self_attention_job {
+    const uint16_t *q, *k, *v;
+    int64_t q_ld, k_ld, v_ld;
+    int streams, tokens, heads, dim;
+    uint16_t *out;
+    float code_scale;
+    uint8_t *codes;
+    int first, step; /* (stream, head) pairs first, first + step, ... */
+};
+
+static void *self_attention_pairs(void *arg)
+{
+    const struct self_attention_job *j = (const struct self_attention_job *)arg;
+    const int dim = j->dim, T = j->tokens, width = j->heads * dim;
+    const double c = oracle_half_to_double(oracle_half_from_float((float)pow((double)dim, -0.25)));
+    double *ks = (double *)malloc((size_t)T * dim * sizeof(double));
+    double *qs = (double *)malloc((size_t)dim * sizeof(double));
+    double *score = (double *)malloc((size_t)T * sizeof(double));
+    if (!ks || !qs || !score)
+        goto done;
+    for (int pair = j->first; pair < j->streams * j->heads; pair += j->step) {
+        const int s = pair / j->heads, h = pair % j->heads;
+        for (int t = 0; t < T; ++t)
+            for (int d = 0; d < dim; ++d)
+                ks[(size_t)t * dim + d] = oracle_half_to_double(oracle_half_from_double(
+                    oracle_half_to_double(j->k[((size_t)s * T + t) * j->k_ld + h * dim + d]) * c));
+        for (int i = 0; i < T; ++i) {
+            for (int d = 0; d < dim; ++d)
+                qs[d] = oracle_half_to_double(oracle_half_from_double(
+                    oracle_half_to_double(j->q[((size_t)s * T + i) * j->q_ld + h * dim + d]) * c));
+            double best = -INFINITY;
+            for (int t = 0; t < T; ++t) {
+                double acc = 0.0;
+                for (int d = 0; d < dim; ++d)
+                    acc += qs[d] * ks[(size_t)t * dim + d];
+                score[t] = oracle_half_to_double(oracle_half_from_double(acc));
+                if (score[t] > best)
+                    best = score[t];
+            }
+            double total = 0.0;
+            for (int t = 0; t < T; ++t) {
+                score[t] = exp(score[t] - best);
+                total += score[t];
+            }
+            for (int t = 0; t < T; ++t)
+                score[t] = oracle_half_to_double(oracle_half_from_double(score[t] / total));
+            for (int d = 0; d < dim; ++d) {
+                double acc = 0.0;
+                for (int t = 0; t < T; ++t)
+                    acc += score[t] * oracle_half_to_double(j->v[((size_t)s * T + t) * j->v_ld + h * dim + d]);
+                const uint16_t o = oracle_half_from_double(acc);
+                const size_t idx = ((size_t)s * T + i) * width + h * dim + d;
+                j->out[idx] = o;
+                if (j->codes)
+                    j->codes[idx] = quantize_one(o, j->code_scale);
+            }
+        }
+    }
+done:
+    free(ks);
+    free(qs);
+    free(score);
+    return NULL;
+}
+
+void oracle_self_attention(const uint16_t *q, const uint16_t *k, const uint16_t *v, int64_t q_ld, int64_t k_ld,
+                           int64_t v_ld, int streams, int tokens, int heads, int dim, uint16_t *out,
+                           float code_scale, uint8_t *codes)
+{
+    int threads = oracle_threads();
+    if (threads > streams * heads)
+        threads = streams * heads;
+    if (threads < 1)
+        threads = 1;
+    if (threads > 256)
+        threads = 256;
+    struct self_attention_job jobs[256];
+    pthread_t handles[256];
+    for (int t = 0; t < threads; ++t) {
+        jobs[t] = (struct self_attention_job){q, k, v, q_ld, k_ld, v_ld, streams, tokens, heads, dim,
+                                              out, code_scale, codes, t, threads};
+        if (threads == 1 || pthread_create(&handles[t], NULL, self_attention_pairs, &jobs[t]) != 0) {
+            self_attention_pairs(&jobs[t]);
+            handles[t] = 0;
+        }
+    }
+    for (int t = 0; t < threads; ++t)
+        if (threads > 1 && handles[t])
+            pthread_join(handles[t], NULL);
+}
+
 void oracle_quantize_rows(const uint16_t *x, int64_t rows, int64_t cols, const float *scales,
                           uint8_t *codes)
 {

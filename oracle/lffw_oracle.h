@@ -87,6 +87,16 @@ void oracle_layer_norm(const uint16_t *x, const uint16_t *residual, int64_t rows
 void oracle_cross_attention(const uint16_t *q, const uint16_t *k, const uint16_t *v, int streams, int queries,
                             int heads, int dim, int keys, uint16_t *out, float code_scale, uint8_t *codes);
 
+/* Encoder self-attention (cpp/src/network_graph.cpp:235-247 `attention`: `attend` on
+ * the layer's own q/k/v projections, no mask), per stream s, head h, query row i:
+ * the same fp16 edges as oracle_cross_attention over the stream's `tokens` keys.
+ * q, k, v rows: row s * tokens + t, column h * dim + d, row strides q_ld, k_ld, v_ld
+ * (elements; e.g. the fused QKV output with q, k, v at column offsets 0, width,
+ * 2 * width and stride 3 * width).  out: [streams * tokens, heads * dim]. */
+void oracle_self_attention(const uint16_t *q, const uint16_t *k, const uint16_t *v, int64_t q_ld, int64_t k_ld,
+                           int64_t v_ld, int streams, int tokens, int heads, int dim, uint16_t *out,
+                           float code_scale, uint8_t *codes);
+
 /* fp16(erf(x)) of an fp16 x, erf in binary64, round to nearest even. */
 uint16_t oracle_erf_fp16(uint16_t x);
 /* GELU on an fp16 value with every graph edge rounded to fp16. */

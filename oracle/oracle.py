@@ -62,6 +62,10 @@ def lib() -> ctypes.CDLL:
             _u16p, _u16p, _u16p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _u16p,
             ctypes.c_float, _u8p,
         ]
+        L.oracle_self_attention.argtypes = [
+            _u16p, _u16p, _u16p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+            ctypes.c_int, ctypes.c_int, _u16p, ctypes.c_float, _u8p,
+        ]
         L.oracle_erf_fp16.argtypes = [ctypes.c_uint16]
         L.oracle_erf_fp16.restype = ctypes.c_uint16
         _lib = L
@@ -160,6 +164,25 @@ def cross_attention(q, k, v, queries: int, code_scale=None):
     lib().oracle_cross_attention(_ptr(qb, _u16p), _ptr(kb, _u16p), _ptr(vb, _u16p), streams, queries, heads, dim,
                                  keys, _ptr(out, _u16p),
                                  float(np.float32(code_scale)) if code_scale is not None else 1.0, _ptr(codes, _u8p))
+    return out, codes
+
+
+def self_attention(qkv, streams: int, heads: int, code_scale=None):
+    """(out, codes) of the encoder self-attention (network_graph.cpp:235-247) on a fused
+    QKV projection output [streams * tokens, 3 * heads * 64] (q | k | v columns)."""
+    b = bits16(qkv)
+    rows, cols = b.shape
+    width = cols // 3
+    dim = width // heads
+    tokens = rows // streams
+    out = np.empty((rows, width), np.uint16)
+    codes = np.empty((rows, width), np.uint8) if code_scale is not None else None
+    base = b.ctypes.data
+    u16 = np.dtype(np.uint16).itemsize
+    ptr = lambda off: ctypes.cast(base + off * u16, _u16p)
+    lib().oracle_self_attention(ptr(0), ptr(width), ptr(2 * width), cols, cols, cols, streams, tokens, heads, dim,
+                                _ptr(out, _u16p), float(np.float32(code_scale)) if code_scale is not None else 1.0,
+                                _ptr(codes, _u8p))
     return out, codes
 
 

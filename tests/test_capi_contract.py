@@ -130,6 +130,34 @@ def test_cross_attention_abi_mismatch_and_null(native, lib):
     assert lib.lffw_cross_attention(None, None) == native.INVALID_ARGUMENT
 
 
+def _self_args(native, **over):
+    a = native.SelfAttentionArgs()
+    a.struct_size = ctypes.sizeof(native.SelfAttentionArgs)
+    a.streams, a.tokens, a.heads, a.head_dim = 8, 1500, 20, 64
+    a.q, a.k, a.v, a.out = 0x10000, 0x10000 + 2560, 0x10000 + 5120, 0x40000
+    a.q_ld = a.k_ld = a.v_ld = 3840
+    for key, value in over.items():
+        setattr(a, key, value)
+    return a
+
+
+@pytest.mark.parametrize("change", [
+    {"head_dim": 32}, {"tokens": 0}, {"streams": 0}, {"heads": 0}, {"streams": 2**16, "tokens": 2**15},
+    {"q_ld": 1000}, {"k_ld": 3844}, {"v_ld": 0}, {"q": None}, {"out": None}, {"k": 0x10004},
+    {"out_codes": 0x50000, "code_scale": float("inf")},
+])
+def test_self_attention_rejects_invalid_arguments(native, lib, change):
+    a = _self_args(native, **change)
+    assert lib.lffw_self_attention(ctypes.byref(a), None) == native.INVALID_ARGUMENT
+
+
+def test_self_attention_abi_mismatch_and_null(native, lib):
+    a = _self_args(native)
+    a.struct_size = 16
+    assert lib.lffw_self_attention(ctypes.byref(a), None) == native.ABI_MISMATCH
+    assert lib.lffw_self_attention(None, None) == native.INVALID_ARGUMENT
+
+
 def test_device_gate_without_sm100(native, lib):
     import torch
 

@@ -45,3 +45,25 @@ def test_uniform_scores_average_the_values(oracle):
     # p = half(1/10) each; sum of 10 * half(0.1) * v differs from v by the rounding of 0.1
     expected = (np.float64(np.float16(0.1)) * 10 * v[0, 0, 0].astype(np.float64)).astype(np.float16)
     np.testing.assert_array_equal(out[0], expected.view(np.uint16))
+
+
+@pytest.mark.parametrize("streams,tokens,heads", [(1, 1, 1), (2, 70, 3), (1, 129, 2)])
+def test_self_attention_matches_float64_restatement(oracle, streams, tokens, heads):
+    """Encoder self-attention (network_graph.cpp:235-247) on a fused QKV output."""
+    import torch
+
+    rng = np.random.default_rng(streams * 10 + tokens)
+    width = heads * 64
+    qkv = halves(rng, (streams * tokens, 3 * width))
+    out, codes = oracle.self_attention(qkv, streams, heads, code_scale=0.004)
+    q, k, v = qkv[:, :width], qkv[:, width:2 * width], qkv[:, 2 * width:]
+    c = np.float16(64 ** -0.25)
+    split = lambda a: a.reshape(streams, tokens, heads, 64).transpose(0, 2, 1, 3)
+    qs = split((q.astype(np.float32) * np.float32(c)).astype(np.float16).astype(np.float64))
+    ks = split((k.astype(np.float32) * np.float32(c)).astype(np.float16).astype(np.float64))
+    scores = np.einsum("shid,shjd->shij", qs, ks).astype(np.float16).astype(np.float64)
+    p = torch.softmax(torch.from_numpy(scores), -1).numpy().astype(np.float16).astype(np.float64)
+    want = np.einsum("shij,shjd->shid", p, split(v.astype(np.float64))).astype(np.float16)
+    want = want.transpose(0, 2, 1, 3).reshape(streams * tokens, width)
+    np.testing.assert_array_equal(out, want.view(np.uint16))
+    np.testing.assert_array_equal(codes, oracle.quantize(out, np.float32(0.004)))
