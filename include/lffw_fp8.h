@@ -24,7 +24,7 @@
 #include <stdint.h>
 
 #define LFFW_FP8_ABI_MAJOR 1
-#define LFFW_FP8_ABI_MINOR 4
+#define LFFW_FP8_ABI_MINOR 5
 #define LFFW_FP8_API __attribute__((visibility("default")))
 #if defined(__cplusplus)
 #define LFFW_FP8_NOEXCEPT noexcept
@@ -105,6 +105,23 @@ LFFW_FP8_API lffw_status lffw_fp8_linear(const lffw_fp8_linear_args *args,
 LFFW_FP8_API lffw_status lffw_fp8_quantize(const uint16_t *x, int64_t count, float scale,
                                            const float *scale_ptr, uint8_t *codes,
                                            void *stream) LFFW_FP8_NOEXCEPT;
+
+/* A chain of dependent small-m linears in one persistent launch (no counterpart in
+ * the reference; it runs the decoder step's linears back to back).  Link i may read
+ * what earlier links wrote: its activations are loaded only after every row block
+ * of link i-1 is written.  Each link is an lffw_fp8_linear call with the same m
+ * (<= 32), packed weights (w_layout = LFFW_WEIGHTS_SKINNY_TILES), a static or
+ * device act_scale, and y and/or next_codes; results equal lffw_fp8_linear's bit
+ * for bit.  lffw_chain_create validates the links and ALLOCATES device memory
+ * for their descriptors (freed by lffw_chain_destroy); the pointers in the links
+ * are bound at creation.  lffw_chain_run launches once (capturable in a graph);
+ * runs of one chain must not overlap on the GPU. */
+typedef struct lffw_chain lffw_chain;
+
+LFFW_FP8_API lffw_status lffw_chain_create(const lffw_fp8_linear_args *links, int32_t count,
+                                           lffw_chain **chain) LFFW_FP8_NOEXCEPT;
+LFFW_FP8_API lffw_status lffw_chain_run(const lffw_chain *chain, void *stream) LFFW_FP8_NOEXCEPT;
+LFFW_FP8_API void lffw_chain_destroy(lffw_chain *chain) LFFW_FP8_NOEXCEPT;
 
 /* LayerNorm producer for the linear that follows it (network_graph.cpp:160-166
  * `norm`, with the fp16 residual add of :285-287 before it), per row of `cols`:

@@ -174,6 +174,9 @@ def library() -> ctypes.CDLL:
         "lffw_layer_norm": ([ctypes.POINTER(LayerNormArgs), _vp], _i32),
         "lffw_cross_attention": ([ctypes.POINTER(CrossAttentionArgs), _vp], _i32),
         "lffw_self_attention": ([ctypes.POINTER(SelfAttentionArgs), _vp], _i32),
+        "lffw_chain_create": ([ctypes.POINTER(LinearArgs), _i32, ctypes.POINTER(_vp)], _i32),
+        "lffw_chain_run": ([_vp, _vp], _i32),
+        "lffw_chain_destroy": ([_vp], None),
         "lffw_fp8_quantize_rows": ([_vp, _i64, _i64, _vp, _vp, _vp], _i32),
         "lffw_fp8_weight_scales": ([_vp, _i64, _i64, _vp, _vp], _i32),
         "lffw_fp8_dynamic_scale": ([_vp, _i64, _vp, _vp, _vp], _i32),

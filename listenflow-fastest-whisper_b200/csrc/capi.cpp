@@ -152,6 +152,71 @@ lffw_status lffw_fp8_linear(const lffw_fp8_linear_args *args, void *stream) noex
     return run_linear(args, static_cast<cudaStream_t>(stream));
 }
 
+struct lffw_chain {
+    lffw::ChainPlan *plan;
+};
+
+lffw_status lffw_chain_create(const lffw_fp8_linear_args *links, int32_t count, lffw_chain **chain) noexcept
+{
+    if (chain == nullptr)
+        return LFFW_INVALID_ARGUMENT;
+    *chain = nullptr;
+    if (links == nullptr || count < 1 || count > (1 << 20))
+        return LFFW_INVALID_ARGUMENT;
+    std::vector<lffw::LinearLaunch> launches(static_cast<size_t>(count));
+    for (int32_t i = 0; i < count; ++i) {
+        const lffw_fp8_linear_args *a = &links[i];
+        const lffw_status v = validate_linear(a);
+        if (v != LFFW_SUCCESS)
+            return v;
+        if (weight_layout(a) != LFFW_WEIGHTS_SKINNY_TILES || a->m != links[0].m)
+            return LFFW_INVALID_ARGUMENT;
+        lffw::LinearLaunch &L = launches[i];
+        L.m = a->m;
+        L.n = a->n;
+        L.k = a->k;
+        L.x_codes = a->x_codes;
+        L.act_scale = a->act_scale;
+        L.act_scale_ptr = a->act_scale_ptr;
+        L.w_codes = a->w_codes;
+        L.w_scales = a->w_scales;
+        L.bias = a->bias;
+        L.gelu = a->epilogue == LFFW_EPILOGUE_GELU;
+        L.y = a->y;
+        L.next_scale = a->next_scale;
+        L.next_codes = a->next_codes;
+        L.w_packed = true;
+    }
+    lffw_status s = current_device_gate();
+    if (s != LFFW_SUCCESS)
+        return s;
+    auto *handle = new (std::nothrow) lffw_chain{nullptr};
+    if (handle == nullptr)
+        return LFFW_OUT_OF_MEMORY;
+    const cudaError_t err = lffw::chain_create(launches.data(), count, &handle->plan);
+    if (err != cudaSuccess) {
+        delete handle;
+        return err == cudaErrorMemoryAllocation ? LFFW_OUT_OF_MEMORY : LFFW_CUDA_ERROR;
+    }
+    *chain = handle;
+    return LFFW_SUCCESS;
+}
+
+lffw_status lffw_chain_run(const lffw_chain *chain, void *stream) noexcept
+{
+    if (chain == nullptr || chain->plan == nullptr)
+        return LFFW_INVALID_ARGUMENT;
+    return from_cuda(lffw::chain_run(chain->plan, static_cast<cudaStream_t>(stream)));
+}
+
+void lffw_chain_destroy(lffw_chain *chain) noexcept
+{
+    if (chain == nullptr)
+        return;
+    lffw::chain_destroy(chain->plan);
+    delete chain;
+}
+
 lffw_status lffw_fp8_quantize(const uint16_t *x, int64_t count, float scale, const float *scale_ptr,
                               uint8_t *codes, void *stream) noexcept
 {

@@ -26,9 +26,11 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <new>
 #include <string>
 #include <set>
 #include <utility>
+#include <vector>
 
 #include "launch.h"
 #include "lffw_fp8.h"
@@ -1015,6 +1017,275 @@ __global__ void __launch_bounds__(256)
 }
 
 } // namespace skinny
+
+// ---------------------------------------------------------------------------
+// Chain of small-M linears in one persistent launch (a decoder step's linears).
+// The per-launch skinny kernel pays, for every dependent linear, the grid's exit
+// and the next grid's release; here clusters of kCS CTAs stay resident and walk
+// the links in order.  Each cluster takes the 128-row blocks b = cluster,
+// cluster + clusters, ... of a link, splits K over its CTAs and reduces the
+// partials through DSMEM as the skinny kernel does.  When a cluster has finished
+// its blocks of link i, its leader adds their count to done[i] (release, after
+// a cluster barrier that orders every rank's stores); a link's activations are
+// loaded only after done[i - 1] reaches the previous link's block count
+// (acquire), so each link sees all of its predecessor's outputs and no link
+// overwrites a buffer an earlier link still reads.  The next unit's weight tiles
+// are requested before that wait.  Every wait is bounded.
+
+namespace chain {
+
+using skinny::kAct;
+using skinny::kBK;
+using skinny::kRedStride;
+using skinny::kRows;
+using skinny::kWBytes;
+using skinny::kXBytes;
+constexpr int kThreads = 128;
+constexpr int kCS = 8; // CTAs per cluster (K split)
+constexpr int kStages = 2;
+constexpr int kStageBytes = kWBytes + kXBytes;
+constexpr int kOffX = kStages * kWBytes;
+constexpr int kOffRed = kOffX + kStages * kXBytes; // not aliased: the next unit's weights arrive early
+constexpr int kRedBytes = kAct * kRedStride * 4;
+constexpr int kOffBar = (kOffRed + kRedBytes + 127) / 128 * 128;
+constexpr int kSmemBytes = kOffBar + 128 + 1024;
+
+struct Link {
+    const uint8_t *w; // packed 16 KB tiles (lffw_pack_skinny_weights)
+    const float *w_scales;
+    const uint16_t *bias;
+    const float *act_scale_ptr;
+    uint16_t *y;
+    uint8_t *codes;
+    int n, num_kb, gelu, next_lean;
+    float act_scale, next_scale, next_recip, pad;
+};
+
+struct Params {
+    const Link *links;
+    const CUtensorMap *x_maps; // one per link: activation codes [m, k], 128-byte x 32-row boxes, SW128
+    unsigned int *done;        // per link: 128-row blocks finished
+    int count, m, clusters;
+};
+
+__device__ __forceinline__ int blocks_of(const Link &l) { return (l.n + kRows - 1) / kRows; }
+
+__global__ void __launch_bounds__(kThreads) chain_kernel(const Params p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+    const uint32_t sbase = smem_u32(smem);
+    const int warp = threadIdx.x / 32;
+    const int rank = static_cast<int>(blockIdx.x) % kCS;
+    const int cl = static_cast<int>(blockIdx.x) / kCS;
+    const uint32_t bar_full = sbase + kOffBar;
+    const uint32_t bar_empty = bar_full + 8 * kStages;
+    const uint32_t bar_acc = bar_empty + 8 * kStages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 8 * (2 * kStages + 1));
+    float *red = reinterpret_cast<float *>(smem + kOffRed);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(bar_full + 8 * s, 1);
+            mbar_init(bar_empty + 8 * s, 1);
+        }
+        mbar_init(bar_acc, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), 32);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    // This cluster's units in link order: (link li, unit u) -> row block cl + u * clusters.
+    auto first_unit = [&](int li, int u, int &oli, int &ou) {
+        while (li < p.count && cl + u * p.clusters >= blocks_of(p.links[li])) {
+            ++li;
+            u = 0;
+        }
+        oli = li;
+        ou = u;
+    };
+    auto kb_range = [&](const Link &l, int &k0, int &k1) {
+        k0 = static_cast<int>((static_cast<int64_t>(l.num_kb) * rank) / kCS);
+        k1 = static_cast<int>((static_cast<int64_t>(l.num_kb) * (rank + 1)) / kCS);
+    };
+    bool ok = true;
+    uint32_t pos = 0;      // ring stages used so far (producer and MMA count the same sequence)
+    uint32_t acc_uses = 0; // accumulator commits so far
+    int waited = 0;        // links [0, waited) are known complete
+    int pre = 0;           // stages of the current unit already armed with their weights
+    int li, u;
+    first_unit(0, 0, li, u);
+    if (threadIdx.x == 0 && li < p.count) {
+        // Weights of the first unit before anything else.
+        const Link &l = p.links[li];
+        int k0, k1;
+        kb_range(l, k0, k1);
+        const uint8_t *tiles = l.w + static_cast<size_t>(cl + u * p.clusters) * l.num_kb * kWBytes;
+        pre = k1 - k0 < kStages ? k1 - k0 : kStages;
+        for (int j = 0; j < pre; ++j) {
+            mbar_arrive_expect_tx(bar_full + 8 * ((pos + j) % kStages), kStageBytes);
+            bulk_load(sbase + ((pos + j) % kStages) * kWBytes, tiles + static_cast<size_t>(k0 + j) * kWBytes,
+                      kWBytes, bar_full + 8 * ((pos + j) % kStages));
+        }
+    }
+    while (li < p.count) {
+        const Link &l = p.links[li];
+        const int block = cl + u * p.clusters;
+        const int n0 = block * kRows;
+        int k0, k1;
+        kb_range(l, k0, k1);
+        const int nkb = k1 - k0;
+        // Row constants for the epilogue, requested early.
+        const int my_row = rank * (kRows / kCS) + static_cast<int>(threadIdx.x) % (kRows / kCS);
+        const int my_n = n0 + my_row;
+        float my_ws = 0.0f;
+        uint16_t my_bias = 0;
+        if (my_n < l.n) {
+            my_ws = __ldg(l.w_scales + my_n);
+            if (l.bias)
+                my_bias = __ldg(l.bias + my_n);
+        }
+        // The next unit of this cluster (for the early weight requests).
+        int nli, nu;
+        first_unit(li, u + 1, nli, nu);
+
+        if (threadIdx.x == 0) {
+            // ---------------- producer ----------------
+            if (li > 0 && waited < li) {
+                // Every block of the previous link is done before its outputs are read.
+                const int need = blocks_of(p.links[li - 1]);
+                const uint64_t start = global_timer_ns();
+                for (uint32_t spin = 0; ok && ld_acquire_gpu(p.done + li - 1) < static_cast<unsigned>(need); ++spin)
+                    if ((spin & 63u) == 63u && global_timer_ns() - start > 2000000000ull) {
+                        atomicCAS(&g_device_error, 0, kSiteChainDependency);
+                        ok = false;
+                    }
+                fence_proxy_async_global();
+                waited = li;
+            }
+            const uint8_t *tiles = l.w + static_cast<size_t>(block) * l.num_kb * kWBytes;
+            for (int j = 0; j < nkb; ++j) {
+                const uint32_t q = pos + j, slot = q % kStages;
+                if (j >= pre) {
+                    if (!mbar_wait(bar_empty + 8 * slot, ((q / kStages) & 1u) ^ 1u, kSiteProducerEmpty))
+                        ok = false;
+                    mbar_arrive_expect_tx(bar_full + 8 * slot, kStageBytes);
+                    bulk_load(sbase + slot * kWBytes, tiles + static_cast<size_t>(k0 + j) * kWBytes, kWBytes,
+                              bar_full + 8 * slot);
+                }
+                tma_load_2d(sbase + kOffX + slot * kXBytes, &p.x_maps[li], bar_full + 8 * slot, (k0 + j) * kBK, 0);
+            }
+            // Weights of the next unit's first stages.
+            pre = 0;
+            if (nli < p.count) {
+                const Link &nl = p.links[nli];
+                int nk0, nk1;
+                kb_range(nl, nk0, nk1);
+                const uint8_t *ntiles = nl.w + static_cast<size_t>(cl + nu * p.clusters) * nl.num_kb * kWBytes;
+                pre = nk1 - nk0 < kStages ? nk1 - nk0 : kStages;
+                for (int j = 0; j < pre; ++j) {
+                    const uint32_t q = pos + nkb + j, slot = q % kStages;
+                    if (!mbar_wait(bar_empty + 8 * slot, ((q / kStages) & 1u) ^ 1u, kSiteProducerEmpty))
+                        ok = false;
+                    mbar_arrive_expect_tx(bar_full + 8 * slot, kStageBytes);
+                    bulk_load(sbase + slot * kWBytes, ntiles + static_cast<size_t>(nk0 + j) * kWBytes, kWBytes,
+                              bar_full + 8 * slot);
+                }
+            }
+        } else if (threadIdx.x == 32) {
+            // ---------------- MMA issuer ----------------
+            constexpr uint32_t idesc = idesc_e4m3_f32<kRows, kAct>();
+            for (int j = 0; j < nkb; ++j) {
+                const uint32_t q = pos + j, slot = q % kStages;
+                if (!mbar_wait(bar_full + 8 * slot, (q / kStages) & 1u, kSiteMmaFull))
+                    ok = false;
+                tc_fence_after();
+#pragma unroll
+                for (int k = 0; k < kBK / 32; ++k)
+                    mma_f8f6f4(tmem_base, smem_desc_k_sw128(sbase + slot * kWBytes + k * 32),
+                               smem_desc_k_sw128(sbase + kOffX + slot * kXBytes + k * 32), idesc, (j | k) != 0);
+                mma_commit(bar_empty + 8 * slot);
+            }
+            if (nkb > 0)
+                mma_commit(bar_acc);
+        }
+        pos += nkb;
+
+        // ---------------- epilogue: partials, cluster reduction, outputs ----------------
+        uint32_t v[kAct];
+        if (nkb > 0) {
+            ok = __all_sync(0xffffffffu, mbar_wait(bar_acc, acc_uses & 1u, kSiteEpilogueAccFull)) && ok;
+            ++acc_uses;
+            tc_fence_after();
+            tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(warp * 32) << 16), v);
+            tmem_wait_ld();
+            tc_fence_before();
+        } else {
+#pragma unroll
+            for (int i = 0; i < kAct; ++i)
+                v[i] = 0u; // this CTA's K slice is empty
+        }
+#pragma unroll
+        for (int i = 0; i < kAct; ++i)
+            red[i * kRedStride + threadIdx.x] = __uint_as_float(v[i]);
+        cluster_sync();
+        float acc[kAct / 2];
+        if (my_n < l.n)
+            skinny::reduce_rows<kCS>(red, my_row, p.m, acc);
+        const float act_scale = l.act_scale_ptr ? *l.act_scale_ptr : l.act_scale;
+        const float cs = act_scale * my_ws;
+        const uint64_t neg_scale2 = f2_bits(-l.next_scale, -l.next_scale);
+        const uint64_t recip2 = f2_bits(l.next_recip, l.next_recip);
+        if (my_n < l.n) {
+            const int g = static_cast<int>(threadIdx.x) / (kRows / kCS);
+#pragma unroll
+            for (int j = 0; j < kAct / kCS; ++j) {
+                const int m = g + j * kCS;
+                if (m >= p.m)
+                    continue;
+                uint32_t z = f2h_rn(acc[j] * cs);
+                if (l.bias)
+                    z = hadd_rn(static_cast<uint16_t>(z), my_bias);
+                if (l.gelu)
+                    z = gemm::gelu_fp16x2(z, g_erf_table) & 0xFFFFu;
+                const size_t o = static_cast<size_t>(m) * l.n + my_n;
+                if (l.y)
+                    l.y[o] = static_cast<uint16_t>(z);
+                if (l.codes)
+                    l.codes[o] = static_cast<uint8_t>(e4m3x2_quotient(z, neg_scale2, recip2) & 0xFFu);
+            }
+        }
+        // Later links read these codes with TMA (the async proxy).
+        fence_proxy_async_global();
+        // Peers have read this CTA's partials and every rank's outputs are written.
+        cluster_sync();
+        if (nli != li && rank == 0 && threadIdx.x == 0) {
+            // This cluster's last block of link li: publish its blocks.
+            const unsigned int mine = static_cast<unsigned int>((blocks_of(l) - 1 - cl) / p.clusters + 1);
+            fence_gpu();
+            red_release_gpu_add(p.done + li, mine);
+        }
+        li = nli;
+        u = nu;
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, 32);
+    }
+    cluster_sync();
+}
+
+} // namespace chain
 
 // ---------------------------------------------------------------------------
 // Quantize / scale kernels.
@@ -2531,6 +2802,132 @@ cudaError_t launch_self_attention(const SelfAttentionLaunch &L, cudaStream_t str
     const cudaError_t err = cudaLaunchKernelEx(&config, sattn::self_attention_kernel, tm_q, tm_k, tm_v, p);
     count_launch();
     return err != cudaSuccess ? err : cudaGetLastError();
+}
+
+struct ChainPlan {
+    void *device = nullptr; // [x maps][links][done counters]
+    const CUtensorMap *maps = nullptr;
+    const chain::Link *links = nullptr;
+    unsigned int *done = nullptr;
+    int count = 0, m = 0, clusters = 0, device_id = 0;
+};
+
+cudaError_t chain_create(const LinearLaunch *links, int count, ChainPlan **plan)
+{
+    *plan = nullptr;
+    std::vector<CUtensorMap> maps(static_cast<size_t>(count));
+    std::vector<chain::Link> host(static_cast<size_t>(count));
+    int max_blocks = 1;
+    for (int i = 0; i < count; ++i) {
+        const LinearLaunch &L = links[i];
+        if (!make_map(&maps[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.x_codes, L.m, L.k, skinny::kBK, skinny::kAct,
+                      CU_TENSOR_MAP_SWIZZLE_128B))
+            return cudaErrorInvalidValue;
+        chain::Link &c = host[i];
+        c.w = L.w_codes;
+        c.w_scales = L.w_scales;
+        c.bias = L.bias;
+        c.act_scale_ptr = L.act_scale_ptr;
+        c.y = L.y;
+        c.codes = L.next_codes;
+        c.n = static_cast<int>(L.n);
+        c.num_kb = static_cast<int>((L.k + skinny::kBK - 1) / skinny::kBK);
+        c.gelu = L.gelu ? 1 : 0;
+        c.act_scale = L.act_scale;
+        c.next_scale = L.next_scale;
+        c.next_recip = L.next_codes ? static_cast<float>(1.0 / static_cast<double>(L.next_scale)) : 0.0f;
+        c.next_lean = L.next_codes && lean_scale(L.next_scale) ? 1 : 0;
+        max_blocks = std::max(max_blocks, (c.n + skinny::kRows - 1) / skinny::kRows);
+    }
+    cudaError_t err = ensure_smem(chain::chain_kernel, chain::kSmemBytes);
+    if (err != cudaSuccess)
+        return err;
+    // As many clusters as the widest link has row blocks, if that many can be
+    // resident at once (each spins on the others' progress).
+    cudaLaunchConfig_t config{};
+    config.gridDim = dim3(chain::kCS);
+    config.blockDim = dim3(chain::kThreads);
+    config.dynamicSmemBytes = chain::kSmemBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = chain::kCS;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    config.attrs = attr;
+    config.numAttrs = 1;
+    int resident = 0;
+    err = cudaOccupancyMaxActiveClusters(&resident, chain::chain_kernel, &config);
+    if (err != cudaSuccess || resident < 1)
+        return err != cudaSuccess ? err : cudaErrorInvalidConfiguration;
+    auto *plan_ptr = new (std::nothrow) ChainPlan();
+    if (!plan_ptr)
+        return cudaErrorMemoryAllocation;
+    const size_t maps_bytes = sizeof(CUtensorMap) * static_cast<size_t>(count);
+    const size_t links_bytes = (sizeof(chain::Link) * static_cast<size_t>(count) + 255) / 256 * 256;
+    const size_t done_bytes = sizeof(unsigned int) * static_cast<size_t>(count);
+    err = cudaMalloc(&plan_ptr->device, maps_bytes + links_bytes + done_bytes);
+    if (err != cudaSuccess) {
+        delete plan_ptr;
+        return err;
+    }
+    auto *base = static_cast<uint8_t *>(plan_ptr->device);
+    err = cudaMemcpy(base, maps.data(), maps_bytes, cudaMemcpyHostToDevice);
+    if (err == cudaSuccess)
+        err = cudaMemcpy(base + maps_bytes, host.data(), sizeof(chain::Link) * static_cast<size_t>(count),
+                         cudaMemcpyHostToDevice);
+    if (err != cudaSuccess) {
+        cudaFree(plan_ptr->device);
+        delete plan_ptr;
+        return err;
+    }
+    plan_ptr->maps = reinterpret_cast<const CUtensorMap *>(base);
+    plan_ptr->links = reinterpret_cast<const chain::Link *>(base + maps_bytes);
+    plan_ptr->done = reinterpret_cast<unsigned int *>(base + maps_bytes + links_bytes);
+    plan_ptr->count = count;
+    plan_ptr->m = static_cast<int>(links[0].m);
+    plan_ptr->clusters = std::min(max_blocks, resident);
+    plan_ptr->device_id = current_device();
+    *plan = plan_ptr;
+    return cudaSuccess;
+}
+
+cudaError_t chain_run(const ChainPlan *plan, cudaStream_t stream)
+{
+    if (current_device() != plan->device_id)
+        return cudaErrorInvalidDevice; // descriptors live on the creating device
+    cudaError_t err = cudaMemsetAsync(plan->done, 0, sizeof(unsigned int) * static_cast<size_t>(plan->count), stream);
+    if (err != cudaSuccess)
+        return err;
+    chain::Params p{};
+    p.links = plan->links;
+    p.x_maps = plan->maps;
+    p.done = plan->done;
+    p.count = plan->count;
+    p.m = plan->m;
+    p.clusters = plan->clusters;
+    cudaLaunchConfig_t config{};
+    config.gridDim = dim3(static_cast<unsigned>(plan->clusters * chain::kCS));
+    config.blockDim = dim3(chain::kThreads);
+    config.dynamicSmemBytes = chain::kSmemBytes;
+    config.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = chain::kCS;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    config.attrs = attr;
+    config.numAttrs = 1;
+    err = cudaLaunchKernelEx(&config, chain::chain_kernel, p);
+    count_launch();
+    return err != cudaSuccess ? err : cudaGetLastError();
+}
+
+void chain_destroy(ChainPlan *plan)
+{
+    if (!plan)
+        return;
+    cudaFree(plan->device);
+    delete plan;
 }
 
 cudaError_t launch_quantize_rows(const uint16_t *w, int64_t rows, int64_t cols, const float *scales,

@@ -71,6 +71,11 @@ struct SelfAttentionLaunch {
     uint8_t *codes;
 };
 cudaError_t launch_self_attention(const SelfAttentionLaunch &p, cudaStream_t stream);
+// Persistent chain of small-M linears (packed weights, one m).
+struct ChainPlan; // device descriptors, opaque to callers
+cudaError_t chain_create(const LinearLaunch *links, int count, ChainPlan **plan);
+cudaError_t chain_run(const ChainPlan *plan, cudaStream_t stream);
+void chain_destroy(ChainPlan *plan);
 cudaError_t launch_quantize(const uint16_t *x, int64_t count, float scale, const float *scale_ptr,
                             uint8_t *codes, cudaStream_t stream);
 cudaError_t launch_quantize_rows(const uint16_t *w, int64_t rows, int64_t cols,

@@ -21,6 +21,7 @@ enum WaitSite : int {
     kSiteEpilogueAccFull = 4,
     kSiteDrain = 5,
     kSiteClusterExchange = 6,
+    kSiteChainDependency = 7,
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p)
@@ -358,6 +359,25 @@ __device__ __forceinline__ void fence_cluster()
 {
     asm volatile("fence.acq_rel.cluster;" ::: "memory");
 }
+
+// Chain dependencies through global counters: a release add by the producer of
+// a result, an acquire load by its consumers, then a proxy fence so that the
+// consumer's TMA (async proxy) reads see what generic stores wrote.
+__device__ __forceinline__ void red_release_gpu_add(unsigned int *addr, unsigned int v)
+{
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int *addr)
+{
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void fence_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
 // Store into another CTA's shared memory (a cluster address from map_to_rank).
 __device__ __forceinline__ void st_shared_cluster_f32(uint32_t cluster_addr, float v)

@@ -268,6 +268,60 @@ def linear(x_codes: torch.Tensor, w_codes: torch.Tensor, w_scales: torch.Tensor,
     return (out if want_y else None), next_codes
 
 
+class LinearChain:
+    """Dependent small-m linears (m <= 32, packed weights) run back to back in one
+    persistent launch: link i reads what earlier links wrote.  Each link is a dict
+    of fp8.linear's arguments: x_codes, w_packed, w_scales, act_scale and
+    optionally bias, gelu, out (fp16 y), next_scale + next_codes.  The tensors are
+    bound at construction (they must stay alive); run() launches the chain."""
+
+    def __init__(self, links: list[dict]):
+        self._handle = None
+        self._keep = []  # tensors the device descriptors point to
+        args = (native.LinearArgs * len(links))()
+        for a, link in zip(args, links):
+            x_codes, w_packed, w_scales = link["x_codes"], link["w_packed"], link["w_scales"]
+            _require(x_codes, torch.uint8, "x_codes")
+            _require(w_packed, torch.uint8, "w_packed")
+            _require(w_scales, torch.float32, "w_scales")
+            k = x_codes.shape[-1]
+            a.struct_size = ctypes.sizeof(native.LinearArgs)
+            a.m, a.n, a.k = x_codes.numel() // k, w_scales.shape[0], k
+            a.x_codes = x_codes.data_ptr()
+            scale = link["act_scale"]
+            if isinstance(scale, torch.Tensor):
+                _require(scale, torch.float32, "act_scale")
+                a.act_scale_ptr = scale.data_ptr()
+            else:
+                a.act_scale = float(scale)
+            a.w_codes = w_packed.data_ptr()
+            a.w_layout = native.WEIGHTS_SKINNY_TILES
+            a.w_scales = w_scales.data_ptr()
+            a.bias = _ptr(link.get("bias"))
+            a.epilogue = native.EPILOGUE_GELU if link.get("gelu") else native.EPILOGUE_NONE
+            a.y = _ptr(link.get("out"))
+            a.next_scale = float(link["next_scale"]) if link.get("next_codes") is not None else 0.0
+            a.next_codes = _ptr(link.get("next_codes"))
+            self._keep.append(link)
+        handle = ctypes.c_void_p()
+        native.check(native.library().lffw_chain_create(args, len(links), ctypes.byref(handle)), "lffw_chain_create")
+        self._handle = handle
+
+    def run(self, stream=None) -> None:
+        native.check(native.library().lffw_chain_run(self._handle, _stream(stream)), "lffw_chain_run")
+
+    def close(self) -> None:
+        if self._handle is not None:
+            native.library().lffw_chain_destroy(self._handle)
+            self._handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 @dataclass
 class QuantizedWeight:
     """A linear's device-resident E4M3 weight, per-channel scales and fp16 bias."""

@@ -56,6 +56,40 @@ def test_linear_abi_mismatch_and_null(native, lib):
     assert lib.lffw_fp8_linear(None, None) == native.INVALID_ARGUMENT
 
 
+def _chain(native, lib, links):
+    arr = (native.LinearArgs * len(links))(*links)
+    handle = ctypes.c_void_p(0x1234)
+    status = lib.lffw_chain_create(arr, len(links), ctypes.byref(handle))
+    return status, handle.value
+
+
+@pytest.mark.parametrize("links", [
+    # row-major weights, m above the small-m limit, links of different m, a bad link
+    lambda n: [_linear_args(n, m=4)],
+    lambda n: [_linear_args(n, m=33, w_layout=n.WEIGHTS_SKINNY_TILES)],
+    lambda n: [_linear_args(n, m=4, w_layout=n.WEIGHTS_SKINNY_TILES),
+               _linear_args(n, m=5, w_layout=n.WEIGHTS_SKINNY_TILES)],
+    lambda n: [_linear_args(n, m=4, w_layout=n.WEIGHTS_SKINNY_TILES),
+               _linear_args(n, m=4, w_layout=n.WEIGHTS_SKINNY_TILES, act_scale=0.0)],
+])
+def test_chain_rejects_invalid_links(native, lib, links):
+    status, handle = _chain(native, lib, links(native))
+    assert status == native.INVALID_ARGUMENT
+    assert handle is None  # the out-pointer is cleared on failure
+
+
+def test_chain_null_and_count(native, lib):
+    bad = native.INVALID_ARGUMENT
+    one = (native.LinearArgs * 1)(_linear_args(native, m=4, w_layout=native.WEIGHTS_SKINNY_TILES))
+    handle = ctypes.c_void_p()
+    assert lib.lffw_chain_create(None, 1, ctypes.byref(handle)) == bad
+    assert lib.lffw_chain_create(one, 0, ctypes.byref(handle)) == bad
+    assert lib.lffw_chain_create(one, -1, ctypes.byref(handle)) == bad
+    assert lib.lffw_chain_create(one, 1, None) == bad
+    assert lib.lffw_chain_run(None, None) == bad
+    lib.lffw_chain_destroy(None)  # a no-op
+
+
 def test_other_entry_points_reject_invalid_arguments(native, lib):
     bad = native.INVALID_ARGUMENT
     assert lib.lffw_fp8_quantize(0x1000, 16, 0.0, None, 0x2000, None) == bad
