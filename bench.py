@@ -520,7 +520,10 @@ def run_decoder(fp8, native, device, steps: int, warmup: int, seed: int, layers_
     ms_calls = measure(step)
     calls_out = (outs["fc2"].clone(), logits.clone())
     ms_chain = measure(chained_step)
-    if not (torch.equal(calls_out[0], outs["fc2"]) and torch.equal(calls_out[1], logits)):
+    # Same products, another fp32 summation order: a loose check against gross
+    # errors (the tests bound both paths against the oracle).
+    if not (torch.allclose(calls_out[0].float(), outs["fc2"].float(), rtol=2.0**-6, atol=2.0**-6)
+            and torch.equal(calls_out[1], logits)):
         raise RuntimeError("the chained decoder step differs from the per-call step")
     chain.close()
     ms = min(ms_calls, ms_chain)

@@ -28,6 +28,7 @@
 #include <mutex>
 #include <new>
 #include <string>
+#include <tuple>
 #include <set>
 #include <utility>
 #include <vector>
@@ -1034,21 +1035,40 @@ __global__ void __launch_bounds__(256)
 
 namespace chain {
 
+// Persistent chain of small-m linears.  One CTA per SM owns a fixed list of
+// units in chain order; a unit is one 128-row block of one link's weights over
+// a K slice of at most kMaxUnitKb 16 KB tiles.  Each role walks the same list:
+//   warp 0: loads a unit's weight tiles as soon as the previous unit's MMAs
+//           are done -- normally a layer before the unit's activations exist;
+//   warp 1: loads a unit's activations once every row block of the previous
+//           link is complete (a release/acquire counter per link);
+//   warp 2: issues the unit's MMAs into one of two TMEM accumulators;
+//   warps 3-6: epilogue.  An unsplit unit finishes its rows directly; the K
+//           slices of a split unit write fp32 partials and the last slice to
+//           arrive (an atomic counter per row block) sums them in slice order.
+// Each buffer is one unit long and each handoff is one mbarrier phase per unit
+// (a completed-phase wait still costs ~100 cycles, so per-tile barriers would
+// dominate a unit's critical path).  Nothing waits on another CTA except
+// through the link counters, so the only requirement is that all CTAs are
+// resident (one per SM).
 using skinny::kAct;
 using skinny::kBK;
-using skinny::kRedStride;
 using skinny::kRows;
 using skinny::kWBytes;
 using skinny::kXBytes;
-constexpr int kThreads = 128;
-constexpr int kCS = 8; // CTAs per cluster (K split)
-constexpr int kStages = 2;
-constexpr int kStageBytes = kWBytes + kXBytes;
-constexpr int kOffX = kStages * kWBytes;
-constexpr int kOffRed = kOffX + kStages * kXBytes; // not aliased: the next unit's weights arrive early
-constexpr int kRedBytes = kAct * kRedStride * 4;
-constexpr int kOffBar = (kOffRed + kRedBytes + 127) / 128 * 128;
+constexpr int kMaxUnitKb = 10; // 160 KB of weights per unit
+constexpr int kEpiWarp0 = 3;
+constexpr int kEpiThreads = 128;
+constexpr int kThreads = 32 * kEpiWarp0 + kEpiThreads;
+constexpr int kOffX = kMaxUnitKb * kWBytes;
+constexpr int kOffBar = kOffX + kMaxUnitKb * kXBytes;
+constexpr int kBars = 9; // w_full, x_full[2] (the unit's two halves), acc_full[2], acc_empty[2], drain
 constexpr int kSmemBytes = kOffBar + 128 + 1024;
+static_assert(kSmemBytes <= 232448, "shared memory budget");
+// Distinct activation tensor maps passed as kernel parameters (TMA reads a
+// parameter-space descriptor without a global fetch per load); chains with
+// more distinct activation buffers keep them in global memory.
+constexpr int kParamMaps = 48;
 
 struct Link {
     const uint8_t *w; // packed 16 KB tiles (lffw_pack_skinny_weights)
@@ -1057,232 +1077,289 @@ struct Link {
     const float *act_scale_ptr;
     uint16_t *y;
     uint8_t *codes;
-    int n, num_kb, gelu, next_lean;
-    float act_scale, next_scale, next_recip, pad;
+    float *partials;        // split links: [blocks][split][kAct][kRows] fp32
+    unsigned int *arrivals; // split links: K slices finished, per row block
+    int n, num_kb, split, slice_kb, gelu, map; // map: index of the link's activation tensor map
+    float act_scale, next_scale, next_recip, pad1;
+};
+
+struct Unit {
+    int link, block, k0, k1;
 };
 
 struct Params {
+    CUtensorMap maps[kParamMaps]; // activation codes [m, k], 128-byte x 32-row boxes, SW128
+    const CUtensorMap *global_maps; // used instead when non-null
     const Link *links;
-    const CUtensorMap *x_maps; // one per link: activation codes [m, k], 128-byte x 32-row boxes, SW128
-    unsigned int *done;        // per link: 128-row blocks finished
-    int count, m, clusters;
+    const Unit *units;         // CTA c's units are units[first[c] .. first[c + 1])
+    const int *first;
+    unsigned int *done; // per link: row blocks finished
+    int m;
 };
 
-__device__ __forceinline__ int blocks_of(const Link &l) { return (l.n + kRows - 1) / kRows; }
+__device__ __forceinline__ unsigned int blocks_of(const Link &l) { return (l.n + kRows - 1) / kRows; }
 
-__global__ void __launch_bounds__(kThreads) chain_kernel(const Params p)
+__global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constant__ Params p)
 {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
     const uint32_t sbase = smem_u32(smem);
     const int warp = threadIdx.x / 32;
-    const int rank = static_cast<int>(blockIdx.x) % kCS;
-    const int cl = static_cast<int>(blockIdx.x) / kCS;
-    const uint32_t bar_full = sbase + kOffBar;
-    const uint32_t bar_empty = bar_full + 8 * kStages;
-    const uint32_t bar_acc = bar_empty + 8 * kStages;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 8 * (2 * kStages + 1));
-    float *red = reinterpret_cast<float *>(smem + kOffRed);
+    const int lane = threadIdx.x % 32;
+    const uint32_t w_full = sbase + kOffBar;
+    const uint32_t x_full = w_full + 8; // [2]: K blocks [0, h) and [h, nkb), h = (nkb + 1) / 2
+    const uint32_t acc_full = x_full + 16;
+    const uint32_t acc_empty = acc_full + 16;
+    const uint32_t drain = acc_empty + 16;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 8 * kBars);
+    volatile int *last_flag = reinterpret_cast<volatile int *>(smem + kOffBar + 8 * kBars + 4);
+    const int u_begin = p.first[blockIdx.x];
+    const int u_end = p.first[blockIdx.x + 1];
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(bar_full + 8 * s, 1);
-            mbar_init(bar_empty + 8 * s, 1);
+        mbar_init(w_full, 1);
+        mbar_init(x_full, 1);
+        mbar_init(x_full + 8, 1);
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(acc_full + 8 * a, 1);
+            mbar_init(acc_empty + 8 * a, kEpiThreads / 32);
         }
-        mbar_init(bar_acc, 1);
+        mbar_init(drain, 1);
         fence_barrier_init();
     }
-    if (warp == 1) {
-        tmem_alloc(smem_u32(tmem_slot), 32);
+    if (warp == 2) {
+        tmem_alloc(smem_u32(tmem_slot), 2 * kAct);
         tmem_relinquish();
     }
     tc_fence_before();
     __syncthreads();
-    cluster_sync();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-
-    // This cluster's units in link order: (link li, unit u) -> row block cl + u * clusters.
-    auto first_unit = [&](int li, int u, int &oli, int &ou) {
-        while (li < p.count && cl + u * p.clusters >= blocks_of(p.links[li])) {
-            ++li;
-            u = 0;
-        }
-        oli = li;
-        ou = u;
+    // The previous unit's MMAs are complete (its buffers are free): acc_full
+    // of unit local - 1, waited on by the producers as well as the epilogue.
+    auto previous_done = [&](int local) {
+        return local == 0 || mbar_wait(acc_full + 8 * ((local - 1) & 1), ((local - 1) >> 1) & 1u, kSiteProducerEmpty);
     };
-    auto kb_range = [&](const Link &l, int &k0, int &k1) {
-        k0 = static_cast<int>((static_cast<int64_t>(l.num_kb) * rank) / kCS);
-        k1 = static_cast<int>((static_cast<int64_t>(l.num_kb) * (rank + 1)) / kCS);
-    };
-    bool ok = true;
-    uint32_t pos = 0;      // ring stages used so far (producer and MMA count the same sequence)
-    uint32_t acc_uses = 0; // accumulator commits so far
-    int waited = 0;        // links [0, waited) are known complete
-    int pre = 0;           // stages of the current unit already armed with their weights
-    int li, u;
-    first_unit(0, 0, li, u);
-    if (threadIdx.x == 0 && li < p.count) {
-        // Weights of the first unit before anything else.
-        const Link &l = p.links[li];
-        int k0, k1;
-        kb_range(l, k0, k1);
-        const uint8_t *tiles = l.w + static_cast<size_t>(cl + u * p.clusters) * l.num_kb * kWBytes;
-        pre = k1 - k0 < kStages ? k1 - k0 : kStages;
-        for (int j = 0; j < pre; ++j) {
-            mbar_arrive_expect_tx(bar_full + 8 * ((pos + j) % kStages), kStageBytes);
-            bulk_load(sbase + ((pos + j) % kStages) * kWBytes, tiles + static_cast<size_t>(k0 + j) * kWBytes,
-                      kWBytes, bar_full + 8 * ((pos + j) % kStages));
-        }
-    }
-    while (li < p.count) {
-        const Link &l = p.links[li];
-        const int block = cl + u * p.clusters;
-        const int n0 = block * kRows;
-        int k0, k1;
-        kb_range(l, k0, k1);
-        const int nkb = k1 - k0;
-        // Row constants for the epilogue, requested early.
-        const int my_row = rank * (kRows / kCS) + static_cast<int>(threadIdx.x) % (kRows / kCS);
-        const int my_n = n0 + my_row;
-        float my_ws = 0.0f;
-        uint16_t my_bias = 0;
-        if (my_n < l.n) {
-            my_ws = __ldg(l.w_scales + my_n);
-            if (l.bias)
-                my_bias = __ldg(l.bias + my_n);
-        }
-        // The next unit of this cluster (for the early weight requests).
-        int nli, nu;
-        first_unit(li, u + 1, nli, nu);
 
-        if (threadIdx.x == 0) {
-            // ---------------- producer ----------------
-            if (li > 0 && waited < li) {
-                // Every block of the previous link is done before its outputs are read.
-                const int need = blocks_of(p.links[li - 1]);
-                const uint64_t start = global_timer_ns();
-                for (uint32_t spin = 0; ok && ld_acquire_gpu(p.done + li - 1) < static_cast<unsigned>(need); ++spin)
-                    if ((spin & 63u) == 63u && global_timer_ns() - start > 2000000000ull) {
-                        atomicCAS(&g_device_error, 0, kSiteChainDependency);
-                        ok = false;
-                    }
-                fence_proxy_async_global();
-                waited = li;
+    if (warp == 0) {
+        // ---------------- weight producer ----------------
+        if (lane == 0) {
+            int issued = 0; // units whose loads were issued
+            for (int i = u_begin, local = 0; i < u_end; ++i, ++local) {
+                if (!previous_done(local))
+                    break;
+                const Unit un = p.units[i];
+                const uint8_t *tiles = p.links[un.link].w + static_cast<size_t>(un.block) * p.links[un.link].num_kb * kWBytes;
+                mbar_arrive_expect_tx(w_full, static_cast<uint32_t>(un.k1 - un.k0) * kWBytes);
+                for (int kb = un.k0; kb < un.k1; ++kb)
+                    bulk_load(sbase + (kb - un.k0) * kWBytes, tiles + static_cast<size_t>(kb) * kWBytes, kWBytes, w_full);
+                issued = local + 1;
             }
-            const uint8_t *tiles = l.w + static_cast<size_t>(block) * l.num_kb * kWBytes;
-            for (int j = 0; j < nkb; ++j) {
-                const uint32_t q = pos + j, slot = q % kStages;
-                if (j >= pre) {
-                    if (!mbar_wait(bar_empty + 8 * slot, ((q / kStages) & 1u) ^ 1u, kSiteProducerEmpty))
-                        ok = false;
-                    mbar_arrive_expect_tx(bar_full + 8 * slot, kStageBytes);
-                    bulk_load(sbase + slot * kWBytes, tiles + static_cast<size_t>(k0 + j) * kWBytes, kWBytes,
-                              bar_full + 8 * slot);
+            // A load still in flight (only after an abandoned wait) lands before exit.
+            if (issued > 0)
+                for (int t = 0; t < (1 << 20) && !mbar_try_wait(w_full, (issued - 1) & 1u); ++t) {
                 }
-                tma_load_2d(sbase + kOffX + slot * kXBytes, &p.x_maps[li], bar_full + 8 * slot, (k0 + j) * kBK, 0);
-            }
-            // Weights of the next unit's first stages.
-            pre = 0;
-            if (nli < p.count) {
-                const Link &nl = p.links[nli];
-                int nk0, nk1;
-                kb_range(nl, nk0, nk1);
-                const uint8_t *ntiles = nl.w + static_cast<size_t>(cl + nu * p.clusters) * nl.num_kb * kWBytes;
-                pre = nk1 - nk0 < kStages ? nk1 - nk0 : kStages;
-                for (int j = 0; j < pre; ++j) {
-                    const uint32_t q = pos + nkb + j, slot = q % kStages;
-                    if (!mbar_wait(bar_empty + 8 * slot, ((q / kStages) & 1u) ^ 1u, kSiteProducerEmpty))
-                        ok = false;
-                    mbar_arrive_expect_tx(bar_full + 8 * slot, kStageBytes);
-                    bulk_load(sbase + slot * kWBytes, ntiles + static_cast<size_t>(nk0 + j) * kWBytes, kWBytes,
-                              bar_full + 8 * slot);
+        }
+    } else if (warp == 1) {
+        // ---------------- activation producer ----------------
+        if (lane == 0) {
+            int issued = 0;
+            int ready = 0; // links [0, ready) are complete
+            for (int i = u_begin, local = 0; i < u_end; ++i, ++local) {
+                const Unit un = p.units[i];
+                const int mi = p.links[un.link].map;
+                const CUtensorMap *map = p.global_maps ? p.global_maps + mi : &p.maps[mi];
+                prefetch_tensor_map(map);
+                if (!previous_done(local))
+                    break;
+                if (un.link > ready) {
+                    const unsigned int need = blocks_of(p.links[un.link - 1]);
+                    const uint64_t start = global_timer_ns();
+                    bool ok = true;
+                    for (uint32_t spin = 0; ld_acquire_gpu(p.done + un.link - 1) < need; ++spin)
+                        if ((spin & 63u) == 63u &&
+                            (device_error_raised() || global_timer_ns() - start > 2000000000ull)) {
+                            atomicCAS(&g_device_error, 0, kSiteChainDependency);
+                            ok = false;
+                            break;
+                        }
+                    if (!ok)
+                        break;
+                    // The previous links' outputs were written by generic stores; TMA reads them.
+                    fence_proxy_async_global();
+                    ready = un.link;
                 }
+                // Two halves, so that the MMAs start while the second half lands.
+                const int nkb = un.k1 - un.k0, h = (nkb + 1) / 2;
+                mbar_arrive_expect_tx(x_full, static_cast<uint32_t>(h) * kXBytes);
+                mbar_arrive_expect_tx(x_full + 8, static_cast<uint32_t>(nkb - h) * kXBytes);
+                for (int j = 0; j < nkb; ++j)
+                    tma_load_2d(sbase + kOffX + j * kXBytes, map, x_full + (j < h ? 0 : 8), (un.k0 + j) * kBK, 0);
+                issued = local + 1;
             }
-        } else if (threadIdx.x == 32) {
-            // ---------------- MMA issuer ----------------
+            for (int half = 0; issued > 0 && half < 2; ++half)
+                for (int t = 0; t < (1 << 20) && !mbar_try_wait(x_full + 8 * half, (issued - 1) & 1u); ++t) {
+                }
+        }
+    } else if (warp == 2) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
             constexpr uint32_t idesc = idesc_e4m3_f32<kRows, kAct>();
-            for (int j = 0; j < nkb; ++j) {
-                const uint32_t q = pos + j, slot = q % kStages;
-                if (!mbar_wait(bar_full + 8 * slot, (q / kStages) & 1u, kSiteMmaFull))
-                    ok = false;
-                tc_fence_after();
+            for (int i = u_begin, local = 0; i < u_end; ++i, ++local) {
+                const Unit un = p.units[i];
+                const uint32_t a = local & 1;
+                if (!mbar_wait(acc_empty + 8 * a, ((local >> 1) & 1u) ^ 1u, kSiteMmaAccEmpty) ||
+                    !mbar_wait(w_full, local & 1u, kSiteMmaFull))
+                    break;
+                const uint32_t d = tmem_base + a * kAct;
+                const int nkb = un.k1 - un.k0, h = (nkb + 1) / 2;
+                bool ok = true;
+                for (int half = 0; ok && half < 2; ++half) {
+                    if (!mbar_wait(x_full + 8 * half, local & 1u, kSiteMmaFull)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    for (int kb = half ? h : 0; kb < (half ? nkb : h); ++kb)
 #pragma unroll
-                for (int k = 0; k < kBK / 32; ++k)
-                    mma_f8f6f4(tmem_base, smem_desc_k_sw128(sbase + slot * kWBytes + k * 32),
-                               smem_desc_k_sw128(sbase + kOffX + slot * kXBytes + k * 32), idesc, (j | k) != 0);
-                mma_commit(bar_empty + 8 * slot);
+                        for (int k = 0; k < kBK / 32; ++k)
+                            mma_f8f6f4(d, smem_desc_k_sw128(sbase + kb * kWBytes + k * 32),
+                                       smem_desc_k_sw128(sbase + kOffX + kb * kXBytes + k * 32), idesc,
+                                       (kb | k) != 0 ? 1u : 0u);
+                }
+                if (!ok)
+                    break;
+                mma_commit(acc_full + 8 * a);
             }
-            if (nkb > 0)
-                mma_commit(bar_acc);
+            // Every MMA of this thread completes before TMEM is freed.
+            mma_commit(drain);
+            for (int tries = 0; tries < (1 << 22) && !mbar_try_wait(drain, 0); ++tries) {
+            }
         }
-        pos += nkb;
-
-        // ---------------- epilogue: partials, cluster reduction, outputs ----------------
-        uint32_t v[kAct];
-        if (nkb > 0) {
-            ok = __all_sync(0xffffffffu, mbar_wait(bar_acc, acc_uses & 1u, kSiteEpilogueAccFull)) && ok;
-            ++acc_uses;
+    } else {
+        // ---------------- epilogue: 4 warps, one accumulator row per thread ----------------
+        // Every epilogue thread walks all units, even after a wait has given up
+        // (waits then return at once), so the named barriers always match.
+        const int et = static_cast<int>(threadIdx.x) - 32 * kEpiWarp0;
+        const int row = 32 * (warp & 3) + lane; // TMEM lane = weight row in the block
+        for (int i = u_begin, local = 0; i < u_end; ++i, ++local) {
+            const Unit un = p.units[i];
+            const Link l = p.links[un.link]; // a copy: the stores below cannot alias it
+            const int n = un.block * kRows + row;
+            float ws = 0.0f;
+            uint16_t bias = 0;
+            if (n < l.n) {
+                ws = __ldg(l.w_scales + n);
+                if (l.bias)
+                    bias = __ldg(l.bias + n);
+            }
+            const uint32_t a = local & 1;
+            bool ok = true;
+            if (lane == 0)
+                ok = mbar_wait(acc_full + 8 * a, (local >> 1) & 1u, kSiteEpilogueAccFull);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
             tc_fence_after();
-            tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(warp * 32) << 16), v);
+            uint32_t v[kAct];
+            tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) + a * kAct, v);
             tmem_wait_ld();
             tc_fence_before();
-        } else {
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(acc_empty + 8 * a);
+            float acc[kAct];
 #pragma unroll
-            for (int i = 0; i < kAct; ++i)
-                v[i] = 0u; // this CTA's K slice is empty
-        }
+            for (int m = 0; m < kAct; ++m)
+                acc[m] = ok ? __uint_as_float(v[m]) : 0.0f;
+            bool finish = true;
+            if (l.split > 1) {
+                const int slice = un.k0 / l.slice_kb;
+                float *mine = l.partials + (static_cast<size_t>(un.block) * l.split + slice) * (kAct * kRows);
 #pragma unroll
-        for (int i = 0; i < kAct; ++i)
-            red[i * kRedStride + threadIdx.x] = __uint_as_float(v[i]);
-        cluster_sync();
-        float acc[kAct / 2];
-        if (my_n < l.n)
-            skinny::reduce_rows<kCS>(red, my_row, p.m, acc);
-        const float act_scale = l.act_scale_ptr ? *l.act_scale_ptr : l.act_scale;
-        const float cs = act_scale * my_ws;
-        const uint64_t neg_scale2 = f2_bits(-l.next_scale, -l.next_scale);
-        const uint64_t recip2 = f2_bits(l.next_recip, l.next_recip);
-        if (my_n < l.n) {
-            const int g = static_cast<int>(threadIdx.x) / (kRows / kCS);
+                for (int m = 0; m < kAct; ++m)
+                    if (m < p.m)
+                        mine[m * kRows + row] = acc[m];
+                __threadfence();
+                named_barrier_sync(1, kEpiThreads);
+                if (et == 0)
+                    *last_flag = static_cast<int>(atomicAdd(l.arrivals + un.block, 1u));
+                named_barrier_sync(1, kEpiThreads);
+                finish = *last_flag == l.split - 1;
+                if (finish) {
+                    // The other slices' partials are visible: each was fenced before its arrival.
+                    __threadfence();
+                    // Sum in slice order; the loads of up to four slices are in flight together.
+                    const float *all = l.partials + static_cast<size_t>(un.block) * l.split * (kAct * kRows) + row;
 #pragma unroll
-            for (int j = 0; j < kAct / kCS; ++j) {
-                const int m = g + j * kCS;
-                if (m >= p.m)
-                    continue;
-                uint32_t z = f2h_rn(acc[j] * cs);
-                if (l.bias)
-                    z = hadd_rn(static_cast<uint16_t>(z), my_bias);
-                if (l.gelu)
-                    z = gemm::gelu_fp16x2(z, g_erf_table) & 0xFFFFu;
-                const size_t o = static_cast<size_t>(m) * l.n + my_n;
-                if (l.y)
-                    l.y[o] = static_cast<uint16_t>(z);
-                if (l.codes)
-                    l.codes[o] = static_cast<uint8_t>(e4m3x2_quotient(z, neg_scale2, recip2) & 0xFFu);
+                    for (int m = 0; m < kAct; ++m)
+                        acc[m] = 0.0f;
+                    for (int q0 = 0; q0 < l.split; q0 += 4) {
+                        float t[4][kAct];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+#pragma unroll
+                            for (int m = 0; m < kAct; ++m)
+                                t[j][m] = q0 + j < l.split && m < p.m
+                                              ? __ldcg(all + (static_cast<size_t>(q0 + j) * kAct + m) * kRows)
+                                              : 0.0f;
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            if (q0 + j < l.split)
+#pragma unroll
+                                for (int m = 0; m < kAct; ++m)
+                                    acc[m] += t[j][m];
+                    }
+                }
+            }
+            if (finish) {
+                const float act_scale = l.act_scale_ptr ? *l.act_scale_ptr : l.act_scale;
+                const float cs = act_scale * ws;
+                const uint64_t neg_scale2 = f2_bits(-l.next_scale, -l.next_scale);
+                const uint64_t recip2 = f2_bits(l.next_recip, l.next_recip);
+                if (n < l.n) {
+                    // Rows in pairs, every row's chain independent (fully unrolled,
+                    // predicated): the GELU table reads of all rows overlap.
+#pragma unroll
+                    for (int m = 0; m < kAct; m += 2) {
+                        if (m < p.m) {
+                            uint32_t z = f2h_rn(acc[m] * cs) | (static_cast<uint32_t>(f2h_rn(acc[m + 1] * cs)) << 16);
+                            if (l.bias)
+                                z = gemm::hadd2_rn(z, static_cast<uint32_t>(bias) * 0x10001u);
+                            if (l.gelu)
+                                z = gemm::gelu_fp16x2(z, g_erf_table);
+                            const size_t o = static_cast<size_t>(m) * l.n + n;
+                            const bool second = m + 1 < p.m;
+                            if (l.y) {
+                                l.y[o] = static_cast<uint16_t>(z & 0xFFFFu);
+                                if (second)
+                                    l.y[o + l.n] = static_cast<uint16_t>(z >> 16);
+                            }
+                            if (l.codes) {
+                                const uint32_t q2 = e4m3x2_quotient(z, neg_scale2, recip2);
+                                l.codes[o] = static_cast<uint8_t>(q2 & 0xFFu);
+                                if (second)
+                                    l.codes[o + l.n] = static_cast<uint8_t>((q2 >> 8) & 0xFFu);
+                            }
+                        }
+                    }
+                }
+                // Later links read these codes with TMA: the reader orders its
+                // async-proxy loads after its acquire with a proxy fence.
+                named_barrier_sync(1, kEpiThreads);
+                if (et == 0) {
+                    fence_gpu();
+                    red_release_gpu_add(p.done + un.link, 1u);
+                }
             }
         }
-        // Later links read these codes with TMA (the async proxy).
-        fence_proxy_async_global();
-        // Peers have read this CTA's partials and every rank's outputs are written.
-        cluster_sync();
-        if (nli != li && rank == 0 && threadIdx.x == 0) {
-            // This cluster's last block of link li: publish its blocks.
-            const unsigned int mine = static_cast<unsigned int>((blocks_of(l) - 1 - cl) / p.clusters + 1);
-            fence_gpu();
-            red_release_gpu_add(p.done + li, mine);
-        }
-        li = nli;
-        u = nu;
     }
+
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == 2) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, 32);
+        tmem_dealloc(tmem_base, 2 * kAct);
     }
-    cluster_sync();
 }
 
 } // namespace chain
@@ -2479,10 +2556,13 @@ cudaError_t launch_fp8_gemm(const LinearLaunch &L, cudaStream_t stream)
     default: break;
     }
     // Measured on B200 (C2 shapes, M = 12000): 256-wide tiles beat 128-wide ones
-    // by ~30% even where 128 would fill the last wave better; CTA pairs (256-row
-    // tiles, half the B traffic per SM) win once the K loop is long, 1-CTA
-    // 128-row tiles win for K = 1280.
-    const bool pair = L.m >= 512 && L.k >= 4096;
+    // by ~30% even where 128 would fill the last wave better.  CTA pairs (256-row
+    // tiles, half the B traffic per SM, six stages instead of four) feed the MMA
+    // better: +12% for K = 5120, +3-4% for K = 1280 with fp16 outputs.  Not for the
+    // GELU code-table epilogue (E4M3 codes as the only output): there the faster
+    // main loop leaves the MMA waiting on the epilogue (-5%).
+    const bool code_table = L.gelu && L.next_codes != nullptr && L.y == nullptr;
+    const bool pair = L.m >= 512 && L.k >= 1024 && !code_table;
     return pair ? run_gemm_epilogue<256, true>(L, stream) : run_gemm_epilogue<256, false>(L, stream);
 }
 
@@ -2805,25 +2885,41 @@ cudaError_t launch_self_attention(const SelfAttentionLaunch &L, cudaStream_t str
 }
 
 struct ChainPlan {
-    void *device = nullptr; // [x maps][links][done counters]
-    const CUtensorMap *maps = nullptr;
+    void *device = nullptr; // [global maps][links][units][first][counters][partials]
+    std::vector<CUtensorMap> maps; // distinct activation maps
+    const CUtensorMap *global_maps = nullptr; // set when there are more than kParamMaps
     const chain::Link *links = nullptr;
-    unsigned int *done = nullptr;
-    int count = 0, m = 0, clusters = 0, device_id = 0;
+    const chain::Unit *units = nullptr;
+    const int *first = nullptr;
+    unsigned int *counters = nullptr; // done per link, then arrivals per split row block
+    size_t counter_bytes = 0;
+    int count = 0, m = 0, ctas = 0, device_id = 0;
 };
 
 cudaError_t chain_create(const LinearLaunch *links, int count, ChainPlan **plan)
 {
+    using chain::kAct;
+    using chain::kRows;
     *plan = nullptr;
-    std::vector<CUtensorMap> maps(static_cast<size_t>(count));
+    std::vector<CUtensorMap> maps; // one per distinct (activation buffer, m, k)
+    std::vector<std::tuple<const void *, int64_t, int64_t>> map_keys;
     std::vector<chain::Link> host(static_cast<size_t>(count));
-    int max_blocks = 1;
+    std::vector<chain::Unit> all;
+    size_t arrivals = 0, partial_floats = 0;
     for (int i = 0; i < count; ++i) {
         const LinearLaunch &L = links[i];
-        if (!make_map(&maps[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.x_codes, L.m, L.k, skinny::kBK, skinny::kAct,
-                      CU_TENSOR_MAP_SWIZZLE_128B))
-            return cudaErrorInvalidValue;
+        const auto key = std::make_tuple(static_cast<const void *>(L.x_codes), L.m, L.k);
+        int map = static_cast<int>(std::find(map_keys.begin(), map_keys.end(), key) - map_keys.begin());
+        if (map == static_cast<int>(map_keys.size())) {
+            CUtensorMap tm{};
+            if (!make_map(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.x_codes, L.m, L.k, skinny::kBK, skinny::kAct,
+                          CU_TENSOR_MAP_SWIZZLE_128B))
+                return cudaErrorInvalidValue;
+            map_keys.push_back(key);
+            maps.push_back(tm);
+        }
         chain::Link &c = host[i];
+        c.map = map;
         c.w = L.w_codes;
         c.w_scales = L.w_scales;
         c.bias = L.bias;
@@ -2832,60 +2928,100 @@ cudaError_t chain_create(const LinearLaunch *links, int count, ChainPlan **plan)
         c.codes = L.next_codes;
         c.n = static_cast<int>(L.n);
         c.num_kb = static_cast<int>((L.k + skinny::kBK - 1) / skinny::kBK);
+        // K slices of at most kMaxUnitKb tiles, none empty.
+        const int want = (c.num_kb + chain::kMaxUnitKb - 1) / chain::kMaxUnitKb;
+        c.slice_kb = (c.num_kb + want - 1) / want;
+        c.split = (c.num_kb + c.slice_kb - 1) / c.slice_kb;
         c.gelu = L.gelu ? 1 : 0;
         c.act_scale = L.act_scale;
         c.next_scale = L.next_scale;
         c.next_recip = L.next_codes ? static_cast<float>(1.0 / static_cast<double>(L.next_scale)) : 0.0f;
-        c.next_lean = L.next_codes && lean_scale(L.next_scale) ? 1 : 0;
-        max_blocks = std::max(max_blocks, (c.n + skinny::kRows - 1) / skinny::kRows);
+        const int blocks = (c.n + kRows - 1) / kRows;
+        if (c.split > 1) {
+            arrivals += static_cast<size_t>(blocks);
+            // One workspace for every split link: link i's slices run only after
+            // every earlier link has finished reading its partials.
+            partial_floats = std::max(partial_floats, static_cast<size_t>(blocks) * c.split * kAct * kRows);
+        }
+        for (int b = 0; b < blocks; ++b)
+            for (int s = 0; s < c.split; ++s)
+                all.push_back(chain::Unit{i, b, s * c.slice_kb, std::min((s + 1) * c.slice_kb, c.num_kb)});
     }
     cudaError_t err = ensure_smem(chain::chain_kernel, chain::kSmemBytes);
     if (err != cudaSuccess)
         return err;
-    // As many clusters as the widest link has row blocks, if that many can be
-    // resident at once (each spins on the others' progress).
-    cudaLaunchConfig_t config{};
-    config.gridDim = dim3(chain::kCS);
-    config.blockDim = dim3(chain::kThreads);
-    config.dynamicSmemBytes = chain::kSmemBytes;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = chain::kCS;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    config.attrs = attr;
-    config.numAttrs = 1;
-    int resident = 0;
-    err = cudaOccupancyMaxActiveClusters(&resident, chain::chain_kernel, &config);
-    if (err != cudaSuccess || resident < 1)
+    // One CTA per SM, all resident: a CTA waits only for units of earlier links,
+    // which sit earlier in every CTA's list.
+    int per_sm = 0;
+    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, chain::chain_kernel, chain::kThreads,
+                                                        chain::kSmemBytes);
+    if (err != cudaSuccess || per_sm < 1)
         return err != cudaSuccess ? err : cudaErrorInvalidConfiguration;
+    const int ctas = static_cast<int>(std::min<size_t>(static_cast<size_t>(sm_count()), all.size()));
+    // Round-robin in chain order: CTA c takes units c, c + ctas, ...
+    std::vector<chain::Unit> units;
+    units.reserve(all.size());
+    std::vector<int> first(static_cast<size_t>(ctas) + 1, 0);
+    for (int c = 0; c < ctas; ++c) {
+        first[c] = static_cast<int>(units.size());
+        for (size_t u = static_cast<size_t>(c); u < all.size(); u += static_cast<size_t>(ctas))
+            units.push_back(all[u]);
+    }
+    first[ctas] = static_cast<int>(units.size());
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = off;
+        off = (off + bytes + 255) / 256 * 256;
+        return at;
+    };
+    const bool param_maps = maps.size() <= static_cast<size_t>(chain::kParamMaps);
+    const size_t o_maps = take(param_maps ? 0 : sizeof(CUtensorMap) * maps.size());
+    const size_t o_links = take(sizeof(chain::Link) * host.size());
+    const size_t o_units = take(sizeof(chain::Unit) * units.size());
+    const size_t o_first = take(sizeof(int) * first.size());
+    const size_t counter_bytes = sizeof(unsigned int) * (static_cast<size_t>(count) + arrivals);
+    const size_t o_counters = take(counter_bytes);
+    const size_t o_partials = take(sizeof(float) * partial_floats);
     auto *plan_ptr = new (std::nothrow) ChainPlan();
     if (!plan_ptr)
         return cudaErrorMemoryAllocation;
-    const size_t maps_bytes = sizeof(CUtensorMap) * static_cast<size_t>(count);
-    const size_t links_bytes = (sizeof(chain::Link) * static_cast<size_t>(count) + 255) / 256 * 256;
-    const size_t done_bytes = sizeof(unsigned int) * static_cast<size_t>(count);
-    err = cudaMalloc(&plan_ptr->device, maps_bytes + links_bytes + done_bytes);
+    err = cudaMalloc(&plan_ptr->device, off);
     if (err != cudaSuccess) {
         delete plan_ptr;
         return err;
     }
     auto *base = static_cast<uint8_t *>(plan_ptr->device);
-    err = cudaMemcpy(base, maps.data(), maps_bytes, cudaMemcpyHostToDevice);
+    auto *counters = reinterpret_cast<unsigned int *>(base + o_counters);
+    size_t next_arrival = static_cast<size_t>(count);
+    for (chain::Link &c : host)
+        if (c.split > 1) {
+            c.partials = reinterpret_cast<float *>(base + o_partials);
+            c.arrivals = counters + next_arrival;
+            next_arrival += static_cast<size_t>((c.n + kRows - 1) / kRows);
+        }
+    if (!param_maps)
+        err = cudaMemcpy(base + o_maps, maps.data(), sizeof(CUtensorMap) * maps.size(), cudaMemcpyHostToDevice);
     if (err == cudaSuccess)
-        err = cudaMemcpy(base + maps_bytes, host.data(), sizeof(chain::Link) * static_cast<size_t>(count),
-                         cudaMemcpyHostToDevice);
+        err = cudaMemcpy(base + o_links, host.data(), sizeof(chain::Link) * host.size(), cudaMemcpyHostToDevice);
+    if (err == cudaSuccess)
+        err = cudaMemcpy(base + o_units, units.data(), sizeof(chain::Unit) * units.size(), cudaMemcpyHostToDevice);
+    if (err == cudaSuccess)
+        err = cudaMemcpy(base + o_first, first.data(), sizeof(int) * first.size(), cudaMemcpyHostToDevice);
     if (err != cudaSuccess) {
         cudaFree(plan_ptr->device);
         delete plan_ptr;
         return err;
     }
-    plan_ptr->maps = reinterpret_cast<const CUtensorMap *>(base);
-    plan_ptr->links = reinterpret_cast<const chain::Link *>(base + maps_bytes);
-    plan_ptr->done = reinterpret_cast<unsigned int *>(base + maps_bytes + links_bytes);
+    plan_ptr->maps = std::move(maps);
+    plan_ptr->global_maps = param_maps ? nullptr : reinterpret_cast<const CUtensorMap *>(base + o_maps);
+    plan_ptr->links = reinterpret_cast<const chain::Link *>(base + o_links);
+    plan_ptr->units = reinterpret_cast<const chain::Unit *>(base + o_units);
+    plan_ptr->first = reinterpret_cast<const int *>(base + o_first);
+    plan_ptr->counters = counters;
+    plan_ptr->counter_bytes = counter_bytes;
     plan_ptr->count = count;
     plan_ptr->m = static_cast<int>(links[0].m);
-    plan_ptr->clusters = std::min(max_blocks, resident);
+    plan_ptr->ctas = ctas;
     plan_ptr->device_id = current_device();
     *plan = plan_ptr;
     return cudaSuccess;
@@ -2895,31 +3031,21 @@ cudaError_t chain_run(const ChainPlan *plan, cudaStream_t stream)
 {
     if (current_device() != plan->device_id)
         return cudaErrorInvalidDevice; // descriptors live on the creating device
-    cudaError_t err = cudaMemsetAsync(plan->done, 0, sizeof(unsigned int) * static_cast<size_t>(plan->count), stream);
+    cudaError_t err = cudaMemsetAsync(plan->counters, 0, plan->counter_bytes, stream);
     if (err != cudaSuccess)
         return err;
     chain::Params p{};
+    if (plan->global_maps == nullptr)
+        std::copy(plan->maps.begin(), plan->maps.end(), p.maps);
+    p.global_maps = plan->global_maps;
     p.links = plan->links;
-    p.x_maps = plan->maps;
-    p.done = plan->done;
-    p.count = plan->count;
+    p.units = plan->units;
+    p.first = plan->first;
+    p.done = plan->counters;
     p.m = plan->m;
-    p.clusters = plan->clusters;
-    cudaLaunchConfig_t config{};
-    config.gridDim = dim3(static_cast<unsigned>(plan->clusters * chain::kCS));
-    config.blockDim = dim3(chain::kThreads);
-    config.dynamicSmemBytes = chain::kSmemBytes;
-    config.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = chain::kCS;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    config.attrs = attr;
-    config.numAttrs = 1;
-    err = cudaLaunchKernelEx(&config, chain::chain_kernel, p);
+    chain::chain_kernel<<<plan->ctas, chain::kThreads, chain::kSmemBytes, stream>>>(p);
     count_launch();
-    return err != cudaSuccess ? err : cudaGetLastError();
+    return cudaGetLastError();
 }
 
 void chain_destroy(ChainPlan *plan)
