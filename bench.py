@@ -706,7 +706,8 @@ def run_self_attention(fp8, native, device, steps: int, seed: int):
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     peak = float(peaks.get("bf16_tflops", 1590.0))
     return {"workload": "encoder self-attention, 8 streams x 1500 tokens x 20 heads x 64, one layer, "
-                        "out_proj E4M3 codes out (m16n8k16 fp16 MMAs)",
+                        "out_proj E4M3 codes out (tcgen05 kind::f16 MMAs, exact two-pass softmax; the second QK^T "
+                        "pass is not counted in the flops)",
             "ms": round(ms, 4), "flops": flops, "value": round(tflops, 1), "unit": "TFLOP/s (QK^T + P.V)",
             "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak,
                          "peak_source": "measured dense bf16 of MEASURED_PEAKS.json (fp16 runs at the bf16 rate)",

@@ -2003,20 +2003,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 namespace sattn {
 
+// Shared by the self-attention kernel (namespace fattn) and its launcher.
 constexpr int kDim = 64;
 constexpr int kBQ = 128;    // query rows per CTA
-constexpr int kChunk = 128; // keys per stage
-constexpr int kStages = 4;
-constexpr int kStageBytes = kChunk * kDim * 2;
-constexpr int kQBytes = kBQ * kDim * 2;
-constexpr int kMathWarps = kBQ / 16;
-constexpr int kThreads = (kMathWarps + 1) * 32; // + the producer warp
-constexpr int kSmemBytes = 1024 + kQBytes + kStages * kStageBytes + 128;
+constexpr int kChunk = 128; // keys per tile
 
 struct Params {
     int streams, tokens, heads;
     int qblocks; // ceil(tokens / kBQ)
-    int nchunks; // ceil(tokens / 128)
+    int nchunks; // ceil(tokens / kChunk)
     uint16_t *out;
     uint32_t scale2; // fp16 head_dim^-0.25 in both halves
     float code_scale, code_recip;
@@ -2042,247 +2037,370 @@ __device__ __forceinline__ float fast_log2(float x)
 
 constexpr float kLog2e = 1.4426950408889634f;
 
-// Scores of one 8-key n-tile: acc = Q'(16 rows) K'^T(8 keys) from the swizzled
-// K stage, then rounded to fp16 (the MatMul output edge) and returned as floats.
-__device__ __forceinline__ void score_tile(const uint32_t (&qa)[4][4], uint32_t stage, int kb, int lane,
-                                           uint32_t scale2, float (&s)[4])
-{
-    uint32_t b[8];
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-        const int mi = lane >> 3, key = kb + (lane & 7);
-        const int chunk16 = 2 * (2 * half + (mi >> 1)) + (mi & 1);
-        uint32_t r[4];
-        ldmatrix_x4(stage + key * 128 + ((chunk16 ^ (key & 7)) << 4), r);
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-            b[4 * half + i] = gemm::hmul2_rn(r[i], scale2);
-    }
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks)
-        mma_m16n8k16_f16_f32(acc, qa[ks], b[2 * ks], b[2 * ks + 1]);
-    const uint32_t lo = gemm::cvt_f16x2(acc[0], acc[1]), hi = gemm::cvt_f16x2(acc[2], acc[3]);
-    s[0] = h2f(static_cast<uint16_t>(lo & 0xFFFFu));
-    s[1] = h2f(static_cast<uint16_t>(lo >> 16));
-    s[2] = h2f(static_cast<uint16_t>(hi & 0xFFFFu));
-    s[3] = h2f(static_cast<uint16_t>(hi >> 16));
-}
+} // namespace sattn
 
-__global__ void __launch_bounds__(kThreads)
-    self_attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                          const __grid_constant__ CUtensorMap tm_v, const Params p)
+// ---------------------------------------------------------------------------
+// Encoder self-attention on tcgen05: the same two-pass exact softmax and fp16
+// edges as the oracle (q' = half(q c), k' = half(k c), s = half(q'.k'),
+// p = half(exp(s - max) / sum), out = half(sum p v)), per (stream, head,
+// 128-query block):
+//   warp 0: TMA producer (Q once; K tiles twice -- once per pass; V in pass 2);
+//   warp 1: MMA issuer.  S = Q' K'^T, kind::f16 128 x 128 x 16, into one of two
+//           TMEM score buffers; O += P V, 128 x 64 x 16 with V read MN-major
+//           straight from its TMA tile, into a third TMEM region;
+//   warp 2: rescales Q and each K tile in shared memory (half(x c)) before the
+//           MMA reads it;
+//   warps 3-10: softmax, two warps per TMEM lane quarter, each over 64 of a
+//           tile's 128 key columns.  Pass 1 keeps a running max and sum per
+//           half row (merged once through shared memory); pass 2 writes P as
+//           fp16 into a K-major 128B-swizzled tile for the P.V MMA.
+// The P.V MMAs of tile c - 1 are issued after the score MMAs of tile c, so the
+// softmax of one tile overlaps the MMAs of the next.
+namespace fattn {
+
+using sattn::kLog2e;
+using sattn::fast_exp2;
+using sattn::fast_log2;
+constexpr int kDim = 64;
+constexpr int kBQ = 128;
+constexpr int kBK = 128;
+constexpr int kKStages = 3;
+constexpr int kVStages = 3;
+constexpr int kTile = kBK * kDim * 2;  // one Q, K or V tile: 16 KB
+constexpr int kPBytes = kBQ * kBK * 2; // one P tile: two 64-key K-major halves, 32 KB
+constexpr int kSoftWarp0 = 3;
+constexpr int kSoftWarps = 8;
+constexpr int kThreads = (kSoftWarp0 + kSoftWarps) * 32;
+constexpr int kOffK = kTile;
+constexpr int kOffV = kOffK + kKStages * kTile;
+constexpr int kOffP = kOffV + kVStages * kTile;
+constexpr int kOffStats = kOffP + 2 * kPBytes; // float m[2][kBQ], l[2][kBQ]
+constexpr int kOffBar = kOffStats + 4 * kBQ * 4;
+constexpr int kBars = 2 + 3 * kKStages + 2 * kVStages + 8 + 2;
+constexpr int kSmemBytes = kOffBar + 8 * kBars + 16 + 1024;
+constexpr uint32_t kTmemCols = 512; // S[2] (2 x 128) + O (64)
+constexpr uint32_t kTmemO = 256;
+static_assert(kSmemBytes <= 232448, "shared memory budget");
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v, const sattn::Params p)
 {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
-    const uint32_t sbase = smem_u32(smem);
-    const uint32_t qs = sbase;
-    const uint32_t ring = sbase + kQBytes;
-    const uint32_t bar_full = ring + kStages * kStageBytes;
-    const uint32_t bar_empty = bar_full + 8 * kStages;
-    const uint32_t bar_q = bar_empty + 8 * kStages;
+    const uint32_t sb = smem_u32(smem);
+    const uint32_t sQ = sb, sK = sb + kOffK, sV = sb + kOffV, sP = sb + kOffP;
+    const uint32_t q_full = sb + kOffBar;
+    const uint32_t q_ready = q_full + 8;
+    const uint32_t k_full = q_ready + 8;
+    const uint32_t k_ready = k_full + 8 * kKStages;
+    const uint32_t k_empty = k_ready + 8 * kKStages;
+    const uint32_t v_full = k_empty + 8 * kKStages;
+    const uint32_t v_empty = v_full + 8 * kVStages;
+    const uint32_t s_full = v_empty + 8 * kVStages;
+    const uint32_t s_empty = s_full + 16;
+    const uint32_t p_full = s_empty + 16;
+    const uint32_t p_empty = p_full + 16;
+    const uint32_t o_full = p_empty + 16;
+    const uint32_t drain = o_full + 8;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 8 * kBars);
+    float *stat_m = reinterpret_cast<float *>(smem + kOffStats);
+    float *stat_l = stat_m + 2 * kBQ;
+
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
     const int qb = static_cast<int>(blockIdx.x) % p.qblocks;
     const int sh = static_cast<int>(blockIdx.x) / p.qblocks;
     const int head = sh % p.heads;
     const int stream = sh / p.heads;
-    const int row_base = stream * p.tokens; // token rows of this stream
+    const int row_base = stream * p.tokens;
     const int q0 = qb * kBQ;
-    const int total = 3 * p.nchunks;        // K (pass 1), then K and V interleaved (pass 2)
+    const int nt = p.nchunks;
 
     if (threadIdx.x == 0) {
         griddepcontrol_launch_dependents();
-        for (int i = 0; i < kStages; ++i) {
-            mbar_init(bar_full + 8 * i, 1);
-            mbar_init(bar_empty + 8 * i, kMathWarps);
+        mbar_init(q_full, 1);
+        mbar_init(q_ready, 1);
+        for (int s = 0; s < kKStages; ++s) {
+            mbar_init(k_full + 8 * s, 1);
+            mbar_init(k_ready + 8 * s, 1);
+            mbar_init(k_empty + 8 * s, 1);
         }
-        mbar_init(bar_q, 1);
+        for (int s = 0; s < kVStages; ++s) {
+            mbar_init(v_full + 8 * s, 1);
+            mbar_init(v_empty + 8 * s, 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(s_full + 8 * b, 1);
+            mbar_init(s_empty + 8 * b, kSoftWarps);
+            mbar_init(p_full + 8 * b, kSoftWarps);
+            mbar_init(p_empty + 8 * b, 1);
+        }
+        mbar_init(o_full, 1);
+        mbar_init(drain, 1);
         fence_barrier_init();
         prefetch_tensor_map(&tm_q);
         prefetch_tensor_map(&tm_k);
         prefetch_tensor_map(&tm_v);
     }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
     __syncthreads();
-    griddepcontrol_wait(); // the projections are written by earlier kernels
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    griddepcontrol_wait(); // q, k and v are written by earlier kernels
 
-    if (warp == kMathWarps) {
-        // ---------------- producer (one thread) ----------------
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
         if (lane == 0) {
-            mbar_arrive_expect_tx(bar_q, kQBytes);
-            tma_load_2d(qs, &tm_q, bar_q, head * kDim, row_base + q0);
-            int issued = 0;
-            for (int i = 0; i < total; ++i, ++issued) {
-                const int st = i % kStages;
-                if (!mbar_wait(bar_empty + 8 * st, ((i / kStages) & 1u) ^ 1u, kSiteProducerEmpty))
+            mbar_arrive_expect_tx(q_full, kTile);
+            tma_load_2d(sQ, &tm_q, q_full, head * kDim, row_base + q0);
+            int k_issued = 0, v_issued = 0;
+            for (int j = 0; j < 2 * nt; ++j) {
+                const int s = j % kKStages;
+                if (!mbar_wait(k_empty + 8 * s, ((j / kKStages) & 1u) ^ 1u, kSiteProducerEmpty))
                     break;
-                const bool is_v = i >= p.nchunks && ((i - p.nchunks) & 1);
-                const int c = i < p.nchunks ? i : (i - p.nchunks) >> 1;
-                mbar_arrive_expect_tx(bar_full + 8 * st, kStageBytes);
-                tma_load_2d(ring + st * kStageBytes, is_v ? &tm_v : &tm_k, bar_full + 8 * st, head * kDim,
-                            row_base + c * kChunk);
-            }
-            for (int i = issued > kStages ? issued - kStages : 0; i < issued; ++i)
-                for (int tries = 0; tries < (1 << 22) &&
-                                    !mbar_try_wait(bar_full + 8 * (i % kStages), (i / kStages) & 1u);
-                     ++tries) {
+                mbar_arrive_expect_tx(k_full + 8 * s, kTile);
+                tma_load_2d(sK + s * kTile, &tm_k, k_full + 8 * s, head * kDim, row_base + (j % nt) * kBK);
+                ++k_issued;
+                if (j >= nt) {
+                    const int c = j - nt, vs = c % kVStages;
+                    if (!mbar_wait(v_empty + 8 * vs, ((c / kVStages) & 1u) ^ 1u, kSiteProducerEmpty))
+                        break;
+                    mbar_arrive_expect_tx(v_full + 8 * vs, kTile);
+                    tma_load_2d(sV + vs * kTile, &tm_v, v_full + 8 * vs, head * kDim, row_base + c * kBK);
+                    ++v_issued;
                 }
-            for (int tries = 0; tries < (1 << 22) && !mbar_try_wait(bar_q, 0); ++tries) {
             }
+            // Loads still in flight (only after an abandoned wait) land before exit.
+            for (int j = k_issued > kKStages ? k_issued - kKStages : 0; j < k_issued; ++j)
+                for (int t = 0; t < (1 << 20) && !mbar_try_wait(k_full + 8 * (j % kKStages), (j / kKStages) & 1u); ++t) {
+                }
+            for (int c = v_issued > kVStages ? v_issued - kVStages : 0; c < v_issued; ++c)
+                for (int t = 0; t < (1 << 20) && !mbar_try_wait(v_full + 8 * (c % kVStages), (c / kVStages) & 1u); ++t) {
+                }
+            for (int t = 0; t < (1 << 20) && !mbar_try_wait(q_full, 0); ++t) {
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t id_s = idesc_f16_f32<kBQ, kBK>();
+            constexpr uint32_t id_o = idesc_f16_f32<kBQ, kDim>() | (1u << 16); // B (V) MN-major
+            bool ok = mbar_wait(q_ready, 0, kSiteMmaFull);
+            auto score_mma = [&](int u) { // u: score tile 0 .. 2 nt - 1 (pass 1, then pass 2)
+                const uint32_t b = u & 1;
+                const int ks = u % kKStages;
+                ok = ok && mbar_wait(s_empty + 8 * b, ((u >> 1) & 1u) ^ 1u, kSiteMmaAccEmpty) &&
+                     mbar_wait(k_ready + 8 * ks, (u / kKStages) & 1u, kSiteMmaFull);
+                if (!ok)
+                    return;
+                tc_fence_after();
+#pragma unroll
+                for (int k = 0; k < kDim / 16; ++k)
+                    mma_f16(tmem + b * kBK, smem_desc_k_sw128(sQ + k * 32),
+                            smem_desc_k_sw128(sK + ks * kTile + k * 32), id_s, k != 0);
+                mma_commit(k_empty + 8 * ks);
+                mma_commit(s_full + 8 * b);
+            };
+            auto pv_mma = [&](int c) {
+                const uint32_t pb = c & 1;
+                const int vs = c % kVStages;
+                ok = ok && mbar_wait(p_full + 8 * pb, (c >> 1) & 1u, kSiteMmaFull) &&
+                     mbar_wait(v_full + 8 * vs, (c / kVStages) & 1u, kSiteMmaFull);
+                if (!ok)
+                    return;
+                tc_fence_after();
+#pragma unroll
+                for (int k = 0; k < kBK / 16; ++k)
+                    mma_f16(tmem + kTmemO, smem_desc_k_sw128(sP + pb * kPBytes + (k / 4) * (kPBytes / 2) + (k % 4) * 32),
+                            smem_desc_mn_sw128(sV + vs * kTile + k * 16 * 128), id_o, (c | k) != 0);
+                mma_commit(v_empty + 8 * vs);
+                mma_commit(p_empty + 8 * pb);
+            };
+            for (int c = 0; c < nt; ++c)
+                score_mma(c);
+            for (int c = 0; c < nt; ++c) {
+                score_mma(nt + c);
+                if (c > 0)
+                    pv_mma(c - 1);
+            }
+            pv_mma(nt - 1);
+            if (ok)
+                mma_commit(o_full);
+            // Every MMA of this thread completes before TMEM is freed.
+            mma_commit(drain);
+            for (int t = 0; t < (1 << 22) && !mbar_try_wait(drain, 0); ++t) {
+            }
+        }
+    } else if (warp == 2) {
+        // ---------------- operand scaling: x' = half(x c), in place ----------------
+        auto scale_tile = [&](uint32_t tile) {
+#pragma unroll 4
+            for (int i = 0; i < kTile / 16 / 32; ++i) {
+                const uint32_t a = tile + (i * 32 + lane) * 16;
+                uint32_t v0, v1, v2, v3;
+                asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v0), "=r"(v1), "=r"(v2), "=r"(v3) : "r"(a));
+                v0 = gemm::hmul2_rn(v0, p.scale2);
+                v1 = gemm::hmul2_rn(v1, p.scale2);
+                v2 = gemm::hmul2_rn(v2, p.scale2);
+                v3 = gemm::hmul2_rn(v3, p.scale2);
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v0), "r"(v1), "r"(v2), "r"(v3)
+                             : "memory");
+            }
+            fence_proxy_async_smem(); // the MMA (async proxy) reads what these stores wrote
+            __syncwarp();
+        };
+        bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, kSiteMmaFull));
+        if (ok) {
+            scale_tile(sQ);
+            if (lane == 0)
+                mbar_arrive(q_ready);
+        }
+        for (int j = 0; ok && j < 2 * nt; ++j) {
+            const int s = j % kKStages;
+            ok = __all_sync(0xffffffffu, mbar_wait(k_full + 8 * s, (j / kKStages) & 1u, kSiteMmaFull));
+            if (!ok)
+                break;
+            scale_tile(sK + s * kTile);
+            if (lane == 0)
+                mbar_arrive(k_ready + 8 * s);
         }
     } else {
-        const int g = lane >> 2, tig = lane & 3;
-        bool ok = __all_sync(0xffffffffu, mbar_wait(bar_q, 0, kSiteMmaFull));
-        // Q' = half(q * c) as A fragments for this warp's 16 rows (4 k-steps of 16 dims).
-        uint32_t qa[4][4];
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-            const int mi = lane >> 3;
-            const int row = warp * 16 + (lane & 7) + (mi & 1) * 8;
-            const int chunk16 = ks * 2 + (mi >> 1);
-            uint32_t r[4];
-            ldmatrix_x4(qs + row * 128 + ((chunk16 ^ (row & 7)) << 4), r);
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-                qa[ks][i] = gemm::hmul2_rn(r[i], p.scale2);
-        }
-        // ---------------- pass 1: row max and sum of exp over all keys ----------------
-        float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f}; // rows g and g + 8 (this thread's part of l)
-        for (int c = 0; c < p.nchunks; ++c) {
-            const int st = c % kStages;
-            ok = ok && __all_sync(0xffffffffu, mbar_wait(bar_full + 8 * st, (c / kStages) & 1u, kSiteMmaFull));
-            const uint32_t stage = ring + st * kStageBytes;
-            const int kc = p.tokens - c * kChunk < kChunk ? p.tokens - c * kChunk : kChunk;
-            for (int sub = 0; ok && sub * 32 < kc; ++sub) {
-                float sv[4][4];
-#pragma unroll
-                for (int nt = 0; nt < 4; ++nt) {
-                    const int kb = sub * 32 + nt * 8;
-                    if (kb < kc)
-                        score_tile(qa, stage, kb, lane, p.scale2, sv[nt]);
-                }
-                if (sub * 32 + 32 > kc) { // keys past the stream's tokens (the last block only)
-#pragma unroll
-                    for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-                        for (int e = 0; e < 4; ++e)
-                            if (sub * 32 + nt * 8 + 2 * tig + (e & 1) >= kc)
-                                sv[nt][e] = -INFINITY;
-                }
-#pragma unroll
-                for (int r = 0; r < 2; ++r) {
-                    float bm = -INFINITY;
-#pragma unroll
-                    for (int nt = 0; nt < 4; ++nt)
-                        bm = fmaxf(bm, fmaxf(sv[nt][2 * r], sv[nt][2 * r + 1]));
-                    bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 1));
-                    bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 2));
-                    const float mn = fmaxf(m[r], bm);
-                    const float mn2 = mn * kLog2e;
-                    float add = 0.0f;
-#pragma unroll
-                    for (int nt = 0; nt < 4; ++nt)
-                        add += fast_exp2(fmaf(sv[nt][2 * r], kLog2e, -mn2)) +
-                               fast_exp2(fmaf(sv[nt][2 * r + 1], kLog2e, -mn2));
-                    l[r] = (m[r] == -INFINITY ? 0.0f : l[r] * fast_exp2((m[r] - mn) * kLog2e)) + add;
-                    m[r] = mn;
-                }
-            }
+        // ---------------- softmax: 8 warps, (lane quarter, 64-column half) each ----------------
+        // Every softmax warp walks every tile, even after a wait has given up
+        // (waits then return at once), so the named barrier always matches.
+        const int quarter = warp & 3;
+        const int half = (warp - kSoftWarp0) >> 2;
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + half * 64;
+        bool ok = true;
+        auto wait_lane0 = [&](uint32_t bar, uint32_t parity, int site) {
+            bool r = true;
+            if (lane == 0)
+                r = mbar_wait(bar, parity, site);
+            ok = __shfl_sync(0xffffffffu, r ? 1 : 0, 0) != 0 && ok;
+        };
+        // Scores of tile u for this half row, rounded to fp16 (the MatMul edge);
+        // keys past the stream's tokens are -inf.  Frees the TMEM buffer.
+        auto load_scores = [&](int u, int c, float (&s)[64]) {
+            const uint32_t b = u & 1;
+            wait_lane0(s_full + 8 * b, (u >> 1) & 1u, kSiteEpilogueAccFull);
+            tc_fence_after();
+            uint32_t v[64];
+            tmem_ld_32x32b_x32(lane_base + b * kBK, *reinterpret_cast<uint32_t(*)[32]>(v));
+            tmem_ld_32x32b_x32(lane_base + b * kBK + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+            tmem_wait_ld();
+            tc_fence_before();
             __syncwarp();
             if (lane == 0)
-                mbar_arrive(bar_empty + 8 * st);
-        }
-        // p = exp(s - m) / sum = 2^(s log2(e) - (m log2(e) + log2(sum))): one fma and one ex2.
-        float off[2];
+                mbar_arrive(s_empty + 8 * b);
+            const int valid = min(max(p.tokens - c * kBK - half * 64, 0), 64);
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            float t = l[r];
-            t += __shfl_xor_sync(0xffffffffu, t, 1);
-            t += __shfl_xor_sync(0xffffffffu, t, 2);
-            off[r] = m[r] * kLog2e + fast_log2(t);
-        }
-        // ---------------- pass 2: p = half(exp(s - max) / sum), out = P.V ----------------
-        float o[8][4];
-#pragma unroll
-        for (int d = 0; d < 8; ++d)
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-                o[d][e] = 0.0f;
-        for (int c = 0; c < p.nchunks; ++c) {
-            const int ik = p.nchunks + 2 * c, iv = ik + 1;
-            const int sk = ik % kStages, sv_st = iv % kStages;
-            ok = ok && __all_sync(0xffffffffu, mbar_wait(bar_full + 8 * sk, (ik / kStages) & 1u, kSiteMmaFull));
-            ok = ok && __all_sync(0xffffffffu, mbar_wait(bar_full + 8 * sv_st, (iv / kStages) & 1u, kSiteMmaFull));
-            const uint32_t kst = ring + sk * kStageBytes, vst = ring + sv_st * kStageBytes;
-            const int kc = p.tokens - c * kChunk < kChunk ? p.tokens - c * kChunk : kChunk;
-            for (int sub = 0; ok && sub * 32 < kc; ++sub) {
-                uint32_t pa[2][4]; // A fragments of P for two 16-key steps
-#pragma unroll
-                for (int nt = 0; nt < 4; ++nt) {
-                    const int kb = sub * 32 + nt * 8;
-                    float sv[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-                    if (kb < kc)
-                        score_tile(qa, kst, kb, lane, p.scale2, sv);
-                    float pv[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        pv[e] = fast_exp2(fmaf(sv[e], kLog2e, -off[e >> 1]));
-                    if (kb + 8 > kc) // keys past the stream's tokens (the last block only)
-#pragma unroll
-                        for (int e = 0; e < 4; ++e)
-                            if (kb + 2 * tig + (e & 1) >= kc)
-                                pv[e] = 0.0f;
-                    // n-tile nt is keys (nt & 1) * 8 .. + 7 of 16-key step nt >> 1
-                    pa[nt >> 1][(nt & 1) * 2 + 0] = gemm::cvt_f16x2(pv[0], pv[1]); // row g
-                    pa[nt >> 1][(nt & 1) * 2 + 1] = gemm::cvt_f16x2(pv[2], pv[3]); // row g + 8
-                }
-#pragma unroll
-                for (int kk = 0; kk < 2; ++kk) {
-                    const int kbase = sub * 32 + kk * 16;
-#pragma unroll
-                    for (int dn = 0; dn < 8; dn += 2) {
-                        const int mi = lane >> 3;
-                        const int key = kbase + (mi & 1) * 8 + (lane & 7);
-                        const int chunk16 = dn + (mi >> 1);
-                        uint32_t r[4];
-                        ldmatrix_x4_trans(vst + key * 128 + ((chunk16 ^ (key & 7)) << 4), r);
-                        mma_m16n8k16_f16_f32(o[dn], pa[kk], r[0], r[1]);
-                        mma_m16n8k16_f16_f32(o[dn + 1], pa[kk], r[2], r[3]);
-                    }
-                }
+            for (int i = 0; i < 64; i += 2) {
+                const uint32_t h2 = gemm::cvt_f16x2(__uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+                s[i] = i < valid ? h2f(static_cast<uint16_t>(h2 & 0xFFFFu)) : -INFINITY;
+                s[i + 1] = i + 1 < valid ? h2f(static_cast<uint16_t>(h2 >> 16)) : -INFINITY;
             }
+        };
+        // ---- pass 1: running max and sum of exp over this half row ----
+        float m = -INFINITY, l = 0.0f;
+        for (int c = 0; c < nt; ++c) {
+            float s[64];
+            load_scores(c, c, s);
+            float bm = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 64; ++i)
+                bm = fmaxf(bm, s[i]);
+            if (bm != -INFINITY) {
+                const float mn = fmaxf(m, bm);
+                const float mn2 = mn * kLog2e;
+                float add = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 64; ++i)
+                    add += fast_exp2(fmaf(s[i], kLog2e, -mn2));
+                l = (m == -INFINITY ? 0.0f : l * fast_exp2((m - mn) * kLog2e)) + add;
+                m = mn;
+            }
+        }
+        // ---- merge the two halves of each row ----
+        stat_m[half * kBQ + row] = m;
+        stat_l[half * kBQ + row] = l;
+        named_barrier_sync(2, kSoftWarps * 32);
+        const float m2 = stat_m[(half ^ 1) * kBQ + row], l2 = stat_l[(half ^ 1) * kBQ + row];
+        const float mm = fmaxf(m, m2);
+        const float ll = (m == -INFINITY ? 0.0f : l * fast_exp2((m - mm) * kLog2e)) +
+                         (m2 == -INFINITY ? 0.0f : l2 * fast_exp2((m2 - mm) * kLog2e));
+        // p = exp(s - max) / sum = 2^(s log2(e) - (max log2(e) + log2(sum)))
+        const float off = mm * kLog2e + fast_log2(ll);
+        // ---- pass 2: P = half(p) into the K-major swizzled P tile ----
+        for (int c = 0; c < nt; ++c) {
+            float s[64];
+            load_scores(nt + c, c, s);
+            uint32_t pk[32];
+#pragma unroll
+            for (int i = 0; i < 64; i += 2)
+                pk[i / 2] = gemm::cvt_f16x2(fast_exp2(fmaf(s[i], kLog2e, -off)), fast_exp2(fmaf(s[i + 1], kLog2e, -off)));
+            const uint32_t pb = c & 1;
+            wait_lane0(p_empty + 8 * pb, ((c >> 1) & 1u) ^ 1u, kSiteProducerEmpty);
+            const uint32_t prow = sP + pb * kPBytes + half * (kPBytes / 2) + row * 128;
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc)
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(prow + ((cc ^ (row & 7)) << 4)),
+                             "r"(pk[4 * cc]), "r"(pk[4 * cc + 1]), "r"(pk[4 * cc + 2]), "r"(pk[4 * cc + 3])
+                             : "memory");
+            fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(bar_empty + 8 * sk);
-                mbar_arrive(bar_empty + 8 * sv_st);
-            }
+            if (lane == 0)
+                mbar_arrive(p_full + 8 * pb);
         }
-        const float scale = p.code_scale_ptr ? *p.code_scale_ptr : p.code_scale;
-        const float recip = p.code_scale_ptr ? __frcp_rn(scale) : p.code_recip;
-        const uint64_t neg_scale2 = f2_bits(-scale, -scale), recip2 = f2_bits(recip, recip);
-        const int width = p.heads * kDim;
+        // ---- epilogue: out = half(O), this warp's 32 of the 64 dims ----
+        wait_lane0(o_full, 0, kSiteEpilogueAccFull);
+        tc_fence_after();
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(tmem + kTmemO + (static_cast<uint32_t>(quarter * 32) << 16) + half * 32, o);
+        tmem_wait_ld();
+        const int token = q0 + row;
+        if (ok && token < p.tokens) {
+            const float scale = p.code_scale_ptr ? *p.code_scale_ptr : p.code_scale;
+            const float recip = p.code_scale_ptr ? __frcp_rn(scale) : p.code_recip;
+            const uint64_t neg_scale2 = f2_bits(-scale, -scale), recip2 = f2_bits(recip, recip);
+            const size_t idx = static_cast<size_t>(row_base + token) * (p.heads * kDim) + head * kDim + half * 32;
+            uint32_t h[16], q[8];
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-            const int token = q0 + warp * 16 + g + 8 * e;
-            if (!ok || token >= p.tokens)
-                continue;
+            for (int i = 0; i < 16; ++i)
+                h[i] = gemm::cvt_f16x2(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1]));
+            if (p.out) {
+                uint4 *dst = reinterpret_cast<uint4 *>(p.out + idx);
 #pragma unroll
-            for (int dn = 0; dn < 8; ++dn) {
-                const uint32_t pair = gemm::cvt_f16x2(o[dn][2 * e], o[dn][2 * e + 1]);
-                const size_t idx = static_cast<size_t>(row_base + token) * width + head * kDim + dn * 8 + 2 * tig;
-                if (p.out)
-                    *reinterpret_cast<uint32_t *>(p.out + idx) = pair;
-                if (p.codes)
-                    *reinterpret_cast<uint16_t *>(p.codes + idx) =
-                        static_cast<uint16_t>(e4m3x2_quotient(pair, neg_scale2, recip2));
+                for (int j = 0; j < 4; ++j)
+                    dst[j] = make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+            }
+            if (p.codes) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    q[j] = (e4m3x2_quotient(h[2 * j], neg_scale2, recip2) & 0xFFFFu) |
+                           (e4m3x2_quotient(h[2 * j + 1], neg_scale2, recip2) << 16);
+                uint4 *dst = reinterpret_cast<uint4 *>(p.codes + idx);
+                dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
+                dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
             }
         }
     }
+
+    tc_fence_before();
     __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
 }
 
-} // namespace sattn
+} // namespace fattn
 
 // ---------------------------------------------------------------------------
 // fp16 single-token projections (the reference plugins' kernels on sm_100a).
@@ -2866,20 +2984,20 @@ cudaError_t launch_self_attention(const SelfAttentionLaunch &L, cudaStream_t str
         !make_map_ld(&tm_v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.v, rows, width, L.v_ld, sattn::kDim,
                      sattn::kChunk, CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
-    const cudaError_t attr = ensure_smem(sattn::self_attention_kernel, sattn::kSmemBytes);
+    const cudaError_t attr = ensure_smem(fattn::attention_kernel, fattn::kSmemBytes);
     if (attr != cudaSuccess)
         return attr;
     cudaLaunchConfig_t config{};
     config.gridDim = dim3(static_cast<unsigned>(static_cast<int64_t>(L.streams) * L.heads * p.qblocks));
-    config.blockDim = dim3(sattn::kThreads);
-    config.dynamicSmemBytes = sattn::kSmemBytes;
+    config.blockDim = dim3(fattn::kThreads);
+    config.dynamicSmemBytes = fattn::kSmemBytes;
     config.stream = stream;
     cudaLaunchAttribute attr_pdl[1];
     attr_pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr_pdl[0].val.programmaticStreamSerializationAllowed = 1;
     config.attrs = attr_pdl;
     config.numAttrs = 1;
-    const cudaError_t err = cudaLaunchKernelEx(&config, sattn::self_attention_kernel, tm_q, tm_k, tm_v, p);
+    const cudaError_t err = cudaLaunchKernelEx(&config, fattn::attention_kernel, tm_q, tm_k, tm_v, p);
     count_launch();
     return err != cudaSuccess ? err : cudaGetLastError();
 }

@@ -255,6 +255,21 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t smem_addr)
     return desc;
 }
 
+// Shared-memory matrix descriptor for an MN-major operand tile written by TMA with
+// 128-byte swizzling as rows of 128 bytes (64 fp16 along MN), one row per K index:
+// 8-row (1024-byte) swizzle atoms stacked along K.  The tile is one atom wide along
+// MN (N = 64 fp16), so both byte offsets are the atom size: the field that steps
+// along K is 1024 bytes and the MN step is never taken.
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t smem_addr)
+{
+    uint64_t desc = static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+    desc |= static_cast<uint64_t>(1024u >> 4) << 16;
+    desc |= static_cast<uint64_t>(1024u >> 4) << 32;
+    desc |= static_cast<uint64_t>(1u) << 46;
+    desc |= static_cast<uint64_t>(2u) << 61;
+    return desc;
+}
+
 // Instruction descriptor, kind::f8f6f4: D fp32 (bits 4-5 = 1), A and B E4M3
 // (bits 7-9, 10-12 = 0), both K-major (bits 15, 16 = 0), N>>3 at bit 17,
 // M>>4 at bit 24.
