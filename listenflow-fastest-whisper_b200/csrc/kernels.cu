@@ -2048,12 +2048,12 @@ constexpr float kLog2e = 1.4426950408889634f;
 //   warp 1: MMA issuer.  S = Q' K'^T, kind::f16 128 x 128 x 16, into one of two
 //           TMEM score buffers; O += P V, 128 x 64 x 16 with V read MN-major
 //           straight from its TMA tile, into a third TMEM region;
-//   warp 2: rescales Q and each K tile in shared memory (half(x c)) before the
-//           MMA reads it;
-//   warps 3-10: softmax, two warps per TMEM lane quarter, each over 64 of a
-//           tile's 128 key columns.  Pass 1 keeps a running max and sum per
-//           half row (merged once through shared memory); pass 2 writes P as
-//           fp16 into a K-major 128B-swizzled tile for the P.V MMA.
+//   warps 2-5: rescale Q and each K tile in shared memory (half(x c)) before
+//           the MMA reads it, a quarter of the tile each;
+//   warps 6-21: softmax, kSplit warps per TMEM lane quarter, each over kCols of
+//           a tile's 128 key columns.  Pass 1 keeps a running max and sum per
+//           part of a row (merged once through shared memory); pass 2 writes P
+//           as fp16 into a K-major 128B-swizzled tile for the P.V MMA.
 // The P.V MMAs of tile c - 1 are issued after the score MMAs of tile c, so the
 // softmax of one tile overlaps the MMAs of the next.
 namespace fattn {
@@ -2068,14 +2068,18 @@ constexpr int kKStages = 3;
 constexpr int kVStages = 3;
 constexpr int kTile = kBK * kDim * 2;  // one Q, K or V tile: 16 KB
 constexpr int kPBytes = kBQ * kBK * 2; // one P tile: two 64-key K-major halves, 32 KB
-constexpr int kSoftWarp0 = 3;
-constexpr int kSoftWarps = 8;
+constexpr int kScaleWarp0 = 2;
+constexpr int kScaleWarps = 4;
+constexpr int kSoftWarp0 = kScaleWarp0 + kScaleWarps;
+constexpr int kSplit = 4;                 // softmax warps per TMEM lane quarter
+constexpr int kSoftWarps = 4 * kSplit;
+constexpr int kCols = kBK / kSplit;       // score columns per softmax warp
 constexpr int kThreads = (kSoftWarp0 + kSoftWarps) * 32;
 constexpr int kOffK = kTile;
 constexpr int kOffV = kOffK + kKStages * kTile;
 constexpr int kOffP = kOffV + kVStages * kTile;
-constexpr int kOffStats = kOffP + 2 * kPBytes; // float m[2][kBQ], l[2][kBQ]
-constexpr int kOffBar = kOffStats + 4 * kBQ * 4;
+constexpr int kOffStats = kOffP + 2 * kPBytes; // float m[kSplit][kBQ], l[kSplit][kBQ]
+constexpr int kOffBar = kOffStats + 2 * kSplit * kBQ * 4;
 constexpr int kBars = 2 + 3 * kKStages + 2 * kVStages + 8 + 2;
 constexpr int kSmemBytes = kOffBar + 8 * kBars + 16 + 1024;
 constexpr uint32_t kTmemCols = 512; // S[2] (2 x 128) + O (64)
@@ -2106,7 +2110,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t drain = o_full + 8;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 8 * kBars);
     float *stat_m = reinterpret_cast<float *>(smem + kOffStats);
-    float *stat_l = stat_m + 2 * kBQ;
+    float *stat_l = stat_m + kSplit * kBQ;
 
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
@@ -2121,10 +2125,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         griddepcontrol_launch_dependents();
         mbar_init(q_full, 1);
-        mbar_init(q_ready, 1);
+        mbar_init(q_ready, kScaleWarps);
         for (int s = 0; s < kKStages; ++s) {
             mbar_init(k_full + 8 * s, 1);
-            mbar_init(k_ready + 8 * s, 1);
+            mbar_init(k_ready + 8 * s, kScaleWarps);
             mbar_init(k_empty + 8 * s, 1);
         }
         for (int s = 0; s < kVStages; ++s) {
@@ -2237,12 +2241,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int t = 0; t < (1 << 22) && !mbar_try_wait(drain, 0); ++t) {
             }
         }
-    } else if (warp == 2) {
+    } else if (warp < kSoftWarp0) {
         // ---------------- operand scaling: x' = half(x c), in place ----------------
+        const int part = warp - kScaleWarp0; // this warp's quarter of each tile
         auto scale_tile = [&](uint32_t tile) {
-#pragma unroll 4
-            for (int i = 0; i < kTile / 16 / 32; ++i) {
-                const uint32_t a = tile + (i * 32 + lane) * 16;
+#pragma unroll
+            for (int i = 0; i < kTile / 16 / 32 / kScaleWarps; ++i) {
+                const uint32_t a = tile + part * (kTile / kScaleWarps) + (i * 32 + lane) * 16;
                 uint32_t v0, v1, v2, v3;
                 asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v0), "=r"(v1), "=r"(v2), "=r"(v3) : "r"(a));
                 v0 = gemm::hmul2_rn(v0, p.scale2);
@@ -2271,13 +2276,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive(k_ready + 8 * s);
         }
     } else {
-        // ---------------- softmax: 8 warps, (lane quarter, 64-column half) each ----------------
+        // ---------------- softmax: (lane quarter, column part) per warp ----------------
         // Every softmax warp walks every tile, even after a wait has given up
         // (waits then return at once), so the named barrier always matches.
         const int quarter = warp & 3;
-        const int half = (warp - kSoftWarp0) >> 2;
+        const int part = (warp - kSoftWarp0) >> 2; // which kCols columns of a tile
+        const int col0 = part * kCols;
         const int row = quarter * 32 + lane;
-        const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + half * 64;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + col0;
         bool ok = true;
         auto wait_lane0 = [&](uint32_t bar, uint32_t parity, int site) {
             bool r = true;
@@ -2285,109 +2291,143 @@ __global__ void __launch_bounds__(kThreads, 1)
                 r = mbar_wait(bar, parity, site);
             ok = __shfl_sync(0xffffffffu, r ? 1 : 0, 0) != 0 && ok;
         };
-        // Scores of tile u for this half row, rounded to fp16 (the MatMul edge);
+        // This warp's kCols scores of tile u, rounded to fp16 (the MatMul edge);
         // keys past the stream's tokens are -inf.  Frees the TMEM buffer.
-        auto load_scores = [&](int u, int c, float (&s)[64]) {
+        auto load_scores = [&](int u, int c, float (&s)[kCols]) {
             const uint32_t b = u & 1;
             wait_lane0(s_full + 8 * b, (u >> 1) & 1u, kSiteEpilogueAccFull);
             tc_fence_after();
-            uint32_t v[64];
-            tmem_ld_32x32b_x32(lane_base + b * kBK, *reinterpret_cast<uint32_t(*)[32]>(v));
-            tmem_ld_32x32b_x32(lane_base + b * kBK + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+            uint32_t v[kCols];
+#pragma unroll
+            for (int j = 0; j < kCols; j += 32)
+                tmem_ld_32x32b_x32(lane_base + b * kBK + j, *reinterpret_cast<uint32_t(*)[32]>(v + j));
             tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
             if (lane == 0)
                 mbar_arrive(s_empty + 8 * b);
-            const int valid = min(max(p.tokens - c * kBK - half * 64, 0), 64);
 #pragma unroll
-            for (int i = 0; i < 64; i += 2) {
+            for (int i = 0; i < kCols; i += 2) {
                 const uint32_t h2 = gemm::cvt_f16x2(__uint_as_float(v[i]), __uint_as_float(v[i + 1]));
-                s[i] = i < valid ? h2f(static_cast<uint16_t>(h2 & 0xFFFFu)) : -INFINITY;
-                s[i + 1] = i + 1 < valid ? h2f(static_cast<uint16_t>(h2 >> 16)) : -INFINITY;
+                s[i] = h2f(static_cast<uint16_t>(h2 & 0xFFFFu));
+                s[i + 1] = h2f(static_cast<uint16_t>(h2 >> 16));
             }
+            const int valid = min(max(p.tokens - c * kBK - col0, 0), kCols);
+            if (valid < kCols) // keys past the stream's tokens (the last tile only)
+#pragma unroll
+                for (int i = 0; i < kCols; ++i)
+                    if (i >= valid)
+                        s[i] = -INFINITY;
         };
-        // ---- pass 1: running max and sum of exp over this half row ----
+        // ---- pass 1: running max and sum of exp over this part of the row ----
+        // (eight independent partial maxima and sums per tile: short dependency chains)
         float m = -INFINITY, l = 0.0f;
         for (int c = 0; c < nt; ++c) {
-            float s[64];
+            float s[kCols];
             load_scores(c, c, s);
-            float bm = -INFINITY;
+            float pm[8];
 #pragma unroll
-            for (int i = 0; i < 64; ++i)
-                bm = fmaxf(bm, s[i]);
+            for (int j = 0; j < 8; ++j)
+                pm[j] = s[j];
+#pragma unroll
+            for (int i = 8; i < kCols; ++i)
+                pm[i & 7] = fmaxf(pm[i & 7], s[i]);
+            const float bm = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                                   fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
             if (bm != -INFINITY) {
                 const float mn = fmaxf(m, bm);
                 const float mn2 = mn * kLog2e;
-                float add = 0.0f;
+                float ps[8];
 #pragma unroll
-                for (int i = 0; i < 64; ++i)
-                    add += fast_exp2(fmaf(s[i], kLog2e, -mn2));
+                for (int j = 0; j < 8; ++j)
+                    ps[j] = fast_exp2(fmaf(s[j], kLog2e, -mn2));
+#pragma unroll
+                for (int i = 8; i < kCols; ++i)
+                    ps[i & 7] += fast_exp2(fmaf(s[i], kLog2e, -mn2));
+                const float add = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
                 l = (m == -INFINITY ? 0.0f : l * fast_exp2((m - mn) * kLog2e)) + add;
                 m = mn;
             }
         }
-        // ---- merge the two halves of each row ----
-        stat_m[half * kBQ + row] = m;
-        stat_l[half * kBQ + row] = l;
+        // ---- merge the parts of each row (in part order) ----
+        stat_m[part * kBQ + row] = m;
+        stat_l[part * kBQ + row] = l;
         named_barrier_sync(2, kSoftWarps * 32);
-        const float m2 = stat_m[(half ^ 1) * kBQ + row], l2 = stat_l[(half ^ 1) * kBQ + row];
-        const float mm = fmaxf(m, m2);
-        const float ll = (m == -INFINITY ? 0.0f : l * fast_exp2((m - mm) * kLog2e)) +
-                         (m2 == -INFINITY ? 0.0f : l2 * fast_exp2((m2 - mm) * kLog2e));
+        float mm = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < kSplit; ++j)
+            mm = fmaxf(mm, stat_m[j * kBQ + row]);
+        float ll = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kSplit; ++j) {
+            const float mj = stat_m[j * kBQ + row];
+            ll += mj == -INFINITY ? 0.0f : stat_l[j * kBQ + row] * fast_exp2((mj - mm) * kLog2e);
+        }
         // p = exp(s - max) / sum = 2^(s log2(e) - (max log2(e) + log2(sum)))
         const float off = mm * kLog2e + fast_log2(ll);
         // ---- pass 2: P = half(p) into the K-major swizzled P tile ----
         for (int c = 0; c < nt; ++c) {
-            float s[64];
+            float s[kCols];
             load_scores(nt + c, c, s);
-            uint32_t pk[32];
+            uint32_t pk[kCols / 2];
 #pragma unroll
-            for (int i = 0; i < 64; i += 2)
+            for (int i = 0; i < kCols; i += 2)
                 pk[i / 2] = gemm::cvt_f16x2(fast_exp2(fmaf(s[i], kLog2e, -off)), fast_exp2(fmaf(s[i + 1], kLog2e, -off)));
             const uint32_t pb = c & 1;
             wait_lane0(p_empty + 8 * pb, ((c >> 1) & 1u) ^ 1u, kSiteProducerEmpty);
-            const uint32_t prow = sP + pb * kPBytes + half * (kPBytes / 2) + row * 128;
+            // columns col0 .. col0 + kCols - 1 sit in 64-key half col0 / 64, 16-byte chunks from (col0 % 64) / 8
+            const uint32_t prow = sP + pb * kPBytes + (col0 / 64) * (kPBytes / 2) + row * 128;
 #pragma unroll
-            for (int cc = 0; cc < 8; ++cc)
+            for (int j = 0; j < kCols / 8; ++j) {
+                const int cc = (col0 % 64) / 8 + j;
                 asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(prow + ((cc ^ (row & 7)) << 4)),
-                             "r"(pk[4 * cc]), "r"(pk[4 * cc + 1]), "r"(pk[4 * cc + 2]), "r"(pk[4 * cc + 3])
+                             "r"(pk[4 * j]), "r"(pk[4 * j + 1]), "r"(pk[4 * j + 2]), "r"(pk[4 * j + 3])
                              : "memory");
+            }
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0)
                 mbar_arrive(p_full + 8 * pb);
         }
-        // ---- epilogue: out = half(O), this warp's 32 of the 64 dims ----
+        // ---- epilogue: out = half(O), this warp's kOutCols of the 64 dims ----
+        constexpr int kOutCols = kDim / kSplit;
         wait_lane0(o_full, 0, kSiteEpilogueAccFull);
         tc_fence_after();
-        uint32_t o[32];
-        tmem_ld_32x32b_x32(tmem + kTmemO + (static_cast<uint32_t>(quarter * 32) << 16) + half * 32, o);
+        uint32_t o[kOutCols];
+        static_assert(kOutCols == 16 || kOutCols == 32, "output columns per softmax warp");
+        if constexpr (kOutCols == 32)
+            tmem_ld_32x32b_x32(tmem + kTmemO + (static_cast<uint32_t>(quarter * 32) << 16) + part * kOutCols,
+                               *reinterpret_cast<uint32_t(*)[32]>(o));
+        else
+            tmem_ld_32x32b_x16(tmem + kTmemO + (static_cast<uint32_t>(quarter * 32) << 16) + part * kOutCols,
+                               *reinterpret_cast<uint32_t(*)[16]>(o));
         tmem_wait_ld();
         const int token = q0 + row;
         if (ok && token < p.tokens) {
             const float scale = p.code_scale_ptr ? *p.code_scale_ptr : p.code_scale;
             const float recip = p.code_scale_ptr ? __frcp_rn(scale) : p.code_recip;
             const uint64_t neg_scale2 = f2_bits(-scale, -scale), recip2 = f2_bits(recip, recip);
-            const size_t idx = static_cast<size_t>(row_base + token) * (p.heads * kDim) + head * kDim + half * 32;
-            uint32_t h[16], q[8];
+            const size_t idx = static_cast<size_t>(row_base + token) * (p.heads * kDim) + head * kDim + part * kOutCols;
+            uint32_t h[kOutCols / 2];
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
+            for (int i = 0; i < kOutCols / 2; ++i)
                 h[i] = gemm::cvt_f16x2(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1]));
             if (p.out) {
                 uint4 *dst = reinterpret_cast<uint4 *>(p.out + idx);
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
+                for (int j = 0; j < kOutCols / 8; ++j)
                     dst[j] = make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
             }
             if (p.codes) {
+                uint32_t q[kOutCols / 4];
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
+                for (int j = 0; j < kOutCols / 4; ++j)
                     q[j] = (e4m3x2_quotient(h[2 * j], neg_scale2, recip2) & 0xFFFFu) |
                            (e4m3x2_quotient(h[2 * j + 1], neg_scale2, recip2) << 16);
                 uint4 *dst = reinterpret_cast<uint4 *>(p.codes + idx);
-                dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
-                dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
+#pragma unroll
+                for (int j = 0; j < kOutCols / 16; ++j)
+                    dst[j] = make_uint4(q[4 * j], q[4 * j + 1], q[4 * j + 2], q[4 * j + 3]);
             }
         }
     }
