@@ -248,12 +248,14 @@ struct Cfg {
     static constexpr int kOffTable = kOffStaging + kStagingBytes;
     static constexpr int kOffBar = kOffTable + kTableBytes;
     static constexpr int kSmemBytes = kOffBar + kBarBytes + 1024;
-    static constexpr int kTmemCols = 2 * BN;
+    static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512; // two accumulators, allocated as a power of two
+    static constexpr int kSubs = BN / kSub;                      // 32-column store boxes per tile
+    static_assert(BN % kSub == 0 && kSubs <= 8, "tile width: a multiple of 32, at most 256");
     static constexpr int kAccEmptyArrivals = kPair ? 2 * kEpiWarps : kEpiWarps;
     static_assert(kStages >= 3, "pipeline depth");
     static_assert(kSmemBytes <= 232448, "shared memory budget");
     static_assert((2 * kStages + 5) * 8 + 8 <= kBarBytes, "barrier area");
-    static_assert(kTmemCols <= 512, "TMEM columns");
+    static_assert(2 * BN <= kTmemCols, "TMEM columns");
     static_assert(kY || kCodes, "an output is required");
 };
 
@@ -524,7 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- Epilogue: 16 independent warps ----------------
         const int ew = warp - 2;
         const int quarter = warp & 3; // the TMEM lane quarter this warp may access
-        const int slice = ew >> 2;    // which quarter of the tile's columns
+        const int slice = ew >> 2;    // this warp's 32-column stores: tile subs slice and slice + 4
         const uint64_t neg_scale2 = f2_bits(-p.next_scale, -p.next_scale);
         const uint64_t recip2 = f2_bits(p.next_recip, p.next_recip);
         uint8_t *code_table = smem + C::kOffTable;
@@ -556,13 +558,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int n0 = (t / p.m_tiles) * BN;
             const uint32_t a = local & 1;
             const uint32_t acc_ph = (local >> 1) & 1;
-            const int col_begin = n0 + slice * (BN / 4);
-            // This warp's 64 columns: lane i holds columns 2i and 2i + 1 (combined
-            // scale act * w and the fp16 bias pair), read before the accumulator wait.
+            // This warp's columns: lane i holds columns 2(i % 16) and 2(i % 16) + 1 of
+            // sub slice + 4(i / 16) (combined scale act * w and the fp16 bias pair),
+            // read before the accumulator wait.
             float2 my_cs = make_float2(0.0f, 0.0f);
             uint32_t my_b = 0u;
             {
-                const int c = col_begin + 2 * lane;
+                const int c = n0 + (slice + 4 * (lane >> 4)) * kSub + 2 * (lane & 15);
                 if (c < p.n) {
                     const float2 w = __ldg(reinterpret_cast<const float2 *>(p.w_scales + c));
                     my_cs = make_float2(act_scale * w.x, act_scale * w.y);
@@ -574,15 +576,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok)
                 break;
             tc_fence_after();
-            int subs = (p.n - col_begin + kSub - 1) / kSub;
-            subs = subs < 0 ? 0 : (subs > BN / 4 / kSub ? BN / 4 / kSub : subs);
+            // Active subs are a prefix: sub k is tile sub slice + 4k, columns increase with k.
+            int subs = 0;
+            while (subs < 2 && slice + 4 * subs < C::kSubs && n0 + (slice + 4 * subs) * kSub < p.n)
+                ++subs;
             const int row0 = m0 + quarter * 32;
             if (row0 >= p.m)
                 subs = 0; // every row of this warp is padding: nothing to load or store
-            const uint32_t t_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN + slice * (BN / 4);
+            const uint32_t t_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN;
 #pragma unroll 1
             for (int sub = 0; sub < subs; ++sub) {
-                const int col0 = col_begin + sub * kSub;
+                const int tsub = slice + 4 * sub;
+                const int col0 = n0 + tsub * kSub;
                 // The previous store from this warp's staging buffer has read it.
                 if (lane == 0)
                     bulk_wait_group_read0();
@@ -591,7 +596,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {
                     uint32_t v[16];
-                    tmem_ld_32x32b_x16(t_base + sub * kSub + hf * 16, v);
+                    tmem_ld_32x32b_x16(t_base + tsub * kSub + hf * 16, v);
                     tmem_wait_ld();
                     if (sub == subs - 1 && hf == 1) {
                         tc_fence_before();
@@ -2721,7 +2726,20 @@ cudaError_t launch_fp8_gemm(const LinearLaunch &L, cudaStream_t stream)
     // main loop leaves the MMA waiting on the epilogue (-5%).
     const bool code_table = L.gelu && L.next_codes != nullptr && L.y == nullptr;
     const bool pair = L.m >= 512 && L.k >= 1024 && !code_table;
-    return pair ? run_gemm_epilogue<256, true>(L, stream) : run_gemm_epilogue<256, false>(L, stream);
+    // Tile width 224 or 256: fewer, fuller waves at a narrower tile.  A tile's time
+    // is ~0.44 fixed + 0.56 x width/256 of a 256-wide one (measured from 128- and
+    // 256-wide tiles), so the estimate is waves x that.  N = 1280 (out_proj, fc2):
+    // 470 tiles = 3.18 waves at 256, 564 = 3.81 waves at 224.
+    const int64_t units = pair ? sm_count() / 2 : sm_count();
+    const int64_t m_tiles = (L.m + (pair ? 255 : 127)) / (pair ? 256 : 128);
+    auto cost = [&](int bn) {
+        const int64_t tiles = m_tiles * ((L.n + bn - 1) / bn);
+        return static_cast<double>((tiles + units - 1) / units) * (0.44 + 0.56 * bn / 256.0);
+    };
+    const bool narrow = cost(224) < cost(256);
+    if (pair)
+        return narrow ? run_gemm_epilogue<224, true>(L, stream) : run_gemm_epilogue<256, true>(L, stream);
+    return narrow ? run_gemm_epilogue<224, false>(L, stream) : run_gemm_epilogue<256, false>(L, stream);
 }
 
 namespace {
