@@ -95,9 +95,11 @@ def test_cross_attention_identical_keys_average_values(cuda, fp8, oracle):
 
 
 @pytest.mark.parametrize("streams,tokens,heads", [
-    # one and several 64-row query blocks and 128-key chunks, ragged tails, the
-    # C2 head count
+    # one and several 128-row query blocks and 128-key tiles, ragged tails (the
+    # last tile's rows belong to the next stream), exact tile multiples, a key
+    # count at or below one 32- or 64-column softmax part, the C2 head count
     (1, 1, 1), (1, 64, 2), (2, 130, 3), (1, 1500, 2), (3, 257, 4), (8, 100, 20),
+    (2, 127, 2), (2, 128, 2), (3, 129, 1), (1, 256, 3), (2, 33, 2), (1, 2048, 1),
 ])
 def test_self_attention_matches_oracle(cuda, fp8, oracle, native, streams, tokens, heads):
     """Encoder self-attention on the fused QKV output, same bound as above."""
