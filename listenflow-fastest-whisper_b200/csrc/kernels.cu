@@ -2091,6 +2091,24 @@ constexpr uint32_t kTmemCols = 512; // S[2] (2 x 128) + O (64)
 constexpr uint32_t kTmemO = 256;
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
+// Packed fp16 maximum (a NaN operand yields the other operand, like fmaxf).
+__device__ __forceinline__ uint32_t max_f16x2(uint32_t a, uint32_t b)
+{
+    uint32_t r;
+    asm("max.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+// (lo - c, hi - c) of a packed fp16 pair as fp32, one rounding each: the mixed-
+// precision add takes the fp16 operand as is, with no separate conversion.
+__device__ __forceinline__ void sub_f16x2_f32(uint32_t h2, float c, float &lo, float &hi)
+{
+    asm("{\n\t.reg .f16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+        "add.rn.f32.f16 %0, l, %3;\n\tadd.rn.f32.f16 %1, h, %3;\n\t}"
+        : "=f"(lo), "=f"(hi)
+        : "r"(h2), "f"(-c));
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const sattn::Params p)
@@ -2298,7 +2316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
         // This warp's kCols scores of tile u, rounded to fp16 (the MatMul edge);
         // keys past the stream's tokens are -inf.  Frees the TMEM buffer.
-        auto load_scores = [&](int u, int c, float (&s)[kCols]) {
+        auto load_scores = [&](int u, int c, uint32_t (&h)[kCols / 2]) {
             const uint32_t b = u & 1;
             wait_lane0(s_full + 8 * b, (u >> 1) & 1u, kSiteEpilogueAccFull);
             tc_fence_after();
@@ -2312,43 +2330,49 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0)
                 mbar_arrive(s_empty + 8 * b);
 #pragma unroll
-            for (int i = 0; i < kCols; i += 2) {
-                const uint32_t h2 = gemm::cvt_f16x2(__uint_as_float(v[i]), __uint_as_float(v[i + 1]));
-                s[i] = h2f(static_cast<uint16_t>(h2 & 0xFFFFu));
-                s[i + 1] = h2f(static_cast<uint16_t>(h2 >> 16));
-            }
+            for (int i = 0; i < kCols; i += 2)
+                h[i / 2] = gemm::cvt_f16x2(__uint_as_float(v[i]), __uint_as_float(v[i + 1]));
             const int valid = min(max(p.tokens - c * kBK - col0, 0), kCols);
-            if (valid < kCols) // keys past the stream's tokens (the last tile only)
+            if (valid < kCols) // keys past the stream's tokens (the last tile only): fp16 -inf
 #pragma unroll
-                for (int i = 0; i < kCols; ++i)
+                for (int i = 0; i < kCols; i += 2) {
                     if (i >= valid)
-                        s[i] = -INFINITY;
+                        h[i / 2] = (h[i / 2] & 0xFFFF0000u) | 0xFC00u;
+                    if (i + 1 >= valid)
+                        h[i / 2] = (h[i / 2] & 0x0000FFFFu) | 0xFC000000u;
+                }
         };
         // ---- pass 1: running max and sum of exp over this part of the row ----
-        // (eight independent partial maxima and sums per tile: short dependency chains)
+        // The scores stay packed fp16 pairs: the tile maximum is a packed max, and
+        // s - max is one mixed-precision add per score (f16 operand, f32 result),
+        // so no score goes through a conversion back to fp32.  Eight independent
+        // partial chains per tile keep the dependency chains short.
         float m = -INFINITY, l = 0.0f;
         for (int c = 0; c < nt; ++c) {
-            float s[kCols];
-            load_scores(c, c, s);
-            float pm[8];
+            uint32_t h[kCols / 2];
+            load_scores(c, c, h);
+            uint32_t pm[4];
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-                pm[j] = s[j];
+            for (int j = 0; j < 4; ++j)
+                pm[j] = h[j];
 #pragma unroll
-            for (int i = 8; i < kCols; ++i)
-                pm[i & 7] = fmaxf(pm[i & 7], s[i]);
-            const float bm = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                                   fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+            for (int i = 4; i < kCols / 2; ++i)
+                pm[i & 3] = max_f16x2(pm[i & 3], h[i]);
+            const uint32_t m2 = max_f16x2(max_f16x2(pm[0], pm[1]), max_f16x2(pm[2], pm[3]));
+            const float bm = fmaxf(h2f(static_cast<uint16_t>(m2 & 0xFFFFu)), h2f(static_cast<uint16_t>(m2 >> 16)));
             if (bm != -INFINITY) {
                 const float mn = fmaxf(m, bm);
-                const float mn2 = mn * kLog2e;
                 float ps[8];
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
-                    ps[j] = fast_exp2(fmaf(s[j], kLog2e, -mn2));
+                    ps[j] = 0.0f;
 #pragma unroll
-                for (int i = 8; i < kCols; ++i)
-                    ps[i & 7] += fast_exp2(fmaf(s[i], kLog2e, -mn2));
+                for (int i = 0; i < kCols / 2; ++i) {
+                    float d0, d1;
+                    sub_f16x2_f32(h[i], mn, d0, d1);
+                    ps[(2 * i) & 7] += fast_exp2(d0 * kLog2e);
+                    ps[(2 * i + 1) & 7] += fast_exp2(d1 * kLog2e);
+                }
                 const float add = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
                 l = (m == -INFINITY ? 0.0f : l * fast_exp2((m - mn) * kLog2e)) + add;
                 m = mn;
@@ -2368,16 +2392,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float mj = stat_m[j * kBQ + row];
             ll += mj == -INFINITY ? 0.0f : stat_l[j * kBQ + row] * fast_exp2((mj - mm) * kLog2e);
         }
-        // p = exp(s - max) / sum = 2^(s log2(e) - (max log2(e) + log2(sum)))
-        const float off = mm * kLog2e + fast_log2(ll);
+        // p = exp(s - max) / sum = 2^((s - max) log2(e) - log2(sum))
+        const float lg = fast_log2(ll);
         // ---- pass 2: P = half(p) into the K-major swizzled P tile ----
         for (int c = 0; c < nt; ++c) {
-            float s[kCols];
-            load_scores(nt + c, c, s);
+            uint32_t h[kCols / 2];
+            load_scores(nt + c, c, h);
             uint32_t pk[kCols / 2];
 #pragma unroll
-            for (int i = 0; i < kCols; i += 2)
-                pk[i / 2] = gemm::cvt_f16x2(fast_exp2(fmaf(s[i], kLog2e, -off)), fast_exp2(fmaf(s[i + 1], kLog2e, -off)));
+            for (int i = 0; i < kCols / 2; ++i) {
+                float d0, d1;
+                sub_f16x2_f32(h[i], mm, d0, d1);
+                pk[i] = gemm::cvt_f16x2(fast_exp2(fmaf(d0, kLog2e, -lg)), fast_exp2(fmaf(d1, kLog2e, -lg)));
+            }
             const uint32_t pb = c & 1;
             wait_lane0(p_empty + 8 * pb, ((c >> 1) & 1u) ^ 1u, kSiteProducerEmpty);
             // columns col0 .. col0 + kCols - 1 sit in 64-key half col0 / 64, 16-byte chunks from (col0 % 64) / 8
