@@ -74,9 +74,11 @@ def parse_args(argv=None):
                    help="timed replays of the C3 decoder-step graph (0 skips it)")
     p.add_argument("--decoder-layers", type=int, default=32,
                    help="decoder layers in the C3 step (32 is the measured configuration)")
-    p.add_argument("--only", choices=("all", "c2", "ln", "attention", "self_attention", "decoder"), default="all",
+    p.add_argument("--only", choices=("all", "c2", "ln", "attention", "self_attention", "decoder", "encoder"),
+                   default="all",
                    help="run one section alone and print its line (profiling): 'c2' the timed C2 steps, "
-                        "'ln' the LayerNorm producer, 'attention' the cross-attention, 'decoder' the C3 step")
+                        "'ln' the LayerNorm producer, 'attention' the cross-attention, 'decoder' the C3 step, "
+                        "'encoder' the 32-layer encoder forward")
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="target CPU-baseline sample time (0 skips the CPU baseline, for profiling runs)")
     return p.parse_args(argv)
@@ -349,6 +351,7 @@ def run_ours(args, rank, local_rank, world):
     ln = run_ln_producer(fp8, native, device, 20, seed=31 + rank) if full else None
     attention = run_cross_attention(fp8, native, device, 10, seed=41 + rank) if full else None
     self_attn = run_self_attention(fp8, native, device, 10, seed=51 + rank) if full else None
+    encoder = run_encoder(fp8, native, device, 5, 2, seed=61 + rank) if full else None
     decoder = None
     if full and args.decoder_steps > 0:
         del flush, scrub
@@ -413,6 +416,7 @@ def run_ours(args, rank, local_rank, world):
             result["ln_producer"] = ln
             result["cross_attention"] = attention
             result["self_attention"] = self_attn
+            result["encoder_forward"] = encoder
         if decoder is not None:
             result["decoder_step"] = decoder
         if full and world == 1 and args.cpu_seconds > 0:
@@ -562,11 +566,97 @@ def run_section_only(args, local_rank):
     elif args.only == "attention":
         result = run_cross_attention(fp8, native, device, max(1, args.steps), seed=41, layers=args.decoder_layers)
         result.update(metric="decoder cross-attention K/V throughput")
+    elif args.only == "encoder":
+        result = run_encoder(fp8, native, device, max(1, args.decoder_steps), max(1, args.warmup), seed=61)
+        result.update(metric="encoder forward audio-s/s (32 layers, this library's kernels only)")
     else:
         result = run_self_attention(fp8, native, device, max(1, args.steps), seed=51)
         result.update(metric="encoder self-attention TFLOP/s")
     result.update(n_gpus=1, higher_is_better=True, impl="ours")
     return result
+
+
+def run_encoder(fp8, native, device, steps: int, warmup: int, seed: int, layers_count: int = 32):
+    """The Whisper large-v3 encoder's 32 transformer layers for 8 streams x 1500
+    positions, every kernel this library's: LayerNorm -> E4M3 codes, QKV linear,
+    self-attention -> codes, out_proj, residual add + LayerNorm -> codes, fc1 + GELU
+    -> fc2 codes, fc2; the residual add after fc2 is done by the next layer's
+    LayerNorm (network_graph.cpp:285-287).  One CUDA graph per forward.  Random
+    weights (~N(0, 0.02), per-channel E4M3), fixed activation scales; the conv
+    front-end and the log-mel are not included."""
+    import torch
+
+    streams, heads = 8, 20
+    rows = streams * 1500
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def weight(n, k):
+        w = (torch.randn(n, k, generator=g, device=device) * 0.02).half()
+        b = (torch.randn(n, generator=g, device=device) * 0.02).half()
+        q = fp8.QuantizedWeight.from_half(w, b)
+        del w
+        return q
+
+    def norm_params():
+        gamma = (1 + 0.1 * torch.randn(D, generator=g, device=device)).float()
+        beta = (0.1 * torch.randn(D, generator=g, device=device)).float()
+        return gamma, beta
+
+    layers = [dict(qkv=weight(3840, D), out=weight(D, D), fc1=weight(5120, D), fc2=weight(D, 5120),
+                   ln1=norm_params(), ln2=norm_params()) for _ in range(layers_count)]
+    x0 = torch.randn(rows, D, generator=g, device=device).half()
+    s_ln, s_attn, s_gelu = 0.012, 0.004, 0.006  # activation scales (amax / 448 of typical values)
+
+    def forward():
+        x, r = x0, None
+        for L in layers:
+            x, _, h = fp8.layer_norm(x, *L["ln1"], residual=r, code_scale=s_ln, want_y=False, want_sum=True)
+            qkv, _ = fp8.linear(h, L["qkv"].codes, L["qkv"].scales, s_ln, bias=L["qkv"].bias)
+            _, a = fp8.self_attention(qkv, streams, heads, code_scale=s_attn, want_out=False)
+            o, _ = fp8.linear(a, L["out"].codes, L["out"].scales, s_attn, bias=L["out"].bias)
+            x, _, h2 = fp8.layer_norm(x, *L["ln2"], residual=o, code_scale=s_ln, want_y=False, want_sum=True)
+            _, f = fp8.linear(h2, L["fc1"].codes, L["fc1"].scales, s_ln, bias=L["fc1"].bias, gelu=True,
+                              want_y=False, next_scale=s_gelu)
+            r, _ = fp8.linear(f, L["fc2"].codes, L["fc2"].scales, s_gelu, bias=L["fc2"].bias)
+        return x, r
+
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, warmup)):
+            forward()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    launches_before = native.launch_count()
+    with torch.cuda.graph(graph, stream=stream):
+        out = forward()
+    launches = native.launch_count() - launches_before
+    for _ in range(max(1, warmup)):
+        graph.replay()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    if native.device_error() != 0:
+        raise RuntimeError("device-side wait timed out in the encoder forward")
+    if not bool(torch.isfinite(out[0]).all()):
+        raise RuntimeError("non-finite encoder output")
+    del graph, out
+    ms = statistics.median(times)
+    tokens = 1500
+    flops = layers_count * (FLOPS_PER_STEP + 4 * tokens * tokens * 64 * heads * streams)
+    return {"workload": f"Whisper large-v3 encoder, {layers_count} layers x (LayerNorm, QKV, self-attention, out_proj, "
+                        "residual + LayerNorm, fc1 + GELU, fc2), 8 streams x 1500 positions, one CUDA graph; "
+                        "conv front-end and log-mel not included",
+            "ms_per_forward": round(ms, 3), "streams": streams,
+            "value": round(streams * 30.0 / (ms / 1e3), 1), "unit": "audio-s/s (30 s streams)",
+            "tflops": round(flops / (ms / 1e3) / 1e12, 1),
+            "flops_note": "linears + QK^T + P.V (the second QK^T pass of the exact softmax not counted)",
+            "launches_per_forward": int(launches)}
 
 
 def run_ln_producer(fp8, native, device, reps: int, seed: int):
@@ -843,7 +933,7 @@ def main(argv=None):
     rank, local_rank, world = dist_env()
     if args.impl == "reference":
         result = run_reference(args, rank, world)
-    elif args.only in ("decoder", "ln", "attention", "self_attention"):
+    elif args.only in ("decoder", "ln", "attention", "self_attention", "encoder"):
         result = run_section_only(args, local_rank)
     else:
         result = run_ours(args, rank, local_rank, world)
