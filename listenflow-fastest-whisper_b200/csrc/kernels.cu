@@ -2060,7 +2060,11 @@ constexpr float kLog2e = 1.4426950408889634f;
 //           part of a row (merged once through shared memory); pass 2 writes P
 //           as fp16 into a K-major 128B-swizzled tile for the P.V MMA.
 // The P.V MMAs of tile c - 1 are issued after the score MMAs of tile c, so the
-// softmax of one tile overlaps the MMAs of the next.
+// softmax of one tile overlaps the MMAs of the next.  The kernel is persistent:
+// one CTA per SM walks (stream, head, query block) items, its rings and
+// barrier phases running on across items.  Q is double-buffered by item parity,
+// so the next item's Q and first K tiles load and scale while the current item
+// finishes, and its score MMAs start as soon as the softmax frees a buffer.
 namespace fattn {
 
 using sattn::kLog2e;
@@ -2080,12 +2084,12 @@ constexpr int kSplit = 4;                 // softmax warps per TMEM lane quarter
 constexpr int kSoftWarps = 4 * kSplit;
 constexpr int kCols = kBK / kSplit;       // score columns per softmax warp
 constexpr int kThreads = (kSoftWarp0 + kSoftWarps) * 32;
-constexpr int kOffK = kTile;
+constexpr int kOffK = 2 * kTile; // Q double-buffered by item parity
 constexpr int kOffV = kOffK + kKStages * kTile;
 constexpr int kOffP = kOffV + kVStages * kTile;
-constexpr int kOffStats = kOffP + 2 * kPBytes; // float m[kSplit][kBQ], l[kSplit][kBQ]
-constexpr int kOffBar = kOffStats + 2 * kSplit * kBQ * 4;
-constexpr int kBars = 2 + 3 * kKStages + 2 * kVStages + 8 + 2;
+constexpr int kOffStats = kOffP + 2 * kPBytes; // [2 by item parity] float m[kSplit][kBQ], l[kSplit][kBQ]
+constexpr int kOffBar = kOffStats + 2 * 2 * kSplit * kBQ * 4;
+constexpr int kBars = 4 + 3 * kKStages + 2 * kVStages + 8 + 5;
 constexpr int kSmemBytes = kOffBar + 8 * kBars + 16 + 1024;
 constexpr uint32_t kTmemCols = 512; // S[2] (2 x 128) + O (64)
 constexpr uint32_t kTmemO = 256;
@@ -2118,9 +2122,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
     const uint32_t sb = smem_u32(smem);
     const uint32_t sQ = sb, sK = sb + kOffK, sV = sb + kOffV, sP = sb + kOffP;
-    const uint32_t q_full = sb + kOffBar;
-    const uint32_t q_ready = q_full + 8;
-    const uint32_t k_full = q_ready + 8;
+    const uint32_t q_full = sb + kOffBar; // [2] by item parity, like q_ready and q_empty
+    const uint32_t q_ready = q_full + 16;
+    const uint32_t k_full = q_ready + 16;
     const uint32_t k_ready = k_full + 8 * kKStages;
     const uint32_t k_empty = k_ready + 8 * kKStages;
     const uint32_t v_full = k_empty + 8 * kKStages;
@@ -2131,24 +2135,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t p_empty = p_full + 16;
     const uint32_t o_full = p_empty + 16;
     const uint32_t drain = o_full + 8;
+    const uint32_t q_empty = drain + 8; // [2] the item's Q is no longer read (after its last score MMA)
+    const uint32_t o_empty = q_empty + 16; // the item's O has been read (by the softmax warps)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 8 * kBars);
-    float *stat_m = reinterpret_cast<float *>(smem + kOffStats);
-    float *stat_l = stat_m + kSplit * kBQ;
+    float *stats = reinterpret_cast<float *>(smem + kOffStats); // [item parity][m | l][kSplit][kBQ]
 
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
-    const int qb = static_cast<int>(blockIdx.x) % p.qblocks;
-    const int sh = static_cast<int>(blockIdx.x) / p.qblocks;
-    const int head = sh % p.heads;
-    const int stream = sh / p.heads;
-    const int row_base = stream * p.tokens;
-    const int q0 = qb * kBQ;
     const int nt = p.nchunks;
+    const int items = p.streams * p.heads * p.qblocks;
+    struct Item {
+        int head, row_base, q0;
+    };
+    auto item_of = [&](int it) {
+        const int qb = it % p.qblocks;
+        const int sh = it / p.qblocks;
+        return Item{sh % p.heads, (sh / p.heads) * p.tokens, qb * kBQ};
+    };
 
     if (threadIdx.x == 0) {
         griddepcontrol_launch_dependents();
-        mbar_init(q_full, 1);
-        mbar_init(q_ready, kScaleWarps);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(q_full + 8 * b, 1);
+            mbar_init(q_ready + 8 * b, kScaleWarps);
+            mbar_init(q_empty + 8 * b, 1);
+        }
         for (int s = 0; s < kKStages; ++s) {
             mbar_init(k_full + 8 * s, 1);
             mbar_init(k_ready + 8 * s, kScaleWarps);
@@ -2166,6 +2177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(o_full, 1);
         mbar_init(drain, 1);
+        mbar_init(o_empty, kSoftWarps);
         fence_barrier_init();
         prefetch_tensor_map(&tm_q);
         prefetch_tensor_map(&tm_k);
@@ -2184,23 +2196,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
-            mbar_arrive_expect_tx(q_full, kTile);
-            tma_load_2d(sQ, &tm_q, q_full, head * kDim, row_base + q0);
-            int k_issued = 0, v_issued = 0;
-            for (int j = 0; j < 2 * nt; ++j) {
-                const int s = j % kKStages;
-                if (!mbar_wait(k_empty + 8 * s, ((j / kKStages) & 1u) ^ 1u, kSiteProducerEmpty))
+            int k_issued = 0, v_issued = 0, q_issued = 0;
+            bool ok = true;
+            for (int it = blockIdx.x, local = 0; ok && it < items; it += gridDim.x, ++local) {
+                const Item w = item_of(it);
+                const uint32_t qb = local & 1;
+                if (!mbar_wait(q_empty + 8 * qb, ((local >> 1) & 1u) ^ 1u, kSiteProducerEmpty))
                     break;
-                mbar_arrive_expect_tx(k_full + 8 * s, kTile);
-                tma_load_2d(sK + s * kTile, &tm_k, k_full + 8 * s, head * kDim, row_base + (j % nt) * kBK);
-                ++k_issued;
-                if (j >= nt) {
-                    const int c = j - nt, vs = c % kVStages;
-                    if (!mbar_wait(v_empty + 8 * vs, ((c / kVStages) & 1u) ^ 1u, kSiteProducerEmpty))
+                mbar_arrive_expect_tx(q_full + 8 * qb, kTile);
+                tma_load_2d(sQ + qb * kTile, &tm_q, q_full + 8 * qb, w.head * kDim, w.row_base + w.q0);
+                ++q_issued;
+                for (int j = 0; j < 2 * nt; ++j) {
+                    const int s = k_issued % kKStages;
+                    if (!mbar_wait(k_empty + 8 * s, ((k_issued / kKStages) & 1u) ^ 1u, kSiteProducerEmpty)) {
+                        ok = false;
                         break;
-                    mbar_arrive_expect_tx(v_full + 8 * vs, kTile);
-                    tma_load_2d(sV + vs * kTile, &tm_v, v_full + 8 * vs, head * kDim, row_base + c * kBK);
-                    ++v_issued;
+                    }
+                    mbar_arrive_expect_tx(k_full + 8 * s, kTile);
+                    tma_load_2d(sK + s * kTile, &tm_k, k_full + 8 * s, w.head * kDim, w.row_base + (j % nt) * kBK);
+                    ++k_issued;
+                    if (j >= nt) {
+                        const int vs = v_issued % kVStages;
+                        if (!mbar_wait(v_empty + 8 * vs, ((v_issued / kVStages) & 1u) ^ 1u, kSiteProducerEmpty)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(v_full + 8 * vs, kTile);
+                        tma_load_2d(sV + vs * kTile, &tm_v, v_full + 8 * vs, w.head * kDim, w.row_base + (j - nt) * kBK);
+                        ++v_issued;
+                    }
                 }
             }
             // Loads still in flight (only after an abandoned wait) land before exit.
@@ -2210,16 +2234,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c = v_issued > kVStages ? v_issued - kVStages : 0; c < v_issued; ++c)
                 for (int t = 0; t < (1 << 20) && !mbar_try_wait(v_full + 8 * (c % kVStages), (c / kVStages) & 1u); ++t) {
                 }
-            for (int t = 0; t < (1 << 20) && !mbar_try_wait(q_full, 0); ++t) {
-            }
+            for (int q = q_issued > 2 ? q_issued - 2 : 0; q < q_issued; ++q)
+                for (int t = 0; t < (1 << 20) && !mbar_try_wait(q_full + 8 * (q & 1), (q >> 1) & 1u); ++t) {
+                }
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             constexpr uint32_t id_s = idesc_f16_f32<kBQ, kBK>();
             constexpr uint32_t id_o = idesc_f16_f32<kBQ, kDim>() | (1u << 16); // B (V) MN-major
-            bool ok = mbar_wait(q_ready, 0, kSiteMmaFull);
-            auto score_mma = [&](int u) { // u: score tile 0 .. 2 nt - 1 (pass 1, then pass 2)
+            bool ok = true;
+            int u_all = 0, c_all = 0; // score tiles and P tiles issued over all items
+            uint32_t sQi = sQ; // this item's Q buffer
+            auto score_mma = [&](int u) { // u: score tile over all items (K tile u)
                 const uint32_t b = u & 1;
                 const int ks = u % kKStages;
                 ok = ok && mbar_wait(s_empty + 8 * b, ((u >> 1) & 1u) ^ 1u, kSiteMmaAccEmpty) &&
@@ -2229,12 +2256,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
 #pragma unroll
                 for (int k = 0; k < kDim / 16; ++k)
-                    mma_f16(tmem + b * kBK, smem_desc_k_sw128(sQ + k * 32),
+                    mma_f16(tmem + b * kBK, smem_desc_k_sw128(sQi + k * 32),
                             smem_desc_k_sw128(sK + ks * kTile + k * 32), id_s, k != 0);
                 mma_commit(k_empty + 8 * ks);
                 mma_commit(s_full + 8 * b);
             };
-            auto pv_mma = [&](int c) {
+            auto pv_mma = [&](int c, int first) { // c: P tile over all items; first: the item's first
                 const uint32_t pb = c & 1;
                 const int vs = c % kVStages;
                 ok = ok && mbar_wait(p_full + 8 * pb, (c >> 1) & 1u, kSiteMmaFull) &&
@@ -2245,20 +2272,31 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int k = 0; k < kBK / 16; ++k)
                     mma_f16(tmem + kTmemO, smem_desc_k_sw128(sP + pb * kPBytes + (k / 4) * (kPBytes / 2) + (k % 4) * 32),
-                            smem_desc_mn_sw128(sV + vs * kTile + k * 16 * 128), id_o, (c | k) != 0);
+                            smem_desc_mn_sw128(sV + vs * kTile + k * 16 * 128), id_o, (first == 0 || k != 0) ? 1u : 0u);
                 mma_commit(v_empty + 8 * vs);
                 mma_commit(p_empty + 8 * pb);
             };
-            for (int c = 0; c < nt; ++c)
-                score_mma(c);
-            for (int c = 0; c < nt; ++c) {
-                score_mma(nt + c);
-                if (c > 0)
-                    pv_mma(c - 1);
+            for (int it = blockIdx.x, local = 0; ok && it < items; it += gridDim.x, ++local) {
+                const uint32_t qb = local & 1;
+                sQi = sQ + qb * kTile;
+                ok = ok && mbar_wait(q_ready + 8 * qb, (local >> 1) & 1u, kSiteMmaFull);
+                for (int c = 0; c < nt; ++c)
+                    score_mma(u_all++);
+                for (int c = 0; c < nt; ++c) {
+                    score_mma(u_all++);
+                    if (c == nt - 1 && ok)
+                        mma_commit(q_empty + 8 * qb); // the item's Q is read by no later MMA
+                    if (c == 1) // O of the previous item has been read out
+                        ok = ok && mbar_wait(o_empty, (local & 1u) ^ 1u, kSiteMmaAccEmpty);
+                    if (c > 0)
+                        pv_mma(c_all++, c == 1);
+                }
+                if (nt == 1)
+                    ok = ok && mbar_wait(o_empty, (local & 1u) ^ 1u, kSiteMmaAccEmpty);
+                pv_mma(c_all++, nt == 1);
+                if (ok)
+                    mma_commit(o_full);
             }
-            pv_mma(nt - 1);
-            if (ok)
-                mma_commit(o_full);
             // Every MMA of this thread completes before TMEM is freed.
             mma_commit(drain);
             for (int t = 0; t < (1 << 22) && !mbar_try_wait(drain, 0); ++t) {
@@ -2283,20 +2321,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             fence_proxy_async_smem(); // the MMA (async proxy) reads what these stores wrote
             __syncwarp();
         };
-        bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, kSiteMmaFull));
-        if (ok) {
-            scale_tile(sQ);
-            if (lane == 0)
-                mbar_arrive(q_ready);
-        }
-        for (int j = 0; ok && j < 2 * nt; ++j) {
-            const int s = j % kKStages;
-            ok = __all_sync(0xffffffffu, mbar_wait(k_full + 8 * s, (j / kKStages) & 1u, kSiteMmaFull));
+        bool ok = true;
+        int k_scaled = 0;
+        for (int it = blockIdx.x, local = 0; ok && it < items; it += gridDim.x, ++local) {
+            const uint32_t qb = local & 1;
+            ok = __all_sync(0xffffffffu, mbar_wait(q_full + 8 * qb, (local >> 1) & 1u, kSiteMmaFull));
             if (!ok)
                 break;
-            scale_tile(sK + s * kTile);
+            scale_tile(sQ + qb * kTile);
             if (lane == 0)
-                mbar_arrive(k_ready + 8 * s);
+                mbar_arrive(q_ready + 8 * qb);
+            for (int j = 0; ok && j < 2 * nt; ++j, ++k_scaled) {
+                const int s = k_scaled % kKStages;
+                ok = __all_sync(0xffffffffu, mbar_wait(k_full + 8 * s, (k_scaled / kKStages) & 1u, kSiteMmaFull));
+                if (!ok)
+                    break;
+                scale_tile(sK + s * kTile);
+                if (lane == 0)
+                    mbar_arrive(k_ready + 8 * s);
+            }
         }
     } else {
         // ---------------- softmax: (lane quarter, column part) per warp ----------------
@@ -2342,6 +2385,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         h[i / 2] = (h[i / 2] & 0x0000FFFFu) | 0xFC000000u;
                 }
         };
+        int u_all = 0, c_all = 0; // score tiles and P tiles consumed over all items
+        for (int it = blockIdx.x, local = 0; it < items; it += gridDim.x, ++local) {
+        const Item w = item_of(it);
         // ---- pass 1: running max and sum of exp over this part of the row ----
         // The scores stay packed fp16 pairs: the tile maximum is a packed max, and
         // s - max is one mixed-precision add per score (f16 operand, f32 result),
@@ -2350,7 +2396,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float m = -INFINITY, l = 0.0f;
         for (int c = 0; c < nt; ++c) {
             uint32_t h[kCols / 2];
-            load_scores(c, c, h);
+            load_scores(u_all++, c, h);
             uint32_t pm[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j)
@@ -2379,6 +2425,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         // ---- merge the parts of each row (in part order) ----
+        // Stats alternate by item parity: a warp overwrites this item's buffer two
+        // items later, after every warp has read it and passed the next barrier.
+        float *stat_m = stats + (local & 1) * (2 * kSplit * kBQ);
+        float *stat_l = stat_m + kSplit * kBQ;
         stat_m[part * kBQ + row] = m;
         stat_l[part * kBQ + row] = l;
         named_barrier_sync(2, kSoftWarps * 32);
@@ -2397,7 +2447,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---- pass 2: P = half(p) into the K-major swizzled P tile ----
         for (int c = 0; c < nt; ++c) {
             uint32_t h[kCols / 2];
-            load_scores(nt + c, c, h);
+            load_scores(u_all++, c, h);
             uint32_t pk[kCols / 2];
 #pragma unroll
             for (int i = 0; i < kCols / 2; ++i) {
@@ -2405,8 +2455,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 sub_f16x2_f32(h[i], mm, d0, d1);
                 pk[i] = gemm::cvt_f16x2(fast_exp2(fmaf(d0, kLog2e, -lg)), fast_exp2(fmaf(d1, kLog2e, -lg)));
             }
-            const uint32_t pb = c & 1;
-            wait_lane0(p_empty + 8 * pb, ((c >> 1) & 1u) ^ 1u, kSiteProducerEmpty);
+            const uint32_t pb = c_all & 1;
+            wait_lane0(p_empty + 8 * pb, ((c_all >> 1) & 1u) ^ 1u, kSiteProducerEmpty);
             // columns col0 .. col0 + kCols - 1 sit in 64-key half col0 / 64, 16-byte chunks from (col0 % 64) / 8
             const uint32_t prow = sP + pb * kPBytes + (col0 / 64) * (kPBytes / 2) + row * 128;
 #pragma unroll
@@ -2420,10 +2470,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0)
                 mbar_arrive(p_full + 8 * pb);
+            ++c_all;
         }
         // ---- epilogue: out = half(O), this warp's kOutCols of the 64 dims ----
         constexpr int kOutCols = kDim / kSplit;
-        wait_lane0(o_full, 0, kSiteEpilogueAccFull);
+        wait_lane0(o_full, local & 1u, kSiteEpilogueAccFull);
         tc_fence_after();
         uint32_t o[kOutCols];
         static_assert(kOutCols == 16 || kOutCols == 32, "output columns per softmax warp");
@@ -2434,12 +2485,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld_32x32b_x16(tmem + kTmemO + (static_cast<uint32_t>(quarter * 32) << 16) + part * kOutCols,
                                *reinterpret_cast<uint32_t(*)[16]>(o));
         tmem_wait_ld();
-        const int token = q0 + row;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0)
+            mbar_arrive(o_empty); // the next item's P.V MMAs may overwrite O
+        const int token = w.q0 + row;
         if (ok && token < p.tokens) {
             const float scale = p.code_scale_ptr ? *p.code_scale_ptr : p.code_scale;
             const float recip = p.code_scale_ptr ? __frcp_rn(scale) : p.code_recip;
             const uint64_t neg_scale2 = f2_bits(-scale, -scale), recip2 = f2_bits(recip, recip);
-            const size_t idx = static_cast<size_t>(row_base + token) * (p.heads * kDim) + head * kDim + part * kOutCols;
+            const size_t idx = static_cast<size_t>(w.row_base + token) * (p.heads * kDim) + w.head * kDim + part * kOutCols;
             uint32_t h[kOutCols / 2];
 #pragma unroll
             for (int i = 0; i < kOutCols / 2; ++i)
@@ -2461,6 +2516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < kOutCols / 16; ++j)
                     dst[j] = make_uint4(q[4 * j], q[4 * j + 1], q[4 * j + 2], q[4 * j + 3]);
             }
+        }
         }
     }
 
@@ -3073,7 +3129,9 @@ cudaError_t launch_self_attention(const SelfAttentionLaunch &L, cudaStream_t str
     if (attr != cudaSuccess)
         return attr;
     cudaLaunchConfig_t config{};
-    config.gridDim = dim3(static_cast<unsigned>(static_cast<int64_t>(L.streams) * L.heads * p.qblocks));
+    // Persistent: one CTA per SM walks the (stream, head, query block) items.
+    const int64_t items = static_cast<int64_t>(L.streams) * L.heads * p.qblocks;
+    config.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>(items, sm_count())));
     config.blockDim = dim3(fattn::kThreads);
     config.dynamicSmemBytes = fattn::kSmemBytes;
     config.stream = stream;
