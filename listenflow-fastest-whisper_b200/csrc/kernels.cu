@@ -1535,11 +1535,7 @@ __device__ __forceinline__ float warp_sum(float v)
 
 // KV: 16-byte vectors (8 halves) per lane; the row (cols / 8 vectors) is spread
 // over the lanes, vector v on lane v % 32, held in registers between passes.
-// Warps loop over rows (grid-stride) and pull their next row into L2 first.
-__device__ __forceinline__ void prefetch_l2(const void *ptr)
-{
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
-}
+// Warps loop over rows (grid-stride).
 
 template <int KV>
 __global__ void __launch_bounds__(kThreads, KV <= 5 ? 4 : 1) layer_norm_kernel(const Params p)
@@ -1552,16 +1548,6 @@ __global__ void __launch_bounds__(kThreads, KV <= 5 ? 4 : 1) layer_norm_kernel(c
     const int vecs = p.cols / 8;
     const int stride = static_cast<int>(gridDim.x) * kRowsPerBlock;
     for (int row = blockIdx.x * kRowsPerBlock + warp; row < p.rows; row += stride) {
-    {
-        // The next row of this warp moves into L2 while this one is processed.
-        const int next = row + stride;
-        if (next < p.rows)
-            for (int c = lane; c < vecs; c += 32) {
-                prefetch_l2(p.x + static_cast<size_t>(next) * p.cols + 8 * c);
-                if (p.residual)
-                    prefetch_l2(p.residual + static_cast<size_t>(next) * p.cols + 8 * c);
-            }
-    }
     const size_t base = static_cast<size_t>(row) * p.cols;
     uint4 v[KV];
 #pragma unroll
