@@ -1632,9 +1632,10 @@ __global__ void __launch_bounds__(kThreads, KV <= 5 ? 4 : 1) layer_norm_kernel(c
 // serves one (stream, head); all query rows (beams) of the stream share one pass
 // over the head's K and V, each CTA over a contiguous range of the keys.
 // Pass 1 streams K and forms fp16 scores with m16n8k16 MMAs.  The softmax is
-// over all keys: the CTAs exchange their rows' maxima and then their sums of
-// exp through distributed shared memory, so every probability is
-// half(exp(s - max) / sum) with the global max and sum.  Pass 2 streams V and
+// over all keys: in one exchange through distributed shared memory the CTAs
+// share each row's local max m_r and local sum of exp(s - m_r); every CTA then
+// forms the global max M and sum L = sum_r l_r exp(m_r - M) in rank order, so
+// every probability is half(exp(s - M) / L).  Pass 2 streams V and
 // forms each CTA's part of P.V; the parts are summed in rank order by the CTA
 // owning each group of output columns.  K/V tiles arrive by TMA (128B-swizzled,
 // so the ldmatrix fragment reads are conflict-free) through a ring fed by one
@@ -1708,9 +1709,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t xch_s = smem_u32(xch);
     const uint32_t bar_full = xch_s + p.xch_bytes;
     const uint32_t bar_empty = bar_full + 8 * depth;
-    const uint32_t bar_max = bar_empty + 8 * depth; // S arrivals: every rank's maxima are here
-    const uint32_t bar_sum = bar_max + 8;             // S arrivals: every rank's sums
-    const uint32_t bar_out = bar_sum + 8;             // S arrivals: every rank's parts of my columns
+    const uint32_t bar_stats = bar_empty + 8 * depth; // S arrivals: every rank's maxima and sums are here
+    const uint32_t bar_out = bar_stats + 8;            // S arrivals: every rank's parts of my columns
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
     const int S = p.cluster;
@@ -1730,8 +1730,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(bar_full + 8 * i, 1);
             mbar_init(bar_empty + 8 * i, kConsumerWarps);
         }
-        mbar_init(bar_max, S);
-        mbar_init(bar_sum, S);
+        mbar_init(bar_stats, S);
         mbar_init(bar_out, S);
         fence_barrier_init();
         prefetch_tensor_map(&tm_k);
@@ -1850,44 +1849,39 @@ __global__ void __launch_bounds__(kThreads, 1)
                     sr[j] = f2h_rn(__fdiv_rn(expf(h2f(sr[j]) - mx), sum));
             }
         } else {
-        // Row maxima of this CTA's keys, pushed to every rank: xch[kXMax][rank][row].
+        // Row max m_r and sum of exp(s - m_r) over this CTA's keys, pushed to
+        // every rank: xch[kXMax][rank][row] and xch[kXSum][rank][row].
         for (int row = warp; row < kMaxQueries; row += kConsumerWarps) {
             float mx = -INFINITY;
             if (row < p.queries)
                 for (int j = lane; j < lk; j += 32)
                     mx = fmaxf(mx, h2f(scores[row * p.pstride + j]));
             mx = warp_max(mx);
-            if (lane < S)
-                st_shared_cluster_f32(map_to_rank(xch_s + kXMax + (rank * kMaxQueries + row) * 4, lane), mx);
-        }
-        fence_cluster();
-        named_barrier_sync(1, kConsumers);
-        if (threadIdx.x < S)
-            mbar_arrive_cluster(map_to_rank(bar_max, threadIdx.x));
-        ok = ok && __all_sync(0xffffffffu, mbar_wait_cluster(bar_max, 0, kSiteClusterExchange));
-        for (int row = warp; row < kMaxQueries; row += kConsumerWarps) {
-            float mx = -INFINITY;
-            for (int r = 0; r < S; ++r)
-                mx = fmaxf(mx, xch[kXMax / 4 + r * kMaxQueries + row]);
             float sum = 0.0f;
             if (row < p.queries && mx != -INFINITY)
                 for (int j = lane; j < lk; j += 32)
                     sum += expf(h2f(scores[row * p.pstride + j]) - mx);
             sum = norm::warp_sum(sum);
-            if (lane < S)
+            if (lane < S) {
+                st_shared_cluster_f32(map_to_rank(xch_s + kXMax + (rank * kMaxQueries + row) * 4, lane), mx);
                 st_shared_cluster_f32(map_to_rank(xch_s + kXSum + (rank * kMaxQueries + row) * 4, lane), sum);
+            }
         }
         fence_cluster();
         named_barrier_sync(1, kConsumers);
         if (threadIdx.x < S)
-            mbar_arrive_cluster(map_to_rank(bar_sum, threadIdx.x));
-        ok = ok && __all_sync(0xffffffffu, mbar_wait_cluster(bar_sum, 0, kSiteClusterExchange));
-        // p = half(exp(s - max) / sum), the sum over ranks taken in rank order.
+            mbar_arrive_cluster(map_to_rank(bar_stats, threadIdx.x));
+        ok = ok && __all_sync(0xffffffffu, mbar_wait_cluster(bar_stats, 0, kSiteClusterExchange));
+        // p = half(exp(s - M) / L): M the max over ranks, L = sum_r l_r exp(m_r - M)
+        // taken in rank order (a rank without keys adds nothing).
         for (int row = warp; row < p.queries; row += kConsumerWarps) {
             float mx = -INFINITY, sum = 0.0f;
-            for (int r = 0; r < S; ++r) {
+            for (int r = 0; r < S; ++r)
                 mx = fmaxf(mx, xch[kXMax / 4 + r * kMaxQueries + row]);
-                sum += xch[kXSum / 4 + r * kMaxQueries + row];
+            for (int r = 0; r < S; ++r) {
+                const float mr = xch[kXMax / 4 + r * kMaxQueries + row];
+                if (mr != -INFINITY)
+                    sum += xch[kXSum / 4 + r * kMaxQueries + row] * expf(mr - mx);
             }
             for (int j = lane; j < lk; j += 32)
                 scores[row * p.pstride + j] =
