@@ -7,7 +7,14 @@ TensorRT's graph does.  A score can therefore land one fp16 ulp away, which move
 a probability by about one fp16 ulp.  The output, a convex combination of the v
 rows, stays within the linear's bound 2^-11 + 2^-10 |ref| of the oracle for inputs
 ~N(0, 1): about one fp16 ulp of the output.  The E4M3 codes are bit-exact against Q
-of the GPU's own fp16 output."""
+of the GPU's own fp16 output.
+
+Over millions of self-attention outputs, a row whose dominant score lands one ulp
+away can leave that fixed bound by a few ulps (8 x 384 tokens x 20 heads: 19 of
+3.9M outputs, all in one row of one head).  The self-attention test therefore adds
+the first-order effect of such score flips, computed from the oracle's own scores
+(_score_flip_slack).  A test that needs no tolerance checks that the persistent
+kernel's output does not depend on how items are spread over its CTAs."""
 
 from __future__ import annotations
 
@@ -25,6 +32,40 @@ def _within(got, want_bits):
     want = want_bits.view(np.float16).astype(np.float64)
     err = np.abs(got.astype(np.float64) - want)
     return err, bool(np.all(err <= ATOL + RTOL * np.abs(want)))
+
+
+def _score_flip_slack(qkv, streams, heads, ref):
+    """Per output element, how far the output may move when scores land one fp16
+    ulp away from the exactly summed ones.
+
+    The GPU sums q'.k' in fp32 in its own order, so a score s_j close to an fp16
+    rounding boundary can round to the neighbouring fp16 value: it moves by at most
+    ulp(s_j), and exp(s_j - max) by a factor of at most 1 + ulp(s_j) (first order).
+    With p = softmax(s) and out = sum_j p_j v_j, the output then moves by at most
+    sum_j p_j ulp(s_j) |v_j - out| <= (P' |V|) + |out| rowsum(P'), with P'_ij =
+    p_ij ulp(s_ij).  Scores, probabilities and ulps come from the oracle's own
+    edges: q' = half(q c), k' = half(k c), s = half(q'.k') with an exact sum."""
+    rows, width = qkv.shape
+    tokens = rows // streams
+    d = width // (3 * heads)
+    c = float(np.float16(d ** -0.25))
+    x = qkv.astype(np.float64)
+    slack = np.zeros((rows, heads * d))
+    for st in range(streams):
+        blk = slice(st * tokens, (st + 1) * tokens)
+        for h in range(heads):
+            q = (x[blk, h * d:(h + 1) * d] * c).astype(np.float16).astype(np.float64)
+            k = (x[blk, (heads + h) * d:(heads + h + 1) * d] * c).astype(np.float16).astype(np.float64)
+            v = x[blk, (2 * heads + h) * d:(2 * heads + h + 1) * d]
+            s16 = (q @ k.T).astype(np.float16)
+            ulp = np.abs(np.spacing(s16)).astype(np.float64)
+            s = s16.astype(np.float64)
+            p = np.exp(s - s.max(axis=1, keepdims=True))
+            p /= p.sum(axis=1, keepdims=True)
+            pu = p * ulp
+            o = np.abs(ref[blk, h * d:(h + 1) * d])
+            slack[blk, h * d:(h + 1) * d] = pu @ np.abs(v) + o * pu.sum(axis=1, keepdims=True)
+    return slack
 
 
 def _data(rng, streams, queries, heads, keys):
@@ -100,9 +141,14 @@ def test_cross_attention_identical_keys_average_values(cuda, fp8, oracle):
     # count at or below one 32- or 64-column softmax part, the C2 head count
     (1, 1, 1), (1, 64, 2), (2, 130, 3), (1, 1500, 2), (3, 257, 4), (8, 100, 20),
     (2, 127, 2), (2, 128, 2), (3, 129, 1), (1, 256, 3), (2, 33, 2), (1, 2048, 1),
+    # more (stream, head, query block) items than SMs: each persistent CTA walks
+    # two (200 items of two key tiles) or three to four (480 items of three tiles)
+    # items, so the double-buffered Q and the O hand-over change phase per item
+    (5, 140, 20), (8, 384, 20),
 ])
 def test_self_attention_matches_oracle(cuda, fp8, oracle, native, streams, tokens, heads):
-    """Encoder self-attention on the fused QKV output, same bound as above."""
+    """Encoder self-attention on the fused QKV output, within the bound above plus
+    the slack of scores that land one fp16 ulp away (_score_flip_slack)."""
     import torch
 
     rng = np.random.default_rng(streams * 1000 + tokens + heads)
@@ -112,8 +158,31 @@ def test_self_attention_matches_oracle(cuda, fp8, oracle, native, streams, token
     assert native.device_error() == 0
     want, _ = oracle.self_attention(qkv, streams, heads)
     got = out.cpu().numpy()
-    err, ok = _within(got, want)
+    ref = want.view(np.float16).astype(np.float64)
+    err = np.abs(got.astype(np.float64) - ref)
+    slack = _score_flip_slack(qkv, streams, heads, ref)
     print(f"self s={streams} t={tokens} h={heads}: max_abs={err.max():.3g} "
-          f"exact={(got.view(np.uint16) == want).mean():.4f}")
-    assert ok
+          f"exact={(got.view(np.uint16) == want).mean():.4f} "
+          f"outside the fixed bound={int((err > ATOL + RTOL * np.abs(ref)).sum())}")
+    assert np.all(err <= ATOL + RTOL * np.abs(ref) + slack)
     np.testing.assert_array_equal(codes.cpu().numpy(), oracle.quantize(got.view(np.uint16), np.float32(0.004)))
+
+
+def test_self_attention_independent_of_item_schedule(cuda, fp8, native):
+    """The kernel is persistent: one CTA per SM walks the (stream, head, query block)
+    items, with Q double-buffered and the O hand-over alternating by item.  Each
+    item's arithmetic is the same whichever CTA takes it and in which turn, so 480
+    items (three or four per CTA) must give bit for bit what eight launches of 60
+    items (one per CTA) give."""
+    import torch
+
+    streams, tokens, heads = 8, 384, 20
+    rng = np.random.default_rng(77)
+    qkv = torch.from_numpy(halves(rng, (streams * tokens, 3 * heads * 64))).to(cuda)
+    whole, whole_codes = fp8.self_attention(qkv, streams, heads, code_scale=0.004)
+    parts = [fp8.self_attention(qkv[s * tokens:(s + 1) * tokens].contiguous(), 1, heads, code_scale=0.004)
+             for s in range(streams)]
+    torch.cuda.synchronize()
+    assert native.device_error() == 0
+    assert torch.equal(whole, torch.cat([o for o, _ in parts]))
+    assert torch.equal(whole_codes, torch.cat([c for _, c in parts]))
