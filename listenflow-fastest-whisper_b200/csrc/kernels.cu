@@ -2093,6 +2093,29 @@ __device__ __forceinline__ void sub_f16x2_f32(uint32_t h2, float c, float &lo, f
         : "r"(h2), "f"(-c));
 }
 
+// Packed fp32 pairs (low lane = first value): one instruction rounds each lane as
+// the scalar mul.rn / fma.rn / add.rn would.
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b)
+{
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c)
+{
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b)
+{
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ float lo_f32(uint64_t x) { return __uint_as_float(static_cast<uint32_t>(x)); }
+__device__ __forceinline__ float hi_f32(uint64_t x) { return __uint_as_float(static_cast<uint32_t>(x >> 32)); }
+
 __global__ void __launch_bounds__(kThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const sattn::Params p)
@@ -2388,18 +2411,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float bm = fmaxf(h2f(static_cast<uint16_t>(m2 & 0xFFFFu)), h2f(static_cast<uint16_t>(m2 >> 16)));
             if (bm != -INFINITY) {
                 const float mn = fmaxf(m, bm);
-                float ps[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    ps[j] = 0.0f;
+                // ps[j] holds the partial sums 2j (low) and 2j + 1 (high)
+                uint64_t ps[4] = {0, 0, 0, 0};
+                const uint64_t log2e2 = f2_bits(kLog2e, kLog2e);
 #pragma unroll
                 for (int i = 0; i < kCols / 2; ++i) {
                     float d0, d1;
                     sub_f16x2_f32(h[i], mn, d0, d1);
-                    ps[(2 * i) & 7] += fast_exp2(d0 * kLog2e);
-                    ps[(2 * i + 1) & 7] += fast_exp2(d1 * kLog2e);
+                    const uint64_t x = mul_f32x2(f2_bits(d0, d1), log2e2);
+                    ps[i & 3] = add_f32x2(ps[i & 3], f2_bits(fast_exp2(lo_f32(x)), fast_exp2(hi_f32(x))));
                 }
-                const float add = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+                const float add = ((lo_f32(ps[0]) + hi_f32(ps[0])) + (lo_f32(ps[1]) + hi_f32(ps[1]))) +
+                                  ((lo_f32(ps[2]) + hi_f32(ps[2])) + (lo_f32(ps[3]) + hi_f32(ps[3])));
                 l = (m == -INFINITY ? 0.0f : l * fast_exp2((m - mn) * kLog2e)) + add;
                 m = mn;
             }
@@ -2429,11 +2452,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t h[kCols / 2];
             load_scores(u_all++, c, h);
             uint32_t pk[kCols / 2];
+            const uint64_t log2e2 = f2_bits(kLog2e, kLog2e), neg_lg2 = f2_bits(-lg, -lg);
 #pragma unroll
             for (int i = 0; i < kCols / 2; ++i) {
                 float d0, d1;
                 sub_f16x2_f32(h[i], mm, d0, d1);
-                pk[i] = gemm::cvt_f16x2(fast_exp2(fmaf(d0, kLog2e, -lg)), fast_exp2(fmaf(d1, kLog2e, -lg)));
+                const uint64_t x = fma_f32x2(f2_bits(d0, d1), log2e2, neg_lg2);
+                pk[i] = gemm::cvt_f16x2(fast_exp2(lo_f32(x)), fast_exp2(hi_f32(x)));
             }
             const uint32_t pb = c_all & 1;
             wait_lane0(p_empty + 8 * pb, ((c_all >> 1) & 1u) ^ 1u, kSiteProducerEmpty);
