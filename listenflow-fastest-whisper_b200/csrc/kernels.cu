@@ -2354,17 +2354,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int row = quarter * 32 + lane;
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + col0;
         bool ok = true;
-        auto wait_lane0 = [&](uint32_t bar, uint32_t parity, int site) {
-            bool r = true;
-            if (lane == 0)
-                r = mbar_wait(bar, parity, site);
-            ok = __shfl_sync(0xffffffffu, r ? 1 : 0, 0) != 0 && ok;
+        // Every lane polls the barrier (one shared word, the same answer for all
+        // lanes), so no broadcast is needed; the warp reconverges before the
+        // warp-wide TMEM and barrier instructions that follow.
+        auto wait_all = [&](uint32_t bar, uint32_t parity, int site) {
+            ok = mbar_wait(bar, parity, site) && ok;
+            __syncwarp();
         };
         // This warp's kCols scores of tile u, rounded to fp16 (the MatMul edge);
         // keys past the stream's tokens are -inf.  Frees the TMEM buffer.
         auto load_scores = [&](int u, int c, uint32_t (&h)[kCols / 2]) {
             const uint32_t b = u & 1;
-            wait_lane0(s_full + 8 * b, (u >> 1) & 1u, kSiteEpilogueAccFull);
+            wait_all(s_full + 8 * b, (u >> 1) & 1u, kSiteEpilogueAccFull);
             tc_fence_after();
             uint32_t v[kCols];
 #pragma unroll
@@ -2461,7 +2462,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 pk[i] = gemm::cvt_f16x2(fast_exp2(lo_f32(x)), fast_exp2(hi_f32(x)));
             }
             const uint32_t pb = c_all & 1;
-            wait_lane0(p_empty + 8 * pb, ((c_all >> 1) & 1u) ^ 1u, kSiteProducerEmpty);
+            wait_all(p_empty + 8 * pb, ((c_all >> 1) & 1u) ^ 1u, kSiteProducerEmpty);
             // columns col0 .. col0 + kCols - 1 sit in 64-key half col0 / 64, 16-byte chunks from (col0 % 64) / 8
             const uint32_t prow = sP + pb * kPBytes + (col0 / 64) * (kPBytes / 2) + row * 128;
 #pragma unroll
@@ -2479,7 +2480,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // ---- epilogue: out = half(O), this warp's kOutCols of the 64 dims ----
         constexpr int kOutCols = kDim / kSplit;
-        wait_lane0(o_full, local & 1u, kSiteEpilogueAccFull);
+        wait_all(o_full, local & 1u, kSiteEpilogueAccFull);
         tc_fence_after();
         uint32_t o[kOutCols];
         static_assert(kOutCols == 16 || kOutCols == 32, "output columns per softmax warp");
