@@ -67,3 +67,41 @@ def test_self_attention_matches_float64_restatement(oracle, streams, tokens, hea
     want = want.transpose(0, 2, 1, 3).reshape(streams * tokens, width)
     np.testing.assert_array_equal(out, want.view(np.uint16))
     np.testing.assert_array_equal(codes, oracle.quantize(out, np.float32(0.004)))
+
+
+def test_score_flip_slack_bounds_one_ulp_score_changes():
+    """The self-attention GPU test allows, beyond the fixed bound, the first-order
+    effect of scores that land one fp16 ulp away (_score_flip_slack).  Check that
+    slack on the CPU: move every score of a small case by -1, 0 or +1 fp16 ulp at
+    random, redo the softmax and P.V exactly, and the output moves by no more than
+    the slack says."""
+    from test_gpu_attention import _score_flip_slack
+
+    streams, tokens, heads, d = 2, 96, 2, 64
+    rng = np.random.default_rng(11)
+    qkv = halves(rng, (streams * tokens, 3 * heads * d), std=2.0)
+    c = float(np.float16(d ** -0.25))
+    x = qkv.astype(np.float64)
+    exact = np.zeros((streams * tokens, heads * d))
+    moved = np.zeros_like(exact)
+    for st in range(streams):
+        blk = slice(st * tokens, (st + 1) * tokens)
+        for h in range(heads):
+            q = (x[blk, h * d:(h + 1) * d] * c).astype(np.float16).astype(np.float64)
+            k = (x[blk, (heads + h) * d:(heads + h + 1) * d] * c).astype(np.float16).astype(np.float64)
+            v = x[blk, (2 * heads + h) * d:(2 * heads + h + 1) * d]
+            s16 = (q @ k.T).astype(np.float16)
+            step = rng.integers(-1, 2, size=s16.shape)
+            step[s16 == 0] = 0  # +-0 would step to a NaN bit pattern
+            bits = s16.view(np.int16).astype(np.int32)
+            # one ulp up or down in magnitude: +-1 on the bit pattern of a nonzero finite fp16
+            s_moved = np.where(step == 0, s16, (bits + step).astype(np.int16).view(np.float16))
+            for s, dst in ((s16.astype(np.float64), exact), (s_moved.astype(np.float64), moved)):
+                p = np.exp(s - s.max(axis=1, keepdims=True))
+                p /= p.sum(axis=1, keepdims=True)
+                dst[blk, h * d:(h + 1) * d] = p @ v
+    slack = _score_flip_slack(qkv, streams, heads, exact)
+    change = np.abs(moved - exact)
+    assert change.max() > 0
+    # first order in ulp(s) <= 2^-8 for these scores; allow 10% for the second order
+    assert np.all(change <= 1.1 * slack + 1e-12), float((change / (slack + 1e-30)).max())
