@@ -189,7 +189,8 @@ LFFW_FP8_API lffw_status lffw_cross_attention(const lffw_cross_attention_args *a
  * (elements).  For the fused QKV linear output [rows, 3 * width], pass q = y,
  * k = y + width, v = y + 2 * width and all strides 3 * width.  out: fp16
  * [streams * tokens, heads * head_dim] (out_proj's input) and/or its E4M3 codes.
- * Requirements: head_dim == 64; tokens >= 1; streams * tokens < 2^31; strides
+ * Requirements: head_dim == 64; tokens >= 1; streams * tokens < 2^31;
+ * streams * heads * ceil(tokens / 128) < 2^31; strides
  * >= heads * 64 and multiples of 8; 16-byte aligned pointers; out and/or out_codes
  * set; code_scale (or *code_scale_ptr) in [2^-125, 2^125]. */
 typedef struct lffw_self_attention_args {

@@ -179,6 +179,8 @@ def _self_args(native, **over):
     {"head_dim": 32}, {"tokens": 0}, {"streams": 0}, {"heads": 0}, {"streams": 2**16, "tokens": 2**15},
     {"q_ld": 1000}, {"k_ld": 3844}, {"v_ld": 0}, {"q": None}, {"out": None}, {"k": 0x10004},
     {"out_codes": 0x50000, "code_scale": float("inf")},
+    # 2^30 rows of one token: 2^30 x 20 (stream, head, query block) items, past 32 bits
+    {"streams": 2**30, "tokens": 1},
 ])
 def test_self_attention_rejects_invalid_arguments(native, lib, change):
     a = _self_args(native, **change)
