@@ -5,9 +5,11 @@ The package directory name is not a Python identifier; import it with
 
 Modules:
   _native  ctypes binding of liblffw_b200.so (include/lffw_fp8.h)
-  fp8      Q/DQ linear host API mirroring the reference's _Fp8Graph
-  plugins  the reference's TensorRT plugin creators restated over the C ABI
+  fp8      Q/DQ linear host API mirroring the reference's _Fp8Graph, plus the
+           LayerNorm, attention and fp16 plugin calls; the TensorRT plugin
+           creators are restated in the C ABI itself (lffw_plugin_*)
   scales   the reference's FP8 activation-scale file loader
+  replicas one process per GPU: rank environment, batch shards, max-over-ranks
   build    in-tree nvcc build of liblffw_b200.so
 """
 

@@ -309,8 +309,10 @@ lffw_status lffw_self_attention(const lffw_self_attention_args *a, void *stream)
     const int64_t width = static_cast<int64_t>(a->heads) * 64;
     if (static_cast<int64_t>(a->streams) * a->tokens >= (int64_t(1) << 31) || width > kMaxDim)
         return LFFW_INVALID_ARGUMENT;
-    // The kernel numbers its (stream, head, 128-query block) items with 32-bit integers.
-    if (static_cast<int64_t>(a->streams) * a->heads * ((a->tokens + 127) / 128) >= (int64_t(1) << 31))
+    // The kernel numbers its (stream, head, 128-query block) items with 32-bit
+    // integers, and its persistent loops step an item index by the grid size
+    // (at most 65535 CTAs): items + 65536 must stay below 2^31.
+    if (static_cast<int64_t>(a->streams) * a->heads * ((a->tokens + 127) / 128) + 65536 >= (int64_t(1) << 31))
         return LFFW_INVALID_ARGUMENT;
     for (const int64_t ld : {a->q_ld, a->k_ld, a->v_ld})
         if (ld < width || ld % 8 != 0)

@@ -3310,9 +3310,23 @@ cudaError_t chain_run(const ChainPlan *plan, cudaStream_t stream)
     p.first = plan->first;
     p.done = plan->counters;
     p.m = plan->m;
-    chain::chain_kernel<<<plan->ctas, chain::kThreads, chain::kSmemBytes, stream>>>(p);
+    // CTAs wait on each other's completion counters, so all of them must be
+    // resident at once: a cooperative launch guarantees that, or fails with
+    // cudaErrorCooperativeLaunchTooLarge instead of stalling on a CTA that
+    // never becomes resident (another context holding SMs, for example).
+    cudaLaunchConfig_t config{};
+    config.gridDim = dim3(static_cast<unsigned>(plan->ctas));
+    config.blockDim = dim3(chain::kThreads);
+    config.dynamicSmemBytes = chain::kSmemBytes;
+    config.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    config.attrs = attr;
+    config.numAttrs = 1;
+    err = cudaLaunchKernelEx(&config, chain::chain_kernel, p);
     count_launch();
-    return cudaGetLastError();
+    return err != cudaSuccess ? err : cudaGetLastError();
 }
 
 void chain_destroy(ChainPlan *plan)
@@ -3433,13 +3447,15 @@ static __device__ __align__(256) uint8_t g_static_scratch[LFFW_STATIC_SCRATCH_BY
 
 namespace {
 
-// Device address of g_static_scratch per device, looked up once with the
-// device current.  The symbol's name in host code is only a host-side handle.
-cudaError_t static_scratch_address(uint8_t **out)
+// Device address of g_static_scratch on `device` (the current device), looked
+// up once per device.  The symbol's name in host code is only a host-side
+// handle.  Ordinals beyond the cache are refused rather than sharing a slot.
+cudaError_t static_scratch_address(int device, uint8_t **out)
 {
     static std::mutex lock;
     static uint8_t *addresses[lffw::kMaxDevices] = {};
-    const int device = lffw::current_device();
+    if (device < 0 || device >= lffw::kMaxDevices)
+        return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> guard(lock);
     if (addresses[device] == nullptr) {
         void *p = nullptr;
@@ -3482,7 +3498,7 @@ extern "C" LFFW_FP8_API lffw_status lffw_fp8_linear_half_static(const uint16_t *
     if (gate != LFFW_SUCCESS)
         return gate;
     uint8_t *codes = nullptr;
-    if (static_scratch_address(&codes) != cudaSuccess) {
+    if (static_scratch_address(device, &codes) != cudaSuccess) {
         cudaGetLastError();
         return LFFW_CUDA_ERROR;
     }

@@ -16,6 +16,17 @@ if str(ROOT) not in sys.path:
 PACKAGE = "listenflow-fastest-whisper_b200"
 
 
+def reference_root() -> Path | None:
+    """The reference checkout: $LFFW_REFERENCE_ROOT, else a directory named
+    ``reference`` beside this repository; None when neither exists (tests that
+    read the reference's own files then skip)."""
+    import os
+
+    env = os.environ.get("LFFW_REFERENCE_ROOT")
+    candidate = Path(env) if env else ROOT.parent / "reference"
+    return candidate if (candidate / "python").is_dir() else None
+
+
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs an sm_100a (B200) GPU and the built CUDA library")
 

@@ -181,6 +181,8 @@ def _self_args(native, **over):
     {"out_codes": 0x50000, "code_scale": float("inf")},
     # 2^30 rows of one token: 2^30 x 20 (stream, head, query block) items, past 32 bits
     {"streams": 2**30, "tokens": 1},
+    # items + 65536 reaches 2^31: the persistent loop's last step would overflow
+    {"streams": 2**31 - 65536, "tokens": 1, "heads": 1},
 ])
 def test_self_attention_rejects_invalid_arguments(native, lib, change):
     a = _self_args(native, **change)

@@ -10,9 +10,10 @@ from pathlib import Path
 
 import pytest
 
-from conftest import PACKAGE
+from conftest import PACKAGE, reference_root
 
-REFERENCE_SCALES = Path("/root/reference/python/src/listenflow/fastest_whisper/assets/fp8-scales.json")
+_ROOT = reference_root()
+REFERENCE_SCALES = (_ROOT / "python/src/listenflow/fastest_whisper/assets/fp8-scales.json") if _ROOT else None
 
 
 @pytest.fixture(scope="module")
@@ -60,7 +61,8 @@ def test_calibration_rule_and_keys(scales_mod):
         scales_mod.validate({}, {"model.encoder.layers.0.fc1"})
 
 
-@pytest.mark.skipif(not REFERENCE_SCALES.exists(), reason="reference tree not mounted")
+@pytest.mark.skipif(REFERENCE_SCALES is None or not REFERENCE_SCALES.exists(),
+                    reason="reference checkout not found (set LFFW_REFERENCE_ROOT)")
 def test_reference_scale_file_supports_fused_projections(scales_mod):
     scales = scales_mod.read_fp8_scales(REFERENCE_SCALES)
     assert set(scales) == scales_mod.linear_keys()
