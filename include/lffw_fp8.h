@@ -24,7 +24,7 @@
 #include <stdint.h>
 
 #define LFFW_FP8_ABI_MAJOR 1
-#define LFFW_FP8_ABI_MINOR 5
+#define LFFW_FP8_ABI_MINOR 6
 #define LFFW_FP8_API __attribute__((visibility("default")))
 #if defined(__cplusplus)
 #define LFFW_FP8_NOEXCEPT noexcept
@@ -190,7 +190,7 @@ LFFW_FP8_API lffw_status lffw_cross_attention(const lffw_cross_attention_args *a
  * k = y + width, v = y + 2 * width and all strides 3 * width.  out: fp16
  * [streams * tokens, heads * head_dim] (out_proj's input) and/or its E4M3 codes.
  * Requirements: head_dim == 64; tokens >= 1; streams * tokens < 2^31;
- * streams * heads * ceil(tokens / 128) < 2^31; strides
+ * streams * heads * ceil(tokens / 128) + 65536 < 2^31; strides
  * >= heads * 64 and multiples of 8; 16-byte aligned pointers; out and/or out_codes
  * set; code_scale (or *code_scale_ptr) in [2^-125, 2^125]. */
 typedef struct lffw_self_attention_args {
@@ -208,6 +208,81 @@ typedef struct lffw_self_attention_args {
 
 LFFW_FP8_API lffw_status lffw_self_attention(const lffw_self_attention_args *args,
                                              void *stream) LFFW_FP8_NOEXCEPT;
+
+/* Encoder front end (network_graph.cpp:257-282): the log-mel input cast to fp16,
+ * the two kernel-3 convolutions with padding 1 (the first stride 1, the second
+ * stride 2), each followed by GELU with fp16 edges, and the positional embedding
+ * added after the second.
+ *
+ * lffw_mel_frames: mel fp32 [streams, mels, frames] -> x fp16 [streams, frames + 2,
+ * mels] with x[s][t + 1][c] = half(mel[s][c][t]) and rows 0 and frames + 1 zero: the
+ * time-major, zero-padded layout lffw_conv1d_gelu reads.  Requirements: streams,
+ * mels, frames >= 1; mels % 8 == 0; 16-byte aligned pointers. */
+LFFW_FP8_API lffw_status lffw_mel_frames(const float *mel, int32_t streams, int32_t mels, int32_t frames,
+                                         uint16_t *x, void *stream) LFFW_FP8_NOEXCEPT;
+
+/* Convolution weights from the checkpoint's [c_out, c_in, 3] (conv1d weight
+ * layout) to the tap-major [c_out, 3, c_in] lffw_conv1d_gelu reads.  Runs once
+ * at load time. */
+LFFW_FP8_API lffw_status lffw_conv1d_weight_layout(const uint16_t *weight, int32_t c_out, int32_t c_in,
+                                                   uint16_t *out, void *stream) LFFW_FP8_NOEXCEPT;
+
+/* One encoder convolution (replaces the addConvolutionNd + gelu pair of
+ * network_graph.cpp:259-275, with the positional add of :280-282 when
+ * `positions` is set), on fp16 tensor cores, per stream s and output row t
+ * (frames_out = frames_in / stride):
+ *   acc  = sum_{j<3} sum_ci w[co][j][ci] * x[s][stride * t + j][ci]   (fp32 accumulate;
+ *          x row r holds input frame r - 1, so rows 0 and frames_in + 1 are the padding)
+ *   z    = half(acc + bias[co])                                      (fp32 add, one rounding)
+ *   z    = GELU with fp16 edges
+ *   z    = half(z + positions[t][co])                                (if positions)
+ *   y[s][y_row0 + t][co] = z                        (y: [streams, y_rows, c_out])
+ * With y_rows = frames_out + 2 and y_row0 = 1 the output is itself the padded input
+ * of the next convolution; rows 0 and y_rows - 1 are not written (zero them once).
+ * Requirements: stride 1 or 2; frames_in >= stride and a multiple of it; c_in % 64
+ * == 0; c_out % 32 == 0; y_row0 >= 0 and y_row0 + frames_out <= y_rows; positions
+ * fp16 [frames_out, c_out] or NULL; 16-byte aligned pointers. */
+typedef struct lffw_conv1d_args {
+    size_t struct_size; /* sizeof(lffw_conv1d_args) */
+    int32_t streams, frames_in, c_in, c_out, stride;
+    const uint16_t *x;
+    const uint16_t *weight;    /* [c_out, 3, c_in], lffw_conv1d_weight_layout */
+    const uint16_t *bias;      /* [c_out] */
+    const uint16_t *positions; /* [frames_out, c_out] or NULL */
+    uint16_t *y;
+    int32_t y_rows, y_row0;
+} lffw_conv1d_args;
+
+LFFW_FP8_API lffw_status lffw_conv1d_gelu(const lffw_conv1d_args *args, void *stream) LFFW_FP8_NOEXCEPT;
+
+/* The cross-attention K/V projections of every decoder layer as one FP8 linear
+ * over the final encoder states (network_graph.cpp:296-300 with project_kv of
+ * :231-234: k_proj without bias, v_proj with bias, both on the encoder output),
+ * with the output stored split by heads, the cross_keys / cross_values layout of
+ * lffw_cross_attention:
+ *   y16 = the lffw_fp8_linear value of row s * tokens + t, column c (bias optional;
+ *         a bias of -0.0 leaves every value, -0 included, unchanged)
+ *   y[c / (64 heads)][s][(c / 64) % heads][t][c % 64] = y16
+ * For the decoder's layers stacked as [k_0, v_0, k_1, v_1, ...] (n = 2 * layers *
+ * heads * 64), group g = 2 * layer + (0 for keys, 1 for values).  x_codes: E4M3
+ * [streams * tokens, k].  Requirements: streams, tokens, heads >= 1; k % 16 == 0;
+ * n a multiple of 64 * heads; 16-byte aligned pointers; act_scale (or
+ * *act_scale_ptr) finite and > 0. */
+typedef struct lffw_fp8_linear_heads_args {
+    size_t struct_size; /* sizeof(lffw_fp8_linear_heads_args) */
+    int32_t streams, tokens, heads;
+    int64_t n, k;
+    const uint8_t *x_codes;
+    float act_scale;
+    const float *act_scale_ptr;
+    const uint8_t *w_codes;
+    const float *w_scales;
+    const uint16_t *bias;
+    uint16_t *y;
+} lffw_fp8_linear_heads_args;
+
+LFFW_FP8_API lffw_status lffw_fp8_linear_heads(const lffw_fp8_linear_heads_args *args,
+                                               void *stream) LFFW_FP8_NOEXCEPT;
 
 /* Q of an fp16 [rows, cols] weight with one scale per row (the per-output-channel
  * weight Q of network_graph.cpp:140-152, axis 2 of the transposed constant). */

@@ -119,6 +119,42 @@ class SelfAttentionArgs(ctypes.Structure):
     ]
 
 
+class Conv1dArgs(ctypes.Structure):
+    _fields_ = [
+        ("struct_size", ctypes.c_size_t),
+        ("streams", ctypes.c_int32),
+        ("frames_in", ctypes.c_int32),
+        ("c_in", ctypes.c_int32),
+        ("c_out", ctypes.c_int32),
+        ("stride", ctypes.c_int32),
+        ("x", ctypes.c_void_p),
+        ("weight", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p),
+        ("positions", ctypes.c_void_p),
+        ("y", ctypes.c_void_p),
+        ("y_rows", ctypes.c_int32),
+        ("y_row0", ctypes.c_int32),
+    ]
+
+
+class HeadsLinearArgs(ctypes.Structure):
+    _fields_ = [
+        ("struct_size", ctypes.c_size_t),
+        ("streams", ctypes.c_int32),
+        ("tokens", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("n", ctypes.c_int64),
+        ("k", ctypes.c_int64),
+        ("x_codes", ctypes.c_void_p),
+        ("act_scale", ctypes.c_float),
+        ("act_scale_ptr", ctypes.c_void_p),
+        ("w_codes", ctypes.c_void_p),
+        ("w_scales", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p),
+        ("y", ctypes.c_void_p),
+    ]
+
+
 class PluginField(ctypes.Structure):
     _fields_ = [
         ("name", ctypes.c_char_p),
@@ -174,6 +210,10 @@ def library() -> ctypes.CDLL:
         "lffw_layer_norm": ([ctypes.POINTER(LayerNormArgs), _vp], _i32),
         "lffw_cross_attention": ([ctypes.POINTER(CrossAttentionArgs), _vp], _i32),
         "lffw_self_attention": ([ctypes.POINTER(SelfAttentionArgs), _vp], _i32),
+        "lffw_mel_frames": ([_vp, _i32, _i32, _i32, _vp, _vp], _i32),
+        "lffw_conv1d_weight_layout": ([_vp, _i32, _i32, _vp, _vp], _i32),
+        "lffw_conv1d_gelu": ([ctypes.POINTER(Conv1dArgs), _vp], _i32),
+        "lffw_fp8_linear_heads": ([ctypes.POINTER(HeadsLinearArgs), _vp], _i32),
         "lffw_chain_create": ([ctypes.POINTER(LinearArgs), _i32, ctypes.POINTER(_vp)], _i32),
         "lffw_chain_run": ([_vp, _vp], _i32),
         "lffw_chain_destroy": ([_vp], None),

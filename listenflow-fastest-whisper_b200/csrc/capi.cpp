@@ -343,6 +343,113 @@ lffw_status lffw_self_attention(const lffw_self_attention_args *a, void *stream)
     return from_cuda(lffw::launch_self_attention(L, static_cast<cudaStream_t>(stream)));
 }
 
+lffw_status lffw_mel_frames(const float *mel, int32_t streams, int32_t mels, int32_t frames, uint16_t *x,
+                            void *stream) noexcept
+{
+    if (mel == nullptr || x == nullptr || streams < 1 || mels < 8 || mels % 8 != 0 || frames < 1 ||
+        streams > 65535 || !aligned16(mel) || !aligned16(x))
+        return LFFW_INVALID_ARGUMENT;
+    if (static_cast<int64_t>(streams) * mels * (static_cast<int64_t>(frames) + 2) >= (int64_t(1) << 40))
+        return LFFW_INVALID_ARGUMENT;
+    lffw_status s = current_device_gate();
+    if (s != LFFW_SUCCESS)
+        return s;
+    return from_cuda(lffw::launch_mel_frames(mel, streams, mels, frames, x, static_cast<cudaStream_t>(stream)));
+}
+
+lffw_status lffw_conv1d_weight_layout(const uint16_t *weight, int32_t c_out, int32_t c_in, uint16_t *out,
+                                      void *stream) noexcept
+{
+    if (weight == nullptr || out == nullptr || c_out < 1 || c_in < 1 || weight == out)
+        return LFFW_INVALID_ARGUMENT;
+    lffw_status s = current_device_gate();
+    if (s != LFFW_SUCCESS)
+        return s;
+    return from_cuda(lffw::launch_conv_weight_layout(weight, c_out, c_in, out, static_cast<cudaStream_t>(stream)));
+}
+
+lffw_status lffw_conv1d_gelu(const lffw_conv1d_args *a, void *stream) noexcept
+{
+    if (a == nullptr || a->struct_size < sizeof(lffw_conv1d_args))
+        return a == nullptr ? LFFW_INVALID_ARGUMENT : LFFW_ABI_MISMATCH;
+    if (a->stride != 1 && a->stride != 2)
+        return LFFW_INVALID_ARGUMENT;
+    if (a->streams < 1 || a->frames_in < a->stride || a->frames_in % a->stride != 0 || a->c_in < 64 ||
+        a->c_in % 64 != 0 || a->c_out < 32 || a->c_out % 32 != 0)
+        return LFFW_INVALID_ARGUMENT;
+    const int64_t frames_out = a->frames_in / a->stride;
+    if (a->y_row0 < 0 || a->y_rows < 1 || a->y_row0 + frames_out > a->y_rows)
+        return LFFW_INVALID_ARGUMENT;
+    // Tile bookkeeping is 32-bit: rows, tiles and K blocks stay well inside it.
+    if (static_cast<int64_t>(a->streams) * (static_cast<int64_t>(a->frames_in) + 2) >= (int64_t(1) << 31) ||
+        static_cast<int64_t>(a->streams) * a->y_rows >= (int64_t(1) << 31) || a->c_in > (1 << 20) ||
+        a->c_out > (1 << 20))
+        return LFFW_INVALID_ARGUMENT;
+    if (a->x == nullptr || a->weight == nullptr || a->bias == nullptr || a->y == nullptr)
+        return LFFW_INVALID_ARGUMENT;
+    if (!aligned16(a->x) || !aligned16(a->weight) || !aligned16(a->bias) || !aligned16(a->positions) ||
+        !aligned16(a->y))
+        return LFFW_INVALID_ARGUMENT;
+    lffw_status s = current_device_gate();
+    if (s != LFFW_SUCCESS)
+        return s;
+    lffw::ConvLaunch L{};
+    L.streams = a->streams;
+    L.t_in = a->frames_in;
+    L.c_in = a->c_in;
+    L.c_out = a->c_out;
+    L.stride = a->stride;
+    L.x = a->x;
+    L.w = a->weight;
+    L.bias = a->bias;
+    L.pos = a->positions;
+    L.y = a->y;
+    L.y_rows = a->y_rows;
+    L.y_row0 = a->y_row0;
+    return from_cuda(lffw::launch_conv_gelu(L, static_cast<cudaStream_t>(stream)));
+}
+
+lffw_status lffw_fp8_linear_heads(const lffw_fp8_linear_heads_args *a, void *stream) noexcept
+{
+    if (a == nullptr || a->struct_size < sizeof(lffw_fp8_linear_heads_args))
+        return a == nullptr ? LFFW_INVALID_ARGUMENT : LFFW_ABI_MISMATCH;
+    if (a->streams < 1 || a->tokens < 1 || a->heads < 1 || a->k < 16 || a->k % 16 != 0 || a->k > kMaxDim ||
+        a->n < 1 || a->n > kMaxDim)
+        return LFFW_INVALID_ARGUMENT;
+    const int64_t group = 64 * static_cast<int64_t>(a->heads);
+    if (a->n % group != 0)
+        return LFFW_INVALID_ARGUMENT;
+    // 32-bit tile bookkeeping: rows and tiles (at most 128 rows x 256 columns each).
+    const int64_t rows = static_cast<int64_t>(a->streams) * a->tokens;
+    if (rows >= (int64_t(1) << 31) ||
+        (static_cast<int64_t>(a->streams) * ((a->tokens + 127) / 128)) * ((a->n + 255) / 256) >= (int64_t(1) << 31))
+        return LFFW_INVALID_ARGUMENT;
+    if (a->x_codes == nullptr || a->w_codes == nullptr || a->w_scales == nullptr || a->y == nullptr)
+        return LFFW_INVALID_ARGUMENT;
+    if (!aligned16(a->x_codes) || !aligned16(a->w_codes) || !aligned16(a->w_scales) || !aligned16(a->bias) ||
+        !aligned16(a->y) || (reinterpret_cast<uintptr_t>(a->act_scale_ptr) & 3u) != 0)
+        return LFFW_INVALID_ARGUMENT;
+    if (a->act_scale_ptr == nullptr && !positive_finite(a->act_scale))
+        return LFFW_INVALID_ARGUMENT;
+    lffw_status s = current_device_gate();
+    if (s != LFFW_SUCCESS)
+        return s;
+    lffw::HeadsLinearLaunch L{};
+    L.streams = a->streams;
+    L.tokens = a->tokens;
+    L.heads = a->heads;
+    L.n = a->n;
+    L.k = a->k;
+    L.x_codes = a->x_codes;
+    L.act_scale = a->act_scale;
+    L.act_scale_ptr = a->act_scale_ptr;
+    L.w_codes = a->w_codes;
+    L.w_scales = a->w_scales;
+    L.bias = a->bias;
+    L.y = a->y;
+    return from_cuda(lffw::launch_fp8_linear_heads(L, static_cast<cudaStream_t>(stream)));
+}
+
 lffw_status lffw_fp8_quantize_rows(const uint16_t *w, int64_t rows, int64_t cols, const float *scales,
                                    uint8_t *codes, void *stream) noexcept
 {

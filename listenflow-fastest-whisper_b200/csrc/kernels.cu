@@ -211,7 +211,27 @@ constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kThreads = 64 + kEpiThreads; // warp 0 TMA, warp 1 MMA, warps 2-17 epilogue
 constexpr int kSub = 32;                   // columns per epilogue store
 
-enum : int { kEpiGelu = 1, kEpiY = 2, kEpiCodes = 4 };
+enum : int {
+    kEpiGelu = 1,
+    kEpiY = 2,
+    kEpiCodes = 4,
+    // Operands are fp16 (kind::f16 MMAs, 64 elements per 128-byte K block) and
+    // the per-channel scale is 1: the encoder's fp16 convolutions.
+    kEpiF16In = 8,
+    // y = fp16(acc * scale + bias) with the bias added in fp32 (one rounding),
+    // a convolution layer's own bias, instead of the linear's fp16 bias edge.
+    kEpiBiasF32 = 16,
+    // After the GELU: y = fp16(y + pos[t]), the positional embedding of row t
+    // of its segment (network_graph.cpp:280-282).
+    kEpiPos = 32,
+    // Rows form segments (streams) of p.seg_rows: tiles never straddle two
+    // segments; A is read through 3-D maps (k, row, segment), one per
+    // convolution tap, and outputs are stored through 3-D maps.
+    kEpiSeg = 64,
+    // The fp16 output is stored split by heads: column c of row t of segment s
+    // lands at [c / (64 H)][s][(c / 64) % H][t][c % 64] (requires kEpiSeg).
+    kEpiHeads = 128,
+};
 
 // kPair: a cluster of two CTAs computes a 256 x BN tile with cta_group::2 MMAs.
 // Each CTA loads its 128 rows of A and its BN/2 rows of B (the pair's B tile is
@@ -222,6 +242,13 @@ struct Cfg {
     static constexpr bool kGelu = (EPI & kEpiGelu) != 0;
     static constexpr bool kY = (EPI & kEpiY) != 0;
     static constexpr bool kCodes = (EPI & kEpiCodes) != 0;
+    static constexpr bool kF16In = (EPI & kEpiF16In) != 0;
+    static constexpr bool kBiasF32 = (EPI & kEpiBiasF32) != 0;
+    static constexpr bool kPos = (EPI & kEpiPos) != 0;
+    static constexpr bool kSeg = (EPI & kEpiSeg) != 0;
+    static constexpr bool kHeads = (EPI & kEpiHeads) != 0;
+    static_assert(!kHeads || (kSeg && kY && !kCodes), "head-split stores: segmented fp16 output only");
+    static constexpr int kKElems = kF16In ? kBK / 2 : kBK; // elements per 128-byte K block
     static constexpr int kTileM = kPair ? 2 * kBM : kBM;
     static constexpr int kBRows = kPair ? BN / 2 : BN; // B rows this CTA loads
     static constexpr int kABytes = kBM * kBK;
@@ -262,6 +289,11 @@ struct Cfg {
 struct Params {
     int m, n, k;
     int m_tiles, num_tiles, num_kb;
+    int seg_rows, seg_tiles; // kEpiSeg: rows per segment, tiles per segment
+    int kb_per_tap;          // kEpiSeg: K blocks per A map (convolution tap)
+    int heads;               // kEpiHeads: H
+    const uint16_t *pos;     // kEpiPos: fp16 [seg_rows, pos_ld]
+    int pos_ld;
     float act_scale;
     const float *act_scale_ptr;
     const float *w_scales;
@@ -330,9 +362,18 @@ template <int BN, int EPI, bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                     const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_c,
+                    const __grid_constant__ CUtensorMap tm_a1, const __grid_constant__ CUtensorMap tm_a2,
                     const Params p)
 {
     using C = Cfg<BN, EPI, kPair>;
+    // Segment and first row (within the segment, or of the whole matrix) of this
+    // CTA's 128 rows of tile t.
+    auto tile_rows = [&](int t, uint32_t r) {
+        const int mt = t % p.m_tiles;
+        if (C::kSeg)
+            return int2{mt / p.seg_tiles, (mt % p.seg_tiles) * C::kTileM + static_cast<int>(r) * kBM};
+        return int2{0, mt * C::kTileM + static_cast<int>(r) * kBM};
+    };
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -368,6 +409,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_barrier_init();
         prefetch_tensor_map(&tm_a);
         prefetch_tensor_map(&tm_b);
+        if (C::kSeg && p.num_kb > p.kb_per_tap) {
+            prefetch_tensor_map(&tm_a1);
+            prefetch_tensor_map(&tm_a2);
+        }
         if (C::kY)
             prefetch_tensor_map(&tm_y);
         if (C::kCodes)
@@ -412,10 +457,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (kPair) {
                     if (leader)
                         mbar_arrive_expect_tx(full, C::kTxBytes);
-                    tma_load_2d_pair(sbase + C::kOffB + stage * C::kBBytes, &tm_b, map_to_rank(full, 0), kb * kBK, n0);
+                    tma_load_2d_pair(sbase + C::kOffB + stage * C::kBBytes, &tm_b, map_to_rank(full, 0),
+                                     kb * C::kKElems, n0);
                 } else {
                     mbar_arrive_expect_tx(full, C::kTxBytes);
-                    tma_load_2d(sbase + C::kOffB + stage * C::kBBytes, &tm_b, full, kb * kBK, n0);
+                    tma_load_2d(sbase + C::kOffB + stage * C::kBBytes, &tm_b, full, kb * C::kKElems, n0);
+                }
+            };
+            // The activation rows of K block kb; segmented A has one 3-D map per tap.
+            auto load_a = [&](int stage, int kb, int seg, int r0) {
+                const uint32_t full = bar_full + 8 * stage;
+                const uint32_t dst = sbase + stage * C::kABytes;
+                if (C::kSeg) {
+                    const int tap = kb / p.kb_per_tap;
+                    const CUtensorMap *map = tap == 0 ? &tm_a : (tap == 1 ? &tm_a1 : &tm_a2);
+                    const int x = (kb - tap * p.kb_per_tap) * C::kKElems;
+                    if (kPair)
+                        tma_load_3d_pair(dst, map, map_to_rank(full, 0), x, r0, seg);
+                    else
+                        tma_load_3d(dst, map, full, x, r0, seg);
+                } else if (kPair) {
+                    tma_load_2d_pair(dst, &tm_a, map_to_rank(full, 0), kb * C::kKElems, r0);
+                } else {
+                    tma_load_2d(dst, &tm_a, full, kb * C::kKElems, r0);
                 }
             };
             for (int kb = 0; kb < pre; ++kb)
@@ -424,26 +488,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             int issued = 0;
             for (int t = tile_first; ok && t < p.num_tiles; t += tile_step) {
                 // In a pair each CTA loads half of the tile's B rows.
-                const int m0 = (t % p.m_tiles) * C::kTileM + static_cast<int>(rank) * kBM;
+                const auto rows = tile_rows(t, rank);
                 const int n0 = (t / p.m_tiles) * BN + static_cast<int>(rank) * C::kBRows;
                 for (int kb = 0; kb < p.num_kb; ++kb, ++issued) {
-                    const uint32_t full = bar_full + 8 * s;
                     if (issued < pre) {
                         // Armed with its B tile above: only the activations remain.
-                        if (kPair)
-                            tma_load_2d_pair(sbase + s * C::kABytes, &tm_a, map_to_rank(full, 0), kb * kBK, m0);
-                        else
-                            tma_load_2d(sbase + s * C::kABytes, &tm_a, full, kb * kBK, m0);
+                        load_a(s, kb, rows.x, rows.y);
                     } else {
                         if (!mbar_wait(bar_empty + 8 * s, ph ^ 1u, kSiteProducerEmpty)) {
                             ok = false;
                             break;
                         }
                         arm_and_load_b(s, kb, n0);
-                        if (kPair)
-                            tma_load_2d_pair(sbase + s * C::kABytes, &tm_a, map_to_rank(full, 0), kb * kBK, m0);
-                        else
-                            tma_load_2d(sbase + s * C::kABytes, &tm_a, full, kb * kBK, m0);
+                        load_a(s, kb, rows.x, rows.y);
                     }
                     used_mask |= 1u << s;
                     parity_mask = (parity_mask & ~(1u << s)) | (ph << s);
@@ -466,7 +523,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer (one thread of the leader) ----------------
         if (lane == 0 && leader) {
-            constexpr uint32_t idesc = idesc_e4m3_f32<C::kTileM, BN>();
+            constexpr uint32_t idesc = C::kF16In ? idesc_f16_f32<C::kTileM, BN>() : idesc_e4m3_f32<C::kTileM, BN>();
             int s = 0;
             uint32_t ph = 0;
             int local = 0;
@@ -492,10 +549,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int k = 0; k < kBK / kUmmaK; ++k) {
                         const uint64_t da = smem_desc_k_sw128(a_addr + k * kUmmaK);
                         const uint64_t db = smem_desc_k_sw128(b_addr + k * kUmmaK);
-                        if (kPair)
+                        // One MMA covers 32 bytes of K: 32 E4M3 or 16 fp16 elements.
+                        if (C::kF16In) {
+                            if (kPair)
+                                mma_f16_pair(d_tmem, da, db, idesc, (kb | k) != 0);
+                            else
+                                mma_f16(d_tmem, da, db, idesc, (kb | k) != 0);
+                        } else if (kPair) {
                             mma_f8f6f4_pair(d_tmem, da, db, idesc, (kb | k) != 0);
-                        else
+                        } else {
                             mma_f8f6f4(d_tmem, da, db, idesc, (kb | k) != 0);
+                        }
                     }
                     // Frees the stage (in both CTAs of a pair) once these MMAs finish.
                     if (kPair)
@@ -553,8 +617,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t *staging = smem + C::kOffStaging + ew * C::kWarpStaging;
         const uint32_t staging_s = smem_u32(staging);
         int local = 0;
+        const int row_limit = C::kSeg ? p.seg_rows : p.m;
         for (int t = tile_first; t < p.num_tiles; t += tile_step, ++local) {
-            const int m0 = (t % p.m_tiles) * C::kTileM + static_cast<int>(rank) * kBM;
+            const auto rows = tile_rows(t, rank);
+            const int seg = rows.x;
+            const int m0 = rows.y;
             const int n0 = (t / p.m_tiles) * BN;
             const uint32_t a = local & 1;
             const uint32_t acc_ph = (local >> 1) & 1;
@@ -566,8 +633,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             {
                 const int c = n0 + (slice + 4 * (lane >> 4)) * kSub + 2 * (lane & 15);
                 if (c < p.n) {
-                    const float2 w = __ldg(reinterpret_cast<const float2 *>(p.w_scales + c));
-                    my_cs = make_float2(act_scale * w.x, act_scale * w.y);
+                    if (C::kF16In) {
+                        my_cs = make_float2(1.0f, 1.0f); // fp16 operands carry no scales
+                    } else {
+                        const float2 w = __ldg(reinterpret_cast<const float2 *>(p.w_scales + c));
+                        my_cs = make_float2(act_scale * w.x, act_scale * w.y);
+                    }
                     if (p.bias)
                         my_b = __ldg(reinterpret_cast<const uint32_t *>(p.bias + c));
                 }
@@ -581,7 +652,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             while (subs < 2 && slice + 4 * subs < C::kSubs && n0 + (slice + 4 * subs) * kSub < p.n)
                 ++subs;
             const int row0 = m0 + quarter * 32;
-            if (row0 >= p.m)
+            if (row0 >= row_limit)
                 subs = 0; // every row of this warp is padding: nothing to load or store
             const uint32_t t_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN;
 #pragma unroll 1
@@ -611,17 +682,40 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // Scale, round to fp16, bias, GELU: two columns per packed op; the
                     // pair's scale and bias come from lane (column offset / 2).
                     uint32_t h[8];
+                    uint4 pos_lo = make_uint4(0u, 0u, 0u, 0u), pos_hi = pos_lo;
+                    if (C::kPos) {
+                        // This lane's row of the positional table (padding rows read the
+                        // last row; the store clips them).
+                        const int prow = min(row0 + lane, row_limit - 1);
+                        const uint16_t *pp = p.pos + static_cast<size_t>(prow) * p.pos_ld + col0 + hf * 16;
+                        pos_lo = __ldg(reinterpret_cast<const uint4 *>(pp));
+                        pos_hi = __ldg(reinterpret_cast<const uint4 *>(pp + 8));
+                    }
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const int src = sub * (kSub / 2) + hf * 8 + i;
                         const float2 cs = make_float2(__shfl_sync(0xffffffffu, my_cs.x, src),
                                                       __shfl_sync(0xffffffffu, my_cs.y, src));
-                        const float2 y = fmul2(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), cs);
-                        uint32_t z = cvt_f16x2(y.x, y.y);
-                        if (p.bias)
-                            z = hadd2_rn(z, __shfl_sync(0xffffffffu, my_b, src));
+                        const float2 acc = make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+                        uint32_t z;
+                        if (C::kBiasF32) {
+                            const uint32_t b2 = __shfl_sync(0xffffffffu, my_b, src);
+                            const float2 y = make_float2(
+                                fmaf(acc.x, cs.x, h2f(static_cast<uint16_t>(b2 & 0xFFFFu))),
+                                fmaf(acc.y, cs.y, h2f(static_cast<uint16_t>(b2 >> 16))));
+                            z = cvt_f16x2(y.x, y.y);
+                        } else {
+                            const float2 y = fmul2(acc, cs);
+                            z = cvt_f16x2(y.x, y.y);
+                            if (p.bias)
+                                z = hadd2_rn(z, __shfl_sync(0xffffffffu, my_b, src));
+                        }
                         if (C::kGelu && !C::kCodeTable)
                             z = gelu_fp16x2(z, erf_table);
+                        if (C::kPos) {
+                            const uint32_t pw = i < 4 ? (&pos_lo.x)[i] : (&pos_hi.x)[i - 4];
+                            z = hadd2_rn(z, pw);
+                        }
                         h[i] = z;
                     }
                     if (C::kY) {
@@ -658,10 +752,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    if (C::kY)
-                        tma_store_2d(&tm_y, staging_s, col0, row0);
-                    if (C::kCodes)
-                        tma_store_2d(&tm_c, staging_s + (C::kY ? C::kYBuf : 0), col0, row0);
+                    if (C::kHeads) {
+                        const int head_cols = 64 * p.heads;
+                        tma_store_5d(&tm_y, staging_s, col0 % 64, row0, (col0 / 64) % p.heads, seg, col0 / head_cols);
+                    } else if (C::kSeg) {
+                        if (C::kY)
+                            tma_store_3d(&tm_y, staging_s, col0, row0, seg);
+                        if (C::kCodes)
+                            tma_store_3d(&tm_c, staging_s + (C::kY ? C::kYBuf : 0), col0, row0, seg);
+                    } else {
+                        if (C::kY)
+                            tma_store_2d(&tm_y, staging_s, col0, row0);
+                        if (C::kCodes)
+                            tma_store_2d(&tm_c, staging_s + (C::kY ? C::kYBuf : 0), col0, row0);
+                    }
                     bulk_commit_group();
                 }
             }
@@ -2604,6 +2708,67 @@ __global__ void __launch_bounds__(kThreads)
 } // namespace proj
 
 // ---------------------------------------------------------------------------
+// Encoder front end: the fp32 log-mel cast to fp16 (network_graph.cpp:257,
+// `half(mel)`) and transposed to the time-major, zero-padded rows the
+// convolution reads, and the convolution weights re-laid tap-major.
+
+namespace front {
+
+constexpr int kTile = 32;
+
+// mel fp32 [streams, mels, frames] -> x fp16 [streams, frames + 2, mels] with
+// x[s][t + 1][c] = half(mel[s][c][t]) and rows 0, frames + 1 zero.  A 32 x 32
+// tile goes through shared memory so both the read (along frames) and the
+// write (along mels) are coalesced.
+__global__ void __launch_bounds__(kTile * 8)
+    mel_frames_kernel(const float *__restrict__ mel, int mels, int frames, uint16_t *__restrict__ x)
+{
+    __shared__ uint16_t tile[kTile][kTile + 2];
+    const int s = blockIdx.z;
+    const int t0 = blockIdx.x * kTile;
+    const int c0 = blockIdx.y * kTile;
+    const float *src = mel + static_cast<size_t>(s) * mels * frames;
+    uint16_t *dst = x + static_cast<size_t>(s) * (frames + 2) * mels;
+    for (int r = threadIdx.y; r < kTile; r += 8) {
+        const int c = c0 + r, t = t0 + threadIdx.x;
+        tile[r][threadIdx.x] = (c < mels && t < frames) ? f2h_rn(src[static_cast<size_t>(c) * frames + t]) : 0;
+    }
+    __syncthreads();
+    for (int r = threadIdx.y; r < kTile; r += 8) {
+        const int t = t0 + r, c = c0 + threadIdx.x;
+        if (t < frames && c < mels)
+            dst[static_cast<size_t>(t + 1) * mels + c] = tile[threadIdx.x][r];
+    }
+    if (blockIdx.x == 0) // the two padding rows of this stream's column range
+        for (int i = threadIdx.y * kTile + threadIdx.x; i < kTile; i += kTile * 8)
+            if (c0 + i < mels) {
+                dst[c0 + i] = 0;
+                dst[static_cast<size_t>(frames + 1) * mels + c0 + i] = 0;
+            }
+}
+
+// w [c_out, c_in, 3] -> out [c_out, 3, c_in]: out[o][j][i] = w[o][i][j].
+__global__ void __launch_bounds__(256)
+    conv_weight_layout_kernel(const uint16_t *__restrict__ w, int64_t c_out, int64_t c_in, uint16_t *__restrict__ out)
+{
+    const int64_t total = c_out * c_in * 3;
+    for (int64_t e = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; e < total;
+         e += static_cast<int64_t>(gridDim.x) * 256) {
+        const int64_t o = e / (3 * c_in);
+        const int64_t rem = e - o * 3 * c_in;
+        const int64_t j = rem / c_in;
+        const int64_t i = rem - j * c_in;
+        out[e] = w[(o * c_in + i) * 3 + j];
+    }
+}
+
+} // namespace front
+
+namespace proj {
+
+} // namespace proj
+
+// ---------------------------------------------------------------------------
 // Host side.
 
 namespace {
@@ -2661,6 +2826,28 @@ bool make_map(CUtensorMap *map, CUtensorMapDataType type, int elem, const void *
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// N-d tensor map (rank <= 5): dims[0] is the contiguous axis, strides_bytes[i]
+// the byte step of axis i + 1.
+bool make_map_nd(CUtensorMap *map, CUtensorMapDataType type, int rank, const void *base, const int64_t *dims,
+                 const int64_t *strides_bytes, const uint32_t *box, CUtensorMapSwizzle swizzle)
+{
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn || rank < 1 || rank > 5)
+        return false;
+    cuuint64_t d[5], st[4];
+    cuuint32_t b[5], es[5];
+    for (int i = 0; i < rank; ++i) {
+        d[i] = static_cast<cuuint64_t>(dims[i]);
+        b[i] = box[i];
+        es[i] = 1;
+        if (i + 1 < rank)
+            st[i] = static_cast<cuuint64_t>(strides_bytes[i]);
+    }
+    return fn(map, type, static_cast<cuuint32_t>(rank), const_cast<void *>(base), d, st, b, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 constexpr int kMaxDevices = 64;
 
 int current_device()
@@ -2700,42 +2887,13 @@ cudaError_t ensure_smem(Kernel kernel, int bytes)
     return err;
 }
 
+// Launches fp8_gemm_kernel<BN, EPI, kPair> over p.num_tiles tiles with
+// persistent CTAs (pairs).  maps: A, B, Y, codes, A of tap 1, A of tap 2.
 template <int BN, int EPI, bool kPair>
-cudaError_t run_gemm(const LinearLaunch &L, cudaStream_t stream)
+cudaError_t launch_gemm_kernel(const CUtensorMap (&maps)[6], const gemm::Params &p, cudaStream_t stream)
 {
     using C = gemm::Cfg<BN, EPI, kPair>;
-    CUtensorMap tm_a{}, tm_b{}, tm_y{}, tm_c{};
-    if (!make_map(&tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.x_codes, L.m, L.k, gemm::kBK, gemm::kBM,
-                  CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map(&tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.w_codes, L.n, L.k, gemm::kBK, C::kBRows,
-                  CU_TENSOR_MAP_SWIZZLE_128B))
-        return cudaErrorInvalidValue;
-    // Epilogue stores: one 32-row x 32-column box per warp and sub-chunk.
-    if (C::kY && !make_map(&tm_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.y, L.m, L.n, gemm::kSub, 32,
-                           CU_TENSOR_MAP_SWIZZLE_64B))
-        return cudaErrorInvalidValue;
-    if (C::kCodes && !make_map(&tm_c, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.next_codes, L.m, L.n, gemm::kSub,
-                               32, CU_TENSOR_MAP_SWIZZLE_32B))
-        return cudaErrorInvalidValue;
-    gemm::Params p{};
-    p.m = static_cast<int>(L.m);
-    p.n = static_cast<int>(L.n);
-    p.k = static_cast<int>(L.k);
-    p.m_tiles = static_cast<int>((L.m + C::kTileM - 1) / C::kTileM);
-    const int n_tiles = static_cast<int>((L.n + BN - 1) / BN);
     const int units = kPair ? sm_count() / 2 : sm_count(); // persistent CTAs (pairs)
-    p.num_tiles = p.m_tiles * n_tiles;
-    p.num_kb = static_cast<int>((L.k + gemm::kBK - 1) / gemm::kBK);
-    p.act_scale = L.act_scale;
-    p.act_scale_ptr = L.act_scale_ptr;
-    p.w_scales = L.w_scales;
-    p.bias = L.bias;
-    p.next_scale = L.next_scale;
-    // Correctly rounded reciprocal: binary64 quotient, one rounding to binary32
-    // (innocuous double rounding for division since 53 >= 2*24 + 2).
-    p.next_recip = L.next_codes ? static_cast<float>(1.0 / static_cast<double>(L.next_scale)) : 0.0f;
-    p.next_lean = L.next_codes && lean_scale(L.next_scale) ? 1 : 0;
-
     auto kernel = gemm::fp8_gemm_kernel<BN, EPI, kPair>;
     const cudaError_t attr = ensure_smem(kernel, C::kSmemBytes);
     if (attr != cudaSuccess)
@@ -2760,9 +2918,147 @@ cudaError_t run_gemm(const LinearLaunch &L, cudaStream_t stream)
     }
     config.attrs = attrs;
     config.numAttrs = count;
-    const cudaError_t err = cudaLaunchKernelEx(&config, kernel, tm_a, tm_b, tm_y, tm_c, p);
+    const cudaError_t err =
+        cudaLaunchKernelEx(&config, kernel, maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p);
     count_launch();
     return err != cudaSuccess ? err : cudaGetLastError();
+}
+
+template <int BN, int EPI, bool kPair>
+cudaError_t run_gemm(const LinearLaunch &L, cudaStream_t stream)
+{
+    using C = gemm::Cfg<BN, EPI, kPair>;
+    CUtensorMap maps[6] = {};
+    CUtensorMap &tm_a = maps[0], &tm_b = maps[1], &tm_y = maps[2], &tm_c = maps[3];
+    if (!make_map(&tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.x_codes, L.m, L.k, gemm::kBK, gemm::kBM,
+                  CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.w_codes, L.n, L.k, gemm::kBK, C::kBRows,
+                  CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    // Epilogue stores: one 32-row x 32-column box per warp and sub-chunk.
+    if (C::kY && !make_map(&tm_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.y, L.m, L.n, gemm::kSub, 32,
+                           CU_TENSOR_MAP_SWIZZLE_64B))
+        return cudaErrorInvalidValue;
+    if (C::kCodes && !make_map(&tm_c, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.next_codes, L.m, L.n, gemm::kSub,
+                               32, CU_TENSOR_MAP_SWIZZLE_32B))
+        return cudaErrorInvalidValue;
+    gemm::Params p{};
+    p.m = static_cast<int>(L.m);
+    p.n = static_cast<int>(L.n);
+    p.k = static_cast<int>(L.k);
+    p.m_tiles = static_cast<int>((L.m + C::kTileM - 1) / C::kTileM);
+    const int n_tiles = static_cast<int>((L.n + BN - 1) / BN);
+    p.num_tiles = p.m_tiles * n_tiles;
+    p.num_kb = static_cast<int>((L.k + gemm::kBK - 1) / gemm::kBK);
+    p.act_scale = L.act_scale;
+    p.act_scale_ptr = L.act_scale_ptr;
+    p.w_scales = L.w_scales;
+    p.bias = L.bias;
+    p.next_scale = L.next_scale;
+    // Correctly rounded reciprocal: binary64 quotient, one rounding to binary32
+    // (innocuous double rounding for division since 53 >= 2*24 + 2).
+    p.next_recip = L.next_codes ? static_cast<float>(1.0 / static_cast<double>(L.next_scale)) : 0.0f;
+    p.next_lean = L.next_codes && lean_scale(L.next_scale) ? 1 : 0;
+    p.kb_per_tap = p.num_kb;
+    return launch_gemm_kernel<BN, EPI, kPair>(maps, p, stream);
+}
+
+// Encoder convolution on fp16 tensor cores (see ConvLaunch).
+template <bool kPair, bool kPos>
+cudaError_t run_conv(const ConvLaunch &L, cudaStream_t stream)
+{
+    using namespace gemm;
+    constexpr int BN = 256;
+    constexpr int EPI = kEpiF16In | kEpiBiasF32 | kEpiGelu | kEpiY | kEpiSeg | (kPos ? kEpiPos : 0);
+    using C = Cfg<BN, EPI, kPair>;
+    const int64_t t_out = L.t_in / L.stride;
+    const int64_t in_rows = static_cast<int64_t>(L.t_in) + 2;
+    CUtensorMap maps[6] = {};
+    // Tap j of output row t reads padded input row stride * t + j (row 0 and
+    // row t_in + 1 of each stream are the zero padding).
+    for (int j = 0; j < 3; ++j) {
+        const int64_t dims[3] = {L.c_in, t_out, L.streams};
+        const int64_t strides[2] = {static_cast<int64_t>(L.stride) * L.c_in * 2, in_rows * L.c_in * 2};
+        const uint32_t box[3] = {static_cast<uint32_t>(C::kKElems), static_cast<uint32_t>(kBM), 1u};
+        if (!make_map_nd(&maps[j == 0 ? 0 : 3 + j], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                         L.x + static_cast<int64_t>(j) * L.c_in, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+            return cudaErrorInvalidValue;
+    }
+    if (!make_map(&maps[1], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.w, L.c_out, 3 * static_cast<int64_t>(L.c_in),
+                  C::kKElems, C::kBRows, CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    {
+        const int64_t dims[3] = {L.c_out, t_out, L.streams};
+        const int64_t strides[2] = {static_cast<int64_t>(L.c_out) * 2, static_cast<int64_t>(L.y_rows) * L.c_out * 2};
+        const uint32_t box[3] = {static_cast<uint32_t>(kSub), 32u, 1u};
+        if (!make_map_nd(&maps[2], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                         L.y + static_cast<int64_t>(L.y_row0) * L.c_out, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_64B))
+            return cudaErrorInvalidValue;
+    }
+    Params p{};
+    p.m = static_cast<int>(t_out * L.streams);
+    p.n = L.c_out;
+    p.k = 3 * L.c_in;
+    p.seg_rows = static_cast<int>(t_out);
+    p.seg_tiles = static_cast<int>((t_out + C::kTileM - 1) / C::kTileM);
+    p.m_tiles = p.seg_tiles * L.streams;
+    p.num_tiles = p.m_tiles * ((L.c_out + BN - 1) / BN);
+    p.kb_per_tap = L.c_in / C::kKElems;
+    p.num_kb = 3 * p.kb_per_tap;
+    p.act_scale = 1.0f;
+    p.bias = L.bias;
+    p.pos = L.pos;
+    p.pos_ld = L.c_out;
+    return launch_gemm_kernel<BN, EPI, kPair>(maps, p, stream);
+}
+
+// FP8 linear with a head-split fp16 output (see HeadsLinearLaunch).
+template <bool kPair>
+cudaError_t run_linear_heads(const HeadsLinearLaunch &L, cudaStream_t stream)
+{
+    using namespace gemm;
+    constexpr int BN = 256;
+    constexpr int EPI = kEpiY | kEpiSeg | kEpiHeads;
+    using C = Cfg<BN, EPI, kPair>;
+    CUtensorMap maps[6] = {};
+    {
+        const int64_t dims[3] = {L.k, L.tokens, L.streams};
+        const int64_t strides[2] = {L.k, static_cast<int64_t>(L.tokens) * L.k};
+        const uint32_t box[3] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(kBM), 1u};
+        if (!make_map_nd(&maps[0], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, L.x_codes, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B))
+            return cudaErrorInvalidValue;
+    }
+    if (!make_map(&maps[1], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.w_codes, L.n, L.k, kBK, C::kBRows,
+                  CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    {
+        const int64_t groups = L.n / (64 * static_cast<int64_t>(L.heads));
+        const int64_t dims[5] = {64, L.tokens, L.heads, L.streams, groups};
+        const int64_t head = static_cast<int64_t>(L.tokens) * 64 * 2;
+        const int64_t strides[4] = {128, head, head * L.heads, head * L.heads * L.streams};
+        const uint32_t box[5] = {static_cast<uint32_t>(kSub), 32u, 1u, 1u, 1u};
+        if (!make_map_nd(&maps[2], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, L.y, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_64B))
+            return cudaErrorInvalidValue;
+    }
+    Params p{};
+    p.m = L.tokens * L.streams;
+    p.n = static_cast<int>(L.n);
+    p.k = static_cast<int>(L.k);
+    p.seg_rows = L.tokens;
+    p.seg_tiles = (L.tokens + C::kTileM - 1) / C::kTileM;
+    p.m_tiles = p.seg_tiles * L.streams;
+    p.num_tiles = p.m_tiles * static_cast<int>((L.n + BN - 1) / BN);
+    p.num_kb = static_cast<int>((L.k + kBK - 1) / kBK);
+    p.kb_per_tap = p.num_kb;
+    p.heads = L.heads;
+    p.act_scale = L.act_scale;
+    p.act_scale_ptr = L.act_scale_ptr;
+    p.w_scales = L.w_scales;
+    p.bias = L.bias;
+    return launch_gemm_kernel<BN, EPI, kPair>(maps, p, stream);
 }
 
 template <int BN, bool kPair>
@@ -2796,6 +3092,21 @@ int tile_override()
         return s == "1x256" ? 1 : s == "1x128" ? 2 : s == "2x256" ? 3 : s == "2x128" ? 4 : 0;
     }();
     return mode;
+}
+
+cudaError_t launch_conv_gelu(const ConvLaunch &L, cudaStream_t stream)
+{
+    // CTA pairs for long K (the 1280-channel convolution, K = 3840), as for the linears.
+    const bool pair = 3 * static_cast<int64_t>(L.c_in) >= 1024 && static_cast<int64_t>(L.t_in) * L.streams >= 512;
+    if (pair)
+        return L.pos ? run_conv<true, true>(L, stream) : run_conv<true, false>(L, stream);
+    return L.pos ? run_conv<false, true>(L, stream) : run_conv<false, false>(L, stream);
+}
+
+cudaError_t launch_fp8_linear_heads(const HeadsLinearLaunch &L, cudaStream_t stream)
+{
+    const bool pair = L.k >= 1024 && static_cast<int64_t>(L.tokens) * L.streams >= 512;
+    return pair ? run_linear_heads<true>(L, stream) : run_linear_heads<false>(L, stream);
 }
 
 cudaError_t launch_fp8_gemm(const LinearLaunch &L, cudaStream_t stream)
@@ -3401,6 +3712,25 @@ cudaError_t launch_fp16_bias(const uint16_t *x, uint16_t bias, uint16_t *y, int6
     blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, static_cast<int64_t>(sm_count()) * 16));
     proj::fp16_bias_kernel<<<static_cast<unsigned>(blocks), proj::kThreads, 0, stream>>>(
         x, bias, y, static_cast<uint32_t>(count));
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_mel_frames(const float *mel, int streams, int mels, int frames, uint16_t *x, cudaStream_t stream)
+{
+    const dim3 grid(static_cast<unsigned>((frames + front::kTile - 1) / front::kTile),
+                    static_cast<unsigned>((mels + front::kTile - 1) / front::kTile), static_cast<unsigned>(streams));
+    front::mel_frames_kernel<<<grid, dim3(front::kTile, 8), 0, stream>>>(mel, mels, frames, x);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_conv_weight_layout(const uint16_t *w, int64_t c_out, int64_t c_in, uint16_t *out,
+                                      cudaStream_t stream)
+{
+    const int64_t total = c_out * c_in * 3;
+    const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4 * 148));
+    front::conv_weight_layout_kernel<<<blocks, 256, 0, stream>>>(w, c_out, c_in, out);
     count_launch();
     return cudaGetLastError();
 }

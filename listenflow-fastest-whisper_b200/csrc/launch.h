@@ -22,6 +22,40 @@ struct LinearLaunch {
     bool w_packed; // w_codes holds skinny-packed tiles (m <= 32 path only)
 };
 
+// Encoder convolution (kernel 3, padding 1, stride 1 or 2) on fp16 tensor cores
+// with the fp32 bias add, the fp16-edge GELU and an optional fp16 positional add.
+// x: [streams, t_in + 2, c_in] time-major, rows 0 and t_in + 1 of each stream
+// zero (the padding); w: [c_out, 3, c_in] (tap-major); output row t of stream s
+// lands at y[s][y_row0 + t] of [streams, y_rows, c_out].
+struct ConvLaunch {
+    int streams, t_in, c_in, c_out, stride; // t_out = t_in / stride
+    const uint16_t *x, *w, *bias;
+    const uint16_t *pos; // [t_out, c_out] or null
+    uint16_t *y;
+    int y_rows, y_row0;
+};
+cudaError_t launch_conv_gelu(const ConvLaunch &p, cudaStream_t stream);
+// fp32 log-mel [streams, mels, frames] -> fp16 [streams, frames + 2, mels] (zero rows 0, frames + 1).
+cudaError_t launch_mel_frames(const float *mel, int streams, int mels, int frames, uint16_t *x,
+                              cudaStream_t stream);
+// Convolution weights [c_out, c_in, 3] -> [c_out, 3, c_in].
+cudaError_t launch_conv_weight_layout(const uint16_t *w, int64_t c_out, int64_t c_in, uint16_t *out,
+                                      cudaStream_t stream);
+// FP8 linear over codes [streams, tokens, k] whose fp16 output column c of
+// token t lands at y[c / (64 heads)][stream][(c / 64) % heads][t][c % 64].
+struct HeadsLinearLaunch {
+    int streams, tokens, heads;
+    int64_t n, k;
+    const uint8_t *x_codes;
+    float act_scale;
+    const float *act_scale_ptr;
+    const uint8_t *w_codes;
+    const float *w_scales;
+    const uint16_t *bias;
+    uint16_t *y;
+};
+cudaError_t launch_fp8_linear_heads(const HeadsLinearLaunch &p, cudaStream_t stream);
+
 // Largest M served by the small-M (skinny) kernels.
 constexpr int64_t kSmallMaxRows = 32;
 

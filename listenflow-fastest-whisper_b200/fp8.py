@@ -191,6 +191,90 @@ def self_attention(qkv: torch.Tensor, streams: int, heads: int, *, code_scale=No
     return out, codes
 
 
+def mel_frames(mel: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """fp32 log-mel [streams, mels, frames] -> fp16 [streams, frames + 2, mels], the
+    time-major zero-padded input of conv1d_gelu (half(mel), network_graph.cpp:257)."""
+    _require(mel, torch.float32, "mel")
+    if mel.dim() != 3:
+        raise ValueError("mel must be [streams, mels, frames]")
+    streams, mels, frames = mel.shape
+    if out is None:
+        out = torch.empty((streams, frames + 2, mels), dtype=torch.float16, device=mel.device)
+    native.check(native.library().lffw_mel_frames(mel.data_ptr(), streams, mels, frames, out.data_ptr(),
+                                                  _stream(stream)), "lffw_mel_frames")
+    return out
+
+
+def conv1d_weight_layout(weight: torch.Tensor, stream=None) -> torch.Tensor:
+    """Checkpoint conv1d weight fp16 [c_out, c_in, 3] -> tap-major [c_out, 3, c_in]."""
+    _require(weight, torch.float16, "weight")
+    c_out, c_in, taps = weight.shape
+    if taps != 3:
+        raise ValueError("kernel size 3 expected")
+    out = torch.empty((c_out, 3, c_in), dtype=torch.float16, device=weight.device)
+    native.check(native.library().lffw_conv1d_weight_layout(weight.data_ptr(), c_out, c_in, out.data_ptr(),
+                                                            _stream(stream)), "lffw_conv1d_weight_layout")
+    return out
+
+
+def conv1d_gelu(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, stride: int, *,
+                positions: torch.Tensor | None = None, out: torch.Tensor | None = None, out_row0: int = 0,
+                stream=None) -> torch.Tensor:
+    """Encoder convolution + GELU (+ positional add) on padded time-major input
+    x fp16 [streams, frames_in + 2, c_in] with the tap-major weight [c_out, 3, c_in]
+    (network_graph.cpp:259-282).  Writes rows out_row0 .. out_row0 + frames_out - 1 of
+    each stream block of `out` ([streams, rows, c_out]; allocated dense when None)."""
+    for t, name in ((x, "x"), (weight, "weight"), (bias, "bias")):
+        _require(t, torch.float16, name)
+    streams, rows_in, c_in = x.shape
+    c_out = weight.shape[0]
+    frames_in = rows_in - 2
+    frames_out = frames_in // stride
+    if out is None:
+        out = torch.empty((streams, frames_out, c_out), dtype=torch.float16, device=x.device)
+    a = native.Conv1dArgs()
+    a.struct_size = ctypes.sizeof(native.Conv1dArgs)
+    a.streams, a.frames_in, a.c_in, a.c_out, a.stride = streams, frames_in, c_in, c_out, stride
+    a.x, a.weight, a.bias = x.data_ptr(), weight.data_ptr(), bias.data_ptr()
+    if positions is not None:
+        _require(positions, torch.float16, "positions")
+        a.positions = positions.data_ptr()
+    a.y = out.data_ptr()
+    a.y_rows, a.y_row0 = out.shape[1], out_row0
+    native.check(native.library().lffw_conv1d_gelu(ctypes.byref(a), _stream(stream)), "lffw_conv1d_gelu")
+    return out
+
+
+def linear_heads(x_codes: torch.Tensor, w_codes: torch.Tensor, w_scales: torch.Tensor, act_scale, *,
+                 streams: int, heads: int, bias: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                 stream=None) -> torch.Tensor:
+    """FP8 linear over codes [streams * tokens, k] whose fp16 output is split by heads:
+    [n / (64 heads), streams, heads, tokens, 64] (the cross_keys / cross_values layout,
+    network_graph.cpp:231-234, 296-300)."""
+    _require(x_codes, torch.uint8, "x_codes")
+    _require(w_codes, torch.uint8, "w_codes")
+    _require(w_scales, torch.float32, "w_scales")
+    rows, k = x_codes.shape
+    n = w_codes.shape[0]
+    tokens = rows // streams
+    if tokens * streams != rows or n % (64 * heads) != 0:
+        raise ValueError("x_codes must be [streams * tokens, k] and n a multiple of 64 * heads")
+    if out is None:
+        out = torch.empty((n // (64 * heads), streams, heads, tokens, 64), dtype=torch.float16, device=x_codes.device)
+    a = native.HeadsLinearArgs()
+    a.struct_size = ctypes.sizeof(native.HeadsLinearArgs)
+    a.streams, a.tokens, a.heads, a.n, a.k = streams, tokens, heads, n, k
+    a.x_codes = x_codes.data_ptr()
+    if isinstance(act_scale, torch.Tensor):
+        _require(act_scale, torch.float32, "act_scale")
+        a.act_scale_ptr = act_scale.data_ptr()
+    else:
+        a.act_scale = float(act_scale)
+    a.w_codes, a.w_scales, a.bias, a.y = w_codes.data_ptr(), w_scales.data_ptr(), _ptr(bias), out.data_ptr()
+    native.check(native.library().lffw_fp8_linear_heads(ctypes.byref(a), _stream(stream)), "lffw_fp8_linear_heads")
+    return out
+
+
 def quantize_rows(w: torch.Tensor, scales: torch.Tensor, stream=None) -> torch.Tensor:
     """E4M3 codes of an fp16 [N, K] weight with one scale per row."""
     _require(w, torch.float16, "w")

@@ -186,6 +186,47 @@ def self_attention(qkv, streams: int, heads: int, code_scale=None):
     return out, codes
 
 
+def mel_frames(mel) -> np.ndarray:
+    """half(mel) (network_graph.cpp:257) as fp16 bits [streams, frames + 2, mels],
+    time-major, with zero rows 0 and frames + 1: the padded convolution input."""
+    m = np.asarray(mel, np.float32)
+    streams, mels, frames = m.shape
+    out = np.zeros((streams, frames + 2, mels), np.uint16)
+    out[:, 1:frames + 1, :] = m.astype(np.float16).view(np.uint16).transpose(0, 2, 1)
+    return out
+
+
+def conv1d_gelu(frames, weight, bias, stride: int, positions=None):
+    """One encoder convolution (network_graph.cpp:259-275: kernel 3, padding 1, the
+    given stride, bias) followed by GELU with fp16 edges and, with `positions`, the
+    fp16 positional add of :280-282.
+
+    frames: fp16 bits [streams, frames_in + 2, c_in] (row r = input frame r - 1,
+    rows 0 and frames_in + 1 zero); weight: fp16 [c_out, c_in, 3] (the checkpoint's
+    conv1d layout); bias fp16 [c_out]; positions fp16 [frames_out, c_out].
+    The sum of fp16 products plus the bias is accumulated in binary64 (each product
+    is exact; the sum's error is below K 2^-53 of the sum of magnitudes) and
+    rounded to fp16 once.  Returns (pre-GELU, GELU, output) fp16 bit arrays
+    [streams, frames_out, c_out]; output is the GELU without positions."""
+    x = halves(bits16(frames)).astype(np.float64)
+    w = halves(bits16(weight)).astype(np.float64)
+    b = halves(bits16(bias)).astype(np.float64)
+    streams, rows, c_in = x.shape
+    frames_in = rows - 2
+    frames_out = frames_in // stride
+    acc = np.zeros((streams, frames_out, w.shape[0]), np.float64)
+    for j in range(3):
+        taps = x[:, j: j + stride * (frames_out - 1) + 1: stride, :]  # padded row stride * t + j
+        acc += taps @ w[:, :, j].T
+    pre = half_from_double(acc + b)
+    act = gelu_fp16(pre)
+    if positions is None:
+        return pre, act, act
+    pos = halves(bits16(positions)).astype(np.float64)
+    out = half_from_double(halves(act).astype(np.float64) + pos[None, :frames_out, :])
+    return pre, act, out
+
+
 def quantize_rows(w, scales) -> np.ndarray:
     b = bits16(w)
     s = np.ascontiguousarray(scales, dtype=np.float32)

@@ -400,3 +400,71 @@ def test_enqueue_rejects_null_and_bad_shapes_without_a_launch(native, lib):
         assert lib.lffw_plugin_enqueue(None, ins, ctypes.byref(out), ptrs, outs, None, None) == -1
     finally:
         lib.lffw_plugin_destroy(plugin)
+
+
+def _conv_args(native, **over):
+    a = native.Conv1dArgs()
+    a.struct_size = ctypes.sizeof(native.Conv1dArgs)
+    a.streams, a.frames_in, a.c_in, a.c_out, a.stride = 2, 3000, 1280, 1280, 2
+    a.x, a.weight, a.bias, a.y = 0x10000, 0x20000, 0x30000, 0x40000
+    a.y_rows, a.y_row0 = 1500, 0
+    for key, value in over.items():
+        setattr(a, key, value)
+    return a
+
+
+@pytest.mark.parametrize("change", [
+    {"stride": 3}, {"stride": 0}, {"streams": 0}, {"frames_in": 1}, {"frames_in": 2999}, {"c_in": 96},
+    {"c_in": 0}, {"c_out": 48}, {"y_rows": 1499}, {"y_row0": 1}, {"y_row0": -1}, {"x": None}, {"weight": None},
+    {"bias": None}, {"y": None}, {"x": 0x10008}, {"positions": 0x50004}, {"streams": 2**20, "y_rows": 2**12},
+])
+def test_conv1d_rejects_invalid_arguments(native, lib, change):
+    a = _conv_args(native, **change)
+    assert lib.lffw_conv1d_gelu(ctypes.byref(a), None) == native.INVALID_ARGUMENT
+
+
+def test_conv1d_abi_mismatch_and_null(native, lib):
+    a = _conv_args(native, struct_size=8)
+    assert lib.lffw_conv1d_gelu(ctypes.byref(a), None) == native.ABI_MISMATCH
+    assert lib.lffw_conv1d_gelu(None, None) == native.INVALID_ARGUMENT
+
+
+def _heads_args(native, **over):
+    a = native.HeadsLinearArgs()
+    a.struct_size = ctypes.sizeof(native.HeadsLinearArgs)
+    a.streams, a.tokens, a.heads, a.n, a.k = 8, 1500, 20, 81920, 1280
+    a.x_codes, a.w_codes, a.w_scales, a.y = 0x10000, 0x20000, 0x30000, 0x40000
+    a.act_scale = 0.01
+    for key, value in over.items():
+        setattr(a, key, value)
+    return a
+
+
+@pytest.mark.parametrize("change", [
+    {"streams": 0}, {"tokens": 0}, {"heads": 0}, {"k": 1288}, {"k": 0}, {"n": 1000}, {"n": 81920 + 64},
+    {"x_codes": None}, {"w_codes": None}, {"w_scales": None}, {"y": None}, {"y": 0x40002},
+    {"act_scale": 0.0}, {"act_scale": float("nan")}, {"streams": 2**20, "tokens": 2**11},
+])
+def test_linear_heads_rejects_invalid_arguments(native, lib, change):
+    a = _heads_args(native, **change)
+    assert lib.lffw_fp8_linear_heads(ctypes.byref(a), None) == native.INVALID_ARGUMENT
+
+
+def test_linear_heads_abi_mismatch_and_null(native, lib):
+    a = _heads_args(native, struct_size=8)
+    assert lib.lffw_fp8_linear_heads(ctypes.byref(a), None) == native.ABI_MISMATCH
+    assert lib.lffw_fp8_linear_heads(None, None) == native.INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("args", [
+    (None, 1, 128, 3000, 0x20000), (0x10000, 0, 128, 3000, 0x20000), (0x10000, 1, 12, 3000, 0x20000),
+    (0x10000, 1, 128, 0, 0x20000), (0x10000, 1, 128, 3000, None), (0x10004, 1, 128, 3000, 0x20000),
+])
+def test_mel_frames_rejects_invalid_arguments(native, lib, args):
+    assert lib.lffw_mel_frames(*args, None) == native.INVALID_ARGUMENT
+
+
+def test_conv_weight_layout_rejects_invalid_arguments(native, lib):
+    assert lib.lffw_conv1d_weight_layout(None, 4, 4, 0x10000, None) == native.INVALID_ARGUMENT
+    assert lib.lffw_conv1d_weight_layout(0x10000, 0, 4, 0x20000, None) == native.INVALID_ARGUMENT
+    assert lib.lffw_conv1d_weight_layout(0x10000, 4, 4, 0x10000, None) == native.INVALID_ARGUMENT
