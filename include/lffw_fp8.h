@@ -263,6 +263,9 @@ LFFW_FP8_API lffw_status lffw_conv1d_gelu(const lffw_conv1d_args *args, void *st
  *   y16 = the lffw_fp8_linear value of row s * tokens + t, column c (bias optional;
  *         a bias of -0.0 leaves every value, -0 included, unchanged)
  *   y[c / (64 heads)][s][(c / 64) % heads][t][c % 64] = y16
+ * y holds y_streams streams per group (y_streams >= streams; 0 means streams), so a
+ * batch computed in slices of streams can write its slice of one larger buffer
+ * (pass y offset by the slice's first stream).
  * For the decoder's layers stacked as [k_0, v_0, k_1, v_1, ...] (n = 2 * layers *
  * heads * 64), group g = 2 * layer + (0 for keys, 1 for values).  x_codes: E4M3
  * [streams * tokens, k].  Requirements: streams, tokens, heads >= 1; k % 16 == 0;
@@ -279,6 +282,7 @@ typedef struct lffw_fp8_linear_heads_args {
     const float *w_scales;
     const uint16_t *bias;
     uint16_t *y;
+    int32_t y_streams;
 } lffw_fp8_linear_heads_args;
 
 LFFW_FP8_API lffw_status lffw_fp8_linear_heads(const lffw_fp8_linear_heads_args *args,

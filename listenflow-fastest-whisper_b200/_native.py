@@ -152,6 +152,7 @@ class HeadsLinearArgs(ctypes.Structure):
         ("w_scales", ctypes.c_void_p),
         ("bias", ctypes.c_void_p),
         ("y", ctypes.c_void_p),
+        ("y_streams", ctypes.c_int32),
     ]
 
 

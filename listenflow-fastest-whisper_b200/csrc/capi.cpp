@@ -431,10 +431,13 @@ lffw_status lffw_fp8_linear_heads(const lffw_fp8_linear_heads_args *a, void *str
         return LFFW_INVALID_ARGUMENT;
     if (a->act_scale_ptr == nullptr && !positive_finite(a->act_scale))
         return LFFW_INVALID_ARGUMENT;
+    if (a->y_streams != 0 && a->y_streams < a->streams)
+        return LFFW_INVALID_ARGUMENT;
     lffw_status s = current_device_gate();
     if (s != LFFW_SUCCESS)
         return s;
     lffw::HeadsLinearLaunch L{};
+    L.y_streams = a->y_streams != 0 ? a->y_streams : a->streams;
     L.streams = a->streams;
     L.tokens = a->tokens;
     L.heads = a->heads;

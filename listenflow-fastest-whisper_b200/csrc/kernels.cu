@@ -3037,7 +3037,7 @@ cudaError_t run_linear_heads(const HeadsLinearLaunch &L, cudaStream_t stream)
         const int64_t groups = L.n / (64 * static_cast<int64_t>(L.heads));
         const int64_t dims[5] = {64, L.tokens, L.heads, L.streams, groups};
         const int64_t head = static_cast<int64_t>(L.tokens) * 64 * 2;
-        const int64_t strides[4] = {128, head, head * L.heads, head * L.heads * L.streams};
+        const int64_t strides[4] = {128, head, head * L.heads, head * L.heads * L.y_streams};
         const uint32_t box[5] = {static_cast<uint32_t>(kSub), 32u, 1u, 1u, 1u};
         if (!make_map_nd(&maps[2], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, L.y, dims, strides, box,
                          CU_TENSOR_MAP_SWIZZLE_64B))

@@ -53,6 +53,7 @@ struct HeadsLinearLaunch {
     const float *w_scales;
     const uint16_t *bias;
     uint16_t *y;
+    int y_streams; // streams per group of y (>= streams)
 };
 cudaError_t launch_fp8_linear_heads(const HeadsLinearLaunch &p, cudaStream_t stream);
 

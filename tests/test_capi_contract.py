@@ -443,7 +443,7 @@ def _heads_args(native, **over):
 @pytest.mark.parametrize("change", [
     {"streams": 0}, {"tokens": 0}, {"heads": 0}, {"k": 1288}, {"k": 0}, {"n": 1000}, {"n": 81920 + 64},
     {"x_codes": None}, {"w_codes": None}, {"w_scales": None}, {"y": None}, {"y": 0x40002},
-    {"act_scale": 0.0}, {"act_scale": float("nan")}, {"streams": 2**20, "tokens": 2**11},
+    {"act_scale": 0.0}, {"act_scale": float("nan")}, {"streams": 2**20, "tokens": 2**11}, {"y_streams": 7},
 ])
 def test_linear_heads_rejects_invalid_arguments(native, lib, change):
     a = _heads_args(native, **change)

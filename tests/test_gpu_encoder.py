@@ -193,18 +193,20 @@ def test_calibrated_scales_cover_every_key(small_encoder, enc):
         enc._scales_for(config, bad)
 
 
-def _codes_close(got, want, what, min_equal=0.98):
+def _codes_close(got, want, what, min_equal=0.98, far=0):
     """E4M3 codes of values that agree to about an fp16 ulp: mostly identical, and
-    otherwise adjacent codes (same sign, magnitude one step apart)."""
+    otherwise adjacent codes (same sign, magnitude one step apart), except for at
+    most `far` codes further apart."""
     got, want = got.astype(np.int32), want.astype(np.int32)
     diff = got != want
     frac = 1 - diff.mean()
     step = np.abs((got & 0x7F) - (want & 0x7F))
     sign_ok = ((got ^ want) & 0x80) == 0
     zero = ((got & 0x7F) == 0) | ((want & 0x7F) == 0)
-    print(f"{what}: {frac:.5f} identical codes")
+    adjacent = (step <= 1) & (sign_ok | zero)
+    print(f"{what}: {frac:.5f} identical codes, {int((diff & ~adjacent).sum())} further apart")
     assert frac >= min_equal, what
-    assert ((step <= 1) & (sign_ok | zero))[diff].all(), what
+    assert int((diff & ~adjacent).sum()) <= far, what
 
 
 def test_encoder_stage_by_stage(small_encoder, enc, fp8, oracle, native, cuda):
@@ -285,7 +287,10 @@ def test_encoder_stage_by_stage(small_encoder, enc, fp8, oracle, native, cuda):
         step("lffw_self_attention")
         attn_codes = host(e.attn_codes)
         _, a_ref = oracle.self_attention(qkv, streams, config.heads, code_scale=sc["out"][i])
-        _codes_close(attn_codes, a_ref, f"layer {i} attention codes")
+        # Where a dominant score rounds to its neighbouring fp16 value, an output moves
+        # by a few ulps (the self-attention tests bound it by the score-flip slack), so a
+        # handful of codes may be two steps apart.
+        _codes_close(attn_codes, a_ref, f"layer {i} attention codes", far=max(4, attn_codes.size // 50000))
 
         step("lffw_fp8_linear")
         o = bits(e.o)
@@ -379,3 +384,21 @@ def test_encoder_forward_end_to_end(small_encoder, enc, oracle, native, cuda):
     # Per-stage rounding (about an fp16 ulp, occasionally one E4M3 step of a code)
     # compounds over the stages; it stays far below the FP8 quantization noise itself.
     assert rel < 1e-2 and rel_kv < 1e-2
+
+
+def test_encoder_stream_slices_are_bit_identical(small_encoder, enc, native, cuda):
+    """Streams computed in slices (chunk) write the same bits as one slice of all."""
+    import torch
+
+    config, ck, weights, scales, mel, mel_d = small_encoder
+    mel3 = torch.cat([mel_d, mel_d[:1].flip(-1).contiguous()])
+    whole = enc.Encoder(weights, scales, 3, chunk=3)
+    states, kv = whole.forward(mel3)
+    torch.cuda.synchronize()
+    states, kv = states.clone(), kv.clone()
+    sliced = enc.Encoder(weights, scales, 3, chunk=2)
+    s2, kv2 = sliced.forward(mel3)
+    torch.cuda.synchronize()
+    assert native.device_error() == 0
+    assert torch.equal(states.view(torch.int16), s2.view(torch.int16))
+    assert torch.equal(kv.view(torch.int16), kv2.view(torch.int16))
