@@ -856,8 +856,9 @@ def run_c4(args, rank, local_rank, world):
     with torch.cuda.graph(graph, stream=stream):
         e.run(stream)
     launches_per_forward = native.launch_count() - launches_before
-    for _ in range(max(3, args.warmup)):
-        graph.replay()
+    with torch.cuda.stream(stream):  # replay() launches on the current stream
+        for _ in range(max(3, args.warmup)):
+            graph.replay()
     torch.cuda.synchronize()
     if native.device_error() != 0:
         raise RuntimeError("device-side wait timed out during the encoder warm-up")
@@ -868,7 +869,7 @@ def run_c4(args, rank, local_rank, world):
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(pci_bus_id(torch, device)) as clocks:
+    with ClockSampler(pci_bus_id(torch, device)) as clocks, torch.cuda.stream(stream):
         for s in range(args.steps):
             ev[s][0].record(stream)
             graph.replay()

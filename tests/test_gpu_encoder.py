@@ -251,13 +251,15 @@ def test_encoder_stage_by_stage(small_encoder, enc, fp8, oracle, native, cuda):
     err = np.abs(_f16(x.reshape(streams, t, d)) - _f16(out))
     assert (err <= conv_bound(h1, w2, act, out, True)).all()
 
-    def linear_check(codes, weight, act_scale, got, what, gelu=False, next_scale=None):
+    def linear_check(codes, weight, act_scale, got, what, gelu=False, next_scale=None, far=0):
         wq, ws = host(weight.codes), host(weight.scales)
         b = host(weight.bias) if weight.bias is not None else None
         y_ref, c_ref = oracle.fp8_linear(codes, wq, act_scale, ws, b, gelu=gelu, next_scale=next_scale,
                                          want_y=next_scale is None)
         if next_scale is not None:
-            _codes_close(got, c_ref, what)
+            # A one-ulp move of the pre-GELU value can move the GELU output by two
+            # ulps, so a few codes may be two steps apart.
+            _codes_close(got, c_ref, what, far=far)
             return
         xa = np.abs(oracle.e4m3_to_float(codes).astype(np.float64))
         wa = np.abs(oracle.e4m3_to_float(wq).astype(np.float64))
@@ -307,7 +309,7 @@ def test_encoder_stage_by_stage(small_encoder, enc, fp8, oracle, native, cuda):
         step("lffw_fp8_linear")
         fc2_codes = host(e.fc2_codes)
         linear_check(ln2_codes, L.fc1, sc["fc1"][i], fc2_codes, f"layer {i} fc1+GELU codes", gelu=True,
-                     next_scale=sc["fc2"][i])
+                     next_scale=sc["fc2"][i], far=max(4, fc2_codes.size // 50000))
         step("lffw_fp8_linear")
         residual = bits(e.r)
         linear_check(fc2_codes, L.fc2, sc["fc2"][i], residual, f"layer {i} fc2")
@@ -330,8 +332,57 @@ def test_encoder_stage_by_stage(small_encoder, enc, fp8, oracle, native, cuda):
     linear_check(kv_codes, weights.cross_kv, sc["cross"][0], flat, "cross k/v")
 
 
+def _oracle_forward(ck, weights, scales, mel, config, oracle, perturb=None):
+    """The oracle's own composition of the encoder stages (states, cross k/v as
+    float64).  With `perturb` (a seed), 0.5% of the conv output values move by one
+    fp16 ulp first: the size of difference the convolution kernel itself shows."""
+    host = lambda tensor: tensor.cpu().numpy()
+    streams = mel.shape[0]
+    t, d = config.positions, config.d_model
+    frames = oracle.mel_frames(mel)
+    _, _, h1 = oracle.conv1d_gelu(frames, host(ck["model.encoder.conv1.weight"]),
+                                  host(ck["model.encoder.conv1.bias"]), 1)
+    h1p = np.zeros((streams, config.frames + 2, d), np.uint16)
+    h1p[:, 1:-1] = h1
+    _, _, x = oracle.conv1d_gelu(h1p, host(ck["model.encoder.conv2.weight"]), host(ck["model.encoder.conv2.bias"]),
+                                 2, host(ck["model.encoder.embed_positions.weight"])[:t])
+    x = x.reshape(streams * t, d).copy()
+    if perturb is not None:
+        rng = np.random.default_rng(perturb)
+        flat = x.reshape(-1)
+        ok = np.flatnonzero(((flat & 0x7FFF) != 0) & ((flat & 0x7FFF) < 0x7BFF))
+        idx = rng.choice(ok, flat.size // 200, replace=False)
+        flat[idx] = (flat[idx].astype(np.int32) + rng.choice([-1, 1], idx.size)).astype(np.uint16)
+    residual = None
+    for i, L in enumerate(weights.layers):
+        lin = lambda codes, w, s, **kw: oracle.fp8_linear(codes, host(w.codes), s, host(w.scales),
+                                                          None if w.bias is None else host(w.bias), **kw)
+        s_x, _, codes = oracle.layer_norm(x, host(L.ln1[0]), host(L.ln1[1]), residual=residual,
+                                          code_scale=scales["qkv"][i])
+        x = s_x
+        qkv, _ = lin(codes, L.qkv, scales["qkv"][i])
+        _, ac = oracle.self_attention(qkv, streams, config.heads, code_scale=scales["out"][i])
+        o, _ = lin(ac, L.out, scales["out"][i])
+        x, _, codes = oracle.layer_norm(x, host(L.ln2[0]), host(L.ln2[1]), residual=o, code_scale=scales["fc1"][i])
+        _, hc = lin(codes, L.fc1, scales["fc1"][i], gelu=True, next_scale=scales["fc2"][i], want_y=False)
+        residual, _ = lin(hc, L.fc2, scales["fc2"][i])
+    _, y, codes = oracle.layer_norm(x, host(weights.ln_post[0]), host(weights.ln_post[1]), residual=residual,
+                                    code_scale=scales["cross"][0])
+    kv, _ = oracle.fp8_linear(codes, host(weights.cross_kv.codes), scales["cross"][0],
+                              host(weights.cross_kv.scales), host(weights.cross_kv.bias))
+    kv = _f16(kv).reshape(streams, t, 2 * config.decoder_layers, config.heads, 64).transpose(2, 0, 3, 1, 4)
+    return _f16(y), kv
+
+
 def test_encoder_forward_end_to_end(small_encoder, enc, oracle, native, cuda):
-    """The whole plan against the oracle's own composition of the same stages."""
+    """The whole plan against the oracle's own composition of the same stages.
+
+    Per-stage rounding differences compound: where a value moves by one fp16 ulp
+    across an E4M3 rounding boundary its code moves a whole step (6-12%), and each
+    following linear spreads that.  The bound is therefore calibrated on the oracle
+    itself: the GPU's distance from the oracle must stay within a small multiple of
+    the distance between two oracle runs whose conv outputs differ by one ulp in
+    0.5% of the values (the conv kernel's own mismatch rate)."""
     import torch
 
     config, ck, weights, scales, mel, mel_d = small_encoder
@@ -348,42 +399,14 @@ def test_encoder_forward_end_to_end(small_encoder, enc, oracle, native, cuda):
     assert np.array_equal(states2.cpu().numpy().astype(np.float64).reshape(streams * t, d), got_states)
     assert torch.equal(kv2.view(torch.int16), torch.from_numpy(got_kv.astype(np.float16)).to(cuda).view(torch.int16))
 
-    host = lambda tensor: tensor.cpu().numpy()
-    sc = e.scales
-    frames = oracle.mel_frames(mel)
-    _, _, h1 = oracle.conv1d_gelu(frames, host(ck["model.encoder.conv1.weight"]),
-                                  host(ck["model.encoder.conv1.bias"]), 1)
-    h1p = np.zeros((streams, config.frames + 2, d), np.uint16)
-    h1p[:, 1:-1] = h1
-    _, _, x = oracle.conv1d_gelu(h1p, host(ck["model.encoder.conv2.weight"]), host(ck["model.encoder.conv2.bias"]),
-                                 2, host(ck["model.encoder.embed_positions.weight"])[:t])
-    x = x.reshape(streams * t, d)
-    residual = None
-    for i, L in enumerate(weights.layers):
-        lin = lambda codes, w, s, **kw: oracle.fp8_linear(codes, host(w.codes), s, host(w.scales),
-                                                          None if w.bias is None else host(w.bias), **kw)
-        s_x, _, codes = oracle.layer_norm(x, host(L.ln1[0]), host(L.ln1[1]), residual=residual,
-                                          code_scale=sc["qkv"][i])
-        x = s_x
-        qkv, _ = lin(codes, L.qkv, sc["qkv"][i])
-        _, ac = oracle.self_attention(qkv, streams, config.heads, code_scale=sc["out"][i])
-        o, _ = lin(ac, L.out, sc["out"][i])
-        x, _, codes = oracle.layer_norm(x, host(L.ln2[0]), host(L.ln2[1]), residual=o, code_scale=sc["fc1"][i])
-        _, hc = lin(codes, L.fc1, sc["fc1"][i], gelu=True, next_scale=sc["fc2"][i], want_y=False)
-        residual, _ = lin(hc, L.fc2, sc["fc2"][i])
-    _, y, codes = oracle.layer_norm(x, host(weights.ln_post[0]), host(weights.ln_post[1]), residual=residual,
-                                    code_scale=sc["cross"][0])
-    kv_ref, _ = oracle.fp8_linear(codes, host(weights.cross_kv.codes), sc["cross"][0],
-                                  host(weights.cross_kv.scales), host(weights.cross_kv.bias))
-    want_states = _f16(y)
-    rel = np.linalg.norm(got_states - want_states) / np.linalg.norm(want_states)
-    want_kv = _f16(kv_ref).reshape(streams, t, 2 * config.decoder_layers, config.heads, 64).transpose(2, 0, 3, 1, 4)
-    rel_kv = np.linalg.norm(got_kv - want_kv) / np.linalg.norm(want_kv)
-    print(f"end to end: states rel-RMS {rel:.2e}, cross k/v rel-RMS {rel_kv:.2e}, "
-          f"states max_abs {np.abs(got_states - want_states).max():.3g}")
-    # Per-stage rounding (about an fp16 ulp, occasionally one E4M3 step of a code)
-    # compounds over the stages; it stays far below the FP8 quantization noise itself.
-    assert rel < 1e-2 and rel_kv < 1e-2
+    want_states, want_kv = _oracle_forward(ck, weights, e.scales, mel, config, oracle)
+    floor_states, floor_kv = _oracle_forward(ck, weights, e.scales, mel, config, oracle, perturb=1)
+    rel = lambda a, b: float(np.linalg.norm(a - b) / np.linalg.norm(b))
+    r_states, r_kv = rel(got_states, want_states), rel(got_kv, want_kv)
+    f_states, f_kv = rel(floor_states, want_states), rel(floor_kv, want_kv)
+    print(f"end to end: states rel-RMS {r_states:.2e} (oracle one-ulp floor {f_states:.2e}), "
+          f"cross k/v {r_kv:.2e} (floor {f_kv:.2e}), states max_abs {np.abs(got_states - want_states).max():.3g}")
+    assert r_states <= 4 * f_states and r_kv <= 4 * f_kv
 
 
 def test_encoder_stream_slices_are_bit_identical(small_encoder, enc, native, cuda):
