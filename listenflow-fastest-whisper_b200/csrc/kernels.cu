@@ -2129,20 +2129,25 @@ constexpr float kLog2e = 1.4426950408889634f;
 } // namespace sattn
 
 // ---------------------------------------------------------------------------
-// Encoder self-attention on tcgen05: the same two-pass exact softmax and fp16
-// edges as the oracle (q' = half(q c), k' = half(k c), s = half(q'.k'),
-// p = half(exp(s - max) / sum), out = half(sum p v)), per (stream, head,
-// 128-query block):
-//   warp 0: TMA producer (Q once; K tiles twice -- once per pass; V in pass 2);
+// Encoder self-attention on tcgen05 with the graph's fp16 edges (q' = half(q c),
+// k' = half(k c), s = half(q'.k'), out = half(sum_j p_j v_j)) and a one-pass
+// (online) softmax, per (stream, head, 128-query block):
+//   warp 0: TMA producer (Q once per item; K and V tiles once each);
 //   warp 1: MMA issuer.  S = Q' K'^T, kind::f16 128 x 128 x 16, into one of two
 //           TMEM score buffers; O += P V, 128 x 64 x 16 with V read MN-major
 //           straight from its TMA tile, into a third TMEM region;
 //   warps 2-5: rescale Q and each K tile in shared memory (half(x c)) before
 //           the MMA reads it, a quarter of the tile each;
 //   warps 6-21: softmax, kSplit warps per TMEM lane quarter, each over kCols of
-//           a tile's 128 key columns.  Pass 1 keeps a running max and sum per
-//           part of a row (merged once through shared memory); pass 2 writes P
-//           as fp16 into a K-major 128B-swizzled tile for the P.V MMA.
+//           a tile's 128 key columns.  Per tile the four warps of a lane quarter
+//           exchange their part maxima through shared memory; each row keeps a
+//           running maximum m that is raised only when a tile's maximum exceeds
+//           it by more than 2^8 in exp (then O and the row sum are rescaled in
+//           place).  P = half(exp(s - m)) goes as fp16 into a K-major 128B-swizzled
+//           tile for the P.V MMA, and out = half(O / sum) at the end.
+// Against the graph's p = half(exp(s - max) / sum) the probabilities round once
+// each at another scale: the output moves by at most 2^-10 sum_j p_j |v_j| (first
+// order), which the tests add to the fp16 bound.
 // The P.V MMAs of tile c - 1 are issued after the score MMAs of tile c, so the
 // softmax of one tile overlaps the MMAs of the next.  The kernel is persistent:
 // one CTA per SM walks (stream, head, query block) items, its rings and
@@ -2171,7 +2176,11 @@ constexpr int kThreads = (kSoftWarp0 + kSoftWarps) * 32;
 constexpr int kOffK = 2 * kTile; // Q double-buffered by item parity
 constexpr int kOffV = kOffK + kKStages * kTile;
 constexpr int kOffP = kOffV + kVStages * kTile;
-constexpr int kOffStats = kOffP + 2 * kPBytes; // [2 by item parity] float m[kSplit][kBQ], l[kSplit][kBQ]
+constexpr int kOffStats = kOffP + 2 * kPBytes; // float tile maxima [2][kSplit][kBQ], row sums [2][kSplit][kBQ]
+constexpr int kOutCols = kDim / kSplit;        // O columns per softmax warp
+// The running maximum is raised only when a tile's maximum exceeds it by more than
+// 2^kLazy in exp: P = exp(s - m) then stays below 2^kLazy, exact in fp16 range.
+constexpr float kLazy = 8.0f;
 constexpr int kOffBar = kOffStats + 2 * 2 * kSplit * kBQ * 4;
 constexpr int kBars = 4 + 3 * kKStages + 2 * kVStages + 8 + 5;
 constexpr int kSmemBytes = kOffBar + 8 * kBars + 16 + 1024;
@@ -2313,25 +2322,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive_expect_tx(q_full + 8 * qb, kTile);
                 tma_load_2d(sQ + qb * kTile, &tm_q, q_full + 8 * qb, w.head * kDim, w.row_base + w.q0);
                 ++q_issued;
-                for (int j = 0; j < 2 * nt; ++j) {
+                for (int j = 0; j < nt; ++j) {
                     const int s = k_issued % kKStages;
                     if (!mbar_wait(k_empty + 8 * s, ((k_issued / kKStages) & 1u) ^ 1u, kSiteProducerEmpty)) {
                         ok = false;
                         break;
                     }
                     mbar_arrive_expect_tx(k_full + 8 * s, kTile);
-                    tma_load_2d(sK + s * kTile, &tm_k, k_full + 8 * s, w.head * kDim, w.row_base + (j % nt) * kBK);
+                    tma_load_2d(sK + s * kTile, &tm_k, k_full + 8 * s, w.head * kDim, w.row_base + j * kBK);
                     ++k_issued;
-                    if (j >= nt) {
-                        const int vs = v_issued % kVStages;
-                        if (!mbar_wait(v_empty + 8 * vs, ((v_issued / kVStages) & 1u) ^ 1u, kSiteProducerEmpty)) {
-                            ok = false;
-                            break;
-                        }
-                        mbar_arrive_expect_tx(v_full + 8 * vs, kTile);
-                        tma_load_2d(sV + vs * kTile, &tm_v, v_full + 8 * vs, w.head * kDim, w.row_base + (j - nt) * kBK);
-                        ++v_issued;
+                    const int vs = v_issued % kVStages;
+                    if (!mbar_wait(v_empty + 8 * vs, ((v_issued / kVStages) & 1u) ^ 1u, kSiteProducerEmpty)) {
+                        ok = false;
+                        break;
                     }
+                    mbar_arrive_expect_tx(v_full + 8 * vs, kTile);
+                    tma_load_2d(sV + vs * kTile, &tm_v, v_full + 8 * vs, w.head * kDim, w.row_base + j * kBK);
+                    ++v_issued;
                 }
             }
             // Loads still in flight (only after an abandoned wait) land before exit.
@@ -2387,8 +2394,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t qb = local & 1;
                 sQi = sQ + qb * kTile;
                 ok = ok && mbar_wait(q_ready + 8 * qb, (local >> 1) & 1u, kSiteMmaFull);
-                for (int c = 0; c < nt; ++c)
-                    score_mma(u_all++);
                 for (int c = 0; c < nt; ++c) {
                     score_mma(u_all++);
                     if (c == nt - 1 && ok)
@@ -2438,7 +2443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             scale_tile(sQ + qb * kTile);
             if (lane == 0)
                 mbar_arrive(q_ready + 8 * qb);
-            for (int j = 0; ok && j < 2 * nt; ++j, ++k_scaled) {
+            for (int j = 0; ok && j < nt; ++j, ++k_scaled) {
                 const int s = k_scaled % kKStages;
                 ok = __all_sync(0xffffffffu, mbar_wait(k_full + 8 * s, (k_scaled / kKStages) & 1u, kSiteMmaFull));
                 if (!ok)
@@ -2451,12 +2456,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ---------------- softmax: (lane quarter, column part) per warp ----------------
         // Every softmax warp walks every tile, even after a wait has given up
-        // (waits then return at once), so the named barrier always matches.
+        // (waits then return at once), so the named barriers always match.
         const int quarter = warp & 3;
         const int part = (warp - kSoftWarp0) >> 2; // which kCols columns of a tile
         const int col0 = part * kCols;
         const int row = quarter * 32 + lane;
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + col0;
+        const uint32_t o_base = tmem + kTmemO + (static_cast<uint32_t>(quarter * 32) << 16) + part * kOutCols;
+        float *tile_max = stats;                    // [tile parity][part][row]
+        float *part_sum = stats + 2 * kSplit * kBQ; // [item parity][part][row]
         bool ok = true;
         // Every lane polls the barrier (one shared word, the same answer for all
         // lanes), so no broadcast is needed; the warp reconverges before the
@@ -2496,15 +2504,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         int u_all = 0, c_all = 0; // score tiles and P tiles consumed over all items
         for (int it = blockIdx.x, local = 0; it < items; it += gridDim.x, ++local) {
         const Item w = item_of(it);
-        // ---- pass 1: running max and sum of exp over this part of the row ----
-        // The scores stay packed fp16 pairs: the tile maximum is a packed max, and
-        // s - max is one mixed-precision add per score (f16 operand, f32 result),
-        // so no score goes through a conversion back to fp32.  Eight independent
-        // partial chains per tile keep the dependency chains short.
-        float m = -INFINITY, l = 0.0f;
+        float m = -INFINITY; // the row's running maximum (the same in all parts)
+        float l = 0.0f;      // this part's sum of exp(s - m)
         for (int c = 0; c < nt; ++c) {
+            const int u = u_all++;
             uint32_t h[kCols / 2];
-            load_scores(u_all++, c, h);
+            load_scores(u, c, h);
+            // Tile maximum: packed fp16 maxima over this part, then over the parts.
             uint32_t pm[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j)
@@ -2513,60 +2519,60 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 4; i < kCols / 2; ++i)
                 pm[i & 3] = max_f16x2(pm[i & 3], h[i]);
             const uint32_t m2 = max_f16x2(max_f16x2(pm[0], pm[1]), max_f16x2(pm[2], pm[3]));
-            const float bm = fmaxf(h2f(static_cast<uint16_t>(m2 & 0xFFFFu)), h2f(static_cast<uint16_t>(m2 >> 16)));
-            if (bm != -INFINITY) {
-                const float mn = fmaxf(m, bm);
-                // ps[j] holds the partial sums 2j (low) and 2j + 1 (high)
-                uint64_t ps[4] = {0, 0, 0, 0};
-                const uint64_t log2e2 = f2_bits(kLog2e, kLog2e);
+            float *xm = tile_max + (u & 1) * (kSplit * kBQ);
+            xm[part * kBQ + row] =
+                fmaxf(h2f(static_cast<uint16_t>(m2 & 0xFFFFu)), h2f(static_cast<uint16_t>(m2 >> 16)));
+            named_barrier_sync(3 + quarter, kSplit * 32);
+            float tm = xm[row];
 #pragma unroll
-                for (int i = 0; i < kCols / 2; ++i) {
-                    float d0, d1;
-                    sub_f16x2_f32(h[i], mn, d0, d1);
-                    const uint64_t x = mul_f32x2(f2_bits(d0, d1), log2e2);
-                    ps[i & 3] = add_f32x2(ps[i & 3], f2_bits(fast_exp2(lo_f32(x)), fast_exp2(hi_f32(x))));
-                }
-                const float add = ((lo_f32(ps[0]) + hi_f32(ps[0])) + (lo_f32(ps[1]) + hi_f32(ps[1]))) +
-                                  ((lo_f32(ps[2]) + hi_f32(ps[2])) + (lo_f32(ps[3]) + hi_f32(ps[3])));
-                l = (m == -INFINITY ? 0.0f : l * fast_exp2((m - mn) * kLog2e)) + add;
-                m = mn;
+            for (int j = 1; j < kSplit; ++j)
+                tm = fmaxf(tm, xm[j * kBQ + row]);
+            // Raise the running maximum on the first tile, or when the tile's
+            // maximum exceeds it by more than 2^kLazy in exp; alpha rescales what
+            // was summed (and accumulated in O) against the old maximum.
+            float alpha = 1.0f;
+            bool raised = false;
+            if (m == -INFINITY || (tm - m) * kLog2e > kLazy) {
+                raised = m != -INFINITY;
+                alpha = raised ? fast_exp2((m - tm) * kLog2e) : 0.0f;
+                l *= alpha;
+                m = tm;
             }
-        }
-        // ---- merge the parts of each row (in part order) ----
-        // Stats alternate by item parity: a warp overwrites this item's buffer two
-        // items later, after every warp has read it and passed the next barrier.
-        float *stat_m = stats + (local & 1) * (2 * kSplit * kBQ);
-        float *stat_l = stat_m + kSplit * kBQ;
-        stat_m[part * kBQ + row] = m;
-        stat_l[part * kBQ + row] = l;
-        named_barrier_sync(2, kSoftWarps * 32);
-        float mm = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < kSplit; ++j)
-            mm = fmaxf(mm, stat_m[j * kBQ + row]);
-        float ll = 0.0f;
-#pragma unroll
-        for (int j = 0; j < kSplit; ++j) {
-            const float mj = stat_m[j * kBQ + row];
-            ll += mj == -INFINITY ? 0.0f : stat_l[j * kBQ + row] * fast_exp2((mj - mm) * kLog2e);
-        }
-        // p = exp(s - max) / sum = 2^((s - max) log2(e) - log2(sum))
-        const float lg = fast_log2(ll);
-        // ---- pass 2: P = half(p) into the K-major swizzled P tile ----
-        for (int c = 0; c < nt; ++c) {
-            uint32_t h[kCols / 2];
-            load_scores(u_all++, c, h);
+            // P = half(exp(s - m)) with packed fp32 pairs; the row sum takes the
+            // unrounded exponentials (four partial pairs keep the chains short).
             uint32_t pk[kCols / 2];
-            const uint64_t log2e2 = f2_bits(kLog2e, kLog2e), neg_lg2 = f2_bits(-lg, -lg);
+            uint64_t ps[4] = {0, 0, 0, 0};
+            const uint64_t log2e2 = f2_bits(kLog2e, kLog2e);
 #pragma unroll
             for (int i = 0; i < kCols / 2; ++i) {
                 float d0, d1;
-                sub_f16x2_f32(h[i], mm, d0, d1);
-                const uint64_t x = fma_f32x2(f2_bits(d0, d1), log2e2, neg_lg2);
-                pk[i] = gemm::cvt_f16x2(fast_exp2(lo_f32(x)), fast_exp2(hi_f32(x)));
+                sub_f16x2_f32(h[i], m, d0, d1);
+                const uint64_t x = mul_f32x2(f2_bits(d0, d1), log2e2);
+                const float e0 = fast_exp2(lo_f32(x)), e1 = fast_exp2(hi_f32(x));
+                ps[i & 3] = add_f32x2(ps[i & 3], f2_bits(e0, e1));
+                pk[i] = gemm::cvt_f16x2(e0, e1);
             }
+            l += ((lo_f32(ps[0]) + hi_f32(ps[0])) + (lo_f32(ps[1]) + hi_f32(ps[1]))) +
+                 ((lo_f32(ps[2]) + hi_f32(ps[2])) + (lo_f32(ps[3]) + hi_f32(ps[3])));
             const uint32_t pb = c_all & 1;
             wait_all(p_empty + 8 * pb, ((c_all >> 1) & 1u) ^ 1u, kSiteProducerEmpty);
+            if (c > 0 && __any_sync(0xffffffffu, raised)) {
+                // O holds this item's P.V of tiles 0 .. c - 1 against the old maximum:
+                // once the last of those MMAs is done, scale this warp's columns of
+                // the raised rows (the other rows by 1: the TMEM access is warp-wide).
+                wait_all(p_empty + 8 * (pb ^ 1u), ((c_all - 1) >> 1) & 1u, kSiteProducerEmpty);
+                tc_fence_after();
+                uint32_t o[kOutCols];
+                tmem_ld_32x32b_x16(o_base, o);
+                tmem_wait_ld();
+                const float f = raised ? alpha : 1.0f;
+#pragma unroll
+                for (int i = 0; i < kOutCols; ++i)
+                    o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+                tmem_st_32x32b_x16(o_base, o);
+                tmem_wait_st();
+                tc_fence_before();
+            }
             // columns col0 .. col0 + kCols - 1 sit in 64-key half col0 / 64, 16-byte chunks from (col0 % 64) / 8
             const uint32_t prow = sP + pb * kPBytes + (col0 / 64) * (kPBytes / 2) + row * 128;
 #pragma unroll
@@ -2582,18 +2588,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive(p_full + 8 * pb);
             ++c_all;
         }
-        // ---- epilogue: out = half(O), this warp's kOutCols of the 64 dims ----
-        constexpr int kOutCols = kDim / kSplit;
+        // ---- the row sum over the parts (one running maximum for all of them) ----
+        // Sums alternate by item parity: a warp overwrites this item's buffer two
+        // items later, after every warp has read it and passed the next barrier.
+        float *sum = part_sum + (local & 1) * (kSplit * kBQ);
+        sum[part * kBQ + row] = l;
+        named_barrier_sync(2, kSoftWarps * 32);
+        float ll = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kSplit; ++j)
+            ll += sum[j * kBQ + row];
+        const float inv = __frcp_rn(ll);
+        // ---- epilogue: out = half(O / sum), this warp's kOutCols of the 64 dims ----
         wait_all(o_full, local & 1u, kSiteEpilogueAccFull);
         tc_fence_after();
         uint32_t o[kOutCols];
-        static_assert(kOutCols == 16 || kOutCols == 32, "output columns per softmax warp");
-        if constexpr (kOutCols == 32)
-            tmem_ld_32x32b_x32(tmem + kTmemO + (static_cast<uint32_t>(quarter * 32) << 16) + part * kOutCols,
-                               *reinterpret_cast<uint32_t(*)[32]>(o));
-        else
-            tmem_ld_32x32b_x16(tmem + kTmemO + (static_cast<uint32_t>(quarter * 32) << 16) + part * kOutCols,
-                               *reinterpret_cast<uint32_t(*)[16]>(o));
+        static_assert(kOutCols == 16, "output columns per softmax warp");
+        tmem_ld_32x32b_x16(o_base, o);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
@@ -2606,9 +2617,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t neg_scale2 = f2_bits(-scale, -scale), recip2 = f2_bits(recip, recip);
             const size_t idx = static_cast<size_t>(w.row_base + token) * (p.heads * kDim) + w.head * kDim + part * kOutCols;
             uint32_t h[kOutCols / 2];
+            const uint64_t inv2 = f2_bits(inv, inv);
 #pragma unroll
-            for (int i = 0; i < kOutCols / 2; ++i)
-                h[i] = gemm::cvt_f16x2(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1]));
+            for (int i = 0; i < kOutCols / 2; ++i) {
+                const uint64_t y = mul_f32x2(f2_bits(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1])), inv2);
+                h[i] = gemm::cvt_f16x2(lo_f32(y), hi_f32(y));
+            }
             if (p.out) {
                 uint4 *dst = reinterpret_cast<uint4 *>(p.out + idx);
 #pragma unroll

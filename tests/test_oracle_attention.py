@@ -105,3 +105,57 @@ def test_score_flip_slack_bounds_one_ulp_score_changes():
     assert change.max() > 0
     # first order in ulp(s) <= 2^-8 for these scores; allow 10% for the second order
     assert np.all(change <= 1.1 * slack + 1e-12), float((change / (slack + 1e-30)).max())
+
+
+def _one_pass_model(s16, v, tile=128, lazy=8.0):
+    """The self-attention kernel's one-pass softmax in exact arithmetic: per tile of
+    `tile` keys the running maximum m is raised (first tile, or when the tile's
+    maximum exceeds it by more than 2^lazy in exp) and what was summed is rescaled;
+    P = half(exp(s - m)) feeds P.V, the row sum takes the unrounded exponentials,
+    and out = half(O / sum)."""
+    s = s16.astype(np.float64)
+    rows, keys = s.shape
+    out = np.zeros((rows, v.shape[1]))
+    for r in range(rows):
+        m, l, o = -np.inf, 0.0, np.zeros(v.shape[1])
+        for c0 in range(0, keys, tile):
+            blk = s[r, c0:c0 + tile]
+            tm = blk.max()
+            if m == -np.inf or (tm - m) * np.log2(np.e) > lazy:
+                alpha = 0.0 if m == -np.inf else np.exp(m - tm)
+                l, o, m = l * alpha, o * alpha, tm
+            e = np.exp(blk - m)
+            l += e.sum()
+            o += e.astype(np.float16).astype(np.float64) @ v[c0:c0 + tile]
+        out[r] = o / l
+    return out.astype(np.float16).astype(np.float64)
+
+
+@pytest.mark.parametrize("std,tokens", [(1.0, 300), (2.0, 300), (3.0, 260), (6.0, 200)])
+def test_one_pass_softmax_within_slack(oracle, std, tokens):
+    """The self-attention GPU test allows the one-pass softmax's probability rounding
+    (2^-10 sum_j p_j |v_j| + 2^-25 sum_j |v_j|, _score_flip_slack(one_pass=True)) on
+    top of the fixed bound.  Check that term on the CPU: the exact model of the
+    kernel's arithmetic (_one_pass_model) stays within the fixed bound plus that term
+    of the oracle's exact two-pass output, on score scales from mild to peaked (std 6
+    raises the running maximum mid-row, exercising the rescale)."""
+    from test_gpu_attention import ATOL, RTOL, _score_flip_slack
+
+    streams, heads, d = 1, 2, 64
+    rng = np.random.default_rng(int(std * 100) + tokens)
+    qkv = halves(rng, (streams * tokens, 3 * heads * d), std=std)
+    want, _ = oracle.self_attention(qkv, streams, heads)
+    ref = want.view(np.float16).astype(np.float64)
+    c = float(np.float16(d ** -0.25))
+    x = qkv.astype(np.float64)
+    got = np.zeros_like(ref)
+    for h in range(heads):
+        q = (x[:, h * d:(h + 1) * d] * c).astype(np.float16).astype(np.float64)
+        k = (x[:, (heads + h) * d:(heads + h + 1) * d] * c).astype(np.float16).astype(np.float64)
+        v = x[:, (2 * heads + h) * d:(2 * heads + h + 1) * d]
+        got[:, h * d:(h + 1) * d] = _one_pass_model((q @ k.T).astype(np.float16), v)
+    full = _score_flip_slack(qkv, streams, heads, ref, one_pass=True)
+    flips = _score_flip_slack(qkv, streams, heads, ref)
+    err = np.abs(got - ref)
+    assert err.max() > 0
+    assert np.all(err <= ATOL + RTOL * np.abs(ref) + (full - flips))
