@@ -93,6 +93,10 @@ def parse_args(argv=None):
                         "LayerNorm producer, 'attention' the cross-attention, 'self_attention' the encoder "
                         "self-attention, 'decoder' the C3 step")
     p.add_argument("--layers", type=int, default=32, help="encoder layers (32 is the measured configuration)")
+    p.add_argument("--profile-window", action="store_true",
+                   help="after the warm-up, run one encoder forward (plain launches, no graph) between "
+                        "cudaProfilerStart and cudaProfilerStop and exit: the window that "
+                        "`ncu --profile-from-start off` captures")
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="target CPU-baseline sample time (0 skips the CPU baseline, for profiling runs)")
     return p.parse_args(argv)
@@ -862,6 +866,15 @@ def run_c4(args, rank, local_rank, world):
     torch.cuda.synchronize()
     if native.device_error() != 0:
         raise RuntimeError("device-side wait timed out during the encoder warm-up")
+    if args.profile_window:
+        torch.cuda.profiler.start()
+        e.run(stream)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        if dist is not None:
+            dist.destroy_process_group()
+        return ({"profile_window": f"one encoder forward, {streams} streams, {launches_per_forward} launches",
+                 "device_error": native.device_error()} if rank == 0 else None), device
 
     # Timed: K graph replays.  The forward's working set (weights 0.6 GB, activations
     # and cross K/V ~0.3 GB per stream) is far larger than L2, so no flush is needed.
