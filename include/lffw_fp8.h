@@ -288,6 +288,65 @@ typedef struct lffw_fp8_linear_heads_args {
 LFFW_FP8_API lffw_status lffw_fp8_linear_heads(const lffw_fp8_linear_heads_args *args,
                                                void *stream) LFFW_FP8_NOEXCEPT;
 
+/* Decoder step pieces (network_graph.cpp:378-416).  `lengths` (device int32 per
+ * stream) is the number of keys in the stream's self-attention cache before the
+ * step, which is also the position of the step's token; lffw_greedy_select
+ * advances it.  Keeping it on the device lets one captured CUDA graph of a step
+ * serve every step of a greedy decode.
+ *
+ * lffw_decoder_embed: x[s] = half(token_table[tokens[s]] + position_table[lengths[s]])
+ * (the two gathers and the fp16 add of :380-388).  token_table fp16 [vocab, width],
+ * position_table fp16 [positions, width], x fp16 [streams, width].  A token or
+ * position outside its table leaves x[s] unwritten and sets decoder error 1
+ * (lffw_decoder_error).  Requirements: width % 8 == 0; 16-byte aligned pointers. */
+LFFW_FP8_API lffw_status lffw_decoder_embed(const int32_t *tokens, const int32_t *lengths,
+                                            const uint16_t *token_table, const uint16_t *position_table,
+                                            int32_t streams, int32_t width, int32_t vocab, int32_t positions,
+                                            uint16_t *x, void *stream) LFFW_FP8_NOEXCEPT;
+
+/* Decoder self-attention of one layer over its fp16 KV cache (network_graph.cpp:390-399:
+ * the cached keys and values concatenated with the step's own, `attend` with the
+ * graph's fp16 edges as in lffw_cross_attention; the reference's mask is zero for
+ * every cached position, so no mask is taken).  Per stream s and head h:
+ *   cache_k[s][h][lengths[s]] = k, cache_v[s][h][lengths[s]] = v   (the step's row of qkv)
+ *   out over keys 0 .. lengths[s] of the cache: q' = half(q c), k' = half(k c),
+ *   score = half(q'.k'), p = half(softmax_fp32(score)), out = half(sum_j p_j v_j)
+ * qkv: fp16 [streams, qkv_ld] holding q | k | v (heads * 64 columns each) of the
+ * step's fused QKV linear; cache_k, cache_v: fp16 [streams, heads, capacity, 64];
+ * out fp16 and/or out_codes E4M3 [streams, heads * 64].  A length >= capacity sets
+ * decoder error 2 and leaves that (stream, head) untouched.  Requirements: head_dim
+ * == 64; 1 <= capacity <= 512; qkv_ld >= 3 * heads * 64 and a multiple of 8;
+ * 16-byte aligned pointers; code_scale in [2^-125, 2^125] with out_codes. */
+typedef struct lffw_decoder_self_attention_args {
+    size_t struct_size; /* sizeof(lffw_decoder_self_attention_args) */
+    int32_t streams, heads, head_dim, capacity;
+    const uint16_t *qkv;
+    int64_t qkv_ld;
+    uint16_t *cache_k;
+    uint16_t *cache_v;
+    const int32_t *lengths;
+    uint16_t *out;
+    float code_scale;
+    uint8_t *out_codes;
+} lffw_decoder_self_attention_args;
+
+LFFW_FP8_API lffw_status lffw_decoder_self_attention(const lffw_decoder_self_attention_args *args,
+                                                     void *stream) LFFW_FP8_NOEXCEPT;
+
+/* Greedy token choice (network_graph.cpp:332-339 select_token): per stream,
+ * score[v] = fp32(logits[s][v]) + suppression[s][v] and tokens[s] = the smallest v
+ * whose score equals the maximum (vocab when every score is NaN); then, when
+ * `lengths` is not NULL, lengths[s] += 1.  logits fp16 [streams, logits_ld],
+ * suppression fp32 [streams, suppression_ld] (0 or -inf per token).
+ * Requirements: 1 <= vocab <= logits_ld, suppression_ld. */
+LFFW_FP8_API lffw_status lffw_greedy_select(const uint16_t *logits, int64_t logits_ld, const float *suppression,
+                                            int64_t suppression_ld, int32_t streams, int32_t vocab,
+                                            int32_t *tokens, int32_t *lengths, void *stream) LFFW_FP8_NOEXCEPT;
+
+/* Reads and clears the decoder kernels' error word: 0 none, 1 a token or position
+ * outside its table, 2 a full cache.  Synchronises with the device. */
+LFFW_FP8_API lffw_status lffw_decoder_error(int32_t *code) LFFW_FP8_NOEXCEPT;
+
 /* Q of an fp16 [rows, cols] weight with one scale per row (the per-output-channel
  * weight Q of network_graph.cpp:140-152, axis 2 of the transposed constant). */
 LFFW_FP8_API lffw_status lffw_fp8_quantize_rows(const uint16_t *w, int64_t rows, int64_t cols,

@@ -156,6 +156,24 @@ class HeadsLinearArgs(ctypes.Structure):
     ]
 
 
+class DecoderSelfAttentionArgs(ctypes.Structure):
+    _fields_ = [
+        ("struct_size", ctypes.c_size_t),
+        ("streams", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("capacity", ctypes.c_int32),
+        ("qkv", ctypes.c_void_p),
+        ("qkv_ld", ctypes.c_int64),
+        ("cache_k", ctypes.c_void_p),
+        ("cache_v", ctypes.c_void_p),
+        ("lengths", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("code_scale", ctypes.c_float),
+        ("out_codes", ctypes.c_void_p),
+    ]
+
+
 class PluginField(ctypes.Structure):
     _fields_ = [
         ("name", ctypes.c_char_p),
@@ -215,6 +233,10 @@ def library() -> ctypes.CDLL:
         "lffw_conv1d_weight_layout": ([_vp, _i32, _i32, _vp, _vp], _i32),
         "lffw_conv1d_gelu": ([ctypes.POINTER(Conv1dArgs), _vp], _i32),
         "lffw_fp8_linear_heads": ([ctypes.POINTER(HeadsLinearArgs), _vp], _i32),
+        "lffw_decoder_embed": ([_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp], _i32),
+        "lffw_decoder_self_attention": ([ctypes.POINTER(DecoderSelfAttentionArgs), _vp], _i32),
+        "lffw_greedy_select": ([_vp, _i64, _vp, _i64, _i32, _i32, _vp, _vp, _vp], _i32),
+        "lffw_decoder_error": ([ctypes.POINTER(_i32)], _i32),
         "lffw_chain_create": ([ctypes.POINTER(LinearArgs), _i32, ctypes.POINTER(_vp)], _i32),
         "lffw_chain_run": ([_vp, _vp], _i32),
         "lffw_chain_destroy": ([_vp], None),

@@ -409,6 +409,88 @@ lffw_status lffw_conv1d_gelu(const lffw_conv1d_args *a, void *stream) noexcept
     return from_cuda(lffw::launch_conv_gelu(L, static_cast<cudaStream_t>(stream)));
 }
 
+lffw_status lffw_decoder_embed(const int32_t *tokens, const int32_t *lengths, const uint16_t *token_table,
+                               const uint16_t *position_table, int32_t streams, int32_t width, int32_t vocab,
+                               int32_t positions, uint16_t *x, void *stream) noexcept
+{
+    if (tokens == nullptr || lengths == nullptr || token_table == nullptr || position_table == nullptr ||
+        x == nullptr || streams < 1 || streams > 65535 || width < 8 || width % 8 != 0 || vocab < 1 ||
+        positions < 1 || !aligned16(token_table) || !aligned16(position_table) || !aligned16(x))
+        return LFFW_INVALID_ARGUMENT;
+    lffw_status s = current_device_gate();
+    if (s != LFFW_SUCCESS)
+        return s;
+    return from_cuda(lffw::launch_decoder_embed(tokens, lengths, token_table, position_table, streams, width, vocab,
+                                                positions, x, static_cast<cudaStream_t>(stream)));
+}
+
+lffw_status lffw_decoder_self_attention(const lffw_decoder_self_attention_args *a, void *stream) noexcept
+{
+    if (a == nullptr || a->struct_size < sizeof(lffw_decoder_self_attention_args))
+        return a == nullptr ? LFFW_INVALID_ARGUMENT : LFFW_ABI_MISMATCH;
+    if (a->head_dim != 64 || a->streams < 1 || a->heads < 1 || a->capacity < 1 ||
+        a->capacity > lffw::kDecoderMaxCache)
+        return LFFW_INVALID_ARGUMENT;
+    const int64_t width = static_cast<int64_t>(a->heads) * 64;
+    if (static_cast<int64_t>(a->streams) * a->heads >= (int64_t(1) << 31) || width > kMaxDim ||
+        a->qkv_ld < 3 * width || a->qkv_ld % 8 != 0)
+        return LFFW_INVALID_ARGUMENT;
+    if (a->qkv == nullptr || a->cache_k == nullptr || a->cache_v == nullptr || a->lengths == nullptr ||
+        (a->out == nullptr && a->out_codes == nullptr))
+        return LFFW_INVALID_ARGUMENT;
+    if (!aligned16(a->qkv) || !aligned16(a->cache_k) || !aligned16(a->cache_v) || !aligned16(a->out) ||
+        !aligned16(a->out_codes) || (reinterpret_cast<uintptr_t>(a->lengths) & 3u) != 0)
+        return LFFW_INVALID_ARGUMENT;
+    if (a->out_codes != nullptr && !valid_scale(a->code_scale))
+        return LFFW_INVALID_ARGUMENT;
+    lffw_status s = current_device_gate();
+    if (s != LFFW_SUCCESS)
+        return s;
+    lffw::DecoderAttentionLaunch L{};
+    L.streams = a->streams;
+    L.heads = a->heads;
+    L.capacity = a->capacity;
+    L.qkv = a->qkv;
+    L.qkv_ld = a->qkv_ld;
+    L.cache_k = a->cache_k;
+    L.cache_v = a->cache_v;
+    L.lengths = a->lengths;
+    L.out = a->out;
+    L.codes = a->out_codes;
+    L.code_scale = a->code_scale;
+    return from_cuda(lffw::launch_decoder_self_attention(L, static_cast<cudaStream_t>(stream)));
+}
+
+lffw_status lffw_greedy_select(const uint16_t *logits, int64_t logits_ld, const float *suppression,
+                               int64_t suppression_ld, int32_t streams, int32_t vocab, int32_t *tokens,
+                               int32_t *lengths, void *stream) noexcept
+{
+    if (logits == nullptr || suppression == nullptr || tokens == nullptr || streams < 1 || streams > 65535 ||
+        vocab < 1 || logits_ld < vocab || suppression_ld < vocab)
+        return LFFW_INVALID_ARGUMENT;
+    if ((reinterpret_cast<uintptr_t>(logits) & 1u) != 0 || (reinterpret_cast<uintptr_t>(suppression) & 3u) != 0 ||
+        (reinterpret_cast<uintptr_t>(tokens) & 3u) != 0 || (reinterpret_cast<uintptr_t>(lengths) & 3u) != 0)
+        return LFFW_INVALID_ARGUMENT;
+    lffw_status s = current_device_gate();
+    if (s != LFFW_SUCCESS)
+        return s;
+    return from_cuda(lffw::launch_greedy_select(logits, logits_ld, suppression, suppression_ld, streams, vocab, tokens,
+                                                lengths, static_cast<cudaStream_t>(stream)));
+}
+
+lffw_status lffw_decoder_error(int32_t *code) noexcept
+{
+    if (code == nullptr)
+        return LFFW_INVALID_ARGUMENT;
+    const int v = lffw::read_and_clear_decoder_error();
+    if (v < 0) {
+        cudaGetLastError();
+        return LFFW_CUDA_ERROR;
+    }
+    *code = v;
+    return LFFW_SUCCESS;
+}
+
 lffw_status lffw_fp8_linear_heads(const lffw_fp8_linear_heads_args *a, void *stream) noexcept
 {
     if (a == nullptr || a->struct_size < sizeof(lffw_fp8_linear_heads_args))

@@ -2778,6 +2778,259 @@ __global__ void __launch_bounds__(256)
 
 } // namespace front
 
+// ---------------------------------------------------------------------------
+// Decoder step pieces (network_graph.cpp:378-416): the token + position
+// embedding, self-attention over the fp16 KV cache with the step's own key and
+// value appended, and the greedy token choice.  Lengths (cached keys per stream,
+// which is also the new token's position) live in device memory, so one CUDA
+// graph of a step serves every step of a decode.
+
+namespace dec {
+
+// Sticky error word of the decoder kernels (1: token or position outside its
+// table, 2: cache full); read and cleared by read_and_clear_decoder_error.
+__device__ int g_decoder_error = 0;
+
+constexpr int kDim = 64;
+constexpr int kAttnThreads = 128;
+constexpr int kMaxCache = 512;                        // keys per (stream, head), the new one included
+constexpr int kKeysPerThread = kMaxCache / kAttnThreads;
+constexpr int kGroups = kAttnThreads / 16;            // P.V: 16 threads x 4 dims cover a row
+
+// x[s] = half(token_table[tokens[s]] + position_table[lengths[s]]), 8 halves per thread.
+__global__ void __launch_bounds__(256)
+    embed_kernel(const int32_t *__restrict__ tokens, const int32_t *__restrict__ lengths,
+                 const uint16_t *__restrict__ token_table, const uint16_t *__restrict__ position_table, int width,
+                 int vocab, int positions, uint16_t *__restrict__ x)
+{
+    griddepcontrol_wait(); // tokens and lengths come from the previous step
+    const int s = blockIdx.x;
+    const int tok = tokens[s], pos = lengths[s];
+    if (tok < 0 || tok >= vocab || pos < 0 || pos >= positions) {
+        if (threadIdx.x == 0)
+            atomicExch(&g_decoder_error, 1);
+        return;
+    }
+    const uint4 *a = reinterpret_cast<const uint4 *>(token_table + static_cast<size_t>(tok) * width);
+    const uint4 *b = reinterpret_cast<const uint4 *>(position_table + static_cast<size_t>(pos) * width);
+    uint4 *y = reinterpret_cast<uint4 *>(x + static_cast<size_t>(s) * width);
+    for (int i = threadIdx.x; i < width / 8; i += blockDim.x) {
+        const uint4 u = __ldg(a + i), v = __ldg(b + i);
+        y[i] = make_uint4(gemm::hadd2_rn(u.x, v.x), gemm::hadd2_rn(u.y, v.y), gemm::hadd2_rn(u.z, v.z),
+                          gemm::hadd2_rn(u.w, v.w));
+    }
+}
+
+struct AttnParams {
+    int heads, capacity;
+    const uint16_t *qkv;   // [streams, qkv_ld]: q | k | v columns of the step's QKV linear
+    int64_t qkv_ld;
+    uint16_t *cache_k;     // [streams, heads, capacity, 64]
+    uint16_t *cache_v;
+    const int32_t *lengths; // cached keys per stream before this step
+    uint32_t scale2;        // fp16 head_dim^-0.25 in both halves
+    uint16_t *out;          // [streams, heads * 64] or null
+    uint8_t *codes;         // [streams, heads * 64] or null
+    float code_scale, code_recip;
+};
+
+// One CTA per (stream, head): append the step's k and v at row `length` of the
+// cache, then attend q over rows 0 .. length with the graph's fp16 edges:
+// q' = half(q c), k' = half(k c), s = half(q'.k'), p = half(exp(s - max) / sum),
+// out = half(sum_j p_j v_j).  The scores stay in registers, so the exact
+// normalised p costs no second pass over K.
+__global__ void __launch_bounds__(kAttnThreads)
+    self_attention_kernel(const AttnParams p)
+{
+    __shared__ __align__(16) uint16_t q_s[kDim];
+    __shared__ float p_s[kMaxCache];
+    __shared__ float red[kAttnThreads / 32];
+    __shared__ __align__(16) float part[kGroups][kDim];
+    const int sh = blockIdx.x;
+    const int s = sh / p.heads, h = sh % p.heads;
+    const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
+    griddepcontrol_wait(); // the QKV linear and the previous step wrote what is read here
+    const int n0 = p.lengths[s];
+    if (n0 < 0 || n0 >= p.capacity) {
+        if (tid == 0)
+            atomicExch(&g_decoder_error, 2);
+        return;
+    }
+    const int n = n0 + 1;
+    const uint16_t *row = p.qkv + static_cast<size_t>(s) * p.qkv_ld;
+    const size_t base = (static_cast<size_t>(s) * p.heads + h) * p.capacity * kDim;
+    uint16_t *ck = p.cache_k + base;
+    uint16_t *cv = p.cache_v + base;
+    const int width = p.heads * kDim;
+    // the step's k and v rows -> cache row n0; q' -> shared memory
+    if (tid < 8) {
+        reinterpret_cast<uint4 *>(ck + static_cast<size_t>(n0) * kDim)[tid] =
+            reinterpret_cast<const uint4 *>(row + width + h * kDim)[tid];
+    } else if (tid < 16) {
+        reinterpret_cast<uint4 *>(cv + static_cast<size_t>(n0) * kDim)[tid - 8] =
+            reinterpret_cast<const uint4 *>(row + 2 * width + h * kDim)[tid - 8];
+    } else if (tid < 24) {
+        uint4 v = reinterpret_cast<const uint4 *>(row + h * kDim)[tid - 16];
+        v = make_uint4(gemm::hmul2_rn(v.x, p.scale2), gemm::hmul2_rn(v.y, p.scale2), gemm::hmul2_rn(v.z, p.scale2),
+                       gemm::hmul2_rn(v.w, p.scale2));
+        reinterpret_cast<uint4 *>(q_s)[tid - 16] = v;
+    }
+    __syncthreads(); // the appended rows and q' are visible to the whole block
+    uint32_t q2[kDim / 2];
+#pragma unroll
+    for (int i = 0; i < kDim / 8; ++i) {
+        const uint4 v = reinterpret_cast<const uint4 *>(q_s)[i];
+        q2[4 * i] = v.x;
+        q2[4 * i + 1] = v.y;
+        q2[4 * i + 2] = v.z;
+        q2[4 * i + 3] = v.w;
+    }
+    // scores: thread t takes keys t, t + 128, ...
+    float sc[kKeysPerThread];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < kKeysPerThread; ++r) {
+        const int j = tid + r * kAttnThreads;
+        sc[r] = -INFINITY;
+        if (j < n) {
+            const uint4 *kr = reinterpret_cast<const uint4 *>(ck + static_cast<size_t>(j) * kDim);
+            float acc = 0.0f;
+#pragma unroll
+            for (int i = 0; i < kDim / 8; ++i) {
+                const uint4 v = kr[i];
+                const uint32_t w[4] = {gemm::hmul2_rn(v.x, p.scale2), gemm::hmul2_rn(v.y, p.scale2),
+                                       gemm::hmul2_rn(v.z, p.scale2), gemm::hmul2_rn(v.w, p.scale2)};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const uint32_t a = q2[4 * i + e], b = w[e];
+                    acc = fmaf(h2f(static_cast<uint16_t>(a & 0xFFFFu)), h2f(static_cast<uint16_t>(b & 0xFFFFu)), acc);
+                    acc = fmaf(h2f(static_cast<uint16_t>(a >> 16)), h2f(static_cast<uint16_t>(b >> 16)), acc);
+                }
+            }
+            sc[r] = h2f(f2h_rn(acc)); // the MatMul's fp16 edge
+            mx = fmaxf(mx, sc[r]);
+        }
+    }
+    mx = attn::warp_max(mx);
+    if (lane == 0)
+        red[warp] = mx;
+    __syncthreads();
+    mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    __syncthreads();
+    float sum = 0.0f;
+#pragma unroll
+    for (int r = 0; r < kKeysPerThread; ++r) {
+        sc[r] = tid + r * kAttnThreads < n ? __expf(sc[r] - mx) : 0.0f;
+        sum += sc[r];
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off /= 2)
+        sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    if (lane == 0)
+        red[warp] = sum;
+    __syncthreads();
+    sum = (red[0] + red[1]) + (red[2] + red[3]);
+#pragma unroll
+    for (int r = 0; r < kKeysPerThread; ++r) {
+        const int j = tid + r * kAttnThreads;
+        if (j < n)
+            p_s[j] = h2f(f2h_rn(__fdiv_rn(sc[r], sum))); // p = half(softmax)
+    }
+    __syncthreads();
+    // P.V: thread t sums dims 4 (t % 16) .. + 3 over keys j = t / 16 (mod kGroups)
+    const int d0 = 4 * (tid % 16), g = tid / 16;
+    float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int j = g; j < n; j += kGroups) {
+        const uint2 v = *reinterpret_cast<const uint2 *>(cv + static_cast<size_t>(j) * kDim + d0);
+        const float pj = p_s[j];
+        o[0] = fmaf(pj, h2f(static_cast<uint16_t>(v.x & 0xFFFFu)), o[0]);
+        o[1] = fmaf(pj, h2f(static_cast<uint16_t>(v.x >> 16)), o[1]);
+        o[2] = fmaf(pj, h2f(static_cast<uint16_t>(v.y & 0xFFFFu)), o[2]);
+        o[3] = fmaf(pj, h2f(static_cast<uint16_t>(v.y >> 16)), o[3]);
+    }
+    *reinterpret_cast<float4 *>(&part[g][d0]) = make_float4(o[0], o[1], o[2], o[3]);
+    __syncthreads();
+    if (tid < kDim / 2) { // two output dims per thread, key groups summed in order
+        float a = 0.0f, b = 0.0f;
+#pragma unroll
+        for (int k = 0; k < kGroups; ++k) {
+            a += part[k][2 * tid];
+            b += part[k][2 * tid + 1];
+        }
+        const uint32_t h2 = gemm::cvt_f16x2(a, b);
+        const size_t idx = static_cast<size_t>(s) * width + h * kDim + 2 * tid;
+        if (p.out)
+            *reinterpret_cast<uint32_t *>(p.out + idx) = h2;
+        if (p.codes) {
+            const uint64_t neg_scale2 = f2_bits(-p.code_scale, -p.code_scale);
+            const uint64_t recip2 = f2_bits(p.code_recip, p.code_recip);
+            *reinterpret_cast<uint16_t *>(p.codes + idx) =
+                static_cast<uint16_t>(e4m3x2_quotient(h2, neg_scale2, recip2) & 0xFFFFu);
+        }
+    }
+}
+
+// Greedy choice per stream (network_graph.cpp:332-339 select_token):
+// score = fp32(logits) + suppression; token = the smallest index whose score
+// equals the maximum.  Then the stream's length grows by one (the step's key and
+// value are in the cache now).
+constexpr int kSelectThreads = 1024;
+__global__ void __launch_bounds__(kSelectThreads)
+    select_kernel(const uint16_t *__restrict__ logits, int64_t logits_ld, const float *__restrict__ suppression,
+                  int64_t suppression_ld, int vocab, int32_t *__restrict__ tokens, int32_t *__restrict__ lengths)
+{
+    __shared__ float best_v[kSelectThreads / 32];
+    __shared__ int best_i[kSelectThreads / 32];
+    griddepcontrol_wait();
+    const int s = blockIdx.x;
+    const uint16_t *row = logits + static_cast<size_t>(s) * logits_ld;
+    const float *sup = suppression + static_cast<size_t>(s) * suppression_ld;
+    float bv = -INFINITY;
+    int bi = vocab;
+    for (int i = threadIdx.x; i < vocab; i += kSelectThreads) {
+        const float v = h2f(row[i]) + sup[i];
+        if (v > bv) { // increasing i per thread: the first index of a tie stays
+            bv = v;
+            bi = i;
+        }
+    }
+    // (value, index) maximum with ties to the smaller index, over the warp then the block
+#pragma unroll
+    for (int off = 16; off > 0; off /= 2) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    if (threadIdx.x % 32 == 0) {
+        best_v[threadIdx.x / 32] = bv;
+        best_i[threadIdx.x / 32] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        bv = best_v[threadIdx.x];
+        bi = best_i[threadIdx.x];
+#pragma unroll
+        for (int off = 16; off > 0; off /= 2) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (threadIdx.x == 0) {
+            tokens[s] = bi < vocab ? bi : vocab; // vocab: every score was NaN (the graph's sentinel)
+            if (lengths)
+                lengths[s] += 1;
+        }
+    }
+}
+
+} // namespace dec
+
 namespace proj {
 
 } // namespace proj
@@ -3747,6 +4000,72 @@ cudaError_t launch_conv_weight_layout(const uint16_t *w, int64_t c_out, int64_t 
     front::conv_weight_layout_kernel<<<blocks, 256, 0, stream>>>(w, c_out, c_in, out);
     count_launch();
     return cudaGetLastError();
+}
+
+// Launches with programmatic stream serialisation: the kernel waits for the
+// previous grid (griddepcontrol.wait) before reading anything it wrote.
+template <class Kernel, class... Args>
+cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, cudaStream_t stream, Args... args)
+{
+    cudaLaunchConfig_t config{};
+    config.gridDim = grid;
+    config.blockDim = block;
+    config.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    config.attrs = attr;
+    config.numAttrs = 1;
+    const cudaError_t err = cudaLaunchKernelEx(&config, kernel, args...);
+    count_launch();
+    return err != cudaSuccess ? err : cudaGetLastError();
+}
+
+cudaError_t launch_decoder_embed(const int32_t *tokens, const int32_t *lengths, const uint16_t *token_table,
+                                 const uint16_t *position_table, int streams, int width, int vocab, int positions,
+                                 uint16_t *x, cudaStream_t stream)
+{
+    return launch_pdl(dec::embed_kernel, dim3(static_cast<unsigned>(streams)), dim3(256), stream, tokens, lengths,
+                      token_table, position_table, width, vocab, positions, x);
+}
+
+cudaError_t launch_decoder_self_attention(const DecoderAttentionLaunch &L, cudaStream_t stream)
+{
+    dec::AttnParams p{};
+    p.heads = L.heads;
+    p.capacity = L.capacity;
+    p.qkv = L.qkv;
+    p.qkv_ld = L.qkv_ld;
+    p.cache_k = L.cache_k;
+    p.cache_v = L.cache_v;
+    p.lengths = L.lengths;
+    const uint16_t c = __half_as_ushort(__float2half_rn(static_cast<float>(std::pow(64.0, -0.25))));
+    p.scale2 = static_cast<uint32_t>(c) * 0x10001u;
+    p.out = L.out;
+    p.codes = L.codes;
+    p.code_scale = L.code_scale;
+    p.code_recip = L.codes ? static_cast<float>(1.0 / static_cast<double>(L.code_scale)) : 0.0f;
+    return launch_pdl(dec::self_attention_kernel, dim3(static_cast<unsigned>(L.streams * L.heads)),
+                      dim3(dec::kAttnThreads), stream, p);
+}
+
+cudaError_t launch_greedy_select(const uint16_t *logits, int64_t logits_ld, const float *suppression,
+                                 int64_t suppression_ld, int streams, int vocab, int32_t *tokens, int32_t *lengths,
+                                 cudaStream_t stream)
+{
+    return launch_pdl(dec::select_kernel, dim3(static_cast<unsigned>(streams)), dim3(dec::kSelectThreads), stream,
+                      logits, logits_ld, suppression, suppression_ld, vocab, tokens, lengths);
+}
+
+int read_and_clear_decoder_error()
+{
+    int value = 0;
+    if (cudaMemcpyFromSymbol(&value, dec::g_decoder_error, sizeof(int)) != cudaSuccess)
+        return -1;
+    const int zero = 0;
+    if (value != 0 && cudaMemcpyToSymbol(dec::g_decoder_error, &zero, sizeof(int)) != cudaSuccess)
+        return -1;
+    return value;
 }
 
 cudaError_t launch_fp16_gelu(const uint16_t *x, uint16_t *y, int64_t count, cudaStream_t stream)

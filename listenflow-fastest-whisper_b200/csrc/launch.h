@@ -57,6 +57,31 @@ struct HeadsLinearLaunch {
 };
 cudaError_t launch_fp8_linear_heads(const HeadsLinearLaunch &p, cudaStream_t stream);
 
+// Decoder step: token + position embedding, self-attention over the KV cache
+// (appending the step's key and value), greedy selection.  `lengths` (device,
+// int32 per stream) is the number of cached keys, also the new token's position.
+constexpr int kDecoderMaxCache = 512;
+cudaError_t launch_decoder_embed(const int32_t *tokens, const int32_t *lengths, const uint16_t *token_table,
+                                 const uint16_t *position_table, int streams, int width, int vocab, int positions,
+                                 uint16_t *x, cudaStream_t stream);
+struct DecoderAttentionLaunch {
+    int streams, heads, capacity;
+    const uint16_t *qkv;
+    int64_t qkv_ld;
+    uint16_t *cache_k, *cache_v;
+    const int32_t *lengths;
+    uint16_t *out;
+    uint8_t *codes;
+    float code_scale;
+};
+cudaError_t launch_decoder_self_attention(const DecoderAttentionLaunch &p, cudaStream_t stream);
+cudaError_t launch_greedy_select(const uint16_t *logits, int64_t logits_ld, const float *suppression,
+                                 int64_t suppression_ld, int streams, int vocab, int32_t *tokens, int32_t *lengths,
+                                 cudaStream_t stream);
+// Reads and clears the decoder kernels' error word (1: token or position out of
+// its table, 2: cache full); -1 when it cannot be read.
+int read_and_clear_decoder_error();
+
 // Largest M served by the small-M (skinny) kernels.
 constexpr int64_t kSmallMaxRows = 32;
 

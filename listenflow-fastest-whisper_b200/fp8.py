@@ -275,6 +275,75 @@ def linear_heads(x_codes: torch.Tensor, w_codes: torch.Tensor, w_scales: torch.T
     return out
 
 
+def decoder_embed(tokens: torch.Tensor, lengths: torch.Tensor, token_table: torch.Tensor,
+                  position_table: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """x[s] = half(token_table[tokens[s]] + position_table[lengths[s]]) (network_graph.cpp:380-388)."""
+    _require(tokens, torch.int32, "tokens")
+    _require(lengths, torch.int32, "lengths")
+    _require(token_table, torch.float16, "token_table")
+    _require(position_table, torch.float16, "position_table")
+    streams = tokens.numel()
+    vocab, width = token_table.shape
+    if out is None:
+        out = torch.empty((streams, width), dtype=torch.float16, device=tokens.device)
+    native.check(native.library().lffw_decoder_embed(tokens.data_ptr(), lengths.data_ptr(), token_table.data_ptr(),
+                                                     position_table.data_ptr(), streams, width, vocab,
+                                                     position_table.shape[0], out.data_ptr(), _stream(stream)),
+                 "lffw_decoder_embed")
+    return out
+
+
+def decoder_self_attention(qkv: torch.Tensor, cache_k: torch.Tensor, cache_v: torch.Tensor, lengths: torch.Tensor,
+                           *, code_scale=None, want_out: bool = True, out: torch.Tensor | None = None,
+                           codes: torch.Tensor | None = None, stream=None):
+    """One decoder layer's self-attention over its KV cache [streams, heads, capacity, 64],
+    appending the step's k and v (rows of qkv [streams, >= 3 * heads * 64]) at row
+    lengths[s] first (network_graph.cpp:390-399).  Returns (out fp16 or None, codes or None)."""
+    _require(qkv, torch.float16, "qkv")
+    _require(cache_k, torch.float16, "cache_k")
+    _require(cache_v, torch.float16, "cache_v")
+    _require(lengths, torch.int32, "lengths")
+    streams, heads, capacity, dim = cache_k.shape
+    width = heads * dim
+    a = native.DecoderSelfAttentionArgs()
+    a.struct_size = ctypes.sizeof(a)
+    a.streams, a.heads, a.head_dim, a.capacity = streams, heads, dim, capacity
+    a.qkv, a.qkv_ld = qkv.data_ptr(), qkv.shape[1]
+    a.cache_k, a.cache_v, a.lengths = cache_k.data_ptr(), cache_v.data_ptr(), lengths.data_ptr()
+    if want_out and out is None:
+        out = torch.empty((streams, width), dtype=torch.float16, device=qkv.device)
+    if code_scale is not None and codes is None:
+        codes = torch.empty((streams, width), dtype=torch.uint8, device=qkv.device)
+    a.out = out.data_ptr() if want_out else None
+    a.code_scale = float(code_scale) if code_scale is not None else 0.0
+    a.out_codes = _ptr(codes) if code_scale is not None else None
+    native.check(native.library().lffw_decoder_self_attention(ctypes.byref(a), _stream(stream)),
+                 "lffw_decoder_self_attention")
+    return (out if want_out else None), (codes if code_scale is not None else None)
+
+
+def greedy_select(logits: torch.Tensor, suppression: torch.Tensor, tokens: torch.Tensor | None = None,
+                  lengths: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """tokens[s] = the first argmax of fp32(logits[s]) + suppression[s] (network_graph.cpp:332-339);
+    lengths[s] += 1 when lengths is given."""
+    _require(logits, torch.float16, "logits")
+    _require(suppression, torch.float32, "suppression")
+    streams, vocab = logits.shape
+    if tokens is None:
+        tokens = torch.empty(streams, dtype=torch.int32, device=logits.device)
+    native.check(native.library().lffw_greedy_select(logits.data_ptr(), vocab, suppression.data_ptr(),
+                                                     suppression.shape[1], streams, vocab, tokens.data_ptr(),
+                                                     _ptr(lengths), _stream(stream)), "lffw_greedy_select")
+    return tokens
+
+
+def decoder_error() -> int:
+    """Reads and clears the decoder kernels' error word (0 = none)."""
+    code = ctypes.c_int32(0)
+    native.check(native.library().lffw_decoder_error(ctypes.byref(code)), "lffw_decoder_error")
+    return int(code.value)
+
+
 def quantize_rows(w: torch.Tensor, scales: torch.Tensor, stream=None) -> torch.Tensor:
     """E4M3 codes of an fp16 [N, K] weight with one scale per row."""
     _require(w, torch.float16, "w")
