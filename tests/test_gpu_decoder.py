@@ -245,7 +245,8 @@ def test_decoder_step_stage_by_stage(small_decoder, dec, fp8, oracle, native, cu
             step("lffw_decoder_self_attention")
             n = step_no + 1
             kc, vc = host(d.cache_k[i])[:, :, :n].copy(), host(d.cache_v[i])[:, :, :n].copy()
-            np.testing.assert_array_equal(kc[:, :, step_no].reshape(STREAMS, -1), qkv[:, 1280:2560])
+            np.testing.assert_array_equal(kc[:, :, step_no].reshape(STREAMS, -1).view(np.uint16), qkv[:, 1280:2560])
+            np.testing.assert_array_equal(vc[:, :, step_no].reshape(STREAMS, -1).view(np.uint16), qkv[:, 2560:])
             out_ref, codes_ref = oracle.cross_attention(qkv[:, :1280].copy(), kc, vc, 1, code_scale=sc["self_out"][i])
             _codes_close(host(d.attn_codes), codes_ref, "self-attention codes", far=2)
             step("lffw_fp8_linear")
