@@ -86,7 +86,7 @@ def parse_args(argv=None):
                    help="timed replays of the C3 decoder-step graph (0 skips it)")
     p.add_argument("--decoder-layers", type=int, default=32,
                    help="decoder layers in the C3 step (32 is the measured configuration)")
-    p.add_argument("--only", choices=("all", "c4", "c2", "ln", "attention", "self_attention", "decoder"),
+    p.add_argument("--only", choices=("all", "c4", "c2", "c5", "ln", "attention", "self_attention", "decoder"),
                    default="all",
                    help="run one section alone and print its line (profiling): 'c4' the headline encoder "
                         "forward without the secondary sections, 'c2' the timed C2 linear-set steps, 'ln' the "
@@ -547,6 +547,9 @@ def run_section_only(args, local_rank):
     elif args.only == "c2":
         result = run_c2(args, device)
         result.update(metric="C2 encoder-layer FP8 linear set TFLOP/s")
+    elif args.only == "c5":
+        result = run_c5(device)
+        result.update(metric="C5 streaming transcription audio-s/s per GPU")
     else:
         result = run_self_attention(fp8, native, device, max(1, args.steps), seed=51)
         result.update(metric="encoder self-attention TFLOP/s")
@@ -1001,6 +1004,101 @@ def run_c4(args, rank, local_rank, world):
     return result, device
 
 
+# ---------------------------------------------------------------------------
+# C5: streaming transcription, one GPU's share of 128 streams over 8 GPUs.
+
+C5_STREAMS_PER_GPU = 16   # 128 streams / 8 GPUs
+C5_STEPS = 224            # greedy tokens per stream
+
+
+def run_c5(device, streams: int = C5_STREAMS_PER_GPU, steps: int = C5_STEPS, reps: int = 3):
+    """Encoder forward + greedy decoding of `steps` tokens for `streams` 30 s streams
+    (the per-GPU share of BASELINE config 5: 128 streams partitioned over 8 GPUs, no
+    collective), each as one CUDA graph: the encoder forward, then `steps` replays of
+    the decode-step graph (tokens and cache lengths stay on the device)."""
+    import torch
+
+    enc = importlib.import_module(PACKAGE + ".encoder")
+    dec = importlib.import_module(PACKAGE + ".decoder")
+    native = importlib.import_module(PACKAGE + "._native")
+    fp8 = importlib.import_module(PACKAGE + ".fp8")
+    config, dconf = enc.EncoderConfig(), dec.DecoderConfig()
+    mel = torch.from_numpy(mel_batch(list(range(streams)))).to(device)
+    ck = enc.synthetic_checkpoint(config, seed=C4_SEED, device=device)
+    dec.add_synthetic_decoder(ck, dconf, seed=C4_SEED + 1, device=device)
+    ew = enc.EncoderWeights.from_checkpoint(ck, config)
+    dw = dec.DecoderWeights.from_checkpoint(ck, dconf)
+    del ck
+    torch.cuda.empty_cache()
+    e = enc.Encoder(ew, enc.calibrate(ew, mel[:2].contiguous()), streams, device)
+    _, cross_kv = e.forward(mel)
+    torch.cuda.synchronize()
+    d = dec.Decoder(dw, dec.calibrate(dw, cross_kv, min(streams, 4), steps=8), cross_kv, streams)
+    d.suppression[:, dec.EOT + 1:] = -float("inf")  # special and timestamp tokens (synthetic suppression)
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        e.run(stream)
+        d.reset()
+        d.step(stream)
+    torch.cuda.synchronize()
+    enc_graph, step_graph = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(enc_graph, stream=stream):
+        e.run(stream)
+    with torch.cuda.graph(step_graph, stream=stream):
+        d.step(stream)
+
+    def transcribe():
+        enc_graph.replay()
+        d.reset()
+        for _ in range(steps):
+            step_graph.replay()
+
+    with torch.cuda.stream(stream):
+        transcribe()
+    torch.cuda.synchronize()
+    if native.device_error() != 0 or fp8.decoder_error() != 0:
+        raise RuntimeError("device-side error in the C5 warm-up")
+    totals, enc_ms = [], []
+    with torch.cuda.stream(stream):
+        for _ in range(reps):
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            ev[0].record(stream)
+            enc_graph.replay()
+            ev[1].record(stream)
+            d.reset()
+            for _ in range(steps):
+                step_graph.replay()
+            ev[2].record(stream)
+            torch.cuda.synchronize()
+            totals.append(ev[0].elapsed_time(ev[2]))
+            enc_ms.append(ev[0].elapsed_time(ev[1]))
+    if native.device_error() != 0 or fp8.decoder_error() != 0:
+        raise RuntimeError("device-side error in the C5 timed runs")
+    tokens = d.tokens.cpu().numpy()
+    ms, ems = statistics.median(totals), statistics.median(enc_ms)
+    step_ms = (ms - ems) / steps
+    cross_bytes = 2 * dconf.layers * streams * dconf.heads * dconf.audio_positions * 64 * 2
+    self_bytes = 2 * dconf.layers * streams * dconf.heads * 64 * 2 * (steps + 1) / 2  # mean cache length
+    step_bytes = dw.weight_bytes() + cross_bytes + self_bytes
+    hbm, _ = read_hbm_peak()
+    del enc_graph, step_graph
+    return {
+        "workload": f"C5 per-GPU share: {streams} streams (128 over 8 GPUs) x 30 s: log-mel (host, untimed), "
+                    f"encoder forward, greedy decoding of {steps} tokens per stream with an fp16 KV cache "
+                    f"(capacity {d.capacity}); random-init large-v3 weights; suppression of the special and "
+                    "timestamp tokens",
+        "ms_per_transcription": round(ms, 2), "encoder_ms": round(ems, 2), "decode_step_ms": round(step_ms, 4),
+        "value": round(streams * 30.0 / (ms / 1e3), 1), "unit": "audio-s/s per GPU",
+        "launches_per_step": d.launches,
+        "decode_step_bytes": int(step_bytes),
+        "decode_step_gbs": round(step_bytes / (step_ms / 1e3) / 1e9, 1),
+        "decode_step_frac_of_hbm": round(step_bytes / (step_ms / 1e3) / 1e9 / hbm, 4),
+        "bytes_note": "per step: decoder weights (E4M3 + scales + biases, fp16 logits table) + cross K/V of every "
+                      "stream and layer + the self-attention caches at their mean length",
+        "final_tokens_sample": [int(t) for t in tokens[:4]],
+    }
+
+
 def read_bf16_peak():
     try:
         return round(float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"]), 1)
@@ -1216,7 +1314,7 @@ def main(argv=None):
     rank, local_rank, world = dist_env()
     if args.impl == "reference":
         result = run_reference(args, rank, world)
-    elif args.only in ("decoder", "ln", "attention", "self_attention", "c2"):
+    elif args.only in ("decoder", "ln", "attention", "self_attention", "c2", "c5"):
         result = run_section_only(args, local_rank)
     else:
         result, device = run_c4(args, rank, local_rank, world)
@@ -1237,6 +1335,8 @@ def main(argv=None):
             if args.decoder_steps > 0:
                 result["decoder_step"] = run_decoder(fp8, native, device, args.decoder_steps, 3, seed=77,
                                                      layers_count=args.decoder_layers)
+            torch.cuda.empty_cache()
+            result["c5_transcription"] = run_c5(device)
             if args.cpu_seconds > 0:
                 result["cpu_baseline"] = cpu_baselines()
     if result is not None and rank == 0:
