@@ -86,7 +86,7 @@ def parse_args(argv=None):
                    help="timed replays of the C3 decoder-step graph (0 skips it)")
     p.add_argument("--decoder-layers", type=int, default=32,
                    help="decoder layers in the C3 step (32 is the measured configuration)")
-    p.add_argument("--only", choices=("all", "c4", "c2", "c5", "ln", "attention", "self_attention", "decoder"),
+    p.add_argument("--only", choices=("all", "c4", "c2", "c5", "fp16", "ln", "attention", "self_attention", "decoder"),
                    default="all",
                    help="run one section alone and print its line (profiling): 'c4' the headline encoder "
                         "forward without the secondary sections, 'c2' the timed C2 linear-set steps, 'ln' the "
@@ -550,6 +550,9 @@ def run_section_only(args, local_rank):
     elif args.only == "c5":
         result = run_c5(device)
         result.update(metric="C5 streaming transcription audio-s/s per GPU")
+    elif args.only == "fp16":
+        result = run_fp16_plugins(device)
+        result.update(metric="fp16 projection plugins GB/s, ours and the reference's kernels")
     else:
         result = run_self_attention(fp8, native, device, max(1, args.steps), seed=51)
         result.update(metric="encoder self-attention TFLOP/s")
@@ -1005,6 +1008,73 @@ def run_c4(args, rank, local_rank, world):
 
 
 # ---------------------------------------------------------------------------
+# The fp16 projection plugins (LffwFp16Fc1 / LffwFp16Qkv) beside the reference's
+# own kernels compiled for sm_100a on the same box (oracle/_ref).
+
+def run_fp16_plugins(device, reps: int = 10, layers: int = 32):
+    """Single-token fp16 projections streaming `layers` distinct weights back to back
+    (a decoder step's fc1 or qkv of every layer, so each launch reads its weight
+    from HBM): ours (lffw_fp16_fc1 / lffw_fp16_qkv) and the reference's cpp/kernels.cu
+    launched with its plugin geometry.  GB/s = weight bytes / time per launch."""
+    import torch
+
+    from oracle import oracle
+
+    fp8 = importlib.import_module(PACKAGE + ".fp8")
+    kernels = oracle.reference_kernels()
+    g = torch.Generator(device=device).manual_seed(91)
+    hbm, _ = read_hbm_peak()
+    result = {}
+    for name, rows in (("fc1", 5120), ("qkv", 3840)):
+        w = (torch.randn((layers, rows, 1280), generator=g, device=device) / 36).half()
+        b = (torch.randn((layers, rows if name == "fc1" else 1280), generator=g, device=device) * 0.1).half()
+        vb = (torch.randn((layers, 1280), generator=g, device=device) * 0.1).half()
+        x = torch.randn(1280, generator=g, device=device).half()
+        out = torch.empty(rows, dtype=torch.float16, device=device)
+        stream = torch.cuda.current_stream(device).cuda_stream
+
+        def ours():
+            for i in range(layers):
+                if name == "fc1":
+                    fp8.fp16_fc1(x.view(1, -1), w[i], b[i], out=out)
+                else:
+                    fp8.fp16_qkv(x.view(1, -1), w[i], b[i], vb[i], out=out)
+
+        def theirs():
+            qkv_launch, fc1_launch = kernels
+            for i in range(layers):
+                if name == "fc1":
+                    fc1_launch(x.data_ptr(), w[i].data_ptr(), b[i].data_ptr(), out.data_ptr(), stream)
+                else:
+                    qkv_launch(x.data_ptr(), w[i].data_ptr(), b[i].data_ptr(), vb[i].data_ptr(), out.data_ptr(), stream)
+
+        entry = {}
+        for label, fn in (("ours", ours), ("reference", theirs)):
+            if label == "reference" and kernels is None:
+                entry[label] = "unavailable: oracle/_ref/libref_fp16_kernels.so not built"
+                continue
+            fn()
+            torch.cuda.synchronize()
+            times = []
+            for _ in range(reps):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                fn()
+                e1.record()
+                torch.cuda.synchronize()
+                times.append(e0.elapsed_time(e1) / layers)
+            us = statistics.median(times) * 1e3
+            gbs = rows * 1280 * 2 / (us / 1e6) / 1e9
+            entry[label] = {"us_per_launch": round(us, 2), "gbs": round(gbs, 1), "frac_of_hbm": round(gbs / hbm, 4)}
+        result[name] = entry
+        del w, b, vb
+    result["workload"] = (f"single-token fp16 projections, {layers} distinct weights launched back to back "
+                          "(fc1 5120x1280 = 13.1 MB, qkv 3840x1280 = 9.8 MB per launch); reference = "
+                          "cpp/kernels.cu compiled for sm_100a, plugin geometry (128 threads, 4 rows per block)")
+    return result
+
+
+# ---------------------------------------------------------------------------
 # C5: streaming transcription, one GPU's share of 128 streams over 8 GPUs.
 
 C5_STREAMS_PER_GPU = 16   # 128 streams / 8 GPUs
@@ -1314,7 +1384,7 @@ def main(argv=None):
     rank, local_rank, world = dist_env()
     if args.impl == "reference":
         result = run_reference(args, rank, world)
-    elif args.only in ("decoder", "ln", "attention", "self_attention", "c2", "c5"):
+    elif args.only in ("decoder", "ln", "attention", "self_attention", "c2", "c5", "fp16"):
         result = run_section_only(args, local_rank)
     else:
         result, device = run_c4(args, rank, local_rank, world)
@@ -1337,6 +1407,7 @@ def main(argv=None):
                                                      layers_count=args.decoder_layers)
             torch.cuda.empty_cache()
             result["c5_transcription"] = run_c5(device)
+            result["fp16_plugins"] = run_fp16_plugins(device)
             if args.cpu_seconds > 0:
                 result["cpu_baseline"] = cpu_baselines()
     if result is not None and rank == 0:

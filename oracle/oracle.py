@@ -329,3 +329,23 @@ def reference_gelu(dot: float, bias: float) -> float:
     L.ref_gelu.argtypes = [ctypes.c_double, ctypes.c_double]
     L.ref_gelu.restype = ctypes.c_double
     return float(L.ref_gelu(dot, bias))
+
+
+# ---- the reference's own fp16 projection kernels (oracle/_ref, built for sm_100a
+# only where the reference tree is mounted): the same-box baseline ----------------
+
+REF_KERNELS = HERE / "_ref" / "libref_fp16_kernels.so"
+
+
+def reference_kernels():
+    """(qkv_launch, fc1_launch) ctypes functions launching cpp/kernels.cu's qkv_fp16 and
+    fc1_fp16 with the plugins' geometry, or None when oracle/_ref was not built."""
+    if not REF_KERNELS.exists():
+        return None
+    L = ctypes.CDLL(str(REF_KERNELS))
+    vp = ctypes.c_void_p
+    L.ref_qkv_fp16_launch.argtypes = [vp, vp, vp, vp, vp, vp]
+    L.ref_qkv_fp16_launch.restype = ctypes.c_int
+    L.ref_fc1_fp16_launch.argtypes = [vp, vp, vp, vp, vp]
+    L.ref_fc1_fp16_launch.restype = ctypes.c_int
+    return L.ref_qkv_fp16_launch, L.ref_fc1_fp16_launch

@@ -173,3 +173,39 @@ def test_fp8_linear_plugin_with_half_input(cuda, native, oracle, fp8):
         assert np.all(np.abs(got.astype(np.float64) - e) <= 2.0**-11 + 2.0**-9 * np.abs(e))
     finally:
         lib.lffw_plugin_destroy(plugin)
+
+
+@pytest.mark.parametrize("fc1", [True, False])
+def test_reference_kernels_on_this_box(cuda, fp8, oracle, fc1):
+    """The reference's own cpp/kernels.cu, compiled for sm_100a (oracle/_ref), on its
+    seeded test data beside ours: both within the reference's tolerance of its CPU
+    model, and within one fp16 ulp of each other (different fp32 summation orders)."""
+    import torch
+
+    kernels = oracle.reference_kernels()
+    if kernels is None:
+        pytest.skip("oracle/_ref not built (reference tree not mounted when building)")
+    qkv_launch, fc1_launch = kernels
+    x, w, b, vb, expected, keep = full_case(oracle, fc1)
+    t = lambda a: torch.from_numpy(a.view(np.float16).copy()).to(cuda)
+    xd, wd, bd = t(x), t(w), t(b)
+    rows = w.shape[0]
+    ref_out = torch.empty(rows, dtype=torch.float16, device=cuda)
+    stream = torch.cuda.current_stream().cuda_stream
+    if fc1:
+        assert fc1_launch(xd.data_ptr(), wd.data_ptr(), bd.data_ptr(), ref_out.data_ptr(), stream) == 0
+        ours = fp8.fp16_fc1(xd.view(1, -1), wd, bd)
+    else:
+        vbd = t(vb)
+        assert qkv_launch(xd.data_ptr(), wd.data_ptr(), bd.data_ptr(), vbd.data_ptr(), ref_out.data_ptr(), stream) == 0
+        ours = fp8.fp16_qkv(xd.view(1, -1), wd, bd, vbd)
+    torch.cuda.synchronize()
+    theirs = ref_out.cpu().numpy().view(np.uint16)
+    mine = ours.reshape(-1).cpu().numpy().view(np.uint16)
+    atol = 2.0**-11 if fc1 else 2.0**-12
+    check(theirs[:keep], expected, atol)
+    check(mine[:keep], expected, atol)
+    a, b2 = theirs.view(np.float16).astype(np.float64), mine.view(np.float16).astype(np.float64)
+    ulp = np.abs(np.spacing(np.maximum(np.abs(a), np.abs(b2)).astype(np.float16))).astype(np.float64)
+    print(f"{'fc1' if fc1 else 'qkv'}: identical to the reference kernel {np.mean(theirs == mine):.4f}")
+    assert np.all(np.abs(a - b2) <= 2 * ulp + 2.0**-24)
