@@ -2661,7 +2661,198 @@ namespace proj {
 
 constexpr int kThreads = 256;
 
-// One warp per output row; each lane streams 8 halves per 128-bit load.
+// Slab kernel geometry.  Each CTA owns a contiguous run of weight rows (one CTA
+// per SM for the plugins' shapes) and pulls the whole run into shared memory
+// with bulk copies at kernel start, so every byte of the weight is in flight
+// after one DRAM latency and the next launch's copies can start (programmatic
+// dependent launch) while this one finishes its sums.
+constexpr int kSlabThreads = 256;
+constexpr int kSlabMaxBytes = 96 * 1024; // weight rows per CTA
+constexpr int kSlabMaxWidth = 4096;      // DEPTH <= 4096: 128 values per lane
+constexpr int kSlabChunks = 16;          // one mbarrier per chunk of rows
+constexpr int kSlabSmemBytes = kSlabMaxBytes;
+
+// fp32 fma of two fp16 operands: RN(a*b + c) with the product exact (sm_100
+// mixed-precision fma), so fma16(a, b, -0) is the exact product, signed zero
+// included, and fma16(a, b, c) equals fadd(a*b, c) for any c.
+__device__ __forceinline__ float fma16(uint16_t a, uint16_t b, float c)
+{
+    float d;
+    asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(c));
+    return d;
+}
+
+__device__ __forceinline__ uint16_t half_of(const uint2 &v, int e)
+{
+    const uint32_t word = e < 2 ? v.x : v.y;
+    return static_cast<uint16_t>((e & 1) ? word >> 16 : word & 0xFFFFu);
+}
+
+// Two fp32 adds in one packed instruction: (a0 + b0, a1 + b1), each rounded
+// to nearest as a scalar add would be.
+__device__ __forceinline__ float2 add2(float2 a, float2 b)
+{
+    uint64_t d;
+    const uint64_t ua = (static_cast<uint64_t>(__float_as_uint(a.y)) << 32) | __float_as_uint(a.x);
+    const uint64_t ub = (static_cast<uint64_t>(__float_as_uint(b.y)) << 32) | __float_as_uint(b.x);
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(ua), "l"(ub));
+    return make_float2(__uint_as_float(static_cast<uint32_t>(d)), __uint_as_float(static_cast<uint32_t>(d >> 32)));
+}
+
+// x . w for one row in the reference plugins' summation order
+// (cpp/kernels.cu:27-49).  With DEPTH = max(128, the power of two >= width) and
+// V = DEPTH / 32, lane L holds the products for columns (i/4)*128 + 4L + i%4,
+// i < V, and +0 past the width.  The V values are folded by halving strides
+// (p[i] += p[i + s] for s = V/2, ..., 1), then across lanes by shfl_down with
+// offsets 16, ..., 1; lane 0 holds the row's sum.  fp16 x fp16 products are
+// exact in fp32, so this order alone fixes every rounding and the result equals
+// the reference kernel's bit for bit.  The first fold is one fma16 pair per
+// value: p[i] + p[i + V/2] = fma16(x_i, w_i, fma16(x_j, w_j, -0)); the later
+// folds add neighbouring pairs with one packed instruction.  Columns past the
+// width carry x = w = 0, whose product +0 is the reference's padding value
+// (and +0 + -0 = +0 as in its fold).  G > 0 states at compile time that the
+// width is G * 128 (every lane's first G column groups in, the rest out), so
+// padding products become the constant +0; G = 0 tests each group against the
+// runtime width.  xg holds the lane's x groups, ws is the row in shared memory.
+template <int V, int G>
+__device__ __forceinline__ float tree_dot(const uint2 (&xg)[V / 4], const uint16_t *ws, int width, int lane)
+{
+    constexpr int kGroups = G > 0 ? G : V / 4;
+    uint2 wg[V / 4];
+#pragma unroll
+    for (int g = 0; g < V / 4; ++g) {
+        const int col = g * 128 + 4 * lane;
+        // width % 8 == 0: a lane's four columns are all in or all out
+        const bool in = G > 0 ? g < G : col < width;
+        wg[g] = in ? *reinterpret_cast<const uint2 *>(ws + col) : make_uint2(0u, 0u);
+    }
+    float p[V / 2];
+#pragma unroll
+    for (int i = 0; i < V / 2; ++i) {
+        const int j = i + V / 2;
+        if (i / 4 >= kGroups) {
+            p[i] = 0.0f; // +0 + +0
+        } else {
+            const float pj =
+                j / 4 < kGroups ? fma16(half_of(xg[j / 4], j % 4), half_of(wg[j / 4], j % 4), -0.0f) : 0.0f;
+            p[i] = fma16(half_of(xg[i / 4], i % 4), half_of(wg[i / 4], i % 4), pj);
+        }
+    }
+#pragma unroll
+    for (int s = V / 4; s > 1; s /= 2) {
+#pragma unroll
+        for (int i = 0; i < s; i += 2) {
+            const float2 r = add2(make_float2(p[i], p[i + 1]), make_float2(p[i + s], p[i + s + 1]));
+            p[i] = r.x;
+            p[i + 1] = r.y;
+        }
+    }
+    float r = V / 2 > 1 ? __fadd_rn(p[0], p[1]) : p[0];
+#pragma unroll
+    for (int off = 16; off > 0; off /= 2)
+        r = __fadd_rn(r, __shfl_down_sync(0xffffffffu, r, off));
+    return r;
+}
+
+// The row's bias bits as staged in shared memory: fc1 keeps bias[r] in the low
+// half; qkv keeps q_bias[r] (rows < width) low and v_bias[r - 2 width] (rows >=
+// 2 width) high, +0 where the row has none, as the reference's `q`/`v` terms.
+template <bool kFc1>
+__device__ __forceinline__ uint32_t projection_bias(int gr, int width, const uint16_t *__restrict__ b0,
+                                                    const uint16_t *__restrict__ b1)
+{
+    if (kFc1)
+        return b0[gr];
+    const uint32_t q = gr < width ? b0[gr] : 0u;
+    const uint32_t v = gr >= 2 * width ? b1[gr - 2 * width] : 0u;
+    return q | (v << 16);
+}
+
+template <bool kFc1>
+__device__ __forceinline__ uint16_t projection_out(float acc, uint32_t bias)
+{
+    if (kFc1)
+        return gelu_fp16_edges(hadd_rn(f2h_rn(acc), static_cast<uint16_t>(bias)));
+    const float q = h2f(static_cast<uint16_t>(bias & 0xFFFFu));
+    const float v = h2f(static_cast<uint16_t>(bias >> 16));
+    return f2h_rn(__fadd_rn(__fadd_rn(acc, q), v));
+}
+
+// y = the plugin projection of x (fc1 or qkv) for rows_per_cta weight rows per
+// CTA.  Thread 0 issues the CTA's weight rows as up to kSlabChunks bulk copies,
+// each completing on its own mbarrier, and the CTA stages its rows' biases in
+// shared memory, all before griddepcontrol.wait (weights and biases are layer
+// constants); x is read after it, straight into each lane's registers.  Warp w
+// sums rows w, w + 8, ... two at a time as their chunks land.  Waits are
+// bounded; a CTA that gave up still waits (bounded) for its copies before it
+// exits.
+template <int V, int G, bool kFc1>
+__global__ void __launch_bounds__(kSlabThreads)
+    fp16_projection_slab_kernel(const uint16_t *__restrict__ x, const uint16_t *__restrict__ w,
+                                const uint16_t *__restrict__ b0, const uint16_t *__restrict__ b1,
+                                uint16_t *__restrict__ y, int rows, int width, int rows_per_cta, int chunk_rows)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t bars[kSlabChunks];
+    constexpr int kWarps = kSlabThreads / 32;
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    const int row0 = blockIdx.x * rows_per_cta;
+    const int nrows = min(rows_per_cta, rows - row0);
+    const int nchunks = (nrows + chunk_rows - 1) / chunk_rows;
+    const uint32_t row_bytes = static_cast<uint32_t>(width) * 2;
+    const uint16_t *ws = reinterpret_cast<const uint16_t *>(smem);
+    uint32_t *bias_s = reinterpret_cast<uint32_t *>(smem + static_cast<size_t>(rows_per_cta) * row_bytes);
+    const uint32_t bar0 = smem_u32(bars);
+
+    if (threadIdx.x == 0) {
+        for (int c = 0; c < nchunks; ++c)
+            mbar_init(bar0 + 8 * c, 1);
+        fence_barrier_init();
+        for (int c = 0; c < nchunks; ++c) {
+            const int r = c * chunk_rows;
+            const uint32_t bytes = static_cast<uint32_t>(min(chunk_rows, nrows - r)) * row_bytes;
+            mbar_arrive_expect_tx(bar0 + 8 * c, bytes);
+            bulk_load(smem_u32(smem) + static_cast<uint32_t>(r) * row_bytes,
+                      w + static_cast<size_t>(row0 + r) * width, bytes, bar0 + 8 * c);
+        }
+    }
+    for (int r = threadIdx.x; r < nrows; r += kSlabThreads)
+        bias_s[r] = projection_bias<kFc1>(row0 + r, width, b0, b1);
+    griddepcontrol_launch_dependents();
+    griddepcontrol_wait(); // x is written by the previous kernel
+    uint2 xg[V / 4];
+#pragma unroll
+    for (int g = 0; g < V / 4; ++g) {
+        const int col = g * 128 + 4 * lane;
+        xg[g] = col < width ? __ldg(reinterpret_cast<const uint2 *>(x + col)) : make_uint2(0u, 0u);
+    }
+    __syncthreads(); // barrier inits and staged biases are visible to every warp
+
+    bool ok = true;
+    for (int r = warp; r < nrows; r += 2 * kWarps) {
+        const int r2 = r + kWarps;
+        const bool two = r2 < nrows;
+        ok = __all_sync(0xffffffffu, mbar_wait(bar0 + 8 * (r / chunk_rows), 0, kSiteMmaFull) &&
+                                         (!two || mbar_wait(bar0 + 8 * (r2 / chunk_rows), 0, kSiteMmaFull)));
+        if (!ok)
+            break;
+        const float acc = tree_dot<V, G>(xg, ws + static_cast<size_t>(r) * width, width, lane);
+        const float acc2 = two ? tree_dot<V, G>(xg, ws + static_cast<size_t>(r2) * width, width, lane) : 0.0f;
+        if (lane == 0) {
+            y[row0 + r] = projection_out<kFc1>(acc, bias_s[r]);
+            if (two)
+                y[row0 + r2] = projection_out<kFc1>(acc2, bias_s[r2]);
+        }
+    }
+    if (__syncthreads_or(!ok) && threadIdx.x == 0) {
+        for (int c = 0; c < nchunks; ++c)
+            mbar_wait(bar0 + 8 * c, 0, kSiteDrain);
+    }
+}
+
+// One warp per output row; each lane streams 8 halves per 128-bit load.  Used
+// for widths above kSlabMaxWidth (sequential per-lane order, then xor shuffles).
 template <bool kFc1>
 __global__ void __launch_bounds__(kThreads)
     fp16_projection_kernel(const uint16_t *__restrict__ x, const uint16_t *__restrict__ w,
@@ -3949,9 +4140,68 @@ cudaError_t launch_dynamic_scale(const uint16_t *x, int64_t count, float *scale,
     return cudaGetLastError();
 }
 
+// The slab kernel for the plugins' projections: `rows` weight rows of `width`
+// halves split into one run per SM (fewer rows per CTA when a run would exceed
+// kSlabMaxBytes), launched with programmatic stream serialisation.
+template <bool kFc1>
+cudaError_t launch_projection_slab(const uint16_t *x, const uint16_t *w, const uint16_t *b0, const uint16_t *b1,
+                                   uint16_t *y, int64_t rows, int64_t width, cudaStream_t stream)
+{
+    const int64_t row_bytes = width * 2;
+    const int64_t cap = proj::kSlabMaxBytes / (row_bytes + 4); // weight row + staged bias word
+    // About three CTAs per SM: more warps hide the fold's latency, and smaller
+    // CTAs leave room for the next launch's copies.
+    const int64_t ctas = 3 * static_cast<int64_t>(sm_count());
+    const int64_t per_cta = std::max<int64_t>(1, std::min<int64_t>(cap, (rows + ctas - 1) / ctas));
+    const int64_t chunk_rows = (per_cta + proj::kSlabChunks - 1) / proj::kSlabChunks;
+    const unsigned grid = static_cast<unsigned>((rows + per_cta - 1) / per_cta);
+    const int smem = static_cast<int>(per_cta * (row_bytes + 4));
+    int depth = 128;
+    while (depth < width)
+        depth *= 2;
+    auto pick = [&](auto kernel) -> cudaError_t {
+        cudaError_t err = ensure_smem(kernel, proj::kSlabSmemBytes);
+        if (err != cudaSuccess)
+            return err;
+        cudaLaunchConfig_t config{};
+        config.gridDim = dim3(grid);
+        config.blockDim = dim3(proj::kSlabThreads);
+        config.dynamicSmemBytes = static_cast<size_t>(smem);
+        config.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        config.attrs = attr;
+        config.numAttrs = 1;
+        err = cudaLaunchKernelEx(&config, kernel, x, w, b0, b1, y, static_cast<int>(rows), static_cast<int>(width),
+                                 static_cast<int>(per_cta), static_cast<int>(chunk_rows));
+        count_launch();
+        return err != cudaSuccess ? err : cudaGetLastError();
+    };
+    // Whisper's widths (384, 512, 768, 1024, 1280) have every column group full.
+    switch (width) {
+    case 384: return pick(proj::fp16_projection_slab_kernel<16, 3, kFc1>);
+    case 512: return pick(proj::fp16_projection_slab_kernel<16, 4, kFc1>);
+    case 768: return pick(proj::fp16_projection_slab_kernel<32, 6, kFc1>);
+    case 1024: return pick(proj::fp16_projection_slab_kernel<32, 8, kFc1>);
+    case 1280: return pick(proj::fp16_projection_slab_kernel<64, 10, kFc1>);
+    default: break;
+    }
+    switch (depth) {
+    case 128: return pick(proj::fp16_projection_slab_kernel<4, 0, kFc1>);
+    case 256: return pick(proj::fp16_projection_slab_kernel<8, 0, kFc1>);
+    case 512: return pick(proj::fp16_projection_slab_kernel<16, 0, kFc1>);
+    case 1024: return pick(proj::fp16_projection_slab_kernel<32, 0, kFc1>);
+    case 2048: return pick(proj::fp16_projection_slab_kernel<64, 0, kFc1>);
+    default: return pick(proj::fp16_projection_slab_kernel<128, 0, kFc1>);
+    }
+}
+
 cudaError_t launch_fp16_fc1(const uint16_t *x, const uint16_t *w, const uint16_t *bias, uint16_t *y,
                             int64_t rows, int64_t width, cudaStream_t stream)
 {
+    if (width <= proj::kSlabMaxWidth)
+        return launch_projection_slab<true>(x, w, bias, nullptr, y, rows, width, stream);
     const int64_t per_block = proj::kThreads / 32;
     const unsigned blocks = static_cast<unsigned>((rows + per_block - 1) / per_block);
     proj::fp16_projection_kernel<true><<<blocks, proj::kThreads, 0, stream>>>(
@@ -3964,6 +4214,8 @@ cudaError_t launch_fp16_qkv(const uint16_t *x, const uint16_t *w, const uint16_t
                             const uint16_t *v_bias, uint16_t *y, int64_t width, cudaStream_t stream)
 {
     const int64_t rows = 3 * width;
+    if (width <= proj::kSlabMaxWidth)
+        return launch_projection_slab<false>(x, w, q_bias, v_bias, y, rows, width, stream);
     const int64_t per_block = proj::kThreads / 32;
     const unsigned blocks = static_cast<unsigned>((rows + per_block - 1) / per_block);
     proj::fp16_projection_kernel<false><<<blocks, proj::kThreads, 0, stream>>>(

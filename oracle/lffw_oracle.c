@@ -474,6 +474,68 @@ void oracle_fp16_qkv(const uint16_t *x, const uint16_t *w, const uint16_t *q_bia
     }
 }
 
+/* The reference kernel's fp32 sum of x . w (cpp/kernels.cu:27-49).  DEPTH is the
+ * power of two >= width (at least 128) and V = DEPTH / 32.  Lane L forms the
+ * products of columns (i/4)*128 + 4L + i%4, i < V, with +0 past the width, folds
+ * them by halving strides (p[i] += p[i + s], s = V/2 .. 1), and the 32 lane sums
+ * are folded as shfl_down with offsets 16 .. 1 leaves them in lane 0.  fp16 x fp16
+ * products are exact in binary32, so this order alone decides the roundings. */
+static float fp16_dot_kernel_order(const uint16_t *x, const uint16_t *w, int64_t width, float *scratch)
+{
+    int64_t depth = 128;
+    while (depth < width)
+        depth *= 2;
+    const int64_t v = depth / 32;
+    float lanes[32];
+    for (int lane = 0; lane < 32; ++lane) {
+        for (int64_t i = 0; i < v; ++i) {
+            const int64_t col = (i / 4) * 128 + 4 * lane + i % 4;
+            scratch[i] = col < width ? (float)oracle_half_to_double(x[col]) * (float)oracle_half_to_double(w[col])
+                                     : 0.0f;
+        }
+        for (int64_t s = v / 2; s > 0; s /= 2)
+            for (int64_t i = 0; i < s; ++i)
+                scratch[i] = scratch[i] + scratch[i + s];
+        lanes[lane] = scratch[0];
+    }
+    for (int off = 16; off > 0; off /= 2)
+        for (int lane = 0; lane < off; ++lane)
+            lanes[lane] = lanes[lane] + lanes[lane + off];
+    return lanes[0];
+}
+
+int oracle_fp16_fc1_kernel_order(const uint16_t *x, const uint16_t *w, const uint16_t *bias, uint16_t *y,
+                                 int64_t rows, int64_t width)
+{
+    float *scratch = malloc(sizeof(float) * (size_t)(width / 16 + 128)); /* >= DEPTH / 32 */
+    if (!scratch)
+        return -1;
+    for (int64_t r = 0; r < rows; ++r) {
+        const float dot = fp16_dot_kernel_order(x, w + r * width, width, scratch);
+        /* half(half(dot) + bias): the sum of two halves rounded once to fp16 */
+        const double value = round_half(round_half((double)dot) + oracle_half_to_double(bias[r]));
+        y[r] = oracle_gelu_fp16(oracle_half_from_double(value));
+    }
+    free(scratch);
+    return 0;
+}
+
+int oracle_fp16_qkv_kernel_order(const uint16_t *x, const uint16_t *w, const uint16_t *q_bias,
+                                 const uint16_t *v_bias, uint16_t *y, int64_t width)
+{
+    float *scratch = malloc(sizeof(float) * (size_t)(width / 16 + 128)); /* >= DEPTH / 32 */
+    if (!scratch)
+        return -1;
+    for (int64_t r = 0; r < 3 * width; ++r) {
+        const float dot = fp16_dot_kernel_order(x, w + r * width, width, scratch);
+        const float q = r < width ? (float)oracle_half_to_double(q_bias[r]) : 0.0f;
+        const float v = r >= 2 * width ? (float)oracle_half_to_double(v_bias[r - 2 * width]) : 0.0f;
+        y[r] = oracle_half_from_double((double)((dot + q) + v));
+    }
+    free(scratch);
+    return 0;
+}
+
 void oracle_fp16_bias(const uint16_t *x, uint16_t bias, uint16_t *y, int64_t count)
 {
     /* cpp/kernels.cu:10-17 */

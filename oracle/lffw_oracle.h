@@ -107,6 +107,12 @@ void oracle_fp16_fc1(const uint16_t *x, const uint16_t *w, const uint16_t *bias,
                      int64_t rows, int64_t width);
 void oracle_fp16_qkv(const uint16_t *x, const uint16_t *w, const uint16_t *q_bias,
                      const uint16_t *v_bias, uint16_t *y, int64_t width);
+/* The same projections with the reference kernel's fp32 summation order
+ * (cpp/kernels.cu:27-49) instead of the CPU model's binary64 dot; 0 on success. */
+int oracle_fp16_fc1_kernel_order(const uint16_t *x, const uint16_t *w, const uint16_t *bias, uint16_t *y,
+                                 int64_t rows, int64_t width);
+int oracle_fp16_qkv_kernel_order(const uint16_t *x, const uint16_t *w, const uint16_t *q_bias,
+                                 const uint16_t *v_bias, uint16_t *y, int64_t width);
 void oracle_fp16_bias(const uint16_t *x, uint16_t bias, uint16_t *y, int64_t count);
 
 int oracle_threads(void);

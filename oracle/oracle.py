@@ -53,6 +53,8 @@ def lib() -> ctypes.CDLL:
         L.oracle_fp16_fc1.argtypes = [_u16p, _u16p, _u16p, _u16p, ctypes.c_int64, ctypes.c_int64]
         L.oracle_fp16_qkv.argtypes = [_u16p, _u16p, _u16p, _u16p, _u16p, ctypes.c_int64]
         L.oracle_fp16_bias.argtypes = [_u16p, ctypes.c_uint16, _u16p, ctypes.c_int64]
+        L.oracle_fp16_fc1_kernel_order.argtypes = [_u16p, _u16p, _u16p, _u16p, ctypes.c_int64, ctypes.c_int64]
+        L.oracle_fp16_qkv_kernel_order.argtypes = [_u16p, _u16p, _u16p, _u16p, _u16p, ctypes.c_int64]
         L.oracle_threads.restype = ctypes.c_int
         L.oracle_layer_norm.argtypes = [
             _u16p, _u16p, ctypes.c_int64, ctypes.c_int64, _f32p, _f32p, ctypes.c_float, _u16p, _u16p,
@@ -285,6 +287,28 @@ def fp16_qkv(x, w, q_bias, v_bias) -> np.ndarray:
     out = np.empty(3 * width, np.uint16)
     lib().oracle_fp16_qkv(_ptr(xb, _u16p), _ptr(wb, _u16p), _ptr(qb, _u16p), _ptr(vb, _u16p),
                           _ptr(out, _u16p), width)
+    return out
+
+
+def fp16_fc1_kernel_order(x, w, bias) -> np.ndarray:
+    """fp16_fc1 with the reference kernel's fp32 summation order (cpp/kernels.cu:27-49)."""
+    xb, wb, bb = bits16(x), bits16(w), bits16(bias)
+    rows, width = wb.shape
+    out = np.empty(rows, np.uint16)
+    if lib().oracle_fp16_fc1_kernel_order(_ptr(xb, _u16p), _ptr(wb, _u16p), _ptr(bb, _u16p), _ptr(out, _u16p),
+                                          rows, width) != 0:
+        raise MemoryError("oracle_fp16_fc1_kernel_order")
+    return out
+
+
+def fp16_qkv_kernel_order(x, w, q_bias, v_bias) -> np.ndarray:
+    """fp16_qkv with the reference kernel's fp32 summation order (cpp/kernels.cu:27-49)."""
+    xb, wb, qb, vb = bits16(x), bits16(w), bits16(q_bias), bits16(v_bias)
+    width = xb.size
+    out = np.empty(3 * width, np.uint16)
+    if lib().oracle_fp16_qkv_kernel_order(_ptr(xb, _u16p), _ptr(wb, _u16p), _ptr(qb, _u16p), _ptr(vb, _u16p),
+                                          _ptr(out, _u16p), width) != 0:
+        raise MemoryError("oracle_fp16_qkv_kernel_order")
     return out
 
 

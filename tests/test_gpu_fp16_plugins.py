@@ -179,7 +179,8 @@ def test_fp8_linear_plugin_with_half_input(cuda, native, oracle, fp8):
 def test_reference_kernels_on_this_box(cuda, fp8, oracle, fc1):
     """The reference's own cpp/kernels.cu, compiled for sm_100a (oracle/_ref), on its
     seeded test data beside ours: both within the reference's tolerance of its CPU
-    model, and within one fp16 ulp of each other (different fp32 summation orders)."""
+    model, and bit-identical to each other and to the oracle's restatement of the
+    kernel's fp32 summation order (same fp16 products, same fold order, same edges)."""
     import torch
 
     kernels = oracle.reference_kernels()
@@ -205,7 +206,55 @@ def test_reference_kernels_on_this_box(cuda, fp8, oracle, fc1):
     atol = 2.0**-11 if fc1 else 2.0**-12
     check(theirs[:keep], expected, atol)
     check(mine[:keep], expected, atol)
-    a, b2 = theirs.view(np.float16).astype(np.float64), mine.view(np.float16).astype(np.float64)
-    ulp = np.abs(np.spacing(np.maximum(np.abs(a), np.abs(b2)).astype(np.float16))).astype(np.float64)
     print(f"{'fc1' if fc1 else 'qkv'}: identical to the reference kernel {np.mean(theirs == mine):.4f}")
-    assert np.all(np.abs(a - b2) <= 2 * ulp + 2.0**-24)
+    np.testing.assert_array_equal(mine, theirs)
+    kernel_order = oracle.fp16_fc1_kernel_order(x, w, b) if fc1 else oracle.fp16_qkv_kernel_order(x, w, b, vb)
+    np.testing.assert_array_equal(theirs, kernel_order)
+
+
+@pytest.mark.parametrize("width", [8, 120, 128, 136, 384, 504, 512, 640, 768, 1024, 1280, 2048, 2056, 4096, 4104])
+def test_projection_widths_match_kernel_order(cuda, fp8, oracle, width):
+    """Every width class of the slab kernel (DEPTH 128 ... 4096, ragged last
+    column group, several CTAs per SM for narrow rows) is bit-identical to the
+    oracle's restatement of the reference kernel's order; widths above 4096 take
+    the row-per-warp kernel (sequential per-lane order) and meet the plugins'
+    tolerance.  fc1 with a row count that leaves a short last CTA."""
+    import torch
+
+    rng = np.random.default_rng(width)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.float16).copy()).to(cuda)
+    x = rng.standard_normal(width).astype(np.float16).view(np.uint16)
+    for fc1, rows in ((True, 997), (False, 3 * width)):
+        w = (rng.standard_normal((rows, width)) / np.sqrt(width)).astype(np.float16).view(np.uint16)
+        b = rng.uniform(-0.5, 0.5, rows if fc1 else width).astype(np.float16).view(np.uint16)
+        vb = rng.uniform(-0.5, 0.5, width).astype(np.float16).view(np.uint16)
+        if fc1:
+            got = fp8.fp16_fc1(t(x).view(1, -1), t(w), t(b))
+            want = oracle.fp16_fc1_kernel_order(x, w, b)
+            model = oracle.fp16_fc1(x, w, b)
+        else:
+            got = fp8.fp16_qkv(t(x).view(1, -1), t(w), t(b), t(vb))
+            want = oracle.fp16_qkv_kernel_order(x, w, b, vb)
+            model = oracle.fp16_qkv(x, w, b, vb)
+        got = got.reshape(-1).cpu().numpy().view(np.uint16)
+        if width <= 4096:
+            np.testing.assert_array_equal(got, want)
+        check(got, model, 2.0**-11 if fc1 else 2.0**-12)
+
+
+@pytest.mark.parametrize("width", [1024, 1280])
+def test_projection_signed_zero_follows_kernel_order(cuda, fp8, oracle, width):
+    """x = -0 and w = 1 make every product -0.  With DEPTH = width (1024) the
+    fold keeps -0, so fc1 with bias -0 gives -0; with 1280 the +0 padding of
+    DEPTH 2048 turns the sum into +0, as in the reference kernel.  (The binary64
+    CPU model starts from +0 and gives +0 for both.)"""
+    import torch
+
+    t = lambda a: torch.from_numpy(a.view(np.float16).copy()).to(cuda)
+    x = np.full(width, 0x8000, np.uint16)
+    w = np.full((300, width), 0x3C00, np.uint16)
+    b = np.full(300, 0x8000, np.uint16)
+    got = fp8.fp16_fc1(t(x).view(1, -1), t(w), t(b)).cpu().numpy().view(np.uint16)
+    want = oracle.fp16_fc1_kernel_order(x, w, b)
+    np.testing.assert_array_equal(got, want)
+    assert np.all(want == (0x8000 if width == 1024 else 0x0000))
