@@ -2100,6 +2100,7 @@ constexpr int kChunk = 128; // keys per tile
 struct Params {
     int streams, tokens, heads;
     int qblocks; // ceil(tokens / kBQ)
+    int qpairs;  // ceil(qblocks / 2): items per (stream, head), two query tiles each
     int nchunks; // ceil(tokens / kChunk)
     uint16_t *out;
     uint32_t scale2; // fp16 head_dim^-0.25 in both halves
@@ -2131,61 +2132,57 @@ constexpr float kLog2e = 1.4426950408889634f;
 // ---------------------------------------------------------------------------
 // Encoder self-attention on tcgen05 with the graph's fp16 edges (q' = half(q c),
 // k' = half(k c), s = half(q'.k'), out = half(sum_j p_j v_j)) and a one-pass
-// (online) softmax, per (stream, head, 128-query block):
-//   warp 0: TMA producer (Q once per item; K and V tiles once each);
-//   warp 1: MMA issuer.  S = Q' K'^T, kind::f16 128 x 128 x 16, into one of two
-//           TMEM score buffers; O += P V, 128 x 64 x 16 with V read MN-major
-//           straight from its TMA tile, into a third TMEM region;
-//   warps 2-5: rescale Q and each K tile in shared memory (half(x c)) before
-//           the MMA reads it, a quarter of the tile each;
-//   warps 6-21: softmax, kSplit warps per TMEM lane quarter, each over kCols of
-//           a tile's 128 key columns.  Per tile the four warps of a lane quarter
-//           exchange their part maxima through shared memory; each row keeps a
-//           running maximum m that is raised only when a tile's maximum exceeds
-//           it by more than 2^8 in exp (then O and the row sum are rescaled in
-//           place).  P = half(exp(s - m)) goes as fp16 into a K-major 128B-swizzled
-//           tile for the P.V MMA, and out = half(O / sum) at the end.
+// (online) softmax.  An item is two 128-query tiles (slots A and B) of one
+// (stream, head), which share every K and V tile:
+//   warp 0: TMA producer (an item's two Q tiles; K and V tiles once each);
+//   warp 1: MMA issuer.  Per key tile, S_A = Q'_A K'^T and S_B = Q'_B K'^T
+//           (kind::f16 128 x 128 x 16, one TMEM region per slot), then the
+//           previous tile's O_X += P_X V (128 x 64 x 16) with P_X read from
+//           TMEM and V MN-major straight from its TMA tile;
+//   warps 2-3: rescale Q and each K tile in shared memory (half(x c)) before
+//           the MMA reads it, half of the tile each;
+//   warps 4-7 / 8-11: softmax of slot A / B, one thread per query row with
+//           all 128 key columns of a tile, so the row maximum and sum need no
+//           exchange between threads.  Each row keeps a running maximum m
+//           raised only when a tile's maximum exceeds it by more than 2^8 in
+//           exp (then O and the row sum are rescaled in place).
+//           P = half(exp(s - m)) is stored as fp16 pairs into the slot's TMEM
+//           P region, and out = half(O / sum) at the end of the item.
 // Against the graph's p = half(exp(s - max) / sum) the probabilities round once
 // each at another scale: the output moves by at most 2^-10 sum_j p_j |v_j| (first
 // order), which the tests add to the fp16 bound.
-// The P.V MMAs of tile c - 1 are issued after the score MMAs of tile c, so the
-// softmax of one tile overlaps the MMAs of the next.  The kernel is persistent:
-// one CTA per SM walks (stream, head, query block) items, its rings and
-// barrier phases running on across items.  Q is double-buffered by item parity,
-// so the next item's Q and first K tiles load and scale while the current item
-// finishes, and its score MMAs start as soon as the softmax frees a buffer.
+// The two slots' softmax run on different warps while the tensor core works on
+// the other slot's tile.  The kernel is persistent: one CTA per SM walks
+// (stream, head, query-tile pair) items, its rings and barrier phases running on
+// across items; Q is double-buffered by item parity, so the next item's Q and
+// first K tiles load and scale while the current item finishes.
 namespace fattn {
 
 using sattn::kLog2e;
 using sattn::fast_exp2;
-using sattn::fast_log2;
 constexpr int kDim = 64;
-constexpr int kBQ = 128;
-constexpr int kBK = 128;
+constexpr int kBQ = 128;  // query rows per slot
+constexpr int kBK = 128;  // keys per tile
 constexpr int kKStages = 3;
 constexpr int kVStages = 3;
-constexpr int kTile = kBK * kDim * 2;  // one Q, K or V tile: 16 KB
-constexpr int kPBytes = kBQ * kBK * 2; // one P tile: two 64-key K-major halves, 32 KB
+constexpr int kTile = kBK * kDim * 2; // one Q, K or V tile: 16 KB
+constexpr int kQBytes = 2 * kTile;    // an item's two Q tiles
 constexpr int kScaleWarp0 = 2;
-constexpr int kScaleWarps = 4;
-constexpr int kSoftWarp0 = kScaleWarp0 + kScaleWarps;
-constexpr int kSplit = 4;                 // softmax warps per TMEM lane quarter
-constexpr int kSoftWarps = 4 * kSplit;
-constexpr int kCols = kBK / kSplit;       // score columns per softmax warp
-constexpr int kThreads = (kSoftWarp0 + kSoftWarps) * 32;
-constexpr int kOffK = 2 * kTile; // Q double-buffered by item parity
+constexpr int kScaleWarps = 2;
+constexpr int kSoftWarp0 = 4; // slot A: warps 4-7, slot B: 8-11 (warp % 4 = TMEM lane quarter)
+constexpr int kThreads = 12 * 32;
+constexpr int kOffK = 2 * kQBytes; // Q double-buffered by item parity
 constexpr int kOffV = kOffK + kKStages * kTile;
-constexpr int kOffP = kOffV + kVStages * kTile;
-constexpr int kOffStats = kOffP + 2 * kPBytes; // float tile maxima [2][kSplit][kBQ], row sums [2][kSplit][kBQ]
-constexpr int kOutCols = kDim / kSplit;        // O columns per softmax warp
+constexpr int kOffBar = kOffV + kVStages * kTile;
+constexpr int kBars = 6 + 3 * kKStages + 2 * kVStages + 12 + 1;
+constexpr int kSmemBytes = kOffBar + 8 * kBars + 16 + 1024;
 // The running maximum is raised only when a tile's maximum exceeds it by more than
 // 2^kLazy in exp: P = exp(s - m) then stays below 2^kLazy, exact in fp16 range.
 constexpr float kLazy = 8.0f;
-constexpr int kOffBar = kOffStats + 2 * 2 * kSplit * kBQ * 4;
-constexpr int kBars = 4 + 3 * kKStages + 2 * kVStages + 8 + 5;
-constexpr int kSmemBytes = kOffBar + 8 * kBars + 16 + 1024;
-constexpr uint32_t kTmemCols = 512; // S[2] (2 x 128) + O (64)
-constexpr uint32_t kTmemO = 256;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemS = 0;   // S of slot X: columns X * 128 .. + 127 (fp32)
+constexpr uint32_t kTmemP = 256; // P of slot X: X * 64 .. + 63 (fp16 pairs)
+constexpr uint32_t kTmemO = 384; // O of slot X: X * 64 .. + 63 (fp32)
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 // Packed fp16 maximum (a NaN operand yields the other operand, like fmaxf).
@@ -2207,17 +2204,11 @@ __device__ __forceinline__ void sub_f16x2_f32(uint32_t h2, float c, float &lo, f
 }
 
 // Packed fp32 pairs (low lane = first value): one instruction rounds each lane as
-// the scalar mul.rn / fma.rn / add.rn would.
+// the scalar mul.rn / add.rn would.
 __device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b)
 {
     uint64_t r;
     asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c)
-{
-    uint64_t r;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
     return r;
 }
 __device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b)
@@ -2237,36 +2228,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
     const uint32_t sb = smem_u32(smem);
-    const uint32_t sQ = sb, sK = sb + kOffK, sV = sb + kOffV, sP = sb + kOffP;
+    const uint32_t sQ = sb, sK = sb + kOffK, sV = sb + kOffV;
     const uint32_t q_full = sb + kOffBar; // [2] by item parity, like q_ready and q_empty
     const uint32_t q_ready = q_full + 16;
-    const uint32_t k_full = q_ready + 16;
+    const uint32_t q_empty = q_ready + 16; // the item's Q is read by no later MMA
+    const uint32_t k_full = q_empty + 16;
     const uint32_t k_ready = k_full + 8 * kKStages;
     const uint32_t k_empty = k_ready + 8 * kKStages;
     const uint32_t v_full = k_empty + 8 * kKStages;
     const uint32_t v_empty = v_full + 8 * kVStages;
-    const uint32_t s_full = v_empty + 8 * kVStages;
-    const uint32_t s_empty = s_full + 16;
-    const uint32_t p_full = s_empty + 16;
-    const uint32_t p_empty = p_full + 16;
-    const uint32_t o_full = p_empty + 16;
-    const uint32_t drain = o_full + 8;
-    const uint32_t q_empty = drain + 8; // [2] the item's Q is no longer read (after its last score MMA)
-    const uint32_t o_empty = q_empty + 16; // the item's O has been read (by the softmax warps)
+    const uint32_t s_full = v_empty + 8 * kVStages; // [2] by slot, like the five below
+    const uint32_t s_empty = s_full + 16;           // the slot's S has been read
+    const uint32_t p_full = s_empty + 16;           // the slot's P is in TMEM
+    const uint32_t p_empty = p_full + 16;           // the slot's P.V MMAs are done
+    const uint32_t o_full = p_empty + 16;           // the item's last P.V is done
+    const uint32_t o_empty = o_full + 16;           // the slot's O has been read
+    const uint32_t drain = o_empty + 16;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 8 * kBars);
-    float *stats = reinterpret_cast<float *>(smem + kOffStats); // [item parity][m | l][kSplit][kBQ]
 
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
     const int nt = p.nchunks;
-    const int items = p.streams * p.heads * p.qblocks;
+    const int items = p.streams * p.heads * p.qpairs;
     struct Item {
-        int head, row_base, q0;
+        int head, row_base, q0; // q0: slot A's first query; slot B's is q0 + kBQ
     };
     auto item_of = [&](int it) {
-        const int qb = it % p.qblocks;
-        const int sh = it / p.qblocks;
-        return Item{sh % p.heads, (sh / p.heads) * p.tokens, qb * kBQ};
+        const int qp = it % p.qpairs;
+        const int sh = it / p.qpairs;
+        return Item{sh % p.heads, (sh / p.heads) * p.tokens, qp * 2 * kBQ};
     };
 
     if (threadIdx.x == 0) {
@@ -2275,6 +2265,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(q_full + 8 * b, 1);
             mbar_init(q_ready + 8 * b, kScaleWarps);
             mbar_init(q_empty + 8 * b, 1);
+            mbar_init(s_full + 8 * b, 1);
+            mbar_init(s_empty + 8 * b, 4);
+            mbar_init(p_full + 8 * b, 4);
+            mbar_init(p_empty + 8 * b, 1);
+            mbar_init(o_full + 8 * b, 1);
+            mbar_init(o_empty + 8 * b, 4);
         }
         for (int s = 0; s < kKStages; ++s) {
             mbar_init(k_full + 8 * s, 1);
@@ -2285,15 +2281,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(v_full + 8 * s, 1);
             mbar_init(v_empty + 8 * s, 1);
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(s_full + 8 * b, 1);
-            mbar_init(s_empty + 8 * b, kSoftWarps);
-            mbar_init(p_full + 8 * b, kSoftWarps);
-            mbar_init(p_empty + 8 * b, 1);
-        }
-        mbar_init(o_full, 1);
         mbar_init(drain, 1);
-        mbar_init(o_empty, kSoftWarps);
         fence_barrier_init();
         prefetch_tensor_map(&tm_q);
         prefetch_tensor_map(&tm_k);
@@ -2319,8 +2307,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t qb = local & 1;
                 if (!mbar_wait(q_empty + 8 * qb, ((local >> 1) & 1u) ^ 1u, kSiteProducerEmpty))
                     break;
-                mbar_arrive_expect_tx(q_full + 8 * qb, kTile);
-                tma_load_2d(sQ + qb * kTile, &tm_q, q_full + 8 * qb, w.head * kDim, w.row_base + w.q0);
+                mbar_arrive_expect_tx(q_full + 8 * qb, kQBytes);
+                tma_load_2d(sQ + qb * kQBytes, &tm_q, q_full + 8 * qb, w.head * kDim, w.row_base + w.q0);
+                tma_load_2d(sQ + qb * kQBytes + kTile, &tm_q, q_full + 8 * qb, w.head * kDim, w.row_base + w.q0 + kBQ);
                 ++q_issued;
                 for (int j = 0; j < nt; ++j) {
                     const int s = k_issued % kKStages;
@@ -2358,67 +2347,74 @@ __global__ void __launch_bounds__(kThreads, 1)
             constexpr uint32_t id_s = idesc_f16_f32<kBQ, kBK>();
             constexpr uint32_t id_o = idesc_f16_f32<kBQ, kDim>() | (1u << 16); // B (V) MN-major
             bool ok = true;
-            int u_all = 0, c_all = 0; // score tiles and P tiles issued over all items
-            uint32_t sQi = sQ; // this item's Q buffer
-            auto score_mma = [&](int u) { // u: score tile over all items (K tile u)
-                const uint32_t b = u & 1;
-                const int ks = u % kKStages;
-                ok = ok && mbar_wait(s_empty + 8 * b, ((u >> 1) & 1u) ^ 1u, kSiteMmaAccEmpty) &&
-                     mbar_wait(k_ready + 8 * ks, (u / kKStages) & 1u, kSiteMmaFull);
-                if (!ok)
-                    return;
-                tc_fence_after();
+            int u = 0, cc = 0; // score tiles and P tiles issued over all items (per slot)
+            int local = 0;
+            auto pv_mma = [&](int first) { // P.V of P tile cc for both slots
+                const int vs = cc % kVStages;
+                ok = ok && mbar_wait(v_full + 8 * vs, (cc / kVStages) & 1u, kSiteMmaFull);
+                for (int x = 0; x < 2 && ok; ++x) {
+                    if (first)
+                        ok = mbar_wait(o_empty + 8 * x, (local & 1u) ^ 1u, kSiteMmaAccEmpty);
+                    ok = ok && mbar_wait(p_full + 8 * x, cc & 1u, kSiteMmaFull);
+                    if (!ok)
+                        break;
+                    tc_fence_after();
 #pragma unroll
-                for (int k = 0; k < kDim / 16; ++k)
-                    mma_f16(tmem + b * kBK, smem_desc_k_sw128(sQi + k * 32),
-                            smem_desc_k_sw128(sK + ks * kTile + k * 32), id_s, k != 0);
-                mma_commit(k_empty + 8 * ks);
-                mma_commit(s_full + 8 * b);
-            };
-            auto pv_mma = [&](int c, int first) { // c: P tile over all items; first: the item's first
-                const uint32_t pb = c & 1;
-                const int vs = c % kVStages;
-                ok = ok && mbar_wait(p_full + 8 * pb, (c >> 1) & 1u, kSiteMmaFull) &&
-                     mbar_wait(v_full + 8 * vs, (c / kVStages) & 1u, kSiteMmaFull);
-                if (!ok)
-                    return;
-                tc_fence_after();
-#pragma unroll
-                for (int k = 0; k < kBK / 16; ++k)
-                    mma_f16(tmem + kTmemO, smem_desc_k_sw128(sP + pb * kPBytes + (k / 4) * (kPBytes / 2) + (k % 4) * 32),
-                            smem_desc_mn_sw128(sV + vs * kTile + k * 16 * 128), id_o, (first == 0 || k != 0) ? 1u : 0u);
-                mma_commit(v_empty + 8 * vs);
-                mma_commit(p_empty + 8 * pb);
-            };
-            for (int it = blockIdx.x, local = 0; ok && it < items; it += gridDim.x, ++local) {
-                const uint32_t qb = local & 1;
-                sQi = sQ + qb * kTile;
-                ok = ok && mbar_wait(q_ready + 8 * qb, (local >> 1) & 1u, kSiteMmaFull);
-                for (int c = 0; c < nt; ++c) {
-                    score_mma(u_all++);
-                    if (c == nt - 1 && ok)
-                        mma_commit(q_empty + 8 * qb); // the item's Q is read by no later MMA
-                    if (c == 1) // O of the previous item has been read out
-                        ok = ok && mbar_wait(o_empty, (local & 1u) ^ 1u, kSiteMmaAccEmpty);
-                    if (c > 0)
-                        pv_mma(c_all++, c == 1);
+                    for (int k = 0; k < kBK / 16; ++k)
+                        mma_f16_ts(tmem + kTmemO + x * kDim, tmem + kTmemP + x * (kBK / 2) + k * 8,
+                                   smem_desc_mn_sw128(sV + vs * kTile + k * 16 * 128), id_o,
+                                   (first == 0 || k != 0) ? 1u : 0u);
+                    mma_commit(p_empty + 8 * x);
                 }
-                if (nt == 1)
-                    ok = ok && mbar_wait(o_empty, (local & 1u) ^ 1u, kSiteMmaAccEmpty);
-                pv_mma(c_all++, nt == 1);
                 if (ok)
+                    mma_commit(v_empty + 8 * vs);
+                ++cc;
+            };
+            for (int it = blockIdx.x; ok && it < items; it += gridDim.x, ++local) {
+                const uint32_t qb = local & 1;
+                const uint32_t sQi = sQ + qb * kQBytes;
+                ok = mbar_wait(q_ready + 8 * qb, (local >> 1) & 1u, kSiteMmaFull);
+                for (int c = 0; ok && c < nt; ++c) {
+                    const int ks = u % kKStages;
+                    ok = mbar_wait(k_ready + 8 * ks, (u / kKStages) & 1u, kSiteMmaFull);
+                    for (int x = 0; x < 2 && ok; ++x) {
+                        ok = mbar_wait(s_empty + 8 * x, (u & 1u) ^ 1u, kSiteMmaAccEmpty);
+                        if (!ok)
+                            break;
+                        tc_fence_after();
+#pragma unroll
+                        for (int k = 0; k < kDim / 16; ++k)
+                            mma_f16(tmem + kTmemS + x * kBK, smem_desc_k_sw128(sQi + x * kTile + k * 32),
+                                    smem_desc_k_sw128(sK + ks * kTile + k * 32), id_s, k != 0);
+                        mma_commit(s_full + 8 * x);
+                    }
+                    if (!ok)
+                        break;
+                    mma_commit(k_empty + 8 * ks);
+                    if (c == nt - 1)
+                        mma_commit(q_empty + 8 * qb);
+                    ++u;
+                    if (c > 0)
+                        pv_mma(c == 1);
+                }
+                if (!ok)
+                    break;
+                pv_mma(nt == 1);
+                if (ok) {
                     mma_commit(o_full);
+                    mma_commit(o_full + 8);
+                }
             }
             // Every MMA of this thread completes before TMEM is freed.
             mma_commit(drain);
             for (int t = 0; t < (1 << 22) && !mbar_try_wait(drain, 0); ++t) {
             }
         }
-    } else if (warp < kSoftWarp0) {
+    } else if (warp >= kScaleWarp0 && warp < kScaleWarp0 + kScaleWarps) {
         // ---------------- operand scaling: x' = half(x c), in place ----------------
-        const int part = warp - kScaleWarp0; // this warp's quarter of each tile
+        const int part = warp - kScaleWarp0; // this warp's share of each tile
         auto scale_tile = [&](uint32_t tile) {
-#pragma unroll
+#pragma unroll 4
             for (int i = 0; i < kTile / 16 / 32 / kScaleWarps; ++i) {
                 const uint32_t a = tile + part * (kTile / kScaleWarps) + (i * 32 + lane) * 16;
                 uint32_t v0, v1, v2, v3;
@@ -2430,8 +2426,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v0), "r"(v1), "r"(v2), "r"(v3)
                              : "memory");
             }
-            fence_proxy_async_smem(); // the MMA (async proxy) reads what these stores wrote
-            __syncwarp();
         };
         bool ok = true;
         int k_scaled = 0;
@@ -2440,7 +2434,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = __all_sync(0xffffffffu, mbar_wait(q_full + 8 * qb, (local >> 1) & 1u, kSiteMmaFull));
             if (!ok)
                 break;
-            scale_tile(sQ + qb * kTile);
+            scale_tile(sQ + qb * kQBytes);
+            scale_tile(sQ + qb * kQBytes + kTile);
+            fence_proxy_async_smem(); // the MMA (async proxy) reads what these stores wrote
+            __syncwarp();
             if (lane == 0)
                 mbar_arrive(q_ready + 8 * qb);
             for (int j = 0; ok && j < nt; ++j, ++k_scaled) {
@@ -2449,198 +2446,179 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!ok)
                     break;
                 scale_tile(sK + s * kTile);
+                fence_proxy_async_smem();
+                __syncwarp();
                 if (lane == 0)
                     mbar_arrive(k_ready + 8 * s);
             }
         }
-    } else {
-        // ---------------- softmax: (lane quarter, column part) per warp ----------------
-        // Every softmax warp walks every tile, even after a wait has given up
-        // (waits then return at once), so the named barriers always match.
+    } else if (warp >= kSoftWarp0) {
+        // ---------------- softmax: one thread per query row of a slot ----------------
+        const int x = (warp - kSoftWarp0) >> 2; // slot
         const int quarter = warp & 3;
-        const int part = (warp - kSoftWarp0) >> 2; // which kCols columns of a tile
-        const int col0 = part * kCols;
         const int row = quarter * 32 + lane;
-        const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + col0;
-        const uint32_t o_base = tmem + kTmemO + (static_cast<uint32_t>(quarter * 32) << 16) + part * kOutCols;
-        float *tile_max = stats;                    // [tile parity][part][row]
-        float *part_sum = stats + 2 * kSplit * kBQ; // [item parity][part][row]
+        const uint32_t lanes = static_cast<uint32_t>(quarter * 32) << 16;
+        const uint32_t s_base = tmem + lanes + kTmemS + x * kBK;
+        const uint32_t p_base = tmem + lanes + kTmemP + x * (kBK / 2);
+        const uint32_t o_base = tmem + lanes + kTmemO + x * kDim;
         bool ok = true;
         // Every lane polls the barrier (one shared word, the same answer for all
-        // lanes), so no broadcast is needed; the warp reconverges before the
-        // warp-wide TMEM and barrier instructions that follow.
+        // lanes); the warp reconverges before the warp-wide TMEM instructions.
         auto wait_all = [&](uint32_t bar, uint32_t parity, int site) {
-            ok = mbar_wait(bar, parity, site) && ok;
+            ok = ok && mbar_wait(bar, parity, site);
             __syncwarp();
         };
-        // This warp's kCols scores of tile u, rounded to fp16 (the MatMul edge);
-        // keys past the stream's tokens are -inf.  Frees the TMEM buffer.
-        auto load_scores = [&](int u, int c, uint32_t (&h)[kCols / 2]) {
-            const uint32_t b = u & 1;
-            wait_all(s_full + 8 * b, (u >> 1) & 1u, kSiteEpilogueAccFull);
-            tc_fence_after();
-            uint32_t v[kCols];
+        const uint64_t log2e2 = f2_bits(kLog2e, kLog2e);
+        int u = 0, cc = 0;
+        for (int it = blockIdx.x, local = 0; ok && it < items; it += gridDim.x, ++local) {
+            const Item w = item_of(it);
+            float m = -INFINITY; // the row's running maximum
+            float l = 0.0f;      // the row's sum of exp(s - m)
+            for (int c = 0; ok && c < nt; ++c, ++u, ++cc) {
+                // The row's 128 scores of tile c, rounded to fp16 (the MatMul edge);
+                // keys past the stream's tokens are -inf.  Frees the slot's S.
+                wait_all(s_full + 8 * x, u & 1u, kSiteEpilogueAccFull);
+                if (!ok)
+                    break;
+                tc_fence_after();
+                uint32_t h[kBK / 2];
 #pragma unroll
-            for (int j = 0; j < kCols; j += 32)
-                tmem_ld_32x32b_x32(lane_base + b * kBK + j, *reinterpret_cast<uint32_t(*)[32]>(v + j));
+                for (int half = 0; half < 2; ++half) {
+                    uint32_t v[64];
+                    tmem_ld_32x32b_x32(s_base + half * 64, *reinterpret_cast<uint32_t(*)[32]>(v));
+                    tmem_ld_32x32b_x32(s_base + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 64; i += 2)
+                        h[half * 32 + i / 2] = gemm::cvt_f16x2(__uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive(s_empty + 8 * x);
+                const int valid = min(max(p.tokens - c * kBK, 0), kBK);
+                if (valid < kBK) // the last tile only: fp16 -inf past the stream's keys
+#pragma unroll
+                    for (int i = 0; i < kBK; i += 2) {
+                        if (i >= valid)
+                            h[i / 2] = (h[i / 2] & 0xFFFF0000u) | 0xFC00u;
+                        if (i + 1 >= valid)
+                            h[i / 2] = (h[i / 2] & 0x0000FFFFu) | 0xFC000000u;
+                    }
+                // Tile maximum: packed fp16 maxima over eight independent chains.
+                uint32_t pm[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    pm[j] = h[j];
+#pragma unroll
+                for (int i = 8; i < kBK / 2; ++i)
+                    pm[i & 7] = max_f16x2(pm[i & 7], h[i]);
+                const uint32_t m2 = max_f16x2(max_f16x2(max_f16x2(pm[0], pm[1]), max_f16x2(pm[2], pm[3])),
+                                              max_f16x2(max_f16x2(pm[4], pm[5]), max_f16x2(pm[6], pm[7])));
+                const float tm = fmaxf(h2f(static_cast<uint16_t>(m2 & 0xFFFFu)), h2f(static_cast<uint16_t>(m2 >> 16)));
+                // Raise the running maximum on the first tile, or when the tile's
+                // maximum exceeds it by more than 2^kLazy in exp; alpha rescales what
+                // was summed (and accumulated in O) against the old maximum.
+                float alpha = 1.0f;
+                bool raised = false;
+                if (m == -INFINITY || (tm - m) * kLog2e > kLazy) {
+                    raised = m != -INFINITY;
+                    alpha = raised ? fast_exp2((m - tm) * kLog2e) : 0.0f;
+                    l *= alpha;
+                    m = tm;
+                }
+                // P.V of the previous tile is done: P is free and O holds this item's
+                // tiles 0 .. c - 1 against the old maximum.
+                wait_all(p_empty + 8 * x, (cc & 1u) ^ 1u, kSiteProducerEmpty);
+                if (!ok)
+                    break;
+                if (c > 0 && __any_sync(0xffffffffu, raised)) {
+                    // Scale the raised rows of O (the other rows by 1: the TMEM
+                    // access is warp-wide).
+                    tc_fence_after();
+                    uint32_t o[kDim];
+                    tmem_ld_32x32b_x32(o_base, *reinterpret_cast<uint32_t(*)[32]>(o));
+                    tmem_ld_32x32b_x32(o_base + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
+                    tmem_wait_ld();
+                    const float f = raised ? alpha : 1.0f;
+#pragma unroll
+                    for (int i = 0; i < kDim; ++i)
+                        o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+                    tmem_st_32x32b_x32(o_base, *reinterpret_cast<const uint32_t(*)[32]>(o));
+                    tmem_st_32x32b_x32(o_base + 32, *reinterpret_cast<const uint32_t(*)[32]>(o + 32));
+                }
+                // P = half(exp(s - m)) with packed fp32 pairs; the row sum takes the
+                // unrounded exponentials (four partial pairs keep the chains short).
+                uint64_t ps[4] = {0, 0, 0, 0};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        float d0, d1;
+                        sub_f16x2_f32(h[q * 16 + i], m, d0, d1);
+                        const uint64_t e = mul_f32x2(f2_bits(d0, d1), log2e2);
+                        const float e0 = fast_exp2(lo_f32(e)), e1 = fast_exp2(hi_f32(e));
+                        ps[i & 3] = add_f32x2(ps[i & 3], f2_bits(e0, e1));
+                        pk[i] = gemm::cvt_f16x2(e0, e1);
+                    }
+                    tmem_st_32x32b_x16(p_base + q * 16, pk);
+                }
+                l += ((lo_f32(ps[0]) + hi_f32(ps[0])) + (lo_f32(ps[1]) + hi_f32(ps[1]))) +
+                     ((lo_f32(ps[2]) + hi_f32(ps[2])) + (lo_f32(ps[3]) + hi_f32(ps[3])));
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive(p_full + 8 * x);
+            }
+            if (!ok)
+                break;
+            // ---- epilogue: out = half(O / sum) for the row's 64 dims ----
+            const float inv = __frcp_rn(l);
+            wait_all(o_full + 8 * x, local & 1u, kSiteEpilogueAccFull);
+            if (!ok)
+                break;
+            tc_fence_after();
+            uint32_t o[kDim];
+            tmem_ld_32x32b_x32(o_base, *reinterpret_cast<uint32_t(*)[32]>(o));
+            tmem_ld_32x32b_x32(o_base + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
             tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
             if (lane == 0)
-                mbar_arrive(s_empty + 8 * b);
+                mbar_arrive(o_empty + 8 * x); // the next item's P.V MMAs may overwrite O
+            const int token = w.q0 + x * kBQ + row;
+            if (token < p.tokens) {
+                const size_t idx = static_cast<size_t>(w.row_base + token) * (p.heads * kDim) + w.head * kDim;
+                uint32_t hy[kDim / 2];
+                const uint64_t inv2 = f2_bits(inv, inv);
 #pragma unroll
-            for (int i = 0; i < kCols; i += 2)
-                h[i / 2] = gemm::cvt_f16x2(__uint_as_float(v[i]), __uint_as_float(v[i + 1]));
-            const int valid = min(max(p.tokens - c * kBK - col0, 0), kCols);
-            if (valid < kCols) // keys past the stream's tokens (the last tile only): fp16 -inf
-#pragma unroll
-                for (int i = 0; i < kCols; i += 2) {
-                    if (i >= valid)
-                        h[i / 2] = (h[i / 2] & 0xFFFF0000u) | 0xFC00u;
-                    if (i + 1 >= valid)
-                        h[i / 2] = (h[i / 2] & 0x0000FFFFu) | 0xFC000000u;
+                for (int i = 0; i < kDim / 2; ++i) {
+                    const uint64_t y = mul_f32x2(f2_bits(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1])), inv2);
+                    hy[i] = gemm::cvt_f16x2(lo_f32(y), hi_f32(y));
                 }
-        };
-        int u_all = 0, c_all = 0; // score tiles and P tiles consumed over all items
-        for (int it = blockIdx.x, local = 0; it < items; it += gridDim.x, ++local) {
-        const Item w = item_of(it);
-        float m = -INFINITY; // the row's running maximum (the same in all parts)
-        float l = 0.0f;      // this part's sum of exp(s - m)
-        for (int c = 0; c < nt; ++c) {
-            const int u = u_all++;
-            uint32_t h[kCols / 2];
-            load_scores(u, c, h);
-            // Tile maximum: packed fp16 maxima over this part, then over the parts.
-            uint32_t pm[4];
+                if (p.out) {
+                    uint4 *dst = reinterpret_cast<uint4 *>(p.out + idx);
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-                pm[j] = h[j];
+                    for (int j = 0; j < kDim / 8; ++j)
+                        dst[j] = make_uint4(hy[4 * j], hy[4 * j + 1], hy[4 * j + 2], hy[4 * j + 3]);
+                }
+                if (p.codes) {
+                    const float scale = p.code_scale_ptr ? *p.code_scale_ptr : p.code_scale;
+                    const float recip = p.code_scale_ptr ? __frcp_rn(scale) : p.code_recip;
+                    const uint64_t neg_scale2 = f2_bits(-scale, -scale), recip2 = f2_bits(recip, recip);
+                    uint32_t qc[kDim / 4];
 #pragma unroll
-            for (int i = 4; i < kCols / 2; ++i)
-                pm[i & 3] = max_f16x2(pm[i & 3], h[i]);
-            const uint32_t m2 = max_f16x2(max_f16x2(pm[0], pm[1]), max_f16x2(pm[2], pm[3]));
-            float *xm = tile_max + (u & 1) * (kSplit * kBQ);
-            xm[part * kBQ + row] =
-                fmaxf(h2f(static_cast<uint16_t>(m2 & 0xFFFFu)), h2f(static_cast<uint16_t>(m2 >> 16)));
-            named_barrier_sync(3 + quarter, kSplit * 32);
-            float tm = xm[row];
+                    for (int j = 0; j < kDim / 4; ++j)
+                        qc[j] = (e4m3x2_quotient(hy[2 * j], neg_scale2, recip2) & 0xFFFFu) |
+                                (e4m3x2_quotient(hy[2 * j + 1], neg_scale2, recip2) << 16);
+                    uint4 *dst = reinterpret_cast<uint4 *>(p.codes + idx);
 #pragma unroll
-            for (int j = 1; j < kSplit; ++j)
-                tm = fmaxf(tm, xm[j * kBQ + row]);
-            // Raise the running maximum on the first tile, or when the tile's
-            // maximum exceeds it by more than 2^kLazy in exp; alpha rescales what
-            // was summed (and accumulated in O) against the old maximum.
-            float alpha = 1.0f;
-            bool raised = false;
-            if (m == -INFINITY || (tm - m) * kLog2e > kLazy) {
-                raised = m != -INFINITY;
-                alpha = raised ? fast_exp2((m - tm) * kLog2e) : 0.0f;
-                l *= alpha;
-                m = tm;
+                    for (int j = 0; j < kDim / 16; ++j)
+                        dst[j] = make_uint4(qc[4 * j], qc[4 * j + 1], qc[4 * j + 2], qc[4 * j + 3]);
+                }
             }
-            // P = half(exp(s - m)) with packed fp32 pairs; the row sum takes the
-            // unrounded exponentials (four partial pairs keep the chains short).
-            uint32_t pk[kCols / 2];
-            uint64_t ps[4] = {0, 0, 0, 0};
-            const uint64_t log2e2 = f2_bits(kLog2e, kLog2e);
-#pragma unroll
-            for (int i = 0; i < kCols / 2; ++i) {
-                float d0, d1;
-                sub_f16x2_f32(h[i], m, d0, d1);
-                const uint64_t x = mul_f32x2(f2_bits(d0, d1), log2e2);
-                const float e0 = fast_exp2(lo_f32(x)), e1 = fast_exp2(hi_f32(x));
-                ps[i & 3] = add_f32x2(ps[i & 3], f2_bits(e0, e1));
-                pk[i] = gemm::cvt_f16x2(e0, e1);
-            }
-            l += ((lo_f32(ps[0]) + hi_f32(ps[0])) + (lo_f32(ps[1]) + hi_f32(ps[1]))) +
-                 ((lo_f32(ps[2]) + hi_f32(ps[2])) + (lo_f32(ps[3]) + hi_f32(ps[3])));
-            const uint32_t pb = c_all & 1;
-            wait_all(p_empty + 8 * pb, ((c_all >> 1) & 1u) ^ 1u, kSiteProducerEmpty);
-            if (c > 0 && __any_sync(0xffffffffu, raised)) {
-                // O holds this item's P.V of tiles 0 .. c - 1 against the old maximum:
-                // once the last of those MMAs is done, scale this warp's columns of
-                // the raised rows (the other rows by 1: the TMEM access is warp-wide).
-                wait_all(p_empty + 8 * (pb ^ 1u), ((c_all - 1) >> 1) & 1u, kSiteProducerEmpty);
-                tc_fence_after();
-                uint32_t o[kOutCols];
-                tmem_ld_32x32b_x16(o_base, o);
-                tmem_wait_ld();
-                const float f = raised ? alpha : 1.0f;
-#pragma unroll
-                for (int i = 0; i < kOutCols; ++i)
-                    o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-                tmem_st_32x32b_x16(o_base, o);
-                tmem_wait_st();
-                tc_fence_before();
-            }
-            // columns col0 .. col0 + kCols - 1 sit in 64-key half col0 / 64, 16-byte chunks from (col0 % 64) / 8
-            const uint32_t prow = sP + pb * kPBytes + (col0 / 64) * (kPBytes / 2) + row * 128;
-#pragma unroll
-            for (int j = 0; j < kCols / 8; ++j) {
-                const int cc = (col0 % 64) / 8 + j;
-                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(prow + ((cc ^ (row & 7)) << 4)),
-                             "r"(pk[4 * j]), "r"(pk[4 * j + 1]), "r"(pk[4 * j + 2]), "r"(pk[4 * j + 3])
-                             : "memory");
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0)
-                mbar_arrive(p_full + 8 * pb);
-            ++c_all;
-        }
-        // ---- the row sum over the parts (one running maximum for all of them) ----
-        // Sums alternate by item parity: a warp overwrites this item's buffer two
-        // items later, after every warp has read it and passed the next barrier.
-        float *sum = part_sum + (local & 1) * (kSplit * kBQ);
-        sum[part * kBQ + row] = l;
-        named_barrier_sync(2, kSoftWarps * 32);
-        float ll = 0.0f;
-#pragma unroll
-        for (int j = 0; j < kSplit; ++j)
-            ll += sum[j * kBQ + row];
-        const float inv = __frcp_rn(ll);
-        // ---- epilogue: out = half(O / sum), this warp's kOutCols of the 64 dims ----
-        wait_all(o_full, local & 1u, kSiteEpilogueAccFull);
-        tc_fence_after();
-        uint32_t o[kOutCols];
-        static_assert(kOutCols == 16, "output columns per softmax warp");
-        tmem_ld_32x32b_x16(o_base, o);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0)
-            mbar_arrive(o_empty); // the next item's P.V MMAs may overwrite O
-        const int token = w.q0 + row;
-        if (ok && token < p.tokens) {
-            const float scale = p.code_scale_ptr ? *p.code_scale_ptr : p.code_scale;
-            const float recip = p.code_scale_ptr ? __frcp_rn(scale) : p.code_recip;
-            const uint64_t neg_scale2 = f2_bits(-scale, -scale), recip2 = f2_bits(recip, recip);
-            const size_t idx = static_cast<size_t>(w.row_base + token) * (p.heads * kDim) + w.head * kDim + part * kOutCols;
-            uint32_t h[kOutCols / 2];
-            const uint64_t inv2 = f2_bits(inv, inv);
-#pragma unroll
-            for (int i = 0; i < kOutCols / 2; ++i) {
-                const uint64_t y = mul_f32x2(f2_bits(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1])), inv2);
-                h[i] = gemm::cvt_f16x2(lo_f32(y), hi_f32(y));
-            }
-            if (p.out) {
-                uint4 *dst = reinterpret_cast<uint4 *>(p.out + idx);
-#pragma unroll
-                for (int j = 0; j < kOutCols / 8; ++j)
-                    dst[j] = make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
-            }
-            if (p.codes) {
-                uint32_t q[kOutCols / 4];
-#pragma unroll
-                for (int j = 0; j < kOutCols / 4; ++j)
-                    q[j] = (e4m3x2_quotient(h[2 * j], neg_scale2, recip2) & 0xFFFFu) |
-                           (e4m3x2_quotient(h[2 * j + 1], neg_scale2, recip2) << 16);
-                uint4 *dst = reinterpret_cast<uint4 *>(p.codes + idx);
-#pragma unroll
-                for (int j = 0; j < kOutCols / 16; ++j)
-                    dst[j] = make_uint4(q[4 * j], q[4 * j + 1], q[4 * j + 2], q[4 * j + 3]);
-            }
-        }
         }
     }
 
@@ -3882,6 +3860,7 @@ cudaError_t launch_self_attention(const SelfAttentionLaunch &L, cudaStream_t str
     p.tokens = L.tokens;
     p.heads = L.heads;
     p.qblocks = (L.tokens + sattn::kBQ - 1) / sattn::kBQ;
+    p.qpairs = (p.qblocks + 1) / 2;
     p.nchunks = (L.tokens + sattn::kChunk - 1) / sattn::kChunk;
     p.out = L.out;
     const uint16_t c = __half_as_ushort(__float2half_rn(static_cast<float>(std::pow(double(sattn::kDim), -0.25))));
@@ -3904,8 +3883,8 @@ cudaError_t launch_self_attention(const SelfAttentionLaunch &L, cudaStream_t str
     if (attr != cudaSuccess)
         return attr;
     cudaLaunchConfig_t config{};
-    // Persistent: one CTA per SM walks the (stream, head, query block) items.
-    const int64_t items = static_cast<int64_t>(L.streams) * L.heads * p.qblocks;
+    // Persistent: one CTA per SM walks the (stream, head, query-tile pair) items.
+    const int64_t items = static_cast<int64_t>(L.streams) * L.heads * p.qpairs;
     config.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>(items, sm_count())));
     config.blockDim = dim3(fattn::kThreads);
     config.dynamicSmemBytes = fattn::kSmemBytes;
