@@ -2170,10 +2170,13 @@ constexpr int kQBytes = 2 * kTile;    // an item's two Q tiles
 constexpr int kScaleWarp0 = 2;
 constexpr int kScaleWarps = 2;
 constexpr int kSoftWarp0 = 4; // slot A: warps 4-7, slot B: 8-11 (warp % 4 = TMEM lane quarter)
+constexpr int kSlotThreads = 4 * 32;
 constexpr int kThreads = 12 * 32;
+constexpr uint32_t kTurnBar0 = 1; // named barriers 1 (slot A's turn) and 2 (slot B's)
 constexpr int kOffK = 2 * kQBytes; // Q double-buffered by item parity
 constexpr int kOffV = kOffK + kKStages * kTile;
-constexpr int kOffBar = kOffV + kVStages * kTile;
+constexpr int kOffRowMax = kOffV + kVStages * kTile; // float [slot][row]
+constexpr int kOffBar = kOffRowMax + 2 * kBQ * 4;
 constexpr int kBars = 6 + 3 * kKStages + 2 * kVStages + 12 + 1;
 constexpr int kSmemBytes = kOffBar + 8 * kBars + 16 + 1024;
 // The running maximum is raised only when a tile's maximum exceeds it by more than
@@ -2349,9 +2352,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             int u = 0, cc = 0; // score tiles and P tiles issued over all items (per slot)
             int local = 0;
+            // Descriptors are computed once: a tile's descriptor is the base one plus
+            // the tile's byte offset / 16 (the start-address field), so each MMA
+            // issues with one add per operand.  The issuing thread shares its SMSP
+            // with softmax warps, and every instruction it saves shortens the
+            // tensor core's wait for work.
+            const uint64_t d_q = smem_desc_k_sw128(sQ), d_k = smem_desc_k_sw128(sK), d_v = smem_desc_mn_sw128(sV);
             auto pv_mma = [&](int first) { // P.V of P tile cc for both slots
                 const int vs = cc % kVStages;
                 ok = ok && mbar_wait(v_full + 8 * vs, (cc / kVStages) & 1u, kSiteMmaFull);
+                const uint64_t b0 = d_v + static_cast<uint64_t>(vs * (kTile >> 4));
                 for (int x = 0; x < 2 && ok; ++x) {
                     if (first)
                         ok = mbar_wait(o_empty + 8 * x, (local & 1u) ^ 1u, kSiteMmaAccEmpty);
@@ -2359,11 +2369,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!ok)
                         break;
                     tc_fence_after();
+                    const uint32_t d = tmem + kTmemO + x * kDim, a = tmem + kTmemP + x * (kBK / 2);
+                    if (first)
+                        mma_f16_ts_c<0>(d, a, b0, id_o);
+                    else
+                        mma_f16_ts_c<1>(d, a, b0, id_o);
 #pragma unroll
-                    for (int k = 0; k < kBK / 16; ++k)
-                        mma_f16_ts(tmem + kTmemO + x * kDim, tmem + kTmemP + x * (kBK / 2) + k * 8,
-                                   smem_desc_mn_sw128(sV + vs * kTile + k * 16 * 128), id_o,
-                                   (first == 0 || k != 0) ? 1u : 0u);
+                    for (int k = 1; k < kBK / 16; ++k) // 16 keys: 8 TMEM columns of P, 16 rows (2 KB) of V
+                        mma_f16_ts_c<1>(d, a + k * 8, b0 + static_cast<uint64_t>(k * (2048 >> 4)), id_o);
                     mma_commit(p_empty + 8 * x);
                 }
                 if (ok)
@@ -2372,7 +2385,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             };
             for (int it = blockIdx.x; ok && it < items; it += gridDim.x, ++local) {
                 const uint32_t qb = local & 1;
-                const uint32_t sQi = sQ + qb * kQBytes;
                 ok = mbar_wait(q_ready + 8 * qb, (local >> 1) & 1u, kSiteMmaFull);
                 for (int c = 0; ok && c < nt; ++c) {
                     const int ks = u % kKStages;
@@ -2382,10 +2394,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (!ok)
                             break;
                         tc_fence_after();
+                        const uint32_t d = tmem + kTmemS + x * kBK;
+                        const uint64_t a = d_q + static_cast<uint64_t>((qb * kQBytes + x * kTile) >> 4);
+                        const uint64_t b = d_k + static_cast<uint64_t>(ks * (kTile >> 4));
+                        mma_f16_c<0>(d, a, b, id_s);
 #pragma unroll
-                        for (int k = 0; k < kDim / 16; ++k)
-                            mma_f16(tmem + kTmemS + x * kBK, smem_desc_k_sw128(sQi + x * kTile + k * 32),
-                                    smem_desc_k_sw128(sK + ks * kTile + k * 32), id_s, k != 0);
+                        for (int k = 1; k < kDim / 16; ++k) // 16 dims: 32 bytes along the 128-byte rows
+                            mma_f16_c<1>(d, a + 2 * k, b + 2 * k, id_s);
                         mma_commit(s_full + 8 * x);
                     }
                     if (!ok)
@@ -2461,25 +2476,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t s_base = tmem + lanes + kTmemS + x * kBK;
         const uint32_t p_base = tmem + lanes + kTmemP + x * (kBK / 2);
         const uint32_t o_base = tmem + lanes + kTmemO + x * kDim;
+        // The two slots take turns at the exponentials: slot x waits for its turn
+        // barrier (the other slot's arrival) before its exponentials and hands the
+        // turn over after them, so one slot's score loads, maxima and hand-overs
+        // run while the other keeps the MUFU busy.  Slot A takes the first turn.
+        const uint32_t my_turn = kTurnBar0 + x, their_turn = kTurnBar0 + (x ^ 1);
+        const uint32_t m_slot = sb + kOffRowMax + (x * kBQ + row) * 4; // this row's running maximum
         bool ok = true;
         // Every lane polls the barrier (one shared word, the same answer for all
         // lanes); the warp reconverges before the warp-wide TMEM instructions.
+        // After a wait has given up, later waits return at once, but every warp
+        // still walks every tile (its TMEM accesses stay inside this CTA's
+        // allocation) so that the turn barriers always pair up.
         auto wait_all = [&](uint32_t bar, uint32_t parity, int site) {
             ok = ok && mbar_wait(bar, parity, site);
             __syncwarp();
         };
         const uint64_t log2e2 = f2_bits(kLog2e, kLog2e);
         int u = 0, cc = 0;
-        for (int it = blockIdx.x, local = 0; ok && it < items; it += gridDim.x, ++local) {
+        for (int it = blockIdx.x, local = 0; it < items; it += gridDim.x, ++local) {
             const Item w = item_of(it);
             float m = -INFINITY; // the row's running maximum
             float l = 0.0f;      // the row's sum of exp(s - m)
-            for (int c = 0; ok && c < nt; ++c, ++u, ++cc) {
+            for (int c = 0; c < nt; ++c, ++u, ++cc) {
                 // The row's 128 scores of tile c, rounded to fp16 (the MatMul edge);
                 // keys past the stream's tokens are -inf.  Frees the slot's S.
                 wait_all(s_full + 8 * x, u & 1u, kSiteEpilogueAccFull);
-                if (!ok)
-                    break;
                 tc_fence_after();
                 uint32_t h[kBK / 2];
 #pragma unroll
@@ -2530,9 +2552,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // P.V of the previous tile is done: P is free and O holds this item's
                 // tiles 0 .. c - 1 against the old maximum.
                 wait_all(p_empty + 8 * x, (cc & 1u) ^ 1u, kSiteProducerEmpty);
-                if (!ok)
-                    break;
-                if (c > 0 && __any_sync(0xffffffffu, raised)) {
+                if (ok && c > 0 && __any_sync(0xffffffffu, raised)) {
                     // Scale the raised rows of O (the other rows by 1: the TMEM
                     // access is warp-wide).
                     tc_fence_after();
@@ -2547,6 +2567,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_st_32x32b_x32(o_base, *reinterpret_cast<const uint32_t(*)[32]>(o));
                     tmem_st_32x32b_x32(o_base + 32, *reinterpret_cast<const uint32_t(*)[32]>(o + 32));
                 }
+                // The exponentials read m back from shared memory after the turn
+                // barrier, so no compiler stage can hoist them above it; the hand-over
+                // waits for the P stores, so none can sink below it.
+                asm volatile("st.shared.f32 [%0], %1;" ::"r"(m_slot), "f"(m) : "memory");
+                if (x == 1 || u > 0)
+                    turn_wait(my_turn, 2 * kSlotThreads);
+                asm volatile("ld.volatile.shared.f32 %0, [%1];" : "=f"(m) : "r"(m_slot) : "memory");
                 // P = half(exp(s - m)) with packed fp32 pairs; the row sum takes the
                 // unrounded exponentials (four partial pairs keep the chains short).
                 uint64_t ps[4] = {0, 0, 0, 0};
@@ -2564,21 +2591,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     tmem_st_32x32b_x16(p_base + q * 16, pk);
                 }
+                tmem_wait_st();
+                turn_pass(their_turn, 2 * kSlotThreads);
                 l += ((lo_f32(ps[0]) + hi_f32(ps[0])) + (lo_f32(ps[1]) + hi_f32(ps[1]))) +
                      ((lo_f32(ps[2]) + hi_f32(ps[2])) + (lo_f32(ps[3]) + hi_f32(ps[3])));
-                tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0)
                     mbar_arrive(p_full + 8 * x);
             }
-            if (!ok)
-                break;
             // ---- epilogue: out = half(O / sum) for the row's 64 dims ----
             const float inv = __frcp_rn(l);
             wait_all(o_full + 8 * x, local & 1u, kSiteEpilogueAccFull);
-            if (!ok)
-                break;
             tc_fence_after();
             uint32_t o[kDim];
             tmem_ld_32x32b_x32(o_base, *reinterpret_cast<uint32_t(*)[32]>(o));
@@ -2589,7 +2613,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0)
                 mbar_arrive(o_empty + 8 * x); // the next item's P.V MMAs may overwrite O
             const int token = w.q0 + x * kBQ + row;
-            if (token < p.tokens) {
+            if (ok && token < p.tokens) {
                 const size_t idx = static_cast<size_t>(w.row_base + token) * (p.heads * kDim) + w.head * kDim;
                 uint32_t hy[kDim / 2];
                 const uint64_t inv2 = f2_bits(inv, inv);
@@ -2620,6 +2644,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
+        // Slot A takes slot B's last hand-over, so both turn barriers end complete.
+        if (x == 0 && u > 0)
+            turn_wait(my_turn, 2 * kSlotThreads);
     }
 
     tc_fence_before();

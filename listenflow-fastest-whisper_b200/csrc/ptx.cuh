@@ -180,6 +180,19 @@ __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// Producer/consumer hand-over on a named barrier: the consumer waits in
+// turn_wait, the producer signals with turn_pass (it does not wait).  These use
+// the non-.aligned barrier.sync / barrier.arrive: measured on B200, the .aligned
+// bar.sync / bar.arrive pair let a consumer pass before its producer arrived.
+__device__ __forceinline__ void turn_wait(uint32_t id, uint32_t threads)
+{
+    asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ void turn_pass(uint32_t id, uint32_t threads)
+{
+    asm volatile("barrier.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // ---- tcgen05 ---------------------------------------------------------------
 
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t columns)
@@ -354,6 +367,27 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64
                  "setp.ne.b32 p, %4, 0;\n\t"
                  "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
                  "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+                 : "memory");
+}
+
+// mma_f16 / mma_f16_ts with the accumulate flag fixed at compile time (the
+// predicate then costs no instruction at issue).
+template <uint32_t kAccumulate>
+__device__ __forceinline__ void mma_f16_c(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc)
+{
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+                 "l"(a_desc), "l"(b_desc), "r"(idesc), "n"(kAccumulate)
+                 : "memory");
+}
+template <uint32_t kAccumulate>
+__device__ __forceinline__ void mma_f16_ts_c(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc)
+{
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+                 "r"(a_tmem), "l"(b_desc), "r"(idesc), "n"(kAccumulate)
                  : "memory");
 }
 
