@@ -671,8 +671,8 @@ def run_cross_attention(fp8, native, device, steps: int, seed: int, layers: int 
 def run_self_attention(fp8, native, device, steps: int, seed: int):
     """Encoder self-attention for one layer at C2 shapes (8 streams x 1500 tokens x
     20 heads), read in place from a fused QKV output.  Work: 4 * tokens^2 * 64 flops
-    per (stream, head) (QK^T and P.V); the kernel recomputes QK^T once more for the
-    exact fp16 probabilities, which the rate does not count."""
+    per (stream, head) (QK^T and P.V), counted over the real tokens (the kernel's
+    128-key tiles pad 1500 to 1536)."""
     import torch
 
     streams, tokens, heads = 8, 1500, 20
@@ -699,8 +699,8 @@ def run_self_attention(fp8, native, device, steps: int, seed: int):
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     peak = float(peaks.get("bf16_tflops", 1590.0))
     return {"workload": "encoder self-attention, 8 streams x 1500 tokens x 20 heads x 64, one layer, "
-                        "out_proj E4M3 codes out (tcgen05 kind::f16 MMAs, exact two-pass softmax; the second QK^T "
-                        "pass is not counted in the flops)",
+                        "out_proj E4M3 codes out (tcgen05 kind::f16 MMAs, one-pass online softmax over two "
+                        "128-query tiles per CTA sharing K/V, P.V with P read from tensor memory)",
             "ms": round(ms, 4), "flops": flops, "value": round(tflops, 1), "unit": "TFLOP/s (QK^T + P.V)",
             "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak,
                          "peak_source": "measured dense bf16 of MEASURED_PEAKS.json (fp16 runs at the bf16 rate)",
