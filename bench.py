@@ -86,7 +86,8 @@ def parse_args(argv=None):
                    help="timed replays of the C3 decoder-step graph (0 skips it)")
     p.add_argument("--decoder-layers", type=int, default=32,
                    help="decoder layers in the C3 step (32 is the measured configuration)")
-    p.add_argument("--only", choices=("all", "c4", "c2", "c5", "fp16", "ln", "attention", "self_attention", "decoder"),
+    p.add_argument("--only", choices=("all", "c4", "c1", "c2", "c5", "fp16", "ln", "attention", "self_attention",
+                                      "decoder"),
                    default="all",
                    help="run one section alone and print its line (profiling): 'c4' the headline encoder "
                         "forward without the secondary sections, 'c2' the timed C2 linear-set steps, 'ln' the "
@@ -550,6 +551,9 @@ def run_section_only(args, local_rank):
     elif args.only == "c5":
         result = run_c5(device)
         result.update(metric="C5 streaming transcription audio-s/s per GPU")
+    elif args.only == "c1":
+        result = run_c1(fp8, native, device)
+        result.update(metric="C1 fc1 FP8 Q/DQ linear TFLOP/s")
     elif args.only == "fp16":
         result = run_fp16_plugins(device)
         result.update(metric="fp16 projection plugins GB/s, ours and the reference's kernels")
@@ -558,6 +562,54 @@ def run_section_only(args, local_rank):
         result.update(metric="encoder self-attention TFLOP/s")
     result.update(n_gpus=1, higher_is_better=True, impl="ours")
     return result
+
+
+def run_c1(fp8, native, device, reps: int = 50):
+    """Config 1: one encoder fc1 Q/DQ linear, X [1500, 1280] ~ N(0,1),
+    W [5120, 1280] ~ N(0,0.02), b ~ N(0,0.02) drawn from torch.Generator().manual_seed(0),
+    dynamic activation scale amax(X)/448 (computed on the device), per-row weight
+    scales, GELU with the fp16 edges.  A step = dynamic scale + quantize + fc1; the
+    weight codes are prepared once (TensorRT folds the weight Q at build time).  L2
+    is flushed before every step, outside the events."""
+    import torch
+
+    gen = torch.Generator().manual_seed(0)
+    x = torch.randn(1500, 1280, generator=gen).half().to(device)
+    w = (torch.randn(5120, 1280, generator=gen) * 0.02).half().to(device)
+    b = (torch.randn(5120, generator=gen) * 0.02).half().to(device)
+    qw = fp8.QuantizedWeight.from_half(w, b)
+    codes = torch.empty((1500, 1280), dtype=torch.uint8, device=device)
+    y = torch.empty((1500, 5120), dtype=torch.float16, device=device)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+
+    def step():
+        scale, _ = fp8.dynamic_scale(x)
+        fp8.quantize(x, scale, out=codes)
+        fp8.linear(codes, qw.codes, qw.scales, scale, bias=qw.bias, gelu=True, out=y)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(reps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    if native.device_error() != 0:
+        raise RuntimeError("device-side wait timed out in the C1 section")
+    ms = statistics.median(ts)
+    flops = 2 * 1500 * 1280 * 5120
+    fp8_peak, src = read_peaks()
+    tflops = flops / (ms / 1e3) / 1e12
+    return {"workload": "C1: fc1 FP8 Q/DQ linear M=1500 K=1280 N=5120 + bias + GELU, dynamic activation scale; "
+                        "step = amax/448 + quantize + GEMM (3 launches), L2 flushed before every step",
+            "ms": round(ms, 4), "flops": flops, "value": round(tflops, 1), "unit": "TFLOP/s",
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": fp8_peak, "peak_source": src,
+                         "unit": "TFLOP/s", "frac": round(tflops / fp8_peak, 4)}}
 
 
 def run_ln_producer(fp8, native, device, reps: int, seed: int):
@@ -1399,7 +1451,7 @@ def main(argv=None):
     rank, local_rank, world = dist_env()
     if args.impl == "reference":
         result = run_reference(args, rank, world)
-    elif args.only in ("decoder", "ln", "attention", "self_attention", "c2", "c5", "fp16"):
+    elif args.only in ("decoder", "ln", "attention", "self_attention", "c1", "c2", "c5", "fp16"):
         result = run_section_only(args, local_rank)
     else:
         result, device = run_c4(args, rank, local_rank, world)
@@ -1414,6 +1466,7 @@ def main(argv=None):
             c2 = result["c2_linear_set"]
             c2["roofline"]["frac_of_scaled_mm_peak"] = round(
                 c2["roofline"]["achieved"] / result["fp8_peak_scaled_mm_tflops"], 4)
+            result["c1_fc1"] = run_c1(fp8, native, device)
             result["ln_producer"] = run_ln_producer(fp8, native, device, 20, seed=31)
             result["cross_attention"] = run_cross_attention(fp8, native, device, 10, seed=41)
             result["self_attention"] = run_self_attention(fp8, native, device, 10, seed=51)

@@ -219,16 +219,18 @@ class Encoder:
     lffw_cross_attention reads.  The returned tensors are the plan's own buffers,
     overwritten by the next forward.
 
-    Streams run through the layers in slices of `chunk` streams (default 8) that
-    share one set of activation buffers: a slice's activations (a layer's QKV
-    output is 92 MB at 8 streams) stay largely in the 126 MB L2 between the
-    kernels that write and read them, and the buffers stay small."""
+    Streams run through the layers in slices of `chunk` streams (default 16) that
+    share one set of activation buffers: a slice's activations stay largely in the
+    126 MB L2 between the kernels that write and read them, while each launch still
+    has enough tiles that its last partial wave is a small part of it.  Measured on
+    the 64-stream forward (one B200): chunk 8 140.3 ms, 16 137.2 ms, 32 139.1 ms,
+    64 145.5 ms, with bit-identical states."""
 
     def __init__(self, weights: EncoderWeights, scales: Mapping[str, float], streams: int, device=None,
                  chunk: int | None = None):
         c = weights.config
         self.config, self.weights, self.streams = c, weights, streams
-        self.chunk = max(1, min(streams, chunk if chunk is not None else 8))
+        self.chunk = max(1, min(streams, chunk if chunk is not None else 16))
         self.scales = _scales_for(c, scales)
         device = torch.device(device) if device is not None else weights.positions.device
         d, f, t = c.d_model, c.ffn, c.positions
