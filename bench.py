@@ -633,6 +633,9 @@ def run_ln_producer(fp8, native, device, reps: int, seed: int):
         _, y, _ = fp8.layer_norm(x, gamma, beta, residual=r, want_sum=True)
         fp8.quantize(y, 0.01)
 
+    def codes_only():  # the encoder's form: the sum comes from the GEMM epilogue
+        fp8.layer_norm(x, gamma, beta, code_scale=0.01, want_y=False)
+
     def timed(fn):
         for _ in range(3):
             fn()
@@ -648,7 +651,7 @@ def run_ln_producer(fp8, native, device, reps: int, seed: int):
             ts.append(e0.elapsed_time(e1))
         return statistics.median(ts)
 
-    t_fused, t_sep = timed(fused), timed(separate)
+    t_fused, t_sep, t_codes = timed(fused), timed(separate), timed(codes_only)
     if native.device_error() != 0:
         raise RuntimeError("device-side wait timed out in the LayerNorm section")
     elems = M * D
@@ -658,6 +661,10 @@ def run_ln_producer(fp8, native, device, reps: int, seed: int):
     return {"workload": "LayerNorm producer, 12000 x 1280 fp16 + residual -> fp16 sum + E4M3 codes",
             "fused_ms": round(t_fused, 4), "separate_ms": round(t_sep, 4),
             "separate": "LayerNorm writing fp16 y (and the sum), then lffw_fp8_quantize of y",
+            "codes_only_ms": round(t_codes, 4),
+            "codes_only_gbs": round(elems * 3 / (t_codes / 1e3) / 1e9, 1),
+            "codes_only": "the encoder's form: x in (the residual sum written by the previous GEMM's epilogue), "
+                          "E4M3 codes out, 3 bytes per element",
             "value": round(gbs, 1), "unit": "GB/s (algorithmic: 7 bytes per element)",
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm[0], "peak_source": hbm[1],
                          "unit": "GB/s", "frac": round(gbs / hbm[0], 4)},
@@ -850,9 +857,9 @@ def encoder_work(config, streams: int) -> dict:
     conv = 2 * streams * (config.frames * config.mels * 3 * d + t * d * 3 * d)
     attention = 4 * streams * config.layers * config.heads * t * t * 64
     rows = streams * t
-    # LayerNorm bytes: layer 0's first reads x only; the others read x + residual, and
-    # write the sum (2 + 2 + 2 bytes) and codes (1); the final one writes y and codes.
-    ln_bytes = rows * d * ((2 + 1) + (2 * config.layers - 1) * (2 + 2 + 2 + 1) + (2 + 2 + 2 + 1))
+    # LayerNorm bytes: the residual sums come from the GEMM epilogues, so every
+    # LayerNorm reads x (2 bytes) and writes codes (1); the final one also writes y (2).
+    ln_bytes = rows * d * (2 * config.layers * (2 + 1) + (2 + 2 + 1))
     mel_bytes = streams * config.mels * config.frames * (4 + 2)
     return {"fp8_gemm_kernel (kind::f8f6f4)": ("TFLOP/s", linears + cross),
             "fp8_gemm_kernel (fp16 conv mode, kind::f16)": ("TFLOP/s", conv),

@@ -24,7 +24,7 @@
 #include <stdint.h>
 
 #define LFFW_FP8_ABI_MAJOR 1
-#define LFFW_FP8_ABI_MINOR 6
+#define LFFW_FP8_ABI_MINOR 7
 #define LFFW_FP8_API __attribute__((visibility("default")))
 #if defined(__cplusplus)
 #define LFFW_FP8_NOEXCEPT noexcept
@@ -93,6 +93,12 @@ typedef struct lffw_fp8_linear_args {
     float next_scale;
     uint8_t *next_codes;
     int32_t w_layout; /* LFFW_WEIGHTS_*; absent (older struct_size) means ROW_MAJOR */
+    /* Optional fp16 [m, n] row-major, 16-byte aligned (absent in older struct_size
+     * means none): y = half(linear + residual), the graph's fp16 residual add after
+     * the linear's bias (cpp/src/network_graph.cpp:285-287), so the LayerNorm that
+     * follows reads one tensor instead of two.  Requires y, no GELU, no next_codes,
+     * n % 32 == 0 and row-major weights; y may be the residual itself. */
+    const uint16_t *residual;
 } lffw_fp8_linear_args;
 
 LFFW_FP8_API lffw_status lffw_fp8_linear(const lffw_fp8_linear_args *args,

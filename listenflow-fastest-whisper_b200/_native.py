@@ -60,6 +60,7 @@ class LinearArgs(ctypes.Structure):
         ("next_scale", ctypes.c_float),
         ("next_codes", ctypes.c_void_p),
         ("w_layout", ctypes.c_int32),
+        ("residual", ctypes.c_void_p),
     ]
 
 

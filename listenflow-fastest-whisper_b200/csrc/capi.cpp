@@ -85,6 +85,13 @@ int32_t weight_layout(const lffw_fp8_linear_args *a)
                                                                                          : LFFW_WEIGHTS_ROW_MAJOR;
 }
 
+// The residual field exists only in callers built against ABI 1.7+ headers.
+const uint16_t *linear_residual(const lffw_fp8_linear_args *a)
+{
+    return a->struct_size >= offsetof(lffw_fp8_linear_args, residual) + sizeof(a->residual) ? a->residual
+                                                                                           : nullptr;
+}
+
 lffw_status validate_linear(const lffw_fp8_linear_args *a)
 {
     if (a == nullptr)
@@ -114,6 +121,10 @@ lffw_status validate_linear(const lffw_fp8_linear_args *a)
         return LFFW_INVALID_ARGUMENT;
     if (layout == LFFW_WEIGHTS_SKINNY_TILES && a->m > lffw::kSmallMaxRows)
         return LFFW_INVALID_ARGUMENT;
+    const uint16_t *residual = linear_residual(a);
+    if (residual != nullptr && (a->y == nullptr || a->next_codes != nullptr || a->epilogue != LFFW_EPILOGUE_NONE ||
+                                a->n % 32 != 0 || layout != LFFW_WEIGHTS_ROW_MAJOR || !aligned16(residual)))
+        return LFFW_INVALID_ARGUMENT;
     return LFFW_SUCCESS;
 }
 
@@ -134,7 +145,9 @@ lffw_status run_linear(const lffw_fp8_linear_args *a, cudaStream_t stream)
     L.next_scale = a->next_scale;
     L.next_codes = a->next_codes;
     L.w_packed = weight_layout(a) == LFFW_WEIGHTS_SKINNY_TILES;
-    const bool small = a->m <= lffw::kSmallMaxRows;
+    L.residual = linear_residual(a);
+    // The residual add rides on the large-m GEMM's epilogue (which serves any m).
+    const bool small = a->m <= lffw::kSmallMaxRows && L.residual == nullptr;
     return from_cuda(small ? lffw::launch_fp8_skinny(L, stream) : lffw::launch_fp8_gemm(L, stream));
 }
 

@@ -222,7 +222,9 @@ enum : int {
     // a convolution layer's own bias, instead of the linear's fp16 bias edge.
     kEpiBiasF32 = 16,
     // After the GELU: y = fp16(y + pos[t]), the positional embedding of row t
-    // of its segment (network_graph.cpp:280-282).
+    // of its segment (network_graph.cpp:280-282).  Without kEpiSeg, pos is an
+    // [m, pos_ld] tensor read at the output's own row: the residual add of
+    // network_graph.cpp:285-287 after a linear's bias.
     kEpiPos = 32,
     // Rows form segments (streams) of p.seg_rows: tiles never straddle two
     // segments; A is read through 3-D maps (k, row, segment), one per
@@ -292,7 +294,7 @@ struct Params {
     int seg_rows, seg_tiles; // kEpiSeg: rows per segment, tiles per segment
     int kb_per_tap;          // kEpiSeg: K blocks per A map (convolution tap)
     int heads;               // kEpiHeads: H
-    const uint16_t *pos;     // kEpiPos: fp16 [seg_rows, pos_ld]
+    const uint16_t *pos;     // kEpiPos: fp16 [seg_rows, pos_ld] (segmented) or [m, pos_ld] (residual)
     int pos_ld;
     float act_scale;
     const float *act_scale_ptr;
@@ -3423,6 +3425,10 @@ cudaError_t run_gemm(const LinearLaunch &L, cudaStream_t stream)
     p.next_recip = L.next_codes ? static_cast<float>(1.0 / static_cast<double>(L.next_scale)) : 0.0f;
     p.next_lean = L.next_codes && lean_scale(L.next_scale) ? 1 : 0;
     p.kb_per_tap = p.num_kb;
+    if (C::kPos) {
+        p.pos = L.residual;
+        p.pos_ld = static_cast<int>(L.n);
+    }
     return launch_gemm_kernel<BN, EPI, kPair>(maps, p, stream);
 }
 
@@ -3528,9 +3534,11 @@ template <int BN, bool kPair>
 cudaError_t run_gemm_epilogue(const LinearLaunch &L, cudaStream_t stream)
 {
     using namespace gemm;
-    const int epi = (L.gelu ? kEpiGelu : 0) | (L.y ? kEpiY : 0) | (L.next_codes ? kEpiCodes : 0);
+    const int epi = (L.gelu ? kEpiGelu : 0) | (L.y ? kEpiY : 0) | (L.next_codes ? kEpiCodes : 0) |
+                    (L.residual ? kEpiPos : 0);
     switch (epi) {
     case kEpiY: return run_gemm<BN, kEpiY, kPair>(L, stream);
+    case kEpiY | kEpiPos: return run_gemm<BN, kEpiY | kEpiPos, kPair>(L, stream);
     case kEpiCodes: return run_gemm<BN, kEpiCodes, kPair>(L, stream);
     case kEpiY | kEpiCodes: return run_gemm<BN, kEpiY | kEpiCodes, kPair>(L, stream);
     case kEpiGelu | kEpiY: return run_gemm<BN, kEpiGelu | kEpiY, kPair>(L, stream);

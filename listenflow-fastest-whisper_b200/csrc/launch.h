@@ -20,6 +20,7 @@ struct LinearLaunch {
     float next_scale;
     uint8_t *next_codes;
     bool w_packed; // w_codes holds skinny-packed tiles (m <= 32 path only)
+    const uint16_t *residual = nullptr; // fp16 [m, n] added after the bias (large-m path only)
 };
 
 // Encoder convolution (kernel 3, padding 1, stride 1 or 2) on fp16 tensor cores

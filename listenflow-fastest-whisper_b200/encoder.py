@@ -11,8 +11,8 @@ Restates the FP8 encoder graph of cpp/src/network_graph.cpp:255-301:
 Every step is one launch of liblffw_b200.so; the launch arguments are built once
 (an ``Encoder`` is a plan over preallocated device buffers, like an engine's
 bindings), so a forward allocates nothing and can be captured in a CUDA graph.
-The residual adds ride on the LayerNorm producers (the fp16 sum of
-network_graph.cpp:285-287 is written by the LayerNorm that reads it), and every
+The residual adds (the fp16 sums of network_graph.cpp:285-287) ride on the
+epilogues of out_proj and fc2, so each LayerNorm reads one tensor, and every
 LayerNorm or epilogue that feeds an FP8 linear writes that linear's E4M3 codes
 directly.
 
@@ -243,8 +243,6 @@ class Encoder:
         self.h1 = torch.zeros((n, c.frames + 2, d), dtype=torch.float16, device=device)  # rows 0, -1: padding
         self.x0 = empty((n, t, d))
         self.stream_buf = [empty((m, d)), empty((m, d))]
-        self.o = empty((m, d))
-        self.r = empty((m, d))
         self.ln_codes = empty((m, d), torch.uint8)
         self.qkv = empty((m, 3 * d))
         self.attn_codes = empty((m, d), torch.uint8)
@@ -291,7 +289,8 @@ class Encoder:
             a.y, a.code_scale, a.codes = p(y), code_scale, p(codes)
             return ("lffw_layer_norm", lambda s, a=a: lib.lffw_layer_norm(ctypes.byref(a), s))
 
-        def linear(x_codes, weight, act_scale, y=None, gelu=False, next_scale=None, next_codes=None):
+        def linear(x_codes, weight, act_scale, y=None, gelu=False, next_scale=None, next_codes=None,
+                   residual=None):
             a = native.LinearArgs()
             a.struct_size = ctypes.sizeof(a)
             a.m, a.n, a.k = m, weight.scales.shape[0], x_codes.shape[-1]
@@ -302,6 +301,7 @@ class Encoder:
             a.next_scale = next_scale if next_scale is not None else 0.0
             a.next_codes = p(next_codes)
             a.w_layout = native.WEIGHTS_ROW_MAJOR
+            a.residual = p(residual)
             return ("lffw_fp8_linear", lambda s, a=a: lib.lffw_fp8_linear(ctypes.byref(a), s))
 
         def attention(code_scale):
@@ -314,27 +314,26 @@ class Encoder:
             a.out, a.code_scale, a.out_codes = None, code_scale, p(self.attn_codes)
             return ("lffw_self_attention", lambda s, a=a: lib.lffw_self_attention(ctypes.byref(a), s))
 
+        # The residual adds ride on the epilogues of out_proj and fc2 (y = linear +
+        # residual, the same fp16 add), so each LayerNorm reads one tensor and
+        # writes codes only.  Layer l's input x is stream_buf[0] (x0 for layer 0),
+        # its mid-layer sum stream_buf[1], and fc2 writes layer l + 1's input over
+        # stream_buf[0], which out_proj has finished reading.
         x = self.x0.view(-1, d)
-        residual = None
         for i, L in enumerate(w.layers):
             s_qkv, s_out, s_fc1, s_fc2 = sc["qkv"][i], sc["out"][i], sc["fc1"][i], sc["fc2"][i]
-            if residual is None:
-                calls.append(norm(x, None, L.ln1, None, None, s_qkv, self.ln_codes))
-            else:
-                nxt = self.stream_buf[0]
-                calls.append(norm(x, residual, L.ln1, nxt, None, s_qkv, self.ln_codes))
-                x = nxt
+            calls.append(norm(x, None, L.ln1, None, None, s_qkv, self.ln_codes))
             calls.append(linear(self.ln_codes, L.qkv, s_qkv, y=self.qkv))
             calls.append(attention(s_out))
-            calls.append(linear(self.attn_codes, L.out, s_out, y=self.o))
             mid = self.stream_buf[1]
-            calls.append(norm(x, self.o, L.ln2, mid, None, s_fc1, self.ln_codes))
-            x = mid
+            calls.append(linear(self.attn_codes, L.out, s_out, y=mid, residual=x))
+            calls.append(norm(mid, None, L.ln2, None, None, s_fc1, self.ln_codes))
             calls.append(linear(self.ln_codes, L.fc1, s_fc1, gelu=True, next_scale=s_fc2, next_codes=self.fc2_codes))
-            calls.append(linear(self.fc2_codes, L.fc2, s_fc2, y=self.r))
-            residual = self.r
+            nxt = self.stream_buf[0]
+            calls.append(linear(self.fc2_codes, L.fc2, s_fc2, y=nxt, residual=mid))
+            x = nxt
         s_cross = sc["cross"][0]
-        calls.append(norm(x, residual, w.ln_post, None, states, s_cross, self.kv_codes))
+        calls.append(norm(x, None, w.ln_post, None, states, s_cross, self.kv_codes))
 
         a = native.HeadsLinearArgs()
         a.struct_size = ctypes.sizeof(a)

@@ -384,9 +384,12 @@ def pack_skinny(weight: torch.Tensor, stream=None) -> torch.Tensor:
 def linear(x_codes: torch.Tensor, w_codes: torch.Tensor, w_scales: torch.Tensor, act_scale, *,
            bias: torch.Tensor | None = None, gelu: bool = False, out: torch.Tensor | None = None,
            want_y: bool = True, next_scale: float | None = None, next_codes: torch.Tensor | None = None,
-           w_packed: torch.Tensor | None = None, stream=None) -> tuple[torch.Tensor | None, torch.Tensor | None]:
+           w_packed: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+           stream=None) -> tuple[torch.Tensor | None, torch.Tensor | None]:
     """One FP8 Q/DQ linear on E4M3 codes: x_codes [..., K], w_codes [N, K].
     `w_packed` (from pack_skinny(w_codes)) replaces w_codes on the m <= 32 path.
+    `residual` (fp16 [..., N]) is added to y after the bias, the graph's residual
+    add (network_graph.cpp:285-287); `out` may be the residual itself.
 
     Returns (y fp16 [..., N] or None, next-linear E4M3 codes or None)."""
     _require(x_codes, torch.uint8, "x_codes")
@@ -417,6 +420,11 @@ def linear(x_codes: torch.Tensor, w_codes: torch.Tensor, w_scales: torch.Tensor,
     a.y = _ptr(out) if want_y else None
     a.next_scale = float(next_scale) if next_scale is not None else 0.0
     a.next_codes = _ptr(next_codes)
+    if residual is not None:
+        _require(residual, torch.float16, "residual")
+        if residual.numel() != m * n:
+            raise ValueError("residual must hold m x n fp16 values")
+    a.residual = _ptr(residual)
     native.check(native.library().lffw_fp8_linear(ctypes.byref(a), _stream(stream)), "lffw_fp8_linear")
     return (out if want_y else None), next_codes
 

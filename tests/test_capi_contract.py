@@ -44,6 +44,10 @@ def _linear_args(native, **over):
     dict(x_codes=0x10008), dict(y=0x40002), dict(bias=0x50004),
     dict(act_scale=0.0), dict(act_scale=-0.1), dict(act_scale=float("nan")), dict(act_scale=float("inf")),
     dict(next_codes=0x60000, next_scale=0.0), dict(epilogue=7),
+    # the residual add: y only (no GELU, no next codes), n % 32 == 0, aligned, row-major weights
+    dict(residual=0x70000, epilogue=1), dict(residual=0x70000, next_codes=0x60000, next_scale=0.01),
+    dict(residual=0x70000, y=None, next_codes=0x60000, next_scale=0.01), dict(residual=0x70000, n=272),
+    dict(residual=0x70008), dict(residual=0x70000, m=4, w_layout=1),
 ])
 def test_linear_rejects_invalid_arguments(native, lib, change):
     a = _linear_args(native, **change)
@@ -54,6 +58,15 @@ def test_linear_abi_mismatch_and_null(native, lib):
     a = _linear_args(native, struct_size=8)
     assert lib.lffw_fp8_linear(ctypes.byref(a), None) == native.ABI_MISMATCH
     assert lib.lffw_fp8_linear(None, None) == native.INVALID_ARGUMENT
+
+
+def test_linear_residual_field_ignored_for_older_callers(native, lib):
+    """A caller built before the residual field passes a shorter struct_size: whatever
+    lies past it is not read, so a misaligned value there is no argument error."""
+    a = _linear_args(native, residual=0x70008)
+    assert lib.lffw_fp8_linear(ctypes.byref(a), None) == native.INVALID_ARGUMENT
+    a.struct_size = native.LinearArgs.residual.offset
+    assert lib.lffw_fp8_linear(ctypes.byref(a), None) != native.INVALID_ARGUMENT
 
 
 def _chain(native, lib, links):

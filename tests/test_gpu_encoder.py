@@ -269,17 +269,22 @@ def test_encoder_stage_by_stage(small_encoder, enc, fp8, oracle, native, cuda):
         print(f"{what}: max_abs={max_abs:.3g} mismatch={mism}/{got.size}")
         assert excess <= 0, what
 
-    residual = None
+    def fused_residual_check(codes, weight, act_scale, got, residual, what):
+        """The plan's linear adds the residual in its epilogue: the same linear
+        alone (its y checked against the oracle) plus the fp16 residual add must
+        give the plan's output bit for bit."""
+        alone, _ = fp8.linear(torch.from_numpy(codes).to(cuda), weight.codes, weight.scales, act_scale,
+                              bias=weight.bias)
+        torch.cuda.synchronize()
+        y = bits(alone).reshape(got.shape)
+        linear_check(codes, weight, act_scale, y, what)
+        want = (_f16(y).astype(np.float32) + _f16(residual).astype(np.float32)).astype(np.float16)
+        np.testing.assert_array_equal(got, want.view(np.uint16))  # one fp16 rounding of the exact sum
+
     for i, L in enumerate(weights.layers):
         g1, be1 = host(L.ln1[0]), host(L.ln1[1])
         step("lffw_layer_norm")
-        if residual is not None:
-            s_ref, _, c_ref = oracle.layer_norm(x, g1, be1, residual=residual, code_scale=sc["qkv"][i])
-            x_new = bits(e.stream_buf[0])
-            np.testing.assert_array_equal(x_new, s_ref)  # the fp16 residual sum is exact
-            x = x_new
-        else:
-            _, _, c_ref = oracle.layer_norm(x, g1, be1, code_scale=sc["qkv"][i])
+        _, _, c_ref = oracle.layer_norm(x, g1, be1, code_scale=sc["qkv"][i])
         ln_codes = host(e.ln_codes)
         _codes_close(ln_codes, c_ref, f"layer {i} LN1 codes", min_equal=0.99)
 
@@ -303,14 +308,13 @@ def test_encoder_stage_by_stage(small_encoder, enc, fp8, oracle, native, cuda):
         assert np.all(err <= ATOL + RTOL * np.abs(ref) + slack), f"layer {i} attention"
 
         step("lffw_fp8_linear")
-        o = bits(e.o)
-        linear_check(attn_codes, L.out, sc["out"][i], o, f"layer {i} out_proj")
+        mid = bits(e.stream_buf[1])
+        fused_residual_check(attn_codes, L.out, sc["out"][i], mid, x, f"layer {i} out_proj + residual")
+        x = mid
 
         g2, be2 = host(L.ln2[0]), host(L.ln2[1])
         step("lffw_layer_norm")
-        s_ref, _, c_ref = oracle.layer_norm(x, g2, be2, residual=o, code_scale=sc["fc1"][i])
-        x = bits(e.stream_buf[1])
-        np.testing.assert_array_equal(x, s_ref)
+        _, _, c_ref = oracle.layer_norm(x, g2, be2, code_scale=sc["fc1"][i])
         ln2_codes = host(e.ln_codes)
         _codes_close(ln2_codes, c_ref, f"layer {i} LN2 codes", min_equal=0.99)
 
@@ -319,12 +323,13 @@ def test_encoder_stage_by_stage(small_encoder, enc, fp8, oracle, native, cuda):
         linear_check(ln2_codes, L.fc1, sc["fc1"][i], fc2_codes, f"layer {i} fc1+GELU codes", gelu=True,
                      next_scale=sc["fc2"][i], far=max(4, fc2_codes.size // 50000))
         step("lffw_fp8_linear")
-        residual = bits(e.r)
-        linear_check(fc2_codes, L.fc2, sc["fc2"][i], residual, f"layer {i} fc2")
+        nxt = bits(e.stream_buf[0])
+        fused_residual_check(fc2_codes, L.fc2, sc["fc2"][i], nxt, x, f"layer {i} fc2 + residual")
+        x = nxt
 
     gp, bp = host(weights.ln_post[0]), host(weights.ln_post[1])
     step("lffw_layer_norm")
-    _, y_ref, c_ref = oracle.layer_norm(x, gp, bp, residual=residual, code_scale=sc["cross"][0])
+    _, y_ref, c_ref = oracle.layer_norm(x, gp, bp, code_scale=sc["cross"][0])
     states = bits(e.states).reshape(streams * t, d)
     diff = np.abs(_f16(states) - _f16(y_ref))
     ulp = np.spacing(np.abs(_f16(y_ref)).astype(np.float16)).astype(np.float64)

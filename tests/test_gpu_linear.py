@@ -335,3 +335,34 @@ def test_packed_layout_rejected_for_large_m(cuda, fp8, native):
     xq = torch.zeros(64, 256, dtype=torch.uint8, device=cuda)
     with pytest.raises(native.NativeError):
         fp8.linear(xq, q.codes, q.scales, 0.01, w_packed=fp8.pack_skinny(q.codes))
+
+
+@pytest.mark.parametrize("m,n,k", [(7, 256, 128), (200, 1280, 1280), (777, 1280, 5120), (1500, 1280, 1280),
+                                   (2560, 3840, 1280)])
+def test_residual_add_in_epilogue(cuda, fp8, oracle, native, m, n, k):
+    """y = linear + residual from the epilogue equals the linear alone followed by
+    one fp16 rounding of the exact sum, bit for bit: single and paired tiles, both
+    tile widths, ragged M, a small m (which takes the large-m kernel), and the
+    in-place form (out is the residual).  The linear alone is the same kernel with
+    a residual of -0, which leaves every fp16 value (and -0) unchanged; for m > 32
+    it equals the plain linear bit for bit."""
+    import torch
+
+    d = _prepare(torch, fp8, oracle, cuda, m, n, k, seed=m + n + k)
+    rng = np.random.default_rng(m * 7 + 1)
+    residual = halves(rng, (m, n), 1.0)
+    rd = _to_dev(torch, residual, cuda)
+    neg_zero = torch.full((m, n), -0.0, dtype=torch.float16, device=cuda)
+    alone, _ = fp8.linear(d["xq"], d["wq"], d["ws"], float(d["act_scale"]), bias=d["bd"], residual=neg_zero)
+    plain, _ = fp8.linear(d["xq"], d["wq"], d["ws"], float(d["act_scale"]), bias=d["bd"])
+    fused, _ = fp8.linear(d["xq"], d["wq"], d["ws"], float(d["act_scale"]), bias=d["bd"], residual=rd)
+    inplace = rd.clone()
+    fp8.linear(d["xq"], d["wq"], d["ws"], float(d["act_scale"]), bias=d["bd"], residual=inplace, out=inplace)
+    torch.cuda.synchronize()
+    assert native.device_error() == 0
+    if m > 32:
+        np.testing.assert_array_equal(alone.cpu().numpy().view(np.uint16), plain.cpu().numpy().view(np.uint16))
+    a = alone.cpu().numpy().astype(np.float64)
+    want = (a + residual.view(np.float16).astype(np.float64)).astype(np.float16)
+    np.testing.assert_array_equal(fused.cpu().numpy().view(np.uint16), want.view(np.uint16))
+    np.testing.assert_array_equal(inplace.cpu().numpy().view(np.uint16), want.view(np.uint16))
