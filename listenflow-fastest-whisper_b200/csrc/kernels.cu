@@ -1641,14 +1641,24 @@ __device__ __forceinline__ float warp_sum(float v)
 
 // KV: 16-byte vectors (8 halves) per lane; the row (cols / 8 vectors) is spread
 // over the lanes, vector v on lane v % 32, held in registers between passes.
-// Warps loop over rows (grid-stride).
+// Warps loop over rows (grid-stride).  gamma and beta are staged once per block
+// in shared memory (dynamic, 8 bytes per column): every row reads them again.
+// kCodesOnly: x in (no residual), E4M3 codes out only (no sum, no fp16 y), the
+// form that follows a GEMM epilogue which already added the residual.
 
-template <int KV>
+template <int KV, bool kCodesOnly>
 __global__ void __launch_bounds__(kThreads, KV <= 5 ? 4 : 1) layer_norm_kernel(const Params p)
 {
+    extern __shared__ __align__(16) float gb_s[]; // gamma [cols], beta [cols]
     if (threadIdx.x == 0)
         griddepcontrol_launch_dependents();
+    for (int i = threadIdx.x; i < p.cols / 4; i += kThreads) { // layer constants: before the wait
+        reinterpret_cast<float4 *>(gb_s)[i] = __ldg(reinterpret_cast<const float4 *>(p.gamma) + i);
+        reinterpret_cast<float4 *>(gb_s + p.cols)[i] = __ldg(reinterpret_cast<const float4 *>(p.beta) + i);
+    }
+    __syncthreads();
     griddepcontrol_wait();
+    const float *gamma_s = gb_s, *beta_s = gb_s + p.cols;
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
     const int vecs = p.cols / 8;
@@ -1662,12 +1672,12 @@ __global__ void __launch_bounds__(kThreads, KV <= 5 ? 4 : 1) layer_norm_kernel(c
         v[j] = make_uint4(0u, 0u, 0u, 0u);
         if (c < vecs) {
             v[j] = ld_stream16(p.x + base + 8 * c);
-            if (p.residual) {
+            if (!kCodesOnly && p.residual) {
                 const uint4 r = ld_stream16(p.residual + base + 8 * c);
                 v[j] = make_uint4(gemm::hadd2_rn(v[j].x, r.x), gemm::hadd2_rn(v[j].y, r.y),
                                   gemm::hadd2_rn(v[j].z, r.z), gemm::hadd2_rn(v[j].w, r.w));
             }
-            if (p.sum_out)
+            if (!kCodesOnly && p.sum_out)
                 *reinterpret_cast<uint4 *>(p.sum_out + base + 8 * c) = v[j];
         }
     }
@@ -1705,10 +1715,10 @@ __global__ void __launch_bounds__(kThreads, KV <= 5 ? 4 : 1) layer_norm_kernel(c
         const int c = lane + 32 * j;
         if (c >= vecs)
             continue;
-        const float4 g0 = __ldg(reinterpret_cast<const float4 *>(p.gamma + 8 * c));
-        const float4 g1 = __ldg(reinterpret_cast<const float4 *>(p.gamma + 8 * c) + 1);
-        const float4 b0 = __ldg(reinterpret_cast<const float4 *>(p.beta + 8 * c));
-        const float4 b1 = __ldg(reinterpret_cast<const float4 *>(p.beta + 8 * c) + 1);
+        const float4 g0 = reinterpret_cast<const float4 *>(gamma_s + 8 * c)[0];
+        const float4 g1 = reinterpret_cast<const float4 *>(gamma_s + 8 * c)[1];
+        const float4 b0 = reinterpret_cast<const float4 *>(beta_s + 8 * c)[0];
+        const float4 b1 = reinterpret_cast<const float4 *>(beta_s + 8 * c)[1];
         const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
         const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
         const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
@@ -1719,9 +1729,9 @@ __global__ void __launch_bounds__(kThreads, KV <= 5 ? 4 : 1) layer_norm_kernel(c
             const float y1 = fmaf((h2f(static_cast<uint16_t>(w[i] >> 16)) - mean) * rstd, g[2 * i + 1], b[2 * i + 1]);
             out[i] = gemm::cvt_f16x2(y0, y1);
         }
-        if (p.y)
+        if (!kCodesOnly && p.y)
             *reinterpret_cast<uint4 *>(p.y + base + 8 * c) = make_uint4(out[0], out[1], out[2], out[3]);
-        if (p.codes) {
+        if (kCodesOnly || p.codes) {
             const uint32_t lo = e4m3x4(out[0], out[1], lean, neg_scale2, recip2);
             const uint32_t hi = e4m3x4(out[2], out[3], lean, neg_scale2, recip2);
             asm volatile("st.global.v2.u32 [%0], {%1, %2};" ::"l"(p.codes + base + 8 * c), "r"(lo), "r"(hi) : "memory");
@@ -3791,15 +3801,21 @@ cudaError_t launch_layer_norm(const LayerNormLaunch &L, cudaStream_t stream)
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     config.attrs = attr;
     config.numAttrs = 1;
+    config.dynamicSmemBytes = static_cast<size_t>(L.cols) * 8; // gamma and beta
+    const bool codes_only = L.residual == nullptr && L.sum_out == nullptr && L.y == nullptr && L.codes != nullptr;
+    auto launch = [&](auto kernel) {
+        cudaError_t e = ensure_smem(kernel, 4096 * 8);
+        return e != cudaSuccess ? e : cudaLaunchKernelEx(&config, kernel, p);
+    };
     cudaError_t err;
     if (per_lane <= 2)
-        err = cudaLaunchKernelEx(&config, norm::layer_norm_kernel<2>, p);
+        err = codes_only ? launch(norm::layer_norm_kernel<2, true>) : launch(norm::layer_norm_kernel<2, false>);
     else if (per_lane <= 5)
-        err = cudaLaunchKernelEx(&config, norm::layer_norm_kernel<5>, p);
+        err = codes_only ? launch(norm::layer_norm_kernel<5, true>) : launch(norm::layer_norm_kernel<5, false>);
     else if (per_lane <= 8)
-        err = cudaLaunchKernelEx(&config, norm::layer_norm_kernel<8>, p);
+        err = codes_only ? launch(norm::layer_norm_kernel<8, true>) : launch(norm::layer_norm_kernel<8, false>);
     else
-        err = cudaLaunchKernelEx(&config, norm::layer_norm_kernel<16>, p);
+        err = codes_only ? launch(norm::layer_norm_kernel<16, true>) : launch(norm::layer_norm_kernel<16, false>);
     count_launch();
     return err != cudaSuccess ? err : cudaGetLastError();
 }
