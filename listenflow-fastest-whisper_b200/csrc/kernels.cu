@@ -822,30 +822,36 @@ constexpr int kBK = 128;    // K bytes per stage
 constexpr int kWBytes = kRows * kBK;
 constexpr int kXBytes = kAct * kBK;
 constexpr int kStageBytes = kWBytes + kXBytes;
-constexpr int kRedStride = kRows + 4; // floats per activation row of the partials (m-major)
-constexpr int kRedBytes = kAct * kRedStride * 4;
-// The split-K reduction buffer reuses the stage memory: it is written only
-// after every load has landed and every MMA has completed.
-constexpr int kOffRed = 0;
 
-// Shared-memory ring of ST stages.  Two stages and small CTAs (five per SM)
+// Split-K exchange buffer: row r of sender rank q lands at float offset
+// (q * 128 / S + r % (128 / S)) * stride, its activation rows m contiguous;
+// stride = 4 * ceil(m / 4) + 4 floats (16-byte rows, padded against bank
+// conflicts).  Separate from the ring: peers may write it while this CTA still
+// loads and multiplies.
+__host__ __device__ constexpr int recv_stride(int m) { return (m + 3) / 4 * 4 + 4; }
+__host__ __device__ constexpr int recv_bytes(int m) { return kRows * recv_stride(m) * 4; }
+
+// Shared-memory ring of ST stages.  Two stages and small CTAs (four per SM)
 // stream fastest when there are many CTAs (measured on B200: more independent
 // weight streams per SM beat deeper rings); a deep ring is used when the grid
 // is small and each CTA owns more K blocks than two stages hold, so that all
 // of a CTA's weights are requested before it waits for the previous kernel.
+// The split-K exchange buffer (sized by m at launch) follows the barriers.
 template <int ST>
 struct Ring {
     static constexpr int kStages = ST;
     static constexpr int kOffX = ST * kWBytes;
     static constexpr int kRingBytes = kOffX + ST * kXBytes;
-    static constexpr int kOffBar = (kRingBytes > kRedBytes ? kRingBytes : kRedBytes + 1023) / 1024 * 1024;
-    static constexpr int kSmemBytes = kOffBar + 128 + 1024;
-    static_assert((2 * ST + 2) * 8 <= 128, "barrier area");
+    static constexpr int kOffBar = kRingBytes;
+    static constexpr int kOffRecv = kOffBar + 128;
+    static constexpr int kSmemBase = kOffRecv + 1024; // + recv_bytes(m) when S > 1
+    static_assert(kRingBytes % 1024 == 0, "swizzled stages stay 1024-byte aligned");
+    static_assert((2 * ST + 3) * 8 <= 128, "barrier area");
 };
 constexpr int kShallow = 2;
 constexpr int kDeep = 6;
-static_assert(Ring<kShallow>::kSmemBytes <= 46 * 1024, "five CTAs per SM");
-static_assert(Ring<kDeep>::kSmemBytes <= 227 * 1024, "shared memory budget");
+static_assert(Ring<kShallow>::kSmemBase + recv_bytes(20) <= 56 * 1024, "four CTAs per SM at the decoder's m");
+static_assert(Ring<kDeep>::kSmemBase + recv_bytes(kAct) <= 227 * 1024, "shared memory budget");
 constexpr int kMaxCluster = 8;
 
 enum : int { kKindE4M3 = 0, kKindF16 = 1 };
@@ -863,39 +869,32 @@ struct Params {
     const uint8_t *w_packed; // non-null: weights in pre-swizzled 16 KB tiles (pack_kernel)
 };
 
-// Split-K reduction over a cluster of S CTAs.  Each CTA finishes 128 / S of
-// the 128 weight rows; a thread owns one of them (`row`) and the activation
-// rows m = g + j*S (j < 32 / S) below m_count, where g = threadIdx.x / (128 / S).
-// The partials are stored m-major, so a warp's remote loads read runs of
-// consecutive rows.  Every remote partial is requested before the sums, which
-// add the cluster's partials in rank order into acc[j].
+// Split-K sums over a cluster of S CTAs.  Each CTA finishes 128 / S of the
+// 128 weight rows; a thread owns one of them (local index `r_local`) and the
+// activation rows m = g + j*S (j < 32 / S) below m_count, where
+// g = threadIdx.x / (128 / S).  The S partials of a row are added in rank
+// order: slot q of `recv` holds CTA q's, and `own` this CTA's (rank `rank`).
 template <int S>
-__device__ __forceinline__ void reduce_rows(const float *red, int row, int m_count, float (&acc)[kAct / 2])
+__device__ __forceinline__ void sum_rows(const float *recv, const float *own, int rank, int stride, int r_local,
+                                         int m_count, float (&acc)[kAct / 2])
 {
     constexpr int kPer = kAct / S; // activation rows per thread
-    const int g = static_cast<int>(threadIdx.x) / (kRows / S);
-    float part[kPer][S];
+    constexpr int kRowsPer = kRows / S;
+    const int g = static_cast<int>(threadIdx.x) / kRowsPer;
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
         const int m = g + j * S;
+        float sum = 0.0f;
         if (m < m_count) {
-            const uint32_t local = smem_u32(red + m * kRedStride + row);
 #pragma unroll
             for (int q = 0; q < S; ++q)
-                part[j][q] = ld_shared_cluster_f32(map_to_rank(local, static_cast<uint32_t>(q)));
+                sum += (q == rank ? own : recv + q * kRowsPer * stride)[r_local * stride + m];
         }
-    }
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-        float sum = 0.0f;
-#pragma unroll
-        for (int q = 0; q < S; ++q)
-            sum += g + j * S < m_count ? part[j][q] : 0.0f;
         acc[j] = sum;
     }
 }
 
-// The epilogue of the rows reduce_rows<S> summed: finish(acc[j], m) per row m.
+// The epilogue of the rows sum_rows<S> summed: finish(acc[j], m) per row m.
 template <int S, class Finish>
 __device__ __forceinline__ void finish_rows(const float (&acc)[kAct / 2], int m_count, Finish &finish)
 {
@@ -928,8 +927,11 @@ __global__ void __launch_bounds__(kThreads)
     const uint32_t bar_full = sbase + kOffBar;
     const uint32_t bar_empty = bar_full + 8 * kStages;
     const uint32_t bar_acc = bar_empty + 8 * kStages;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 8 * (2 * kStages + 1));
-    float *red = reinterpret_cast<float *>(smem + kOffRed);
+    const uint32_t bar_recv = bar_acc + 8; // split-K partials from the peers have landed
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 8 * (2 * kStages + 2));
+    const uint32_t recv = sbase + Ring<ST>::kOffRecv;
+    const int stride = recv_stride(p.m);
+    const int nvec = (p.m + 3) / 4; // 16-byte pieces of a row's partials
 
     if (threadIdx.x == 0) {
         griddepcontrol_launch_dependents();
@@ -938,6 +940,10 @@ __global__ void __launch_bounds__(kThreads)
             mbar_init(bar_empty + 8 * s, 1);
         }
         mbar_init(bar_acc, 1);
+        mbar_init(bar_recv, 1);
+        // The one local arrival, and the bytes the S - 1 peers will send.
+        if (S > 1)
+            mbar_arrive_expect_tx(bar_recv, static_cast<uint32_t>((S - 1) * (kRows / S) * stride * 4));
         fence_barrier_init();
         prefetch_tensor_map(&tm_w);
         prefetch_tensor_map(&tm_x);
@@ -950,6 +956,10 @@ __global__ void __launch_bounds__(kThreads)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Peers may send partials into this CTA once every CTA of the cluster has
+    // initialised its barriers: arrive now, wait just before the first send.
+    if (S > 1)
+        cluster_arrive();
 
     // The output row this thread finishes (its own TMEM lane when S == 1, else
     // row `threadIdx.x % (128 / S)` of this CTA's share of the reduction) and
@@ -1069,23 +1079,47 @@ __global__ void __launch_bounds__(kThreads)
                     finish(__uint_as_float(v[m]), m);
         }
     } else {
+        // Split-K exchange.  Each thread stages its row (TMEM lane threadIdx.x)
+        // in the ring, idle now that every MMA has completed: row R at float
+        // offset R * stride, so the rows CTA q finishes form one contiguous run.
+        // One thread then copies run q into slot `rank` of CTA q's receive
+        // buffer, one bulk copy per peer, each completing its bytes on the
+        // peer's bar_recv (a few barrier updates instead of one per 16 bytes).
+        const int rows_per = kRows / S;
+        const uint32_t run_bytes = static_cast<uint32_t>(rows_per * stride * 4);
 #pragma unroll
-        for (int i = 0; i < kAct; ++i)
-            red[i * kRedStride + threadIdx.x] = __uint_as_float(v[i]);
-        cluster_sync();
+        for (int i = 0; i < kAct / 4; ++i)
+            if (i < nvec)
+                st_shared_v4(sbase + static_cast<uint32_t>((threadIdx.x * stride + 4 * i) * 4),
+                             make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+        fence_proxy_async_smem(); // the bulk copies (async proxy) read these stores
+        cluster_wait();           // every peer's bar_recv is initialised
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            for (int q = 0; q < S; ++q)
+                if (q != rank)
+                    bulk_copy_to_peer(map_to_rank(recv + static_cast<uint32_t>(rank) * run_bytes, static_cast<uint32_t>(q)),
+                                      sbase + static_cast<uint32_t>(q) * run_bytes, run_bytes,
+                                      map_to_rank(bar_recv, static_cast<uint32_t>(q)));
+        }
+        // A bounded wait that gives up sets the error word; the sums still run.
+        mbar_wait_cluster(bar_recv, 0, kSiteClusterExchange);
+        __syncwarp();
+        // This CTA has everything it was sent: arrive on the exit barrier, which
+        // keeps every CTA's staged runs (the copies' sources) alive until all
+        // peers have received theirs.  Every copy into a CTA has completed
+        // before it arrives, so the arrival orders nothing: relaxed.
+        cluster_arrive_relaxed();
+        const float *rbuf = reinterpret_cast<const float *>(smem + Ring<ST>::kOffRecv);
+        const float *own = reinterpret_cast<const float *>(smem) + rank * rows_per * stride;
+        const int r_local = static_cast<int>(threadIdx.x) % rows_per;
         float acc[kAct / 2];
         if (my_n < p.n) {
             switch (S) {
-            case 2: reduce_rows<2>(red, my_row, p.m, acc); break;
-            case 4: reduce_rows<4>(red, my_row, p.m, acc); break;
-            default: reduce_rows<8>(red, my_row, p.m, acc); break;
+            case 2: sum_rows<2>(rbuf, own, rank, stride, r_local, p.m, acc); break;
+            case 4: sum_rows<4>(rbuf, own, rank, stride, r_local, p.m, acc); break;
+            default: sum_rows<8>(rbuf, own, rank, stride, r_local, p.m, acc); break;
             }
-        }
-        // This thread's remote reads have returned (their values are summed):
-        // arrive now and wait only before exiting, so the barrier's latency
-        // overlaps the epilogue.  Peers read this CTA's partials until the wait.
-        cluster_arrive();
-        if (my_n < p.n) {
             switch (S) {
             case 2: finish_rows<2>(acc, p.m, finish); break;
             case 4: finish_rows<4>(acc, p.m, finish); break;
@@ -3684,8 +3718,9 @@ cudaError_t run_skinny(const void *x, const void *w, int64_t m, int64_t n, int64
     // shallow ring holds takes the deep ring.
     const bool deep = grid <= sm_count() && per_cta > skinny::kShallow;
     auto kernel = deep ? skinny::skinny_kernel<KIND, EPI, skinny::kDeep> : skinny::skinny_kernel<KIND, EPI, skinny::kShallow>;
-    const int smem = deep ? skinny::Ring<skinny::kDeep>::kSmemBytes : skinny::Ring<skinny::kShallow>::kSmemBytes;
-    const cudaError_t attr = ensure_smem(kernel, smem);
+    const int base = deep ? skinny::Ring<skinny::kDeep>::kSmemBase : skinny::Ring<skinny::kShallow>::kSmemBase;
+    const int smem = base + (p.cluster > 1 ? skinny::recv_bytes(p.m) : 0);
+    const cudaError_t attr = ensure_smem(kernel, base + skinny::recv_bytes(skinny::kAct));
     if (attr != cudaSuccess)
         return attr;
     cudaLaunchConfig_t config{};

@@ -462,6 +462,13 @@ __device__ __forceinline__ void cluster_arrive()
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }
 
+// Arrival that orders no memory: for a barrier that only keeps peers' shared
+// memory alive (their data has already been handed over by other means).
+__device__ __forceinline__ void cluster_arrive_relaxed()
+{
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ void cluster_wait()
 {
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -511,6 +518,24 @@ __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence
 __device__ __forceinline__ void st_shared_cluster_f32(uint32_t cluster_addr, float v)
 {
     asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
+}
+
+// Contiguous copy from this CTA's shared memory into a peer CTA's (size and
+// both addresses multiples of 16 B), its bytes completed on the peer's
+// mbarrier `cluster_bar`.  The source must stay unchanged until the peer has
+// seen the barrier complete.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t cluster_dst, uint32_t src, uint32_t bytes,
+                                                  uint32_t cluster_bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(cluster_dst), "r"(src), "r"(bytes), "r"(cluster_bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v)
+{
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
 }
 
 // Parity wait with cluster-scope acquire: stores that peers made before their
