@@ -511,6 +511,48 @@ def run_decoder(fp8, native, device, steps: int, warmup: int, seed: int, layers_
             and torch.equal(calls_out[1], logits)):
         raise RuntimeError("the chained decoder step differs from the per-call step")
     chain.close()
+
+    # Each GEMV shape in isolation: the same kernel over many distinct weights
+    # with no dependency between launches (four streams take turns), so the
+    # weights stream while other launches run their latency chains.  Every
+    # group holds more weights than the 126 MB L2, so each replay reads them
+    # from HBM.
+    groups = (("qkv 1280->3840", ("qkv",)), ("1280->1280 (self_out, cross_q, cross_out)",
+                                              ("self_out", "cross_q", "cross_out")),
+              ("fc1 1280->5120 +GELU -> codes", ("fc1",)), ("fc2 5120->1280", ("fc2",)))
+    side = [torch.cuda.Stream(device) for _ in range(4)]
+    isolated = {}
+    for label, names in groups:
+        units = [(layer[nm], nm) for layer in layers for nm in names]
+        sinks = [{nm: torch.empty(DEC_M, n, dtype=torch.float16 if nm != "fc1" else torch.uint8, device=device)
+                  for nm, _, n in DEC_LINEARS} for _ in side]
+        group_bytes = sum(dict((nm, n * k + n * 6) for nm, k, n in DEC_LINEARS)[nm] for _, nm in units)
+
+        def body(units=units, sinks=sinks):
+            main = torch.cuda.current_stream()
+            fork = torch.cuda.Event()
+            fork.record(main)
+            for s in side:
+                s.wait_event(fork)
+            for i, ((q, packed), nm) in enumerate(units):
+                sink = sinks[i % len(side)]
+                with torch.cuda.stream(side[i % len(side)]):
+                    if nm == "fc1":
+                        fp8.linear(x_codes, None, q.scales, 0.01, bias=q.bias, gelu=True, want_y=False,
+                                   next_scale=0.02, next_codes=sink["fc1"], w_packed=packed)
+                    else:
+                        fp8.linear(fc2_in if nm == "fc2" else x_codes, None, q.scales, 0.02 if nm == "fc2" else 0.01,
+                                   bias=q.bias, out=sink[nm], w_packed=packed)
+            for s in side:
+                join = torch.cuda.Event()
+                join.record(s)
+                main.wait_event(join)
+
+        ms_group = measure(body)
+        gbs_group = group_bytes / (ms_group / 1e3) / 1e9
+        isolated[label] = {"launches": len(units), "us_per_launch": round(ms_group * 1e3 / len(units), 3),
+                           "weight_mb": round(group_bytes / 1e6, 1), "gbs": round(gbs_group, 1),
+                           "frac_of_hbm": round(gbs_group / read_hbm_peak()[0], 4)}
     ms = min(ms_calls, ms_chain)
     hbm = read_hbm_peak()
     gbs = weight_bytes / (ms / 1e3) / 1e9
@@ -523,6 +565,10 @@ def run_decoder(fp8, native, device, steps: int, warmup: int, seed: int, layers_
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm[0], "peak_source": hbm[1],
                          "unit": "GB/s", "frac": round(gbs / hbm[0], 4)},
             "per_call_ms": round(ms_calls, 4), "chain_ms": round(ms_chain, 4),
+            "isolated": isolated,
+            "isolated_note": "each GEMV shape alone: the step's weights of that shape, launches independent "
+                             "(four streams), weights read from HBM; the step itself is a dependent chain of "
+                             "192 linears whose per-link latency, not bandwidth, sets its time",
             "launches_per_step": 2 if ms_chain <= ms_calls else layers_count * 6 + 1}
 
 

@@ -29,6 +29,7 @@
 #include <new>
 #include <string>
 #include <tuple>
+#include <type_traits>
 #include <set>
 #include <utility>
 #include <vector>
@@ -836,7 +837,11 @@ __host__ __device__ constexpr int recv_bytes(int m) { return kRows * recv_stride
 // weight streams per SM beat deeper rings); a deep ring is used when the grid
 // is small and each CTA owns more K blocks than two stages hold, so that all
 // of a CTA's weights are requested before it waits for the previous kernel.
-// The split-K exchange buffer (sized by m at launch) follows the barriers.
+// Five deep stages hold the decoder fc2's share (5120 -> 1280 over clusters of
+// 8: five 16 KB tiles per CTA) at ~113 KB, small enough to become resident
+// beside the previous links' CTAs (measured: 6 stages, 142 KB, made the C3
+// step 3.6% slower).  The split-K exchange buffer (sized by m at launch)
+// follows the barriers.
 template <int ST>
 struct Ring {
     static constexpr int kStages = ST;
@@ -849,7 +854,7 @@ struct Ring {
     static_assert((2 * ST + 3) * 8 <= 128, "barrier area");
 };
 constexpr int kShallow = 2;
-constexpr int kDeep = 6;
+constexpr int kDeep = 5;
 static_assert(Ring<kShallow>::kSmemBase + recv_bytes(20) <= 56 * 1024, "four CTAs per SM at the decoder's m");
 static_assert(Ring<kDeep>::kSmemBase + recv_bytes(kAct) <= 227 * 1024, "shared memory budget");
 constexpr int kMaxCluster = 8;
@@ -892,17 +897,6 @@ __device__ __forceinline__ void sum_rows(const float *recv, const float *own, in
         }
         acc[j] = sum;
     }
-}
-
-// The epilogue of the rows sum_rows<S> summed: finish(acc[j], m) per row m.
-template <int S, class Finish>
-__device__ __forceinline__ void finish_rows(const float (&acc)[kAct / 2], int m_count, Finish &finish)
-{
-    const int g = static_cast<int>(threadIdx.x) / (kRows / S);
-#pragma unroll
-    for (int j = 0; j < kAct / S; ++j)
-        if (g + j * S < m_count)
-            finish(acc[j], g + j * S);
 }
 
 template <int KIND, int EPI, int ST>
@@ -1059,34 +1053,55 @@ __global__ void __launch_bounds__(kThreads)
     const float cs = p.w_scales ? act_scale * my_ws : 1.0f;
     const uint64_t neg_scale2 = f2_bits(-p.next_scale, -p.next_scale);
     const uint64_t recip2 = f2_bits(p.next_recip, p.next_recip);
-    auto finish = [&](float acc, int m) {
-        uint32_t z = f2h_rn(acc * cs);
-        if (p.bias)
-            z = hadd_rn(static_cast<uint16_t>(z), my_bias);
-        if (EPI & 1)
-            z = gemm::gelu_fp16x2(z, g_erf_table) & 0xFFFFu;
-        const size_t o = static_cast<size_t>(m) * p.n + my_n;
-        if (p.y)
-            p.y[o] = static_cast<uint16_t>(z);
-        if (p.next_codes)
-            p.next_codes[o] = static_cast<uint8_t>(e4m3x2_quotient(z, neg_scale2, recip2) & 0xFFu);
+    // The epilogue of C values acc[j] (activation row rows(j)): scale, round to
+    // fp16, bias, then GELU on pairs -- every table lookup is issued before any
+    // store, so the lookups share one memory round trip -- then the stores.
+    auto finish = [&](const auto &acc, auto rows, auto count) {
+        constexpr int C = decltype(count)::value;
+        uint32_t z[C];
+#pragma unroll
+        for (int j = 0; j < C; ++j) {
+            z[j] = f2h_rn(acc[j] * cs);
+            if (p.bias)
+                z[j] = hadd_rn(static_cast<uint16_t>(z[j]), my_bias);
+        }
+        if (EPI & 1) {
+#pragma unroll
+            for (int j = 0; j < C; j += 2) {
+                const uint32_t g = gemm::gelu_fp16x2(z[j] | (z[j + 1] << 16), g_erf_table);
+                z[j] = g & 0xFFFFu;
+                z[j + 1] = g >> 16;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < C; ++j) {
+            const int m = rows(j);
+            if (m < p.m) {
+                const size_t o = static_cast<size_t>(m) * p.n + my_n;
+                if (p.y)
+                    p.y[o] = static_cast<uint16_t>(z[j]);
+                if (p.next_codes)
+                    p.next_codes[o] = static_cast<uint8_t>(e4m3x2_quotient(z[j], neg_scale2, recip2) & 0xFFu);
+            }
+        }
     };
     if (S == 1) {
         if (my_n < p.n) {
+            float acc[kAct];
 #pragma unroll
             for (int m = 0; m < kAct; ++m)
-                if (m < p.m)
-                    finish(__uint_as_float(v[m]), m);
+                acc[m] = __uint_as_float(v[m]);
+            finish(acc, [](int j) { return j; }, std::integral_constant<int, kAct>{});
         }
     } else {
         // Split-K exchange.  Each thread stages its row (TMEM lane threadIdx.x)
         // in the ring, idle now that every MMA has completed: row R at float
-        // offset R * stride, so the rows CTA q finishes form one contiguous run.
-        // One thread then copies run q into slot `rank` of CTA q's receive
-        // buffer, one bulk copy per peer, each completing its bytes on the
-        // peer's bar_recv (a few barrier updates instead of one per 16 bytes).
+        // offset R * stride, so the rows a peer finishes form one contiguous run.
+        // Lane 0 of each warp then copies the warp's 32 rows, one bulk copy per
+        // owner (two when S = 8), into slot `rank` of the owner's receive buffer;
+        // each copy completes its bytes on the owner's bar_recv (a few barrier
+        // updates instead of one per 16 bytes, and no CTA-wide barrier first).
         const int rows_per = kRows / S;
-        const uint32_t run_bytes = static_cast<uint32_t>(rows_per * stride * 4);
 #pragma unroll
         for (int i = 0; i < kAct / 4; ++i)
             if (i < nvec)
@@ -1094,17 +1109,24 @@ __global__ void __launch_bounds__(kThreads)
                              make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
         fence_proxy_async_smem(); // the bulk copies (async proxy) read these stores
         cluster_wait();           // every peer's bar_recv is initialised
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            for (int q = 0; q < S; ++q)
-                if (q != rank)
-                    bulk_copy_to_peer(map_to_rank(recv + static_cast<uint32_t>(rank) * run_bytes, static_cast<uint32_t>(q)),
-                                      sbase + static_cast<uint32_t>(q) * run_bytes, run_bytes,
+        __syncwarp();
+        if (lane == 0) {
+            const int r0 = warp * 32;
+            const int span = rows_per < 32 ? rows_per : 32;
+            for (int r = r0; r < r0 + 32; r += span) {
+                const int q = r / rows_per;
+                if (q != rank) {
+                    const uint32_t dst = recv + static_cast<uint32_t>(((rank * rows_per + r % rows_per) * stride) * 4);
+                    bulk_copy_to_peer(map_to_rank(dst, static_cast<uint32_t>(q)),
+                                      sbase + static_cast<uint32_t>(r * stride * 4),
+                                      static_cast<uint32_t>(span * stride * 4),
                                       map_to_rank(bar_recv, static_cast<uint32_t>(q)));
+                }
+            }
         }
         // A bounded wait that gives up sets the error word; the sums still run.
         mbar_wait_cluster(bar_recv, 0, kSiteClusterExchange);
-        __syncwarp();
+        __syncthreads(); // this CTA's own staged rows, written by other warps
         // This CTA has everything it was sent: arrive on the exit barrier, which
         // keeps every CTA's staged runs (the copies' sources) alive until all
         // peers have received theirs.  Every copy into a CTA has completed
@@ -1120,10 +1142,11 @@ __global__ void __launch_bounds__(kThreads)
             case 4: sum_rows<4>(rbuf, own, rank, stride, r_local, p.m, acc); break;
             default: sum_rows<8>(rbuf, own, rank, stride, r_local, p.m, acc); break;
             }
+            const int g = static_cast<int>(threadIdx.x) / rows_per;
             switch (S) {
-            case 2: finish_rows<2>(acc, p.m, finish); break;
-            case 4: finish_rows<4>(acc, p.m, finish); break;
-            default: finish_rows<8>(acc, p.m, finish); break;
+            case 2: finish(acc, [g](int j) { return g + 2 * j; }, std::integral_constant<int, kAct / 2>{}); break;
+            case 4: finish(acc, [g](int j) { return g + 4 * j; }, std::integral_constant<int, kAct / 4>{}); break;
+            default: finish(acc, [g](int j) { return g + 8 * j; }, std::integral_constant<int, kAct / 8>{}); break;
             }
         }
     }
