@@ -292,6 +292,7 @@ struct Cfg {
 struct Params {
     int m, n, k;
     int m_tiles, num_tiles, num_kb;
+    int n_tiles, group_m;    // raster: see tile_coords
     int seg_rows, seg_tiles; // kEpiSeg: rows per segment, tiles per segment
     int kb_per_tap;          // kEpiSeg: K blocks per A map (convolution tap)
     int heads;               // kEpiHeads: H
@@ -371,8 +372,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     using C = Cfg<BN, EPI, kPair>;
     // Segment and first row (within the segment, or of the whole matrix) of this
     // CTA's 128 rows of tile t.
+    // Tile t -> (M tile, N tile).  group_m = 0 walks the tiles column by column
+    // (M fastest).  Otherwise tiles go in groups of group_m M tiles, each group
+    // column by column, so that the waves in flight share a few A row panels and
+    // every panel is reused from L2 by all N tiles instead of being read once per
+    // column (an A operand larger than L2 is otherwise re-read from DRAM for every
+    // column).  A function of t alone: the producer, MMA and epilogue agree.
+    auto tile_coords = [&](int t) {
+        if (p.group_m <= 0)
+            return int2{t % p.m_tiles, t / p.m_tiles};
+        const int per_group = p.group_m * p.n_tiles;
+        const int g = t / per_group;
+        const int first = g * p.group_m;
+        const int rows = min(p.group_m, p.m_tiles - first);
+        const int r = t - g * per_group;
+        return int2{first + r % rows, r / rows};
+    };
     auto tile_rows = [&](int t, uint32_t r) {
-        const int mt = t % p.m_tiles;
+        const int mt = tile_coords(t).x;
         if (C::kSeg)
             return int2{mt / p.seg_tiles, (mt % p.seg_tiles) * C::kTileM + static_cast<int>(r) * kBM};
         return int2{0, mt * C::kTileM + static_cast<int>(r) * kBM};
@@ -486,13 +503,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             };
             for (int kb = 0; kb < pre; ++kb)
-                arm_and_load_b(kb, kb, (tile_first / p.m_tiles) * BN + static_cast<int>(rank) * C::kBRows);
+                arm_and_load_b(kb, kb, tile_coords(tile_first).y * BN + static_cast<int>(rank) * C::kBRows);
             griddepcontrol_wait();
             int issued = 0;
             for (int t = tile_first; ok && t < p.num_tiles; t += tile_step) {
                 // In a pair each CTA loads half of the tile's B rows.
                 const auto rows = tile_rows(t, rank);
-                const int n0 = (t / p.m_tiles) * BN + static_cast<int>(rank) * C::kBRows;
+                const int n0 = tile_coords(t).y * BN + static_cast<int>(rank) * C::kBRows;
                 for (int kb = 0; kb < p.num_kb; ++kb, ++issued) {
                     if (issued < pre) {
                         // Armed with its B tile above: only the activations remain.
@@ -625,7 +642,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const auto rows = tile_rows(t, rank);
             const int seg = rows.x;
             const int m0 = rows.y;
-            const int n0 = (t / p.m_tiles) * BN;
+            const int n0 = tile_coords(t).y * BN;
             const uint32_t a = local & 1;
             const uint32_t acc_ph = (local >> 1) & 1;
             // This warp's columns: lane i holds columns 2(i % 16) and 2(i % 16) + 1 of
@@ -3456,6 +3473,24 @@ cudaError_t launch_gemm_kernel(const CUtensorMap (&maps)[6], const gemm::Params 
     return err != cudaSuccess ? err : cudaGetLastError();
 }
 
+// M tiles per raster group of a plain linear (tile_coords).  Measured on B200:
+// groups of 8 make the encoder's fc2 (A = 123 MB of codes per 16-stream slice,
+// about the size of L2) 4% faster in the C4 forward and fc2 at M = 12000 (61 MB)
+// 1% faster, but the linears whose A fits in L2 comfortably (15-31 MB) 2-3%
+// slower; so only an A operand above 48 MB is grouped.  LFFW_GEMM_GROUP (tuning)
+// forces a group size for every linear (0 = column by column), read once.
+int gemm_group_m(int64_t a_bytes)
+{
+    static const int forced = [] {
+        const char *v = std::getenv("LFFW_GEMM_GROUP");
+        const int g = v ? std::atoi(v) : -1;
+        return g >= 0 && g <= 1024 ? g : -1;
+    }();
+    if (forced >= 0)
+        return forced;
+    return a_bytes > (int64_t{48} << 20) ? 8 : 0;
+}
+
 template <int BN, int EPI, bool kPair>
 cudaError_t run_gemm(const LinearLaunch &L, cudaStream_t stream)
 {
@@ -3481,6 +3516,8 @@ cudaError_t run_gemm(const LinearLaunch &L, cudaStream_t stream)
     p.m_tiles = static_cast<int>((L.m + C::kTileM - 1) / C::kTileM);
     const int n_tiles = static_cast<int>((L.n + BN - 1) / BN);
     p.num_tiles = p.m_tiles * n_tiles;
+    p.n_tiles = n_tiles;
+    p.group_m = gemm_group_m(L.m * L.k * (C::kF16In ? 2 : 1));
     p.num_kb = static_cast<int>((L.k + gemm::kBK - 1) / gemm::kBK);
     p.act_scale = L.act_scale;
     p.act_scale_ptr = L.act_scale_ptr;
