@@ -94,6 +94,8 @@ def parse_args(argv=None):
                         "LayerNorm producer, 'attention' the cross-attention, 'self_attention' the encoder "
                         "self-attention, 'decoder' the C3 step")
     p.add_argument("--layers", type=int, default=32, help="encoder layers (32 is the measured configuration)")
+    p.add_argument("--chunk", type=int, default=None,
+                   help="C4: streams per encoder slice (tuning; default: the Encoder's own)")
     p.add_argument("--profile-window", action="store_true",
                    help="after the warm-up, run one encoder forward (plain launches, no graph) between "
                         "cudaProfilerStart and cudaProfilerStop and exit: the window that "
@@ -960,7 +962,7 @@ def run_c4(args, rank, local_rank, world):
     scales = enc.calibrate(weights, calib_mel)  # identical on every rank: same weights, same two streams
     del calib_mel
     torch.cuda.empty_cache()
-    e = enc.Encoder(weights, scales, streams, device)
+    e = enc.Encoder(weights, scales, streams, device, chunk=args.chunk)
     e.mel.copy_(mel_host)
     stream = torch.cuda.Stream(device)
     with torch.cuda.stream(stream):

@@ -219,18 +219,20 @@ class Encoder:
     lffw_cross_attention reads.  The returned tensors are the plan's own buffers,
     overwritten by the next forward.
 
-    Streams run through the layers in slices of `chunk` streams (default 16) that
-    share one set of activation buffers: a slice's activations stay largely in the
-    126 MB L2 between the kernels that write and read them, while each launch still
-    has enough tiles that its last partial wave is a small part of it.  Measured on
-    the 64-stream forward (one B200): chunk 8 140.3 ms, 16 137.2 ms, 32 139.1 ms,
-    64 145.5 ms, with bit-identical states."""
+    Streams run through the layers in slices of `chunk` streams (default 32) that
+    share one set of activation buffers.  Smaller slices keep more of a slice's
+    activations in the 126 MB L2 between the kernels that write and read them;
+    larger ones give each launch more tiles, so its last partial wave is a smaller
+    part of it.  Measured on the 64-stream forward (one B200, states bit-identical
+    across slice sizes), since the FP8 GEMM walks large-A linears in row-panel
+    groups: chunk 8 132.6-133.1 ms, 16 127.5-127.9 ms, 32 125.4-126.0 ms on one box;
+    32 127.9-128.3 ms and 64 127.9-128.4 ms on another."""
 
     def __init__(self, weights: EncoderWeights, scales: Mapping[str, float], streams: int, device=None,
                  chunk: int | None = None):
         c = weights.config
         self.config, self.weights, self.streams = c, weights, streams
-        self.chunk = max(1, min(streams, chunk if chunk is not None else 16))
+        self.chunk = max(1, min(streams, chunk if chunk is not None else 32))
         self.scales = _scales_for(c, scales)
         device = torch.device(device) if device is not None else weights.positions.device
         d, f, t = c.d_model, c.ffn, c.positions
