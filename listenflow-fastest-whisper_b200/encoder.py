@@ -253,8 +253,13 @@ class Encoder:
         self.kv_codes = empty((m, d), torch.uint8)
         self.cross_kv = empty((2 * c.decoder_layers, streams, c.heads, t, 64))
         self._calls = []
+        self._slices = []  # (first stream, stream count, its launches in _calls)
         for first in range(0, streams, n):
-            self._calls += self._plan(first, min(n, streams - first))
+            count = min(n, streams - first)
+            begin = len(self._calls)
+            self._calls += self._plan(first, count)
+            self._slices.append((first, count, begin, len(self._calls)))
+        self._copy_stream = None
 
     # -- launch plan ---------------------------------------------------------
     def _plan(self, first: int, count: int):
@@ -357,15 +362,55 @@ class Encoder:
         for name, call in self._calls:
             native.check(call(s), name)
 
-    def forward(self, mel: torch.Tensor, stream=None):
+    def forward(self, mel: torch.Tensor, stream=None, states_out: torch.Tensor | None = None):
         """Copies mel (fp32 [streams, mels, frames], device or pinned host) into the
-        plan and runs it; returns (states, cross_kv)."""
+        plan and runs it; returns (states, cross_kv) on the device.
+
+        With `states_out` (fp16 [streams, positions, d_model], pinned host memory)
+        the states are also copied there.  Host copies run on a side stream slice
+        by slice: every slice's log-mel is copied in up front and each slice starts
+        once its own rows have arrived, and a slice's states go out while the next
+        slice computes.  The copies wait for work already on `stream` before they
+        touch the plan's buffers, and `stream` waits for the last copy, so stream
+        order covers both (synchronise `stream` before reading `states_out`)."""
         if tuple(mel.shape) != tuple(self.mel.shape) or mel.dtype != torch.float32:
             raise ValueError(f"mel must be fp32 {tuple(self.mel.shape)}")
+        if states_out is not None and (tuple(states_out.shape) != tuple(self.states.shape)
+                                       or states_out.dtype != torch.float16):
+            raise ValueError(f"states_out must be fp16 {tuple(self.states.shape)}")
         torch_stream = stream if stream is not None else torch.cuda.current_stream(self.mel.device)
-        with torch.cuda.stream(torch_stream):
-            self.mel.copy_(mel, non_blocking=True)
-        self.run(torch_stream)
+        if mel.is_cuda and states_out is None:
+            with torch.cuda.stream(torch_stream):
+                self.mel.copy_(mel, non_blocking=True)
+            self.run(torch_stream)
+            return self.states, self.cross_kv
+        if self._copy_stream is None:
+            self._copy_stream = torch.cuda.Stream(self.mel.device)
+        side = self._copy_stream
+        start = torch.cuda.Event()
+        start.record(torch_stream)
+        side.wait_event(start)
+        arrived = []
+        for first, count, _, _ in self._slices:
+            with torch.cuda.stream(side):
+                self.mel[first:first + count].copy_(mel[first:first + count], non_blocking=True)
+            event = torch.cuda.Event()
+            event.record(side)
+            arrived.append(event)
+        s = fp8._stream(torch_stream)
+        for (first, count, begin, end), event in zip(self._slices, arrived):
+            torch_stream.wait_event(event)
+            for name, call in self._calls[begin:end]:
+                native.check(call(s), name)
+            if states_out is not None:
+                done = torch.cuda.Event()
+                done.record(torch_stream)
+                side.wait_event(done)
+                with torch.cuda.stream(side):
+                    states_out[first:first + count].copy_(self.states[first:first + count], non_blocking=True)
+        finished = torch.cuda.Event()
+        finished.record(side)
+        torch_stream.wait_event(finished)
         return self.states, self.cross_kv
 
     def flops_per_forward(self) -> int:

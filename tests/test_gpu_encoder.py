@@ -438,3 +438,27 @@ def test_encoder_stream_slices_are_bit_identical(small_encoder, enc, native, cud
     assert native.device_error() == 0
     assert torch.equal(states.view(torch.int16), s2.view(torch.int16))
     assert torch.equal(kv.view(torch.int16), kv2.view(torch.int16))
+
+
+def test_encoder_forward_with_host_buffers(small_encoder, enc, native, cuda):
+    """forward() with log-mel in pinned host memory and states copied back to pinned
+    host memory (copies overlapped slice by slice) gives the same bits as the
+    device-resident forward, on two calls in a row."""
+    import torch
+
+    config, ck, weights, scales, mel, mel_d = small_encoder
+    mel3 = torch.cat([mel_d, mel_d[:1].flip(-1).contiguous()])
+    e = enc.Encoder(weights, scales, 3, chunk=2)
+    states, kv = e.forward(mel3)
+    torch.cuda.synchronize()
+    states, kv = states.clone(), kv.clone()
+    mel_host = mel3.cpu().pin_memory()
+    out = torch.empty(tuple(states.shape), dtype=torch.float16).pin_memory()
+    stream = torch.cuda.Stream()
+    for _ in range(2):
+        out.zero_()
+        _, kv2 = e.forward(mel_host, stream, states_out=out)
+        stream.synchronize()
+        assert native.device_error() == 0
+        assert torch.equal(out.view(torch.int16), states.cpu().view(torch.int16))
+        assert torch.equal(kv2.view(torch.int16), kv.view(torch.int16))
