@@ -253,12 +253,16 @@ class Encoder:
         self.kv_codes = empty((m, d), torch.uint8)
         self.cross_kv = empty((2 * c.decoder_layers, streams, c.heads, t, 64))
         self._calls = []
-        self._slices = []  # (first stream, stream count, its launches in _calls)
+        # (first stream, stream count, its launches in _calls, and the end of the
+        # launch that writes its states: the final LayerNorm, before the cross K/V)
+        self._slices = []
         for first in range(0, streams, n):
             count = min(n, streams - first)
             begin = len(self._calls)
-            self._calls += self._plan(first, count)
-            self._slices.append((first, count, begin, len(self._calls)))
+            plan = self._plan(first, count)
+            states_end = begin + max(i for i, (name, _) in enumerate(plan) if name == "lffw_layer_norm") + 1
+            self._calls += plan
+            self._slices.append((first, count, begin, states_end, len(self._calls)))
         self._copy_stream = None
 
     # -- launch plan ---------------------------------------------------------
@@ -369,8 +373,9 @@ class Encoder:
         With `states_out` (fp16 [streams, positions, d_model], pinned host memory)
         the states are also copied there.  Host copies run on a side stream slice
         by slice: every slice's log-mel is copied in up front and each slice starts
-        once its own rows have arrived, and a slice's states go out while the next
-        slice computes.  The copies wait for work already on `stream` before they
+        once its own rows have arrived, and a slice's states go out as soon as its
+        final LayerNorm has written them, while its cross K/V and the next slice
+        run.  The copies wait for work already on `stream` before they
         touch the plan's buffers, and `stream` waits for the last copy, so stream
         order covers both (synchronise `stream` before reading `states_out`)."""
         if tuple(mel.shape) != tuple(self.mel.shape) or mel.dtype != torch.float32:
@@ -391,16 +396,16 @@ class Encoder:
         start.record(torch_stream)
         side.wait_event(start)
         arrived = []
-        for first, count, _, _ in self._slices:
+        for first, count, _, _, _ in self._slices:
             with torch.cuda.stream(side):
                 self.mel[first:first + count].copy_(mel[first:first + count], non_blocking=True)
             event = torch.cuda.Event()
             event.record(side)
             arrived.append(event)
         s = fp8._stream(torch_stream)
-        for (first, count, begin, end), event in zip(self._slices, arrived):
+        for (first, count, begin, states_end, end), event in zip(self._slices, arrived):
             torch_stream.wait_event(event)
-            for name, call in self._calls[begin:end]:
+            for name, call in self._calls[begin:states_end]:
                 native.check(call(s), name)
             if states_out is not None:
                 done = torch.cuda.Event()
@@ -408,6 +413,8 @@ class Encoder:
                 side.wait_event(done)
                 with torch.cuda.stream(side):
                     states_out[first:first + count].copy_(self.states[first:first + count], non_blocking=True)
+            for name, call in self._calls[states_end:end]:
+                native.check(call(s), name)
         finished = torch.cuda.Event()
         finished.record(side)
         torch_stream.wait_event(finished)
